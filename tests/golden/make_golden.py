@@ -1,0 +1,242 @@
+"""Write the golden fixtures of this folder by running the REFERENCE implementation.
+
+    python tests/golden/make_golden.py [--reference /path/to/lngram-decode]
+
+Needs the reference checkout (imported read-only from ``--reference``) and, for the C++
+drafter fixture, ``oracle/_ref`` built by ``python oracle/build.py``.  Inputs come from
+``cases.py`` (seeded numpy); each ``.npz`` stores small inputs and the reference's outputs.
+The fixtures are committed; the tests replay them without the reference present.
+"""
+
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parents[1]
+sys.path.insert(0, str(REPO))
+
+from tests.golden import cases  # noqa: E402
+
+
+def _t(a, dtype=None):
+    import torch
+
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    return t if dtype is None else t.to(dtype)
+
+
+def reference_memory(case: str):
+    """A reference ``LngramMemory`` (``ffnmem/memory/wrapper.py:50``) loaded with ``cases`` weights."""
+    import torch
+    from ffnmem.memory.wrapper import LngramMemory
+
+    c = cases.MEMORY_CASES[case]
+    cfg = {"routes": c["routes"], "mem_dim": c["mem_dim"], "kv_heads": c["kv_heads"], "q_heads": c["q_heads"],
+           "head_dim": c["head_dim"], "ngrams": list(c["ngrams"]), "bits_per_route": c["bits"],
+           "execution_mode": "full"}
+    mem = LngramMemory(c["d"], cfg, init_std=0.02, norm_eps=1e-5).eval()
+    p = cases.memory_params(case)
+    state = {("router.weight" if k == "router.weight" else "module." + k): _t(v) for k, v in p.items()}
+    mem.load_state_dict(state, strict=True)
+    return mem
+
+
+def write_memory_case(case: str) -> None:
+    import torch
+
+    c = cases.MEMORY_CASES[case]
+    mem = reference_memory(case)
+    m = mem.module
+    inp = cases.memory_inputs(case)
+    h, x = _t(inp["h"]), _t(inp["x"])
+    seg = _t(inp["segment_ids"]) if "segment_ids" in inp else None
+    valid = _t(inp["valid_tokens"]) if "valid_tokens" in inp else None
+    out = {}
+    with torch.no_grad():
+        logits = mem.route_logits(x)
+        codes = m.quantize_route_logits(logits)
+        out["logits"] = logits.numpy()
+        out["codes"] = codes.numpy().astype(np.uint8)
+        out["output_wrapper"] = mem(h, x).numpy()                        # LngramMemory.forward
+        tokens = m._lookup_route_chunk(codes, None, 0, m.num_routes, seg, valid)
+        q = m._project_query(h)
+        key, value = m._project_memory(tokens)
+        head = m._manual_gqa(q, key, value)
+        out["output"] = m(h, codes, segment_ids=seg, valid_tokens=valid).numpy()
+        out["head"] = head.numpy()
+        out["query"] = q.numpy()
+        big = tokens.numel() > 500_000
+        if big:
+            # Row indices (bit-exact addressing) and per-token sums stand in for the 3.3 MB tokens.
+            from ffnmem.memory.lngram_v2 import _aligned_ngram_address
+
+            for n in m.ngrams:
+                a = _aligned_ngram_address(codes.to(torch.int64), n, m.bits_per_route)
+                out[f"rows_{n}"] = (a + torch.arange(m.num_routes).view(1, 1, -1) * (m.alphabet_size ** n)).numpy()
+            out["token_sums"] = tokens.double().sum(-1).numpy()
+            out["key_sums"] = key.double().sum(-1).numpy()
+        else:
+            out["tokens"] = tokens.numpy()
+            out["key"] = key.numpy()
+            out["value"] = value.numpy()
+        if c.get("stream_chunk"):
+            m.execution_mode = "streaming"
+            m.stream_route_chunk_size = int(c["stream_chunk"])
+            out["output_streaming"] = m(h, codes, segment_ids=seg, valid_tokens=valid).numpy()
+            m.execution_mode = "full"
+        if c.get("bf16"):
+            mb = m.to(torch.bfloat16)
+            out["output_bf16_module"] = mb(h.to(torch.bfloat16), codes).float().numpy()
+    for k in ("ids", "segment_ids", "valid_tokens"):
+        if k in inp:
+            out["in_" + k] = inp[k]
+    if inp["h"].size <= 200_000:
+        out["in_h"] = inp["h"]
+        out["in_x"] = inp["x"]
+    np.savez_compressed(HERE / f"memory_{case}.npz", **out)
+    print(f"memory_{case}.npz", {k: v.shape for k, v in out.items()})
+
+
+def write_seams() -> None:
+    """Decode seam (``ffnmem/infer.py:152-182``) and tree block (``drafting/tree.py:178-195``) on the
+    ``tiny_multi`` memory, each against the linear full forward of the same positions."""
+    import torch
+    from drafting.tree import tree_ngram_codes, tree_path, tree_route_tokens, tree_slots
+
+    case = "tiny_multi"
+    mem = reference_memory(case)
+    m = mem.module
+    B, L, n = 2, 11, len(cases.TREE_PARENT)
+    s = cases.seam_inputs(case, B, L, n)
+    hp, hn, cp, cn = (_t(s[k]) for k in ("h_prefix", "h_new", "codes_prefix", "codes_new"))
+    out = {k: v for k, v in s.items()}
+    hist = m.route_history_length
+    lp = m.short_conv.left_padding
+    with torch.no_grad():
+        # decode seam: prefix then n new positions == full forward over L + n
+        full = m(torch.cat((hp, hn), 1), torch.cat((cp, cn), 1))
+        out["step_full"] = full[:, L:].numpy()
+        # reference memory_step semantics on the context window [L-hist, L+n)
+        ctx = torch.cat((cp, cn), 1)[:, max(0, L - hist):]
+        tokens = m._lookup_route_chunk(ctx, None, 0, m.num_routes, None, None, target_length=n)
+        key, value = m._project_memory(tokens)
+        head = m._manual_gqa(m._project_query(hn), key, value)
+        mixed = m.readout_o_proj(head.reshape(B, n, -1))
+        pre = m.readout_o_proj(m._manual_gqa(m._project_query(hp), *m._project_memory(
+            m._lookup_route_chunk(cp, None, 0, m.num_routes, None, None))).reshape(B, L, -1))
+        conv_cache = m.short_conv.norm(pre)
+        window = torch.cat((conv_cache, m.short_conv.norm(mixed)), 1)[:, max(0, L - lp):]
+        if window.shape[1] < lp + n:
+            window = torch.nn.functional.pad(window, (0, 0, lp + n - window.shape[1], 0))
+        conv_out = m.short_conv.act(m.short_conv.conv(window.transpose(1, 2))).transpose(1, 2)
+        out["step_output"] = (mixed + conv_out).numpy()
+        out["conv_cache"] = conv_cache.numpy()
+        # tree block, nodes = TREE_PARENT; reference pieces composed as in tree.py:178-195
+        parent = cases.TREE_PARENT
+        ctxw, valid = tree_ngram_codes(parent, cn, cp[:, max(0, L - hist):L], hist)
+        rt = tree_route_tokens(m, ctxw, valid)
+        key, value = m._project_memory(rt)
+        head = m._manual_gqa(m._project_query(hn), key, value)
+        mixed = m.readout_o_proj(head.reshape(B, n, -1))
+        ci = torch.cat((conv_cache, m.short_conv.norm(mixed)), 1)
+        idx, ok = tree_slots(parent, L, lp)
+        window = ci[:, idx] * ok[None, :, :, None].to(ci.dtype)
+        conv_out = m.short_conv.act(m.short_conv.conv(window.reshape(B * n, lp + 1, -1).transpose(1, 2)))
+        out["tree_output"] = (mixed + conv_out.transpose(1, 2).reshape(B, n, -1)).numpy()
+        out["tree_ctx"] = ctxw.numpy()
+        out["tree_valid"] = valid.numpy()
+        # linearised per-path reference: full forward over prefix + path, last position
+        lin = []
+        for i in range(n):
+            path = tree_path(parent, i)
+            seq_h = torch.cat((hp, hn[:, path]), 1)
+            seq_c = torch.cat((cp, cn[:, path]), 1)
+            lin.append(m(seq_h, seq_c)[:, -1])
+        out["tree_linear"] = torch.stack(lin, 1).numpy()
+        # the reference's own ancestor-window KAT (tests/test_live_tree.py:30-41)
+        kc = torch.tensor([0, 10, 20, 30, 40, 50]).view(1, 6, 1)
+        kh = torch.tensor([100, 101]).view(1, 2, 1)
+        kctx, kok = tree_ngram_codes(cases.KAT_PARENT, kc, kh, 2)
+        out["kat_ctx_hist"] = kctx[0, :, :, 0].numpy()
+        kctx, kok = tree_ngram_codes(cases.KAT_PARENT, kc, None, 2)
+        out["kat_ctx_nohist"] = kctx[0, :, :, 0].numpy()
+        out["kat_ok_nohist"] = kok.numpy()
+    np.savez_compressed(HERE / "seams_tiny_multi.npz", **out)
+    print("seams_tiny_multi.npz", {k: v.shape for k, v in out.items()})
+
+
+def write_draft_case(case: str, n_trace: int, with_cpp: bool) -> None:
+    from drafting.cpu_drafter import RefDrafter
+    from drafting.export_drafter import Bundle
+
+    config, arrays = cases.draft_bundle(case)
+    toks = cases.draft_tokens(case, n_trace)
+    out = {}
+    ref = RefDrafter(Bundle(config, arrays, {}))
+    c, ids, lg = ref.trace(toks)
+    out["trace_codes"] = c
+    k = 8
+    top = np.argsort(-lg, axis=1, kind="stable")[:, :k]
+    out["trace_top_ids"] = np.take_along_axis(ids, top, 1)
+    out["trace_top_logits"] = np.take_along_axis(lg, top, 1)
+    out["trace_logit_sums"] = lg.astype(np.float64).sum(1)
+    if lg.size <= 400_000:
+        out["trace_logits"] = lg
+    prefix = toks[: n_trace // 2]
+    ref.reset()
+    ref.commit(prefix)
+    d = ref.draft(4, last_codes=True)
+    out["draft_tokens"], out["draft_ids"], out["draft_logits"], out["draft_codes"] = (
+        np.asarray(d.tokens), d.topk_ids, d.topk_logits, d.codes)
+    hyp = toks[n_trace // 2: n_trace // 2 + 3]
+    d = ref.draft(3, hyp=hyp)
+    out["hyp_tokens"], out["hyp_ids"], out["hyp_logits"], out["hyp_codes"] = (
+        np.asarray(d.tokens), d.topk_ids, d.topk_logits, d.codes)
+    if with_cpp:
+        sys.path.insert(0, str(REPO))
+        from oracle.build import load_reference_drafter
+
+        ext = load_reference_drafter()
+        if ext is not None:
+            from drafting.cpu_drafter import CppDrafter
+            import drafting.cpu_drafter as cd
+
+            cd._EXT = ext
+            cpp = CppDrafter(Bundle(config, arrays, {}), threads=os.cpu_count() or 1)
+            cc, cids, clg = cpp.trace(toks, codes=c)
+            out["cpp_trace_top_logits"] = np.take_along_axis(clg, top, 1)
+            cc2, _, _ = cpp.trace(toks)
+            out["cpp_code_mismatch"] = np.asarray((cc2 != c).mean())
+    out["tokens"] = np.asarray(toks)
+    np.savez_compressed(HERE / f"draft_{case}.npz", **out)
+    print(f"draft_{case}.npz", {k: np.shape(v) for k, v in out.items()})
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--reference", default=os.environ.get("LNGRAM_REFERENCE", "/root/reference"))
+    ap.add_argument("--only", nargs="*", default=None)
+    args = ap.parse_args(argv)
+    sys.path.insert(0, args.reference)
+    import torch
+
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    todo = args.only or ["memory", "seams", "draft"]
+    if "memory" in todo:
+        for case in cases.MEMORY_CASES:
+            write_memory_case(case)
+    if "seams" in todo:
+        write_seams()
+    if "draft" in todo:
+        write_draft_case("tiny", 60, with_cpp=True)
+        write_draft_case("sdb", 24, with_cpp=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,12 @@
+"""lngram_b200: the Lngram v2 route n-gram memory lookup on B200 (sm_100a).
+
+A drop-in, inference-only replacement for the reference's memory modules
+(``ffnmem/memory/lngram_v2.py``, ``ffnmem/memory/wrapper.py``) and its per-token drafter
+(``drafting/cpu/drafter.cpp``, ``drafting/cpu_drafter.py``), backed by hand-written CUDA kernels
+behind the C ABI of ``include/lngram_b200.h``.  There is no CPU fallback.
+"""
+
+from . import _lib
+from .memory import LngramMemory, RouteNgramMemoryV2
+
+__all__ = ["LngramMemory", "RouteNgramMemoryV2", "_lib"]

@@ -1,0 +1,463 @@
+// Fused gather + sink attention over routes (folded readout core).
+//
+// Reference math (ffnmem/memory/lngram_v2.py): route tokens of _lookup_route_chunk (:1047-1113),
+// RMSNorm + kv_proj of _project_memory (:1120-1131), grouped scores * HD^-1/2 and the sink
+// probabilities of _real_route_probabilities / _manual_gqa (:1877-1920), in the online (route
+// chunk) form of _streaming_gqa (:1944-2070): the running state starts at (max = b0, sum = 1,
+// value = 0), i.e. the zero-value sink, and each chunk of routes updates it.
+//
+// Folded form: with qa = the folded query of the item (w_qk . h, see lng_fold_readout) the score of
+// route r is qscale * rms(tok_r)^-1 * (qa . tok_r) and the output is u = sum_r p_r rms(tok_r)^-1 tok_r,
+// so the tokens are read once, straight from the tables, and never projected.  A route whose
+// n-gram window is invalid has a zero token and still takes part with score 0, exactly as the
+// reference's zero rows do.
+#pragma once
+
+#include <type_traits>
+
+#include "address.cuh"
+
+namespace lng {
+
+struct AttendParams {
+  TableSet ts;
+  CodeSource src;
+  int64_t M;
+  int64_t route_start, route_end;
+  int qh;          // query heads
+  float eps;
+  float sink;      // b0
+  const void* qa;  // [M, qh, Dt]
+  const float* qscale;
+  void* u;         // [M, qh, Dt]
+  int partial;
+  float* m_out;
+  float* l_out;
+};
+
+// ------------------------------------------------------------------ generic CUDA-core version
+// One CTA per item (grid-stride), chunks of ATT_C routes.  Any Dt / heads / table dtype.
+constexpr int ATT_C = 32;
+
+template <typename CodeT, typename TabT, typename QT, typename UT>
+__global__ void __launch_bounds__(128) attend_simt_kernel(AttendParams p) {
+  extern __shared__ float sm[];
+  const int Dt = p.ts.n_orders * int(p.ts.mem_dim);
+  const int QH = p.qh;
+  float* qa = sm;                       // [QH, Dt]
+  float* U = qa + QH * Dt;              // [QH, Dt]
+  float* tok = U + QH * Dt;             // [C, Dt]
+  float* rx = tok + ATT_C * Dt;         // [C]
+  float* sc = rx + ATT_C;               // [QH, C]
+  float* mrow = sc + QH * ATT_C;        // [QH]
+  float* lrow = mrow + QH;              // [QH]
+  float* alpha = lrow + QH;             // [QH]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const bool sink_in = !p.partial || p.route_start == 0;
+
+  for (int64_t item = blockIdx.x; item < p.M; item += gridDim.x) {
+    const float qs = p.qscale ? p.qscale[item] : 1.f;
+    const QT* qg = static_cast<const QT*>(p.qa) + item * QH * Dt;
+    for (int e = threadIdx.x; e < QH * Dt; e += blockDim.x) {
+      qa[e] = to_f32(qg[e]);
+      U[e] = 0.f;
+    }
+    for (int q = threadIdx.x; q < QH; q += blockDim.x) {
+      mrow[q] = sink_in ? p.sink : -INFINITY;
+      lrow[q] = sink_in ? 1.f : 0.f;
+    }
+    __syncthreads();
+    for (int64_t c0 = p.route_start; c0 < p.route_end; c0 += ATT_C) {
+      // gather the chunk's tokens (fp32) and their inverse RMS
+      for (int rl = warp; rl < ATT_C; rl += nwarps) {
+        const int64_t r = c0 + rl;
+        float ss = 0.f;
+        for (int o = 0; o < p.ts.n_orders; ++o) {
+          int64_t row = -1;
+          if (r < p.route_end) row = ngram_row<CodeT>(p.src, item, r, p.ts.order[o], p.ts.bits);
+          const TabT* s = static_cast<const TabT*>(p.ts.tab[o]) + (row < 0 ? 0 : row) * p.ts.mem_dim;
+          for (int j = lane; j < p.ts.mem_dim; j += 32) {
+            const float v = row < 0 ? 0.f : to_f32(s[j]);
+            tok[rl * Dt + o * p.ts.mem_dim + j] = v;
+            ss += v * v;
+          }
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) rx[rl] = rsqrtf(ss / float(Dt) + p.eps);
+      }
+      __syncthreads();
+      for (int e = threadIdx.x; e < QH * ATT_C; e += blockDim.x) {
+        const int q = e / ATT_C, rl = e % ATT_C;
+        float s = -INFINITY;
+        if (c0 + rl < p.route_end) {
+          float acc = 0.f;
+          for (int k = 0; k < Dt; ++k) acc = fmaf(qa[q * Dt + k], tok[rl * Dt + k], acc);
+          s = acc * qs * rx[rl];
+        }
+        sc[e] = s;
+      }
+      __syncthreads();
+      for (int q = threadIdx.x; q < QH; q += blockDim.x) {
+        float mx = mrow[q];
+        for (int rl = 0; rl < ATT_C; ++rl) mx = fmaxf(mx, sc[q * ATT_C + rl]);
+        const float a = expf(mrow[q] - mx);
+        float sum = 0.f;
+        for (int rl = 0; rl < ATT_C; ++rl) {
+          const float e = expf(sc[q * ATT_C + rl] - mx);
+          sc[q * ATT_C + rl] = e * rx[rl];
+          sum += e;
+        }
+        lrow[q] = lrow[q] * a + sum;
+        mrow[q] = mx;
+        alpha[q] = a;
+      }
+      __syncthreads();
+      for (int e = threadIdx.x; e < QH * Dt; e += blockDim.x) {
+        const int q = e / Dt, k = e % Dt;
+        float acc = U[e] * alpha[q];
+        for (int rl = 0; rl < ATT_C; ++rl) acc = fmaf(sc[q * ATT_C + rl], tok[rl * Dt + k], acc);
+        U[e] = acc;
+      }
+      __syncthreads();
+    }
+    if (p.partial) {
+      float* uo = static_cast<float*>(p.u) + item * QH * Dt;
+      for (int e = threadIdx.x; e < QH * Dt; e += blockDim.x) uo[e] = U[e];
+      for (int q = threadIdx.x; q < QH; q += blockDim.x) {
+        p.m_out[item * QH + q] = mrow[q];
+        p.l_out[item * QH + q] = lrow[q];
+      }
+    } else {
+      UT* uo = static_cast<UT*>(p.u) + item * QH * Dt;
+      for (int e = threadIdx.x; e < QH * Dt; e += blockDim.x) {
+        const int q = e / Dt;
+        uo[e] = from_f32<UT>(U[e] / fmaxf(lrow[q], 1.17549435e-38f));
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// ------------------------------------------------------------------ tensor-core version (bf16 / f16)
+// One warp per item; routes in chunks of 32 streamed through a per-warp ring of shared-memory
+// stages by bulk (TMA-engine) copies, one 16-byte-aligned row copy per (route, order).  Scores
+// (16 x 32 per chunk) and the weighted row sum (16 x Dt) are mma.sync m16n8k16 products with fp32
+// accumulation: the per-item products are 16 x 32 x Dt, below the 64-row minimum of a tcgen05 MMA,
+// and every item has its own B operand, so the warp-level MMA is the fitting unit here.
+template <typename T>
+struct MmaType;
+template <>
+struct MmaType<__nv_bfloat16> {
+  static constexpr const char* name = "bf16";
+};
+template <>
+struct MmaType<__half> {
+  static constexpr const char* name = "f16";
+};
+
+__device__ __forceinline__ uint32_t pack2(float lo, float hi, __nv_bfloat16*) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+__device__ __forceinline__ uint32_t pack2(float lo, float hi, __half*) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+template <typename T>
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1);
+template <>
+__device__ __forceinline__ void mma16816<__nv_bfloat16>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                                        uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+template <>
+__device__ __forceinline__ void mma16816<__half>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2_t(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+template <int DT>
+struct AttendMmaCfg {
+  static constexpr int C = 32;                 // routes per chunk (= lanes: one route per lane)
+  static constexpr int KT = (DT + 15) / 16;    // k16 steps of the score product
+  static constexpr int NTU = DT / 8;           // n8 tiles of the weighted row sum
+  static constexpr int ROWB = DT * 2;          // bytes per token row in shared memory
+  static constexpr int STAGE_BYTES = C * ROWB + 32;  // + zero pad read by the last k-step
+};
+
+template <typename CodeT, typename T, int DT, int WARPS, int STAGES>
+__global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) {
+  using Cfg = AttendMmaCfg<DT>;
+  constexpr int C = Cfg::C, KT = Cfg::KT, NTU = Cfg::NTU, ROWB = Cfg::ROWB, SB = Cfg::STAGE_BYTES;
+  static_assert(DT % 8 == 0, "route token width must be a multiple of 8");
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  unsigned char* stage_base = smem_raw + size_t(warp) * STAGES * SB;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw + size_t(WARPS) * STAGES * SB) + warp * STAGES;
+
+  const int64_t nroutes = p.route_end - p.route_start;
+  const int64_t nch = (nroutes + C - 1) / C;
+  const int64_t gwarp = int64_t(blockIdx.x) * WARPS + warp;
+  const int64_t nwarps = int64_t(gridDim.x) * WARPS;
+  const int64_t my_items = gwarp < p.M ? (p.M - 1 - gwarp) / nwarps + 1 : 0;
+  const int64_t jobs = my_items * nch;
+  const bool sink_in = !p.partial || p.route_start == 0;
+  const int mem_dim = int(p.ts.mem_dim);
+
+  if (lane == 0) {
+    for (int s = 0; s < STAGES; ++s) mbar_init(&bars[s], 32);
+    fence_mbar_init();
+  }
+  // zero the pad after every stage (read by the last score k-step for rows near the end)
+  for (int s = 0; s < STAGES; ++s)
+    if (lane < 8) reinterpret_cast<uint32_t*>(stage_base + s * SB + C * ROWB)[lane] = 0u;
+  __syncwarp();
+
+  // issue the gather of job j into its stage: lane = route within the chunk
+  auto issue = [&](int64_t j) {
+    const int s = int(j % STAGES);
+    const int64_t item = gwarp + (j / nch) * nwarps;
+    const int64_t r = p.route_start + (j % nch) * C + lane;
+    unsigned char* row_smem = stage_base + s * SB + lane * ROWB;
+    int64_t rows[LNG_MAX_ORDERS];
+    uint32_t bytes = 0;
+    for (int o = 0; o < p.ts.n_orders; ++o) {
+      rows[o] = r < p.route_end ? ngram_row<CodeT>(p.src, item, r, p.ts.order[o], p.ts.bits) : -1;
+      if (rows[o] >= 0) {
+        bytes += uint32_t(mem_dim * 2);
+      } else {
+        uint4* z = reinterpret_cast<uint4*>(row_smem + o * mem_dim * 2);
+        for (int v = 0; v < mem_dim * 2 / 16; ++v) z[v] = make_uint4(0, 0, 0, 0);
+      }
+    }
+    fence_proxy_async_smem();
+    mbar_arrive_expect_tx(&bars[s], bytes);
+    for (int o = 0; o < p.ts.n_orders; ++o) {
+      if (rows[o] >= 0) {
+        const unsigned char* src = static_cast<const unsigned char*>(p.ts.tab[o]) + rows[o] * int64_t(mem_dim) * 2;
+        bulk_g2s(row_smem + o * mem_dim * 2, src, uint32_t(mem_dim * 2), &bars[s]);
+      }
+    }
+  };
+
+  for (int64_t j = 0; j < STAGES - 1 && j < jobs; ++j) issue(j);
+
+  uint32_t qa_frag[KT][4];
+  float uacc[NTU][4];
+  float m_r[2], l_r[2];
+  float qs = 1.f;
+  const int g = lane >> 2, t4 = lane & 3;
+  T* tag = nullptr;
+
+  for (int64_t j = 0; j < jobs; ++j) {
+    if (j + STAGES - 1 < jobs) issue(j + STAGES - 1);
+    const int s = int(j % STAGES);
+    const int64_t item = gwarp + (j / nch) * nwarps;
+    const int64_t chunk = j % nch;
+    if (chunk == 0) {
+      // new item: its folded query as A fragments (rows = heads, k = token dims), zero padded
+      const T* qg = static_cast<const T*>(p.qa) + item * int64_t(p.qh) * DT;
+#pragma unroll
+      for (int kt = 0; kt < KT; ++kt) {
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const int row = g + ((h & 1) ? 8 : 0);
+          const int col = kt * 16 + t4 * 2 + ((h & 2) ? 8 : 0);
+          uint32_t v = 0u;
+          if (row < p.qh && col < DT) v = *reinterpret_cast<const uint32_t*>(qg + row * DT + col);
+          qa_frag[kt][h] = v;
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < NTU; ++nt) uacc[nt][0] = uacc[nt][1] = uacc[nt][2] = uacc[nt][3] = 0.f;
+      m_r[0] = m_r[1] = sink_in ? p.sink : -INFINITY;
+      l_r[0] = l_r[1] = 0.f;  // per-thread partial sums; the sink's 1 is added at the end
+      qs = p.qscale ? p.qscale[item] : 1.f;
+    }
+    const bool landed = mbar_wait_bounded(&bars[s], uint32_t((j / STAGES) & 1), &g_error_word, DEV_ERR_WAIT_TIMEOUT);
+    if (!__all_sync(0xffffffffu, landed)) return;
+    const unsigned char* st = stage_base + s * SB;
+    const uint32_t st_addr = smem_addr(st);
+
+    // inverse RMS of this lane's route token (row = lane)
+    float rxl;
+    {
+      const uint4* rowv = reinterpret_cast<const uint4*>(st + lane * ROWB);
+      float ss = 0.f;
+#pragma unroll
+      for (int v = 0; v < DT / 8; ++v) {
+        const uint4 w = rowv[v];
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          float lo, hi;
+          if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+            lo = __uint_as_float(ws[h] << 16);
+            hi = __uint_as_float(ws[h] & 0xffff0000u);
+          } else {
+            __half2 h2 = *reinterpret_cast<const __half2*>(&ws[h]);
+            float2 f = __half22float2(h2);
+            lo = f.x;
+            hi = f.y;
+          }
+          ss = fmaf(lo, lo, ss);
+          ss = fmaf(hi, hi, ss);
+        }
+      }
+      rxl = rsqrtf(ss / float(DT) + p.eps);
+    }
+
+    // scores S[16 heads x 32 routes] = qa . tok^T
+    float sacc[4][4];
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
+#pragma unroll
+    for (int kt = 0; kt < KT; ++kt) {
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        // B fragment: rows = routes nt*8..+7, k = kt*16..+15 (two 8x8 matrices)
+        const int rrow = nt * 8 + (lane & 7);
+        const int kcol = kt * 16 + ((lane >> 3) & 1) * 8;
+        uint32_t b0, b1;
+        ldsm_x2(st_addr + rrow * ROWB + kcol * 2, b0, b1);
+        mma16816<T>(sacc[nt], qa_frag[kt], b0, b1);
+      }
+    }
+
+    // online softmax update with the sink seed
+    const int64_t rbase = p.route_start + chunk * C;
+    float mx[2] = {m_r[0], m_r[1]};
+    float sv[4][4];
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const int col = nt * 8 + t4 * 2 + (h & 1);
+        const float rxc = __shfl_sync(0xffffffffu, rxl, col);
+        float v = sacc[nt][h] * qs * rxc;
+        if (rbase + col >= p.route_end) v = -INFINITY;
+        sv[nt][h] = v;
+        mx[h >> 1] = fmaxf(mx[h >> 1], v);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 1));
+      mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 2));
+    }
+    float alpha[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      alpha[i] = expf(m_r[i] - mx[i]);
+      m_r[i] = mx[i];
+      l_r[i] *= alpha[i];
+    }
+    uint32_t pa[2][4];  // P' as A fragments of the two k16 steps
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      float e[4];
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const int col = nt * 8 + t4 * 2 + (h & 1);
+        const float rxc = __shfl_sync(0xffffffffu, rxl, col);
+        const float ex = expf(sv[nt][h] - m_r[h >> 1]);
+        l_r[h >> 1] += ex;
+        e[h] = ex * rxc;
+      }
+      pa[nt >> 1][(nt & 1) * 2 + 0] = pack2(e[0], e[1], tag);
+      pa[nt >> 1][(nt & 1) * 2 + 1] = pack2(e[2], e[3], tag);
+    }
+#pragma unroll
+    for (int nt = 0; nt < NTU; ++nt) {
+      uacc[nt][0] *= alpha[0];
+      uacc[nt][1] *= alpha[0];
+      uacc[nt][2] *= alpha[1];
+      uacc[nt][3] *= alpha[1];
+    }
+    // u += P' . tok   (B = tok rows as [k = route][n = dim], loaded transposed)
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks) {
+      const int rrow = ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+      for (int nt = 0; nt + 1 < NTU; nt += 2) {
+        const int dcol = (nt + (lane >> 4)) * 8;
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(st_addr + rrow * ROWB + dcol * 2, b0, b1, b2, b3);
+        mma16816<T>(uacc[nt], pa[ks], b0, b1);
+        mma16816<T>(uacc[nt + 1], pa[ks], b2, b3);
+      }
+      if (NTU & 1) {
+        uint32_t b0, b1;
+        ldsm_x2_t(st_addr + rrow * ROWB + (NTU - 1) * 8 * 2, b0, b1);
+        mma16816<T>(uacc[NTU - 1], pa[ks], b0, b1);
+      }
+    }
+    __syncwarp();
+
+    if (chunk == nch - 1) {
+      float l[2];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        l[i] = l_r[i];
+        l[i] += __shfl_xor_sync(0xffffffffu, l[i], 1);
+        l[i] += __shfl_xor_sync(0xffffffffu, l[i], 2);
+        if (sink_in) l[i] += expf(p.sink - m_r[i]);  // the sink's seed 1, rescaled to the final max
+      }
+      const int64_t obase = item * int64_t(p.qh) * DT;
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int row = g + i * 8;
+        if (row >= p.qh) continue;
+        if (p.partial) {
+          float* uo = static_cast<float*>(p.u) + obase + row * DT;
+#pragma unroll
+          for (int nt = 0; nt < NTU; ++nt) {
+            *reinterpret_cast<float2*>(uo + nt * 8 + t4 * 2) = make_float2(uacc[nt][i * 2], uacc[nt][i * 2 + 1]);
+          }
+          if (t4 == 0) {
+            p.m_out[item * p.qh + row] = m_r[i];
+            p.l_out[item * p.qh + row] = l[i];
+          }
+        } else {
+          const float inv = 1.f / fmaxf(l[i], 1.17549435e-38f);
+          T* uo = static_cast<T*>(p.u) + obase + row * DT;
+#pragma unroll
+          for (int nt = 0; nt < NTU; ++nt) {
+            *reinterpret_cast<uint32_t*>(uo + nt * 8 + t4 * 2) =
+                pack2(uacc[nt][i * 2] * inv, uacc[nt][i * 2 + 1] * inv, tag);
+          }
+        }
+      }
+    }
+  }
+}
+
+}  // namespace lng

@@ -1,0 +1,703 @@
+// lngram_b200: the C ABI of include/lngram_b200.h (one translation unit, so every kernel shares
+// the device error word and inlines the addressing helpers).
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "address.cuh"
+#include "attend.cuh"
+#include "gemm_simt.cuh"
+#include "gemm_tc.cuh"
+#include "lookup.cuh"
+#include "router.cuh"
+#include "rowops.cuh"
+#include "topk.cuh"
+
+namespace lng {
+
+static thread_local std::string t_last_error;
+
+void set_error(const std::string& msg) { t_last_error = msg; }
+int fail(int status, const std::string& msg) {
+  t_last_error = msg;
+  return status;
+}
+int cuda_status(cudaError_t e, const char* what) {
+  t_last_error = std::string(what) + ": " + cudaGetErrorString(e);
+  return LNG_ERR_CUDA;
+}
+
+int num_sms() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+  return n;
+}
+
+static int grid_for(int64_t work, int threads, int per_sm = 8) {
+  const int64_t want = ceil_div(std::max<int64_t>(work, 1), threads);
+  return int(std::max<int64_t>(1, std::min<int64_t>(want, int64_t(num_sms()) * per_sm)));
+}
+
+static cudaStream_t S(lng_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+static int check_tables(const lng_tables* t) {
+  LNG_REQUIRE(t != nullptr, "tables descriptor is NULL");
+  LNG_REQUIRE(t->n_orders >= 1 && t->n_orders <= LNG_MAX_ORDERS, "n_orders must be in [1, 4]");
+  LNG_REQUIRE(t->bits >= 1 && t->bits <= 16, "bits_per_route must be in [1, 16]");
+  LNG_REQUIRE(t->num_routes >= 1 && t->memory_dim >= 1, "num_routes and memory_dim must be positive");
+  LNG_REQUIRE(t->table_dtype == LNG_F32 || t->table_dtype == LNG_BF16 || t->table_dtype == LNG_F16,
+              "table dtype must be f32, bf16 or f16");
+  for (int o = 0; o < t->n_orders; ++o) {
+    LNG_REQUIRE(t->tables[o] != nullptr, "table pointer is NULL");
+    LNG_REQUIRE(t->orders[o] >= 1 && int64_t(t->bits) * t->orders[o] <= 40, "order * bits must be in [1, 40]");
+    if (o) LNG_REQUIRE(t->orders[o] > t->orders[o - 1], "orders must be ascending and distinct");
+  }
+  return LNG_OK;
+}
+
+static TableSet table_set(const lng_tables* t) {
+  TableSet ts{};
+  for (int o = 0; o < t->n_orders; ++o) {
+    ts.tab[o] = t->tables[o];
+    ts.order[o] = t->orders[o];
+  }
+  ts.n_orders = t->n_orders;
+  ts.bits = t->bits;
+  ts.num_routes = t->num_routes;
+  ts.mem_dim = t->memory_dim;
+  return ts;
+}
+
+static int max_order(const lng_tables* t) { return t->orders[t->n_orders - 1]; }
+
+}  // namespace lng
+
+using namespace lng;
+
+// ====================================================================== basics
+extern "C" int lng_abi_version(void) { return 1; }
+extern "C" const char* lng_last_error(void) { return t_last_error.c_str(); }
+
+extern "C" int lng_device_ok(void) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return 0;
+  return prop.major == 10 ? 1 : 0;
+}
+
+extern "C" int lng_device_error(int clear) {
+  unsigned int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_error_word, sizeof(v)) != cudaSuccess) return -1;
+  if (clear && v) {
+    const unsigned int z = 0;
+    cudaMemcpyToSymbol(g_error_word, &z, sizeof(z));
+  }
+  return int(v);
+}
+
+// ====================================================================== router
+extern "C" int lng_quantize_route_logits(const float* logits, int64_t n, int64_t routes, int32_t bits, void* codes,
+                                         int32_t codes_dtype, lng_stream_t stream) {
+  LNG_REQUIRE(n >= 0 && routes > 0, "bad shape");
+  LNG_REQUIRE(bits >= 1 && bits <= 30, "bits_per_route must be in [1, 30]");
+  LNG_REQUIRE(codes_dtype == LNG_I32 || (codes_dtype == LNG_U8 && bits <= 8), "codes dtype must be i32 or u8 (bits <= 8)");
+  if (n == 0) return LNG_OK;
+  LNG_REQUIRE(logits && codes, "NULL pointer");
+  const int g = grid_for(n * routes, 256);
+  if (codes_dtype == LNG_U8)
+    quantize_logits_kernel<uint8_t><<<g, 256, 0, S(stream)>>>(logits, n, routes, bits, static_cast<uint8_t*>(codes));
+  else
+    quantize_logits_kernel<int32_t><<<g, 256, 0, S(stream)>>>(logits, n, routes, bits, static_cast<int32_t*>(codes));
+  LNG_LAUNCHED("quantize_logits_kernel");
+  return LNG_OK;
+}
+
+extern "C" int lng_route_codes(const void* x, int32_t x_dtype, int64_t n, int64_t in_dim, int64_t x_stride,
+                               const float* weight, int64_t routes, int32_t bits, void* codes, int32_t codes_dtype,
+                               float* logits, lng_stream_t stream) {
+  LNG_REQUIRE(n >= 0 && in_dim > 0 && routes > 0 && x_stride >= in_dim, "bad router shape");
+  LNG_REQUIRE(bits >= 1 && bits <= RT_MAXBITS, "router bits_per_route must be in [1, 8]");
+  LNG_REQUIRE(codes_dtype == LNG_U8 || codes_dtype == LNG_I32, "codes dtype must be u8 or i32");
+  LNG_REQUIRE(x_dtype == LNG_F32 || x_dtype == LNG_BF16, "router input dtype must be f32 or bf16");
+  if (n == 0) return LNG_OK;
+  LNG_REQUIRE(x && weight && codes, "NULL pointer");
+  if (x_dtype == LNG_BF16 && codes_dtype == LNG_U8 && logits == nullptr) {
+    const int st = tc_router_codes(static_cast<const __nv_bfloat16*>(x), n, in_dim, x_stride, weight, routes, bits,
+                                   static_cast<uint8_t*>(codes), S(stream));
+    if (st != LNG_ERR_UNSUPPORTED) return st;
+  }
+  dim3 grid(unsigned(ceil_div(n, RT_ROWS)), unsigned(ceil_div(routes, RT_ROUTES)));
+#define LNG_ROUTER(XT, CT)                                                                                   \
+  router_simt_kernel<XT, CT><<<grid, 256, 0, S(stream)>>>(static_cast<const XT*>(x), n, in_dim, x_stride, weight, \
+                                                          routes, bits, static_cast<CT*>(codes), logits)
+  if (x_dtype == LNG_F32) {
+    if (codes_dtype == LNG_U8) LNG_ROUTER(float, uint8_t); else LNG_ROUTER(float, int32_t);
+  } else {
+    if (codes_dtype == LNG_U8) LNG_ROUTER(__nv_bfloat16, uint8_t); else LNG_ROUTER(__nv_bfloat16, int32_t);
+  }
+#undef LNG_ROUTER
+  LNG_LAUNCHED("router_simt_kernel");
+  return LNG_OK;
+}
+
+extern "C" int lng_embed2_features(const int64_t* cur, const int64_t* prev, int64_t n, const void* embedding,
+                                   int32_t e_dtype, int64_t vocab, int64_t d, const float* prev_w, const float* cur_w,
+                                   const float* start, float eps, float* out, lng_stream_t stream) {
+  LNG_REQUIRE(n >= 0 && vocab > 0 && d > 0, "bad shape");
+  if (n == 0) return LNG_OK;
+  LNG_REQUIRE(cur && embedding && prev_w && cur_w && start && out, "NULL pointer");
+  const int g = int(ceil_div(n * 32, 256));
+  switch (e_dtype) {
+    case LNG_F32:
+      embed2_features_kernel<float><<<g, 256, 0, S(stream)>>>(cur, prev, n, static_cast<const float*>(embedding), vocab,
+                                                               d, prev_w, cur_w, start, eps, out);
+      break;
+    case LNG_BF16:
+      embed2_features_kernel<__nv_bfloat16><<<g, 256, 0, S(stream)>>>(
+          cur, prev, n, static_cast<const __nv_bfloat16*>(embedding), vocab, d, prev_w, cur_w, start, eps, out);
+      break;
+    case LNG_F16:
+      embed2_features_kernel<__half><<<g, 256, 0, S(stream)>>>(cur, prev, n, static_cast<const __half*>(embedding),
+                                                                vocab, d, prev_w, cur_w, start, eps, out);
+      break;
+    default:
+      return fail(LNG_ERR_ARGUMENT, "embedding dtype must be f32, bf16 or f16");
+  }
+  LNG_LAUNCHED("embed2_features_kernel");
+  return LNG_OK;
+}
+
+// ====================================================================== lookup
+template <typename CodeT>
+static int launch_lookup(const lng_tables* t, const CodeSource& src, int64_t M, int64_t rs, int64_t re, void* out,
+                         int32_t out_dtype, cudaStream_t stream) {
+  const TableSet ts = table_set(t);
+  const int64_t warps = M * (re - rs);
+  if (warps == 0) return LNG_OK;
+  const int g = grid_for(warps * 32, 256, 16);
+  const int es = dtype_size(t->table_dtype);
+  if (out_dtype == t->table_dtype && (t->memory_dim * es) % 16 == 0) {
+    for (int o = 0; o < t->n_orders; ++o)
+      LNG_REQUIRE((reinterpret_cast<uintptr_t>(t->tables[o]) & 15) == 0, "table pointers must be 16-byte aligned");
+    LNG_REQUIRE((reinterpret_cast<uintptr_t>(out) & 15) == 0, "output must be 16-byte aligned");
+    lookup_vec_kernel<CodeT><<<g, 256, 0, stream>>>(ts, src, M, rs, re, es, static_cast<uint4*>(out));
+    LNG_LAUNCHED("lookup_vec_kernel");
+    return LNG_OK;
+  }
+#define LNG_LK(TT, OT) lookup_kernel<CodeT, TT, OT><<<g, 256, 0, stream>>>(ts, src, M, rs, re, static_cast<OT*>(out))
+  if (out_dtype == LNG_F32) {
+    if (t->table_dtype == LNG_F32) LNG_LK(float, float);
+    else if (t->table_dtype == LNG_BF16) LNG_LK(__nv_bfloat16, float);
+    else LNG_LK(__half, float);
+  } else if (out_dtype == LNG_BF16 && t->table_dtype == LNG_BF16) {
+    LNG_LK(__nv_bfloat16, __nv_bfloat16);
+  } else if (out_dtype == LNG_F16 && t->table_dtype == LNG_F16) {
+    LNG_LK(__half, __half);
+  } else {
+    return fail(LNG_ERR_ARGUMENT, "output dtype must be f32 or the table dtype");
+  }
+#undef LNG_LK
+  LNG_LAUNCHED("lookup_kernel");
+  return LNG_OK;
+}
+
+extern "C" int lng_lookup_route_chunk(const lng_tables* tables, const void* codes, int32_t codes_dtype, int64_t B,
+                                      int64_t T, int64_t route_start, int64_t route_end, const int64_t* segment_ids,
+                                      const uint8_t* valid_tokens, int64_t target_length, void* out, int32_t out_dtype,
+                                      lng_stream_t stream) {
+  int st = check_tables(tables);
+  if (st) return st;
+  LNG_REQUIRE(B >= 0 && T >= 0, "bad shape");
+  LNG_REQUIRE(0 <= route_start && route_start <= route_end && route_end <= tables->num_routes, "bad route range");
+  LNG_REQUIRE(codes_dtype == LNG_U8 || codes_dtype == LNG_I32, "codes dtype must be u8 or i32");
+  const int64_t tout = target_length > 0 ? std::min(target_length, T) : T;
+  if (B * tout == 0 || route_end == route_start) return LNG_OK;
+  LNG_REQUIRE(codes && out, "NULL pointer");
+  CodeSource src{codes, B, T, 0, tables->num_routes, segment_ids, valid_tokens, nullptr, T - tout, T};
+  if (codes_dtype == LNG_U8)
+    return launch_lookup<uint8_t>(tables, src, B * tout, route_start, route_end, out, out_dtype, S(stream));
+  return launch_lookup<int32_t>(tables, src, B * tout, route_start, route_end, out, out_dtype, S(stream));
+}
+
+extern "C" int lng_lookup_windows(const lng_tables* tables, const void* codes, int32_t codes_dtype, int64_t M,
+                                  int64_t W, const int32_t* seg, void* out, int32_t out_dtype, lng_stream_t stream) {
+  int st = check_tables(tables);
+  if (st) return st;
+  LNG_REQUIRE(M >= 0 && W >= 1, "bad window shape");
+  LNG_REQUIRE(codes_dtype == LNG_U8 || codes_dtype == LNG_I32, "codes dtype must be u8 or i32");
+  if (M == 0) return LNG_OK;
+  LNG_REQUIRE(codes && out, "NULL pointer");
+  CodeSource src{codes, 0, 0, W, tables->num_routes, nullptr, nullptr, seg, 0, 0};
+  if (codes_dtype == LNG_U8) return launch_lookup<uint8_t>(tables, src, M, 0, tables->num_routes, out, out_dtype, S(stream));
+  return launch_lookup<int32_t>(tables, src, M, 0, tables->num_routes, out, out_dtype, S(stream));
+}
+
+// ====================================================================== attention core
+template <int DT, typename CodeT, typename T>
+static int launch_attend_mma(const AttendParams& p, cudaStream_t stream) {
+  constexpr int WARPS = 8, STAGES = 3;
+  using Cfg = AttendMmaCfg<DT>;
+  const size_t smem = size_t(WARPS) * STAGES * Cfg::STAGE_BYTES + size_t(WARPS) * STAGES * sizeof(uint64_t);
+  auto kern = attend_mma_kernel<CodeT, T, DT, WARPS, STAGES>;
+  LNG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  const int64_t blocks_needed = ceil_div(p.M, WARPS);
+  const int grid = int(std::max<int64_t>(1, std::min<int64_t>(blocks_needed, num_sms())));
+  kern<<<grid, WARPS * 32, smem, stream>>>(p);
+  LNG_LAUNCHED("attend_mma_kernel");
+  return LNG_OK;
+}
+
+template <typename CodeT, typename T>
+static int dispatch_attend_mma(int64_t Dt, const AttendParams& p, cudaStream_t stream) {
+  switch (Dt) {
+    case 32: return launch_attend_mma<32, CodeT, T>(p, stream);
+    case 64: return launch_attend_mma<64, CodeT, T>(p, stream);
+    case 128: return launch_attend_mma<128, CodeT, T>(p, stream);
+    case 136: return launch_attend_mma<136, CodeT, T>(p, stream);
+    case 256: return launch_attend_mma<256, CodeT, T>(p, stream);
+    case 272: return launch_attend_mma<272, CodeT, T>(p, stream);
+    default: return LNG_ERR_UNSUPPORTED;
+  }
+}
+
+template <typename CodeT>
+static int attend_impl(const lng_tables* t, const AttendParams& p, int32_t u_dtype, cudaStream_t stream) {
+  const int64_t Dt = int64_t(t->n_orders) * t->memory_dim;
+  // tensor-core path: 16-bit tables, activations of the same type, <= 16 heads, 16-byte rows
+  const bool mma_ok = (t->table_dtype == LNG_BF16 || t->table_dtype == LNG_F16) && u_dtype == t->table_dtype &&
+                      p.qh <= 16 && (t->memory_dim % 8) == 0 && !p.partial;
+  if (mma_ok) {
+    bool aligned = (reinterpret_cast<uintptr_t>(p.qa) & 15) == 0 && (reinterpret_cast<uintptr_t>(p.u) & 15) == 0;
+    for (int o = 0; o < t->n_orders; ++o) aligned = aligned && (reinterpret_cast<uintptr_t>(t->tables[o]) & 15) == 0;
+    if (aligned) {
+      const int st = t->table_dtype == LNG_BF16 ? dispatch_attend_mma<CodeT, __nv_bfloat16>(Dt, p, stream)
+                                                : dispatch_attend_mma<CodeT, __half>(Dt, p, stream);
+      if (st != LNG_ERR_UNSUPPORTED) return st;
+    }
+  }
+  // CUDA-core path (fp32 tables / activations, partial shard states, any width)
+  const int QH = p.qh;
+  const size_t smem = sizeof(float) * (size_t(2 * QH + ATT_C) * Dt + ATT_C + size_t(QH) * ATT_C + 3 * QH);
+  LNG_REQUIRE(smem <= 227 * 1024, "route token width too large for the CUDA-core readout");
+  const int grid = int(std::min<int64_t>(p.M, int64_t(num_sms()) * 8));
+  const int qdt = p.partial ? t->table_dtype : u_dtype;  // qa dtype follows the activations
+  (void)qdt;
+#define LNG_AT(TT, QT, UT)                                                                                   \
+  do {                                                                                                       \
+    auto k = attend_simt_kernel<CodeT, TT, QT, UT>;                                                          \
+    LNG_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));               \
+    k<<<grid, 128, smem, stream>>>(p);                                                                       \
+  } while (0)
+  // qa and (normalised) u share the activation dtype `u_dtype`; partial mode writes fp32 u
+  const int act = u_dtype;
+  if (t->table_dtype == LNG_F32) {
+    if (act == LNG_F32) LNG_AT(float, float, float);
+    else if (act == LNG_BF16) LNG_AT(float, __nv_bfloat16, __nv_bfloat16);
+    else return fail(LNG_ERR_ARGUMENT, "unsupported activation dtype");
+  } else if (t->table_dtype == LNG_BF16) {
+    if (act == LNG_F32) LNG_AT(__nv_bfloat16, float, float);
+    else if (act == LNG_BF16) LNG_AT(__nv_bfloat16, __nv_bfloat16, __nv_bfloat16);
+    else return fail(LNG_ERR_ARGUMENT, "unsupported activation dtype");
+  } else {
+    if (act == LNG_F32) LNG_AT(__half, float, float);
+    else if (act == LNG_F16) LNG_AT(__half, __half, __half);
+    else return fail(LNG_ERR_ARGUMENT, "unsupported activation dtype");
+  }
+#undef LNG_AT
+  LNG_LAUNCHED("attend_simt_kernel");
+  return LNG_OK;
+}
+
+extern "C" int lng_route_attend(const lng_tables* tables, const void* codes, int32_t codes_dtype, int64_t B, int64_t T,
+                                int64_t window, const int64_t* segment_ids, const uint8_t* valid_tokens,
+                                const int32_t* seg, int64_t route_start, int64_t route_end, int32_t num_heads,
+                                float eps, float sink_logit, const void* qa, const float* qscale, void* u,
+                                int32_t u_dtype, int32_t partial, float* m_out, float* l_out, lng_stream_t stream) {
+  int st = check_tables(tables);
+  if (st) return st;
+  LNG_REQUIRE(codes_dtype == LNG_U8 || codes_dtype == LNG_I32, "codes dtype must be u8 or i32");
+  LNG_REQUIRE(num_heads >= 1 && num_heads <= 64, "num_heads must be in [1, 64]");
+  LNG_REQUIRE(0 <= route_start && route_start < route_end && route_end <= tables->num_routes, "bad route range");
+  LNG_REQUIRE(u_dtype == LNG_F32 || u_dtype == LNG_BF16 || u_dtype == LNG_F16, "u dtype must be f32, bf16 or f16");
+  LNG_REQUIRE(!partial || (u_dtype == LNG_F32 && m_out && l_out), "partial mode needs fp32 u, m_out and l_out");
+  const int64_t M = window > 0 ? B : B * T;
+  if (M == 0) return LNG_OK;
+  LNG_REQUIRE(codes && qa && u, "NULL pointer");
+  AttendParams p{};
+  p.ts = table_set(tables);
+  p.src = CodeSource{codes, window > 0 ? 0 : B, window > 0 ? 0 : T, window, tables->num_routes, segment_ids,
+                     valid_tokens, seg, 0, T};
+  p.M = M;
+  p.route_start = route_start;
+  p.route_end = route_end;
+  p.qh = num_heads;
+  p.eps = eps;
+  p.sink = sink_logit;
+  p.qa = qa;
+  p.qscale = qscale;
+  p.u = u;
+  p.partial = partial;
+  p.m_out = m_out;
+  p.l_out = l_out;
+  if (codes_dtype == LNG_U8) return attend_impl<uint8_t>(tables, p, u_dtype, S(stream));
+  return attend_impl<int32_t>(tables, p, u_dtype, S(stream));
+}
+
+// ====================================================================== GEMM
+extern "C" int lng_gemm(const void* A, int32_t a_dtype, int64_t lda, const void* Bm, int32_t b_dtype, int64_t ldb,
+                        void* C, int32_t c_dtype, int64_t ldc, int64_t M, int64_t N, int64_t K, const float* rowscale,
+                        int32_t accumulate, lng_stream_t stream) {
+  LNG_REQUIRE(M >= 0 && N >= 0 && K >= 0 && lda >= K && ldb >= K && ldc >= N, "bad GEMM shape");
+  LNG_REQUIRE(is_float_dtype(a_dtype) && is_float_dtype(b_dtype) && is_float_dtype(c_dtype), "GEMM dtypes must be float");
+  if (M == 0 || N == 0) return LNG_OK;
+  LNG_REQUIRE(A && Bm && C, "NULL pointer");
+  if (a_dtype == LNG_BF16 && b_dtype == LNG_BF16 && !accumulate) {
+    const int st = tc_gemm_bf16(static_cast<const __nv_bfloat16*>(A), lda, static_cast<const __nv_bfloat16*>(Bm), ldb,
+                                C, c_dtype, ldc, M, N, K, rowscale, S(stream));
+    if (st != LNG_ERR_UNSUPPORTED) return st;
+  }
+  dim3 grid(unsigned(ceil_div(N, GS_TILE)), unsigned(ceil_div(M, GS_TILE)));
+#define LNG_G(AT, BT, CT)                                                                                         \
+  gemm_simt_kernel<AT, BT, CT><<<grid, 256, 0, S(stream)>>>(static_cast<const AT*>(A), lda, static_cast<const BT*>(Bm), \
+                                                            ldb, static_cast<CT*>(C), ldc, M, N, K, rowscale, accumulate)
+#define LNG_GC(AT, BT)                                             \
+  do {                                                             \
+    if (c_dtype == LNG_F32) LNG_G(AT, BT, float);                  \
+    else if (c_dtype == LNG_BF16) LNG_G(AT, BT, __nv_bfloat16);    \
+    else LNG_G(AT, BT, __half);                                    \
+  } while (0)
+  if (a_dtype == LNG_F32 && b_dtype == LNG_F32) LNG_GC(float, float);
+  else if (a_dtype == LNG_BF16 && b_dtype == LNG_BF16) LNG_GC(__nv_bfloat16, __nv_bfloat16);
+  else if (a_dtype == LNG_F32 && b_dtype == LNG_BF16) LNG_GC(float, __nv_bfloat16);
+  else if (a_dtype == LNG_BF16 && b_dtype == LNG_F32) LNG_GC(__nv_bfloat16, float);
+  else if (a_dtype == LNG_F16 && b_dtype == LNG_F16) LNG_GC(__half, __half);
+  else if (a_dtype == LNG_F32 && b_dtype == LNG_F16) LNG_GC(float, __half);
+  else return fail(LNG_ERR_UNSUPPORTED, "unsupported GEMM dtype combination");
+#undef LNG_GC
+#undef LNG_G
+  LNG_LAUNCHED("gemm_simt_kernel");
+  return LNG_OK;
+}
+
+// ====================================================================== row ops
+extern "C" int lng_rms_rows(const void* x, int32_t x_dtype, int64_t n, int64_t d, float eps, float* rs,
+                            lng_stream_t stream) {
+  LNG_REQUIRE(n >= 0 && d > 0, "bad shape");
+  if (n == 0) return LNG_OK;
+  LNG_REQUIRE(x && rs, "NULL pointer");
+  const int g = grid_for(n * 32, 256, 16);
+  if (x_dtype == LNG_F32) rms_rows_kernel<float><<<g, 256, 0, S(stream)>>>(static_cast<const float*>(x), n, d, eps, rs);
+  else if (x_dtype == LNG_BF16)
+    rms_rows_kernel<__nv_bfloat16><<<g, 256, 0, S(stream)>>>(static_cast<const __nv_bfloat16*>(x), n, d, eps, rs);
+  else if (x_dtype == LNG_F16) rms_rows_kernel<__half><<<g, 256, 0, S(stream)>>>(static_cast<const __half*>(x), n, d, eps, rs);
+  else return fail(LNG_ERR_ARGUMENT, "x dtype must be float");
+  LNG_LAUNCHED("rms_rows_kernel");
+  return LNG_OK;
+}
+
+extern "C" int lng_rms_norm(const void* x, int32_t x_dtype, int64_t n, int64_t d, const float* w, float eps, void* y,
+                            int32_t y_dtype, lng_stream_t stream) {
+  LNG_REQUIRE(n >= 0 && d > 0, "bad shape");
+  if (n == 0) return LNG_OK;
+  LNG_REQUIRE(x && y, "NULL pointer");
+  const int g = grid_for(n * 32, 256, 16);
+#define LNG_RN(XT, YT) rms_norm_kernel<XT, YT><<<g, 256, 0, S(stream)>>>(static_cast<const XT*>(x), n, d, w, eps, static_cast<YT*>(y))
+  if (x_dtype == LNG_F32 && y_dtype == LNG_F32) LNG_RN(float, float);
+  else if (x_dtype == LNG_BF16 && y_dtype == LNG_BF16) LNG_RN(__nv_bfloat16, __nv_bfloat16);
+  else if (x_dtype == LNG_BF16 && y_dtype == LNG_F32) LNG_RN(__nv_bfloat16, float);
+  else if (x_dtype == LNG_F32 && y_dtype == LNG_BF16) LNG_RN(float, __nv_bfloat16);
+  else if (x_dtype == LNG_F16 && y_dtype == LNG_F16) LNG_RN(__half, __half);
+  else if (x_dtype == LNG_F16 && y_dtype == LNG_F32) LNG_RN(__half, float);
+  else return fail(LNG_ERR_UNSUPPORTED, "unsupported RMSNorm dtype combination");
+#undef LNG_RN
+  LNG_LAUNCHED("rms_norm_kernel");
+  return LNG_OK;
+}
+
+static int check_readout(const lng_readout* ro) {
+  LNG_REQUIRE(ro != nullptr, "readout descriptor is NULL");
+  LNG_REQUIRE(ro->hidden > 0 && ro->num_heads > 0 && ro->num_kv_heads > 0 && ro->head_dim > 0, "bad readout shape");
+  LNG_REQUIRE(ro->num_heads % ro->num_kv_heads == 0, "num_heads must be divisible by num_kv_heads");
+  LNG_REQUIRE(ro->conv_kernel >= 1 && ro->conv_dilation >= 1, "bad conv shape");
+  LNG_REQUIRE(ro->act_dtype == LNG_F32 || ro->act_dtype == LNG_BF16, "activation dtype must be f32 or bf16");
+  LNG_REQUIRE(ro->conv_norm && ro->conv_weight, "conv weights are NULL");
+  return LNG_OK;
+}
+
+static ConvParams conv_params(const lng_readout* ro) {
+  return ConvParams{ro->hidden, ro->conv_kernel, ro->conv_dilation, ro->conv_norm, ro->conv_weight, ro->conv_bias};
+}
+
+static int conv_finish_ws(const lng_readout* ro, const void* mixed, int64_t B, int64_t T, const int64_t* seg,
+                          const uint8_t* valid, void* out, void* conv_in, float* rs, cudaStream_t stream) {
+  const int64_t M = B * T;
+  int st = lng_rms_rows(mixed, ro->act_dtype, M, ro->hidden, ro->eps, rs, reinterpret_cast<lng_stream_t>(stream));
+  if (st) return st;
+  const ConvParams cp = conv_params(ro);
+  const int g = grid_for(M * ro->hidden, 256, 16);
+  if (ro->act_dtype == LNG_F32)
+    conv_seq_kernel<float><<<g, 256, 0, stream>>>(cp, static_cast<const float*>(mixed), rs, B, T, seg, valid,
+                                                  static_cast<float*>(out), static_cast<float*>(conv_in));
+  else
+    conv_seq_kernel<__nv_bfloat16><<<g, 256, 0, stream>>>(cp, static_cast<const __nv_bfloat16*>(mixed), rs, B, T, seg,
+                                                          valid, static_cast<__nv_bfloat16*>(out),
+                                                          static_cast<__nv_bfloat16*>(conv_in));
+  LNG_LAUNCHED("conv_seq_kernel");
+  return LNG_OK;
+}
+
+extern "C" int lng_conv_finish(const lng_readout* ro, const void* mixed, int64_t B, int64_t T,
+                               const int64_t* segment_ids, const uint8_t* valid_tokens, void* out, void* conv_in,
+                               lng_stream_t stream) {
+  int st = check_readout(ro);
+  if (st) return st;
+  LNG_REQUIRE(B >= 0 && T >= 0, "bad shape");
+  if (B * T == 0) return LNG_OK;
+  LNG_REQUIRE(mixed && out && mixed != out, "mixed and out must be distinct non-NULL buffers");
+  float* rs = nullptr;
+  LNG_CUDA(cudaMallocAsync(&rs, sizeof(float) * B * T, S(stream)));
+  st = conv_finish_ws(ro, mixed, B, T, segment_ids, valid_tokens, out, conv_in, rs, S(stream));
+  cudaFreeAsync(rs, S(stream));
+  return st;
+}
+
+extern "C" int lng_conv_window(const lng_readout* ro, const void* mixed, int64_t n, void* cache,
+                               const int64_t* new_slot, const int64_t* slot, void* out, lng_stream_t stream) {
+  int st = check_readout(ro);
+  if (st) return st;
+  if (n <= 0) return LNG_OK;
+  LNG_REQUIRE(mixed && cache && new_slot && slot && out, "NULL pointer");
+  float* rs = nullptr;
+  LNG_CUDA(cudaMallocAsync(&rs, sizeof(float) * n, S(stream)));
+  st = lng_rms_rows(mixed, ro->act_dtype, n, ro->hidden, ro->eps, rs, stream);
+  if (st) {
+    cudaFreeAsync(rs, S(stream));
+    return st;
+  }
+  const ConvParams cp = conv_params(ro);
+  const int g = grid_for(n * ro->hidden, 256, 16);
+  if (ro->act_dtype == LNG_F32) {
+    conv_cache_write_kernel<float><<<g, 256, 0, S(stream)>>>(cp, static_cast<const float*>(mixed), rs, n, new_slot,
+                                                              static_cast<float*>(cache));
+    conv_window_kernel<float><<<g, 256, 0, S(stream)>>>(cp, static_cast<const float*>(mixed), n,
+                                                         static_cast<const float*>(cache), slot, static_cast<float*>(out));
+  } else {
+    conv_cache_write_kernel<__nv_bfloat16><<<g, 256, 0, S(stream)>>>(
+        cp, static_cast<const __nv_bfloat16*>(mixed), rs, n, new_slot, static_cast<__nv_bfloat16*>(cache));
+    conv_window_kernel<__nv_bfloat16><<<g, 256, 0, S(stream)>>>(cp, static_cast<const __nv_bfloat16*>(mixed), n,
+                                                                 static_cast<const __nv_bfloat16*>(cache), slot,
+                                                                 static_cast<__nv_bfloat16*>(out));
+  }
+  cudaFreeAsync(rs, S(stream));
+  LNG_LAUNCHED("conv_window_kernel");
+  return LNG_OK;
+}
+
+extern "C" int lng_sink_gqa(const void* q, const void* k, const void* v, int32_t dtype, int64_t M, int32_t num_kv_heads,
+                            int32_t groups, int64_t routes, int32_t head_dim, float sink_logit, void* out,
+                            lng_stream_t stream) {
+  LNG_REQUIRE(M >= 0 && num_kv_heads > 0 && groups > 0 && routes > 0 && head_dim > 0, "bad shape");
+  if (M == 0) return LNG_OK;
+  LNG_REQUIRE(q && k && v && out, "NULL pointer");
+  const size_t smem = sizeof(float) * (2 * size_t(routes) * head_dim + size_t(groups) * head_dim + size_t(groups) * routes);
+  LNG_REQUIRE(smem <= 227 * 1024, "routes * head_dim too large for the explicit-K/V readout");
+  const float scale = 1.0f / sqrtf(float(head_dim));
+  const unsigned grid = unsigned(M * num_kv_heads);
+#define LNG_SG(T)                                                                                          \
+  do {                                                                                                     \
+    auto kern = sink_gqa_kernel<T>;                                                                        \
+    LNG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));          \
+    kern<<<grid, 128, smem, S(stream)>>>(static_cast<const T*>(q), static_cast<const T*>(k),               \
+                                         static_cast<const T*>(v), M, num_kv_heads, groups, int(routes),    \
+                                         head_dim, scale, sink_logit, static_cast<T*>(out));               \
+  } while (0)
+  if (dtype == LNG_F32) LNG_SG(float);
+  else if (dtype == LNG_BF16) LNG_SG(__nv_bfloat16);
+  else if (dtype == LNG_F16) LNG_SG(__half);
+  else return fail(LNG_ERR_ARGUMENT, "dtype must be float");
+#undef LNG_SG
+  LNG_LAUNCHED("sink_gqa_kernel");
+  return LNG_OK;
+}
+
+// ====================================================================== fold / memory forward
+extern "C" int lng_fold_readout(int64_t d, int64_t Dt, int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+                                const float* q_norm, const float* q_proj, const float* mem_norm, const float* kv_proj,
+                                const float* o_proj, void* w_qk, void* w_vo, int32_t act_dtype, lng_stream_t stream) {
+  LNG_REQUIRE(d > 0 && Dt > 0 && num_heads > 0 && num_kv_heads > 0 && head_dim > 0, "bad readout shape");
+  LNG_REQUIRE(num_heads % num_kv_heads == 0, "num_heads must be divisible by num_kv_heads");
+  LNG_REQUIRE(act_dtype == LNG_F32 || act_dtype == LNG_BF16 || act_dtype == LNG_F16, "bad activation dtype");
+  LNG_REQUIRE(mem_norm && kv_proj, "NULL pointer");
+  const int G = num_heads / num_kv_heads;
+  const float scale = 1.0f / sqrtf(float(head_dim));
+  if (w_qk) {
+    LNG_REQUIRE(q_norm && q_proj, "NULL pointer");
+    const int g = grid_for(int64_t(num_heads) * Dt * d, 256, 16);
+#define LNG_FQ(OT) fold_qk_kernel<OT><<<g, 256, 0, S(stream)>>>(d, Dt, num_heads, G, head_dim, scale, q_norm, q_proj, mem_norm, kv_proj, static_cast<OT*>(w_qk))
+    if (act_dtype == LNG_F32) LNG_FQ(float); else if (act_dtype == LNG_BF16) LNG_FQ(__nv_bfloat16); else LNG_FQ(__half);
+#undef LNG_FQ
+    LNG_LAUNCHED("fold_qk_kernel");
+  }
+  if (w_vo) {
+    LNG_REQUIRE(o_proj, "NULL pointer");
+    const int g = grid_for(d * num_heads * Dt, 256, 16);
+#define LNG_FV(OT) fold_vo_kernel<OT><<<g, 256, 0, S(stream)>>>(d, Dt, num_heads, G, head_dim, num_kv_heads, mem_norm, kv_proj, o_proj, static_cast<OT*>(w_vo))
+    if (act_dtype == LNG_F32) LNG_FV(float); else if (act_dtype == LNG_BF16) LNG_FV(__nv_bfloat16); else LNG_FV(__half);
+#undef LNG_FV
+    LNG_LAUNCHED("fold_vo_kernel");
+  }
+  return LNG_OK;
+}
+
+namespace {
+struct FwdLayout {
+  size_t codes, qa, u, mixed, rs_h, rs_m, total;
+};
+FwdLayout fwd_layout(const lng_tables* t, const lng_readout* ro, int64_t M) {
+  auto al = [](size_t x) { return (x + 255) & ~size_t(255); };
+  const int64_t Dt = int64_t(t->n_orders) * t->memory_dim;
+  const size_t es = size_t(dtype_size(ro->act_dtype));
+  FwdLayout L{};
+  size_t off = 0;
+  L.codes = off; off += al(size_t(M) * t->num_routes);
+  L.qa = off;    off += al(size_t(M) * ro->num_heads * Dt * es);
+  L.u = off;     off += al(size_t(M) * ro->num_heads * Dt * es);
+  L.mixed = off; off += al(size_t(M) * ro->hidden * es);
+  L.rs_h = off;  off += al(size_t(M) * sizeof(float));
+  L.rs_m = off;  off += al(size_t(M) * sizeof(float));
+  L.total = off;
+  return L;
+}
+}  // namespace
+
+extern "C" size_t lng_memory_workspace_bytes(const lng_tables* tables, const lng_readout* ro, int64_t M) {
+  if (!tables || !ro || M < 0) return 0;
+  return fwd_layout(tables, ro, M).total;
+}
+
+extern "C" int lng_memory_forward(const lng_tables* tables, const lng_readout* ro, int64_t B, int64_t T, const void* h,
+                                  const void* router_x, int32_t router_x_dtype, const void* codes_in,
+                                  int32_t codes_in_dtype, const int64_t* segment_ids, const uint8_t* valid_tokens,
+                                  void* out, uint8_t* codes_out, void* workspace, size_t workspace_bytes,
+                                  lng_stream_t stream) {
+  int st = check_tables(tables);
+  if (st) return st;
+  st = check_readout(ro);
+  if (st) return st;
+  LNG_REQUIRE(B >= 0 && T >= 0, "bad shape");
+  const int64_t M = B * T;
+  if (M == 0) return LNG_OK;
+  LNG_REQUIRE(h && out && ro->w_qk && ro->w_vo, "NULL pointer");
+  LNG_REQUIRE(tables->table_dtype == ro->act_dtype || tables->table_dtype == LNG_F32 ||
+                  (ro->act_dtype == LNG_F32),
+              "tables and activations must share a dtype (or be fp32)");
+  const FwdLayout L = fwd_layout(tables, ro, M);
+  LNG_REQUIRE(workspace && workspace_bytes >= L.total, "workspace too small (see lng_memory_workspace_bytes)");
+  unsigned char* ws = static_cast<unsigned char*>(workspace);
+  const int64_t Dt = int64_t(tables->n_orders) * tables->memory_dim;
+  const int64_t QD = int64_t(ro->num_heads) * Dt;
+  const int act = ro->act_dtype;
+  // 1. codes
+  const void* codes = codes_in;
+  int32_t cdt = codes_in_dtype;
+  if (!codes) {
+    LNG_REQUIRE(router_x && ro->router_w, "router input and weight are needed when codes are not given");
+    uint8_t* c = codes_out ? codes_out : reinterpret_cast<uint8_t*>(ws + L.codes);
+    st = lng_route_codes(router_x, router_x_dtype, M, ro->router_in_dim, ro->router_in_dim, ro->router_w,
+                         tables->num_routes, tables->bits, c, LNG_U8, nullptr, stream);
+    if (st) return st;
+    codes = c;
+    cdt = LNG_U8;
+  }
+  // 2. query scale 1/rms(h) and the folded query qa = h . w_qk^T
+  float* rs_h = reinterpret_cast<float*>(ws + L.rs_h);
+  st = lng_rms_rows(h, act, M, ro->hidden, ro->eps, rs_h, stream);
+  if (st) return st;
+  void* qa = ws + L.qa;
+  st = lng_gemm(h, act, ro->hidden, ro->w_qk, act, ro->hidden, qa, act, QD, M, QD, ro->hidden, nullptr, 0, stream);
+  if (st) return st;
+  // 3. fused gather + sink attention over all routes
+  void* u = ws + L.u;
+  st = lng_route_attend(tables, codes, cdt, B, T, 0, segment_ids, valid_tokens, nullptr, 0, tables->num_routes,
+                        ro->num_heads, ro->eps, ro->sink_logit, qa, rs_h, u, act, 0, nullptr, nullptr, stream);
+  if (st) return st;
+  // 4. mixed = u . w_vo^T  (= o_proj(head))
+  void* mixed = ws + L.mixed;
+  st = lng_gemm(u, act, QD, ro->w_vo, act, QD, mixed, act, ro->hidden, M, ro->hidden, QD, nullptr, 0, stream);
+  if (st) return st;
+  // 5. out = mixed + SiLU(conv(RMSNorm(mixed))), masked by valid_tokens
+  return conv_finish_ws(ro, mixed, B, T, segment_ids, valid_tokens, out, nullptr, reinterpret_cast<float*>(ws + L.rs_m),
+                        S(stream));
+}
+
+extern "C" int lng_attend_rescale(const float* m_local, const float* m_glob, float* l, float* u, int64_t M,
+                                  int32_t num_heads, int64_t Dt, lng_stream_t stream) {
+  LNG_REQUIRE(M >= 0 && num_heads > 0 && Dt > 0, "bad shape");
+  if (M == 0) return LNG_OK;
+  LNG_REQUIRE(m_local && m_glob && l && u, "NULL pointer");
+  const int64_t MQ = M * num_heads;
+  attend_rescale_kernel<<<grid_for(MQ * Dt, 256, 16), 256, 0, S(stream)>>>(m_local, m_glob, l, u, MQ, Dt);
+  LNG_LAUNCHED("attend_rescale_kernel");
+  return LNG_OK;
+}
+
+extern "C" int lng_attend_normalize(const float* l, const float* u, int64_t M, int32_t num_heads, int64_t Dt,
+                                    void* u_out, int32_t u_dtype, lng_stream_t stream) {
+  LNG_REQUIRE(M >= 0 && num_heads > 0 && Dt > 0, "bad shape");
+  if (M == 0) return LNG_OK;
+  LNG_REQUIRE(l && u && u_out, "NULL pointer");
+  const int64_t MQ = M * num_heads;
+  const int g = grid_for(MQ * Dt, 256, 16);
+  if (u_dtype == LNG_F32) attend_normalize_kernel<float><<<g, 256, 0, S(stream)>>>(l, u, MQ, Dt, static_cast<float*>(u_out));
+  else if (u_dtype == LNG_BF16)
+    attend_normalize_kernel<__nv_bfloat16><<<g, 256, 0, S(stream)>>>(l, u, MQ, Dt, static_cast<__nv_bfloat16*>(u_out));
+  else return fail(LNG_ERR_ARGUMENT, "u dtype must be f32 or bf16");
+  LNG_LAUNCHED("attend_normalize_kernel");
+  return LNG_OK;
+}
+
+// ====================================================================== logits top-k
+extern "C" size_t lng_logits_topk_scratch_bytes(int64_t n, int64_t vocab, int32_t k) {
+  if (n <= 0 || vocab <= 0 || k <= 0) return 0;
+  const int64_t nch = ceil_div(vocab, TK_VC);
+  return size_t(n) * nch * k * (sizeof(float) + sizeof(int64_t)) + 256;
+}
+
+extern "C" int lng_logits_topk(const float* h, int64_t n, int64_t d, const void* embedding, int32_t e_dtype,
+                               int64_t vocab, int32_t k, int64_t* ids, float* vals, float* logits, void* scratch,
+                               size_t scratch_bytes, lng_stream_t stream) {
+  LNG_REQUIRE(n >= 0 && d > 0 && vocab > 0, "bad shape");
+  LNG_REQUIRE(k >= 1 && k <= TK_MAXK, "k must be in [1, 8]");
+  if (n == 0) return LNG_OK;
+  LNG_REQUIRE(h && embedding && ids && vals, "NULL pointer");
+  const int64_t nch = ceil_div(vocab, TK_VC);
+  const size_t need = lng_logits_topk_scratch_bytes(n, vocab, k);
+  LNG_REQUIRE(scratch && scratch_bytes >= need, "scratch too small (see lng_logits_topk_scratch_bytes)");
+  const size_t smem = sizeof(float) * (size_t(TK_ROWS) * d + size_t(TK_ROWS) * TK_VC);
+  LNG_REQUIRE(smem <= 227 * 1024, "hidden size too large for the top-k kernel");
+  uintptr_t base = (reinterpret_cast<uintptr_t>(scratch) + 15) & ~uintptr_t(15);
+  int64_t* cand_i = reinterpret_cast<int64_t*>(base);
+  float* cand_v = reinterpret_cast<float*>(cand_i + n * nch * k);
+  dim3 grid(unsigned(nch), unsigned(ceil_div(n, TK_ROWS)));
+#define LNG_TK(ET)                                                                                         \
+  do {                                                                                                     \
+    auto kern = logits_chunk_topk_kernel<ET>;                                                              \
+    LNG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));          \
+    kern<<<grid, 256, smem, S(stream)>>>(h, n, d, static_cast<const ET*>(embedding), vocab, k, cand_v, cand_i, logits); \
+  } while (0)
+  if (e_dtype == LNG_F32) LNG_TK(float);
+  else if (e_dtype == LNG_BF16) LNG_TK(__nv_bfloat16);
+  else if (e_dtype == LNG_F16) LNG_TK(__half);
+  else return fail(LNG_ERR_ARGUMENT, "embedding dtype must be float");
+#undef LNG_TK
+  LNG_LAUNCHED("logits_chunk_topk_kernel");
+  topk_merge_kernel<<<unsigned(ceil_div(n * 32, 256)), 256, 0, S(stream)>>>(cand_v, cand_i, n, nch, k, ids, vals);
+  LNG_LAUNCHED("topk_merge_kernel");
+  return LNG_OK;
+}
+
+#include "drafter.cuh"

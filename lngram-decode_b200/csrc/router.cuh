@@ -1,0 +1,126 @@
+// Router: fp32 GEMM x . W^T with the sign-pack epilogue, and the pack of given logits.
+//
+// Reference: ffnmem/memory/wrapper.py:98-101 (fp32 linear router, autocast off),
+// ffnmem/memory/lngram_v2.py:74-89, :1012-1017 (bit j of route r = logit[r*bits + j] > 0).
+#pragma once
+
+#include "address.cuh"
+
+namespace lng {
+
+template <typename CodeOutT>
+__global__ void quantize_logits_kernel(const float* __restrict__ logits, int64_t n, int64_t routes, int bits,
+                                       CodeOutT* __restrict__ codes) {
+  const int64_t total = n * routes;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const float* l = logits + i * bits;
+    int v = 0;
+    for (int j = 0; j < bits; ++j) v |= (l[j] > 0.0f ? 1 : 0) << j;
+    codes[i] = static_cast<CodeOutT>(v);
+  }
+}
+
+// CUDA-core fp32 router: a CTA computes 64 rows x 16 routes (all `bits` logits of each route),
+// thread (ty, tx) owns rows 4*ty..4*ty+3 of route tx, so the pack needs no exchange.
+// Exact fp32 FMAs in ascending k; used for fp32 router inputs and small batches.
+constexpr int RT_ROWS = 64, RT_ROUTES = 16, RT_K = 32, RT_MAXBITS = 8;
+
+template <typename XT, typename CodeOutT>
+__global__ void __launch_bounds__(256) router_simt_kernel(const XT* __restrict__ x, int64_t n, int64_t in_dim,
+                                                          int64_t x_stride, const float* __restrict__ w,
+                                                          int64_t routes, int bits, CodeOutT* __restrict__ codes,
+                                                          float* __restrict__ logits) {
+  __shared__ float As[RT_K][RT_ROWS + 1];
+  __shared__ float Bs[RT_K][RT_ROUTES * RT_MAXBITS + 1];
+  const int tx = threadIdx.x % RT_ROUTES;  // route within the tile
+  const int ty = threadIdx.x / RT_ROUTES;  // row group (4 rows)
+  const int64_t row0 = int64_t(blockIdx.x) * RT_ROWS;
+  const int64_t route0 = int64_t(blockIdx.y) * RT_ROUTES;
+  const int ncol = RT_ROUTES * bits;       // logits columns in the tile
+  const int64_t C = routes * bits;
+  float acc[4][RT_MAXBITS];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < RT_MAXBITS; ++j) acc[i][j] = 0.f;
+
+  for (int64_t k0 = 0; k0 < in_dim; k0 += RT_K) {
+    for (int e = threadIdx.x; e < RT_ROWS * RT_K; e += blockDim.x) {
+      const int r = e / RT_K, k = e % RT_K;
+      const int64_t gr = row0 + r, gk = k0 + k;
+      As[k][r] = (gr < n && gk < in_dim) ? to_f32(x[gr * x_stride + gk]) : 0.f;
+    }
+    for (int e = threadIdx.x; e < ncol * RT_K; e += blockDim.x) {
+      const int c = e / RT_K, k = e % RT_K;
+      const int64_t gc = route0 * bits + c, gk = k0 + k;
+      Bs[k][c] = (gc < C && gk < in_dim) ? w[gc * in_dim + gk] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int k = 0; k < RT_K; ++k) {
+      float a[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = As[k][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < RT_MAXBITS; ++j) {
+        if (j < bits) {
+          const float b = Bs[k][tx * bits + j];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[i][j] = fmaf(a[i], b, acc[i][j]);
+        }
+      }
+    }
+    __syncthreads();
+  }
+  const int64_t r = route0 + tx;
+  if (r >= routes) return;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t gr = row0 + ty * 4 + i;
+    if (gr >= n) continue;
+    int v = 0;
+#pragma unroll
+    for (int j = 0; j < RT_MAXBITS; ++j) {
+      if (j < bits) {
+        v |= (acc[i][j] > 0.f ? 1 : 0) << j;
+        if (logits) logits[gr * C + r * bits + j] = acc[i][j];
+      }
+    }
+    codes[gr * routes + r] = static_cast<CodeOutT>(v);
+  }
+}
+
+// embed2 router features (ffnmem/memory/router.py:50-69): one warp per item.
+template <typename ET>
+__global__ void embed2_features_kernel(const int64_t* __restrict__ cur, const int64_t* __restrict__ prev, int64_t n,
+                                       const ET* __restrict__ E, int64_t vocab, int64_t d,
+                                       const float* __restrict__ prev_w, const float* __restrict__ cur_w,
+                                       const float* __restrict__ start, float eps, float* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (blockIdx.x * int64_t(blockDim.x) + threadIdx.x) >> 5;
+  if (warp >= n) return;
+  const int64_t tc = cur[warp];
+  const int64_t tp = prev ? prev[warp] : -1;
+  if (tc < 0 || tc >= vocab || tp >= vocab) {
+    if (lane == 0) atomicCAS(&g_error_word, 0u, (unsigned int)DEV_ERR_TOKEN_RANGE);
+    return;
+  }
+  float* o = out + warp * 2 * d;
+  for (int part = 0; part < 2; ++part) {
+    const float* wv = part == 0 ? prev_w : cur_w;
+    const int64_t tok = part == 0 ? tp : tc;
+    float ss = 0.f;
+    for (int64_t j = lane; j < d; j += 32) {
+      const float v = tok >= 0 ? to_f32(E[tok * d + j]) : start[j];
+      ss += v * v;
+    }
+    ss = warp_sum(ss);
+    const float rs = rsqrtf(ss / float(d) + eps);
+    for (int64_t j = lane; j < d; j += 32) {
+      const float v = tok >= 0 ? to_f32(E[tok * d + j]) : start[j];
+      o[part * d + j] = v * rs * wv[j];
+    }
+  }
+}
+
+}  // namespace lng

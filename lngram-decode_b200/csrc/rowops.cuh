@@ -1,0 +1,222 @@
+// Row-wise kernels of the readout: RMS statistics, RMSNorm, the short causal conv finish
+// (ffnmem/memory/lngram_v2.py:207-286, :1354-1359), its window form for the decode / tree seams
+// (ffnmem/infer.py:176-182, drafting/tree.py:186-195), the readout fold, and the shard combine.
+#pragma once
+
+#include "address.cuh"
+
+namespace lng {
+
+// rs[i] = 1 / sqrt(mean(x[i]^2) + eps): one warp per row.
+template <typename XT>
+__global__ void rms_rows_kernel(const XT* __restrict__ x, int64_t n, int64_t d, float eps, float* __restrict__ rs) {
+  const int lane = threadIdx.x & 31;
+  for (int64_t row = (blockIdx.x * int64_t(blockDim.x) + threadIdx.x) >> 5; row < n;
+       row += (int64_t(gridDim.x) * blockDim.x) >> 5) {
+    const XT* xr = x + row * d;
+    float ss = 0.f;
+    for (int64_t j = lane; j < d; j += 32) {
+      const float v = to_f32(xr[j]);
+      ss = fmaf(v, v, ss);
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) rs[row] = rsqrtf(ss / float(d) + eps);
+  }
+}
+
+template <typename XT, typename YT>
+__global__ void rms_norm_kernel(const XT* x, int64_t n, int64_t d, const float* __restrict__ w, float eps, YT* y) {
+  const int lane = threadIdx.x & 31;
+  for (int64_t row = (blockIdx.x * int64_t(blockDim.x) + threadIdx.x) >> 5; row < n;
+       row += (int64_t(gridDim.x) * blockDim.x) >> 5) {
+    const XT* xr = x + row * d;
+    float ss = 0.f;
+    for (int64_t j = lane; j < d; j += 32) {
+      const float v = to_f32(xr[j]);
+      ss = fmaf(v, v, ss);
+    }
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / float(d) + eps);
+    __syncwarp();
+    for (int64_t j = lane; j < d; j += 32) {
+      const float v = to_f32(xr[j]) * r;
+      y[row * d + j] = from_f32<YT>(w ? v * w[j] : v);
+    }
+  }
+}
+
+struct ConvParams {
+  int64_t d;
+  int k, dil;
+  const float* norm_w;
+  const float* weight;  // [d, k]
+  const float* bias;    // [d] or null
+};
+
+// Sequence-mode conv finish: out[p, c] = mixed[p, c] + SiLU(bias + sum_tap w[c, tap] y[p - lag, c] ok),
+// y = mixed * rs * g (rs precomputed per position), zero left padding, segment mask, valid mask.
+template <typename T>
+__global__ void conv_seq_kernel(ConvParams cp, const T* __restrict__ mixed, const float* __restrict__ rs, int64_t B,
+                                int64_t T_, const int64_t* __restrict__ seg, const uint8_t* __restrict__ valid,
+                                T* __restrict__ out, T* __restrict__ conv_in) {
+  const int64_t total = B * T_ * cp.d;
+  for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < total; e += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t c = e % cp.d;
+    const int64_t pos = e / cp.d;
+    const int64_t t = pos % T_;
+    const float g = cp.norm_w[c];
+    float acc = cp.bias ? cp.bias[c] : 0.f;
+    for (int tap = 0; tap < cp.k; ++tap) {
+      const int64_t lag = int64_t(cp.k - 1 - tap) * cp.dil;
+      if (t - lag < 0) continue;
+      const int64_t q = pos - lag;
+      if (seg && seg[q] != seg[pos]) continue;
+      const float y = to_f32(mixed[q * cp.d + c]) * rs[q] * g;
+      acc = fmaf(cp.weight[c * cp.k + tap], y, acc);
+    }
+    const float m = to_f32(mixed[e]);
+    float o = m + silu_f(acc);
+    if (valid && !valid[pos]) o = 0.f;
+    out[e] = from_f32<T>(o);
+    if (conv_in) conv_in[e] = from_f32<T>(m * rs[pos] * g);
+  }
+}
+
+// Window form, step 1: cache[new_slot[i]] = RMSNorm(mixed[i]) (rs precomputed).
+template <typename T>
+__global__ void conv_cache_write_kernel(ConvParams cp, const T* __restrict__ mixed, const float* __restrict__ rs,
+                                        int64_t n, const int64_t* __restrict__ new_slot, T* __restrict__ cache) {
+  const int64_t total = n * cp.d;
+  for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < total; e += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t i = e / cp.d, c = e % cp.d;
+    cache[new_slot[i] * cp.d + c] = from_f32<T>(to_f32(mixed[e]) * rs[i] * cp.norm_w[c]);
+  }
+}
+
+// Window form, step 2: out[i] = mixed[i] + SiLU(bias + sum_tap w[:, tap] cache[slot[i, tap]]).
+template <typename T>
+__global__ void conv_window_kernel(ConvParams cp, const T* __restrict__ mixed, int64_t n, const T* __restrict__ cache,
+                                   const int64_t* __restrict__ slot, T* __restrict__ out) {
+  const int64_t total = n * cp.d;
+  for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < total; e += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t i = e / cp.d, c = e % cp.d;
+    float acc = cp.bias ? cp.bias[c] : 0.f;
+    for (int tap = 0; tap < cp.k; ++tap) {
+      const int64_t s = slot[i * cp.k + tap];
+      if (s < 0) continue;
+      acc = fmaf(cp.weight[c * cp.k + tap], to_f32(cache[s * cp.d + c]), acc);
+    }
+    out[e] = from_f32<T>(to_f32(mixed[e]) + silu_f(acc));
+  }
+}
+
+// Readout fold (see lng_readout in the public header): one thread per output element.
+template <typename OT>
+__global__ void fold_qk_kernel(int64_t d, int64_t Dt, int QH, int G, int HD, float scale, const float* __restrict__ q_norm,
+                               const float* __restrict__ q_proj, const float* __restrict__ mem_norm,
+                               const float* __restrict__ kv_proj, OT* __restrict__ w_qk) {
+  const int64_t total = int64_t(QH) * Dt * d;
+  for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < total; e += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t i = e % d;
+    const int64_t k = (e / d) % Dt;
+    const int hg = int(e / (d * Dt));
+    const int h = hg / G;
+    float acc = 0.f;
+    for (int j = 0; j < HD; ++j) acc = fmaf(kv_proj[(int64_t(h) * HD + j) * Dt + k], q_proj[(int64_t(hg) * HD + j) * d + i], acc);
+    w_qk[e] = from_f32<OT>(acc * scale * mem_norm[k] * q_norm[i]);
+  }
+}
+
+template <typename OT>
+__global__ void fold_vo_kernel(int64_t d, int64_t Dt, int QH, int G, int HD, int KV, const float* __restrict__ mem_norm,
+                               const float* __restrict__ kv_proj, const float* __restrict__ o_proj, OT* __restrict__ w_vo) {
+  const int64_t total = d * QH * Dt;
+  const int64_t vbase = int64_t(KV) * HD;  // value rows follow the key rows in kv_proj
+  for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < total; e += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t col = e % (int64_t(QH) * Dt);
+    const int64_t o = e / (int64_t(QH) * Dt);
+    const int hg = int(col / Dt);
+    const int64_t k = col % Dt;
+    const int h = hg / G;
+    float acc = 0.f;
+    for (int j = 0; j < HD; ++j)
+      acc = fmaf(o_proj[o * QH * HD + int64_t(hg) * HD + j], kv_proj[(vbase + int64_t(h) * HD + j) * Dt + k], acc);
+    w_vo[e] = from_f32<OT>(acc * mem_norm[k]);
+  }
+}
+
+// Shard combine: l *= exp(m - m_glob), u *= exp(m - m_glob).
+__global__ void attend_rescale_kernel(const float* __restrict__ m, const float* __restrict__ mg, float* __restrict__ l,
+                                      float* __restrict__ u, int64_t MQ, int64_t Dt) {
+  const int64_t total = MQ * Dt;
+  for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < total; e += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t iq = e / Dt;
+    const float s = expf(m[iq] - mg[iq]);
+    u[e] *= s;
+    if (e % Dt == 0) l[iq] *= s;
+  }
+}
+
+template <typename UT>
+__global__ void attend_normalize_kernel(const float* __restrict__ l, const float* __restrict__ u, int64_t MQ, int64_t Dt,
+                                        UT* __restrict__ out) {
+  const int64_t total = MQ * Dt;
+  for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < total; e += int64_t(gridDim.x) * blockDim.x) {
+    out[e] = from_f32<UT>(u[e] / fmaxf(l[e / Dt], 1.17549435e-38f));
+  }
+}
+
+// Sink attention with explicit K / V (the reference's _manual_gqa, ffnmem/memory/lngram_v2.py:1899-1920):
+// one CTA per (item, kv head); q [M, KV*G, HD], k/v [M, KV, R, HD], out [M, KV*G, HD].
+template <typename T>
+__global__ void sink_gqa_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v, int64_t M,
+                                int KV, int G, int R, int HD, float scale, float sink, T* __restrict__ out) {
+  extern __shared__ float gq_sm[];
+  float* ks = gq_sm;              // [R, HD]
+  float* vs = ks + R * HD;        // [R, HD]
+  float* qs = vs + R * HD;        // [G, HD]
+  float* sc = qs + G * HD;        // [G, R]
+  const int64_t item = blockIdx.x / KV;
+  const int h = blockIdx.x % KV;
+  if (item >= M) return;
+  const T* kb = k + (item * KV + h) * int64_t(R) * HD;
+  const T* vb = v + (item * KV + h) * int64_t(R) * HD;
+  const T* qb = q + (item * KV * G + int64_t(h) * G) * HD;
+  for (int e = threadIdx.x; e < R * HD; e += blockDim.x) {
+    ks[e] = to_f32(kb[e]);
+    vs[e] = to_f32(vb[e]);
+  }
+  for (int e = threadIdx.x; e < G * HD; e += blockDim.x) qs[e] = to_f32(qb[e]);
+  __syncthreads();
+  for (int e = threadIdx.x; e < G * R; e += blockDim.x) {
+    const int g = e / R, r = e % R;
+    float acc = 0.f;
+    for (int j = 0; j < HD; ++j) acc = fmaf(qs[g * HD + j], ks[r * HD + j], acc);
+    sc[e] = acc * scale;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int g = warp; g < G; g += nw) {
+    float mx = sink;
+    for (int r = lane; r < R; r += 32) mx = fmaxf(mx, sc[g * R + r]);
+    mx = warp_max(mx);
+    float sum = 0.f;
+    for (int r = lane; r < R; r += 32) {
+      const float e = expf(sc[g * R + r] - mx);
+      sc[g * R + r] = e;
+      sum += e;
+    }
+    sum = warp_sum(sum) + expf(sink - mx);
+    __syncwarp();
+    for (int r = lane; r < R; r += 32) sc[g * R + r] /= sum;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < G * HD; e += blockDim.x) {
+    const int g = e / HD, j = e % HD;
+    float acc = 0.f;
+    for (int r = 0; r < R; ++r) acc = fmaf(sc[g * R + r], vs[r * HD + j], acc);
+    out[(item * KV * G + int64_t(h) * G + g) * HD + j] = from_f32<T>(acc);
+  }
+}
+
+}  // namespace lng

@@ -1,0 +1,478 @@
+"""Drop-in mirrors of the reference memory modules, running on the lngram_b200 CUDA library.
+
+``RouteNgramMemoryV2`` keeps the constructor arguments, parameter names (so a reference
+``state_dict`` loads unchanged), methods and error behaviour of the reference's
+``ffnmem/memory/lngram_v2.py:830-1407`` for inference; ``LngramMemory`` mirrors the wrapper of
+``ffnmem/memory/wrapper.py:50-125`` (router in fp32, sign codes, module forward).
+
+Every method dispatches to the C ABI (``include/lngram_b200.h``) on the tensors' CUDA device and
+current stream.  There is no CPU path: CPU tensors raise.  Training (gradients through the
+surrogate of ``lngram_v2.py:328-465``) is outside this build's scope and raises as well.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional, Sequence
+
+import torch
+from torch import Tensor, nn
+
+from . import _lib
+from ._lib import check, ptr, stream_ptr
+
+WRAPPER_KEYS = ("routes", "mem_dim", "kv_heads", "q_heads", "head_dim", "router_init_std", "rank1", "router_input",
+                "token_router")
+# Appendix E recipe of the reference wrapper (ffnmem/memory/wrapper.py:37-47)
+APPENDIX_E = dict(bits_per_route=4, ngrams=(2, 3), table_init_std_scale=1.0, output_proj_init_std_scale=0.0,
+                  conv_zero_init=True, conv_kernel_size=4, q_surrogate_enable=True, q_surrogate_mode="approximate",
+                  sink_initial_active_mass=0.5)
+
+
+class _Norm(nn.Module):
+    """Parameter holder with the reference RMSNorm's name (``lngram_v2.py:37-53``)."""
+
+    def __init__(self, size: int, eps: float, device=None, dtype=None):
+        super().__init__()
+        self.hidden_size = int(size)
+        self.eps = float(eps)
+        self.weight = nn.Parameter(torch.ones(size, device=device, dtype=dtype))
+
+
+class _ShortConv(nn.Module):
+    """Parameter holder of ``DepthwiseCausalConv`` (``lngram_v2.py:207-248``)."""
+
+    def __init__(self, d: int, k: int, dilation: int, eps: float, bias: bool, zero_init: bool, device=None, dtype=None):
+        super().__init__()
+        self.hidden_size, self.kernel_size, self.dilation = int(d), int(k), int(dilation)
+        self.left_padding = (self.kernel_size - 1) * self.dilation
+        self.norm = _Norm(d, eps, device=device, dtype=dtype)
+        self.conv = nn.Conv1d(d, d, kernel_size=k, dilation=dilation, groups=d, bias=bias, device=device, dtype=dtype)
+        if zero_init:
+            nn.init.zeros_(self.conv.weight)
+            if self.conv.bias is not None:
+                nn.init.zeros_(self.conv.bias)
+
+
+def _normal_(w: Tensor, std: float) -> None:
+    """fp32 init then cast (``lngram_v2.py:20-33``)."""
+    with torch.no_grad():
+        if std == 0.0:
+            w.zero_()
+        else:
+            w.copy_(torch.empty_like(w, dtype=torch.float32).normal_(0.0, std).to(w.dtype))
+
+
+def _cuda(t: Tensor, what: str) -> Tensor:
+    if not t.is_cuda:
+        raise RuntimeError(f"{what} must be a CUDA tensor: lngram_b200 has no CPU path")
+    return t
+
+
+class RouteNgramMemoryV2(nn.Module):
+    """Inference drop-in for the reference ``RouteNgramMemoryV2`` (sink readout v2)."""
+
+    def __init__(self, hidden_size: int, bits_per_route: int = 4, num_routes: int = 16, memory_dim: int = 128,
+                 ngrams: Sequence[int] = (2, 3), initializer_range: float = 0.02, table_init_std_scale: float = 0.0,
+                 output_proj_init_std_scale: float = 1.0, readout_q_proj_init_std_scale: float = 1.0,
+                 readout_kv_proj_init_std_scale: float = 1.0, readout_num_heads: int = 16,
+                 readout_num_kv_heads: int = 2, readout_head_dim: int = 128, readout_attention_dropout: float = 0.0,
+                 rmsnorm_eps: float = 1e-6, normalization: str = "RMSNorm", conv_kernel_size: int = 4,
+                 conv_dilation: Optional[int] = None, conv_bias: bool = False, conv_zero_init: bool = True,
+                 execution_mode: str = "full", auto_max_kv_mb: float = 384.0, stream_route_chunk_size: int = 64,
+                 readout_checkpoint_streaming: bool = False, q_surrogate_enable: bool = True,
+                 q_surrogate_mode: str = "approximate", q_surrogate_temperature: float = 1.0,
+                 q_surrogate_scale: float = 1.0, dropout: float = 0.0, sink_initial_active_mass: float = 0.5,
+                 device=None, dtype=None):
+        super().__init__()
+        # validation mirrors lngram_v2.py:878-933 (ValueError)
+        self.hidden_size, self.bits_per_route = int(hidden_size), int(bits_per_route)
+        self.num_routes, self.memory_dim = int(num_routes), int(memory_dim)
+        if self.hidden_size <= 0:
+            raise ValueError("hidden_size must be positive")
+        if not 1 <= self.bits_per_route <= 16:
+            raise ValueError("bits_per_route must be in [1, 16]")
+        if self.num_routes <= 0 or self.memory_dim <= 0:
+            raise ValueError("num_routes and memory_dim must be positive")
+        if str(normalization).lower().replace("_", "") != "rmsnorm":
+            raise ValueError("lngram_b200 implements the RMSNorm readout normalisation")
+        if int(conv_kernel_size) <= 0 or (conv_dilation is not None and int(conv_dilation) <= 0):
+            raise ValueError("conv_kernel_size / conv_dilation must be positive")
+        self.ngrams = tuple(sorted({int(v) for v in ngrams}))
+        if not self.ngrams or min(self.ngrams) < 1 or len(self.ngrams) > _lib.MAX_ORDERS:
+            raise ValueError(f"invalid n-gram orders: {self.ngrams}")
+        self.max_ngram_order = max(self.ngrams)
+        self.route_history_length = self.max_ngram_order - 1
+        self.alphabet_size = 1 << self.bits_per_route
+        self.route_logits_dim = self.num_routes * self.bits_per_route
+        self.route_token_dim = len(self.ngrams) * self.memory_dim
+        self.readout_num_heads, self.readout_num_kv_heads = int(readout_num_heads), int(readout_num_kv_heads)
+        self.readout_head_dim = int(readout_head_dim)
+        if self.readout_num_heads % self.readout_num_kv_heads:
+            raise ValueError("readout_num_heads must be divisible by readout_num_kv_heads")
+        if self.readout_num_heads * self.readout_head_dim != self.hidden_size:
+            raise ValueError("LNGram GQA must preserve the full query width: readout_num_heads * readout_head_dim "
+                             f"must equal hidden_size; got {self.readout_num_heads} * {self.readout_head_dim} != "
+                             f"{self.hidden_size}")
+        self.readout_groups = self.readout_num_heads // self.readout_num_kv_heads
+        self.readout_inner_dim = self.readout_num_heads * self.readout_head_dim
+        self.readout_kv_inner_dim = self.readout_num_kv_heads * self.readout_head_dim
+        self.softmax_scale = self.readout_head_dim ** -0.5
+        self.execution_mode = str(execution_mode).lower()
+        if self.execution_mode not in {"full", "streaming", "auto"}:
+            raise ValueError("execution_mode must be full, streaming, or auto")
+        self.stream_route_chunk_size = int(stream_route_chunk_size)
+        mass = float(sink_initial_active_mass)
+        if not math.isfinite(mass) or not 0.0 < mass < 1.0:
+            raise ValueError("sink_initial_active_mass must be finite and in (0, 1)")
+        self.sink_initial_active_mass = mass
+        self.readout_sink_logit = math.log(self.num_routes * (1.0 - mass) / mass)
+        max_rows = max(self.num_routes * self.alphabet_size ** n for n in self.ngrams)
+        self.index_dtype = torch.int32 if max_rows - 1 <= torch.iinfo(torch.int32).max else torch.long
+        eps = float(rmsnorm_eps)
+        self.tables = nn.ModuleDict()
+        for n in self.ngrams:
+            t = nn.Embedding(self.num_routes * self.alphabet_size ** n, self.memory_dim, device=device, dtype=dtype)
+            _normal_(t.weight, initializer_range * table_init_std_scale)
+            self.tables[f"ngram_{n}"] = t
+        self.readout_query_norm = _Norm(hidden_size, eps, device, dtype)
+        self.readout_memory_norm = _Norm(self.route_token_dim, eps, device, dtype)
+        self.readout_q_proj = nn.Linear(hidden_size, self.readout_inner_dim, bias=False, device=device, dtype=dtype)
+        self.readout_kv_proj = nn.Linear(self.route_token_dim, 2 * self.readout_kv_inner_dim, bias=False,
+                                         device=device, dtype=dtype)
+        self.readout_o_proj = nn.Linear(self.readout_inner_dim, hidden_size, bias=False, device=device, dtype=dtype)
+        _normal_(self.readout_q_proj.weight, initializer_range * readout_q_proj_init_std_scale)
+        _normal_(self.readout_kv_proj.weight, initializer_range * readout_kv_proj_init_std_scale)
+        _normal_(self.readout_o_proj.weight, initializer_range * output_proj_init_std_scale)
+        dil = max(self.ngrams) if conv_dilation is None else int(conv_dilation)
+        self.short_conv = _ShortConv(hidden_size, int(conv_kernel_size), dil, eps, bool(conv_bias),
+                                     bool(conv_zero_init), device, dtype)
+        self._fold_key = None
+        self._fold = None
+
+    # ------------------------------------------------------------------ descriptors
+    @property
+    def eps(self) -> float:
+        return self.readout_query_norm.eps
+
+    def _act(self) -> torch.dtype:
+        dt = self.readout_q_proj.weight.dtype
+        if dt not in (torch.float32, torch.bfloat16):
+            raise ValueError("lngram_b200 runs the readout in fp32 or bf16")
+        return dt
+
+    def tables_desc(self, route_tables: dict | None = None) -> _lib.Tables:
+        tabs = route_tables or {n: self.tables[f"ngram_{n}"].weight for n in self.ngrams}
+        t = _lib.Tables()
+        t.n_orders = len(self.ngrams)
+        dts = set()
+        for i, n in enumerate(self.ngrams):
+            w = _cuda(tabs[n], "table")
+            if not w.is_contiguous():
+                raise ValueError("tables must be contiguous")
+            t.orders[i] = n
+            t.tables[i] = w.data_ptr()
+            dts.add(w.dtype)
+        if len(dts) != 1:
+            raise ValueError("all order tables must share a dtype")
+        t.table_dtype = _lib.dtype_code(dts.pop())
+        t.bits = self.bits_per_route
+        t.num_routes = self.num_routes
+        t.memory_dim = self.memory_dim
+        return t
+
+    def _guard(self) -> None:
+        if self.training and torch.is_grad_enabled():
+            raise RuntimeError("lngram_b200 implements the inference forward; the training surrogate "
+                               "(lngram_v2.py:328-465) stays on the reference path")
+
+    def folded(self) -> dict:
+        """w_qk / w_vo of the folded readout (recomputed when any readout parameter changes)."""
+        params = (self.readout_query_norm.weight, self.readout_q_proj.weight, self.readout_memory_norm.weight,
+                  self.readout_kv_proj.weight, self.readout_o_proj.weight)
+        key = tuple((p.data_ptr(), p._version, p.dtype, str(p.device)) for p in params)
+        if self._fold_key == key:
+            return self._fold
+        act = self._act()
+        dev = _cuda(self.readout_q_proj.weight, "readout weights").device
+        lib = _lib.library()
+        f32 = [p.detach().float().contiguous() for p in params]
+        qh, dt, d = self.readout_num_heads, self.route_token_dim, self.hidden_size
+        w_qk = torch.empty(qh * dt, d, device=dev, dtype=act)
+        w_vo = torch.empty(d, qh * dt, device=dev, dtype=act)
+        with torch.cuda.device(dev):
+            check(lib.lng_fold_readout(d, dt, qh, self.readout_num_kv_heads, self.readout_head_dim, ptr(f32[0]),
+                                       ptr(f32[1]), ptr(f32[2]), ptr(f32[3]), ptr(f32[4]), ptr(w_qk), ptr(w_vo),
+                                       _lib.dtype_code(act), stream_ptr()), "fold readout")
+        conv_w = self.short_conv.conv.weight.detach().float().reshape(d, -1).contiguous()
+        conv_b = None if self.short_conv.conv.bias is None else self.short_conv.conv.bias.detach().float().contiguous()
+        self._fold = dict(w_qk=w_qk, w_vo=w_vo, conv_norm=self.short_conv.norm.weight.detach().float().contiguous(),
+                          conv_w=conv_w, conv_b=conv_b)
+        self._fold_key = key
+        return self._fold
+
+    def readout_desc(self, router_w: Tensor | None = None) -> _lib.Readout:
+        f = self.folded()
+        r = _lib.Readout()
+        r.hidden = self.hidden_size
+        r.num_heads, r.num_kv_heads, r.head_dim = self.readout_num_heads, self.readout_num_kv_heads, self.readout_head_dim
+        r.eps = self.eps
+        r.sink_logit = self.readout_sink_logit
+        r.conv_kernel, r.conv_dilation = self.short_conv.kernel_size, self.short_conv.dilation
+        r.act_dtype = _lib.dtype_code(self._act())
+        r.w_qk, r.w_vo = ptr(f["w_qk"]), ptr(f["w_vo"])
+        r.conv_norm, r.conv_weight = ptr(f["conv_norm"]), ptr(f["conv_w"])
+        r.conv_bias = ptr(f["conv_b"])
+        if router_w is not None:
+            r.router_w = ptr(router_w)
+            r.router_in_dim = router_w.shape[1]
+        return r
+
+    # ------------------------------------------------------------------ reference methods
+    def quantize_route_logits(self, q_logits: Tensor) -> Tensor:
+        """``lngram_v2.py:1012-1017`` -> int32 codes [..., R] (bit-exact)."""
+        if q_logits.shape[-1] != self.route_logits_dim:
+            raise ValueError(f"route logits dim={q_logits.shape[-1]}, expected {self.route_logits_dim}")
+        x = _cuda(q_logits, "q_logits").float().contiguous()
+        out = torch.empty(*x.shape[:-1], self.num_routes, device=x.device, dtype=torch.int32)
+        n = x.numel() // self.route_logits_dim
+        with torch.cuda.device(x.device):
+            check(_lib.library().lng_quantize_route_logits(ptr(x), n, self.num_routes, self.bits_per_route, ptr(out),
+                                                           _lib.I32, stream_ptr()), "quantize_route_logits")
+        return out
+
+    def _codes(self, codes: Tensor) -> tuple[Tensor, int]:
+        codes = _cuda(codes, "route codes")
+        if codes.dtype == torch.uint8:
+            return codes.contiguous(), _lib.U8
+        return codes.to(torch.int32).contiguous(), _lib.I32
+
+    def _lookup_route_chunk(self, route_codes: Tensor, q_logits_btrm: Optional[Tensor], route_start: int,
+                            route_end: int, segment_ids: Optional[Tensor], valid_tokens: Optional[Tensor],
+                            target_length: Optional[int] = None) -> Tensor:
+        """``lngram_v2.py:1047-1113``: route tokens [B, T', R', Dt] in the table dtype (exact copies)."""
+        self._guard()
+        b, t, _ = route_codes.shape
+        codes, cdt = self._codes(route_codes)
+        tout = t if target_length is None else min(int(target_length), t)
+        w = self.tables[f"ngram_{self.ngrams[0]}"].weight
+        out = torch.empty(b, tout, route_end - route_start, self.route_token_dim, device=codes.device, dtype=w.dtype)
+        seg = None if segment_ids is None else segment_ids.to(device=codes.device, dtype=torch.int64).contiguous()
+        val = None if valid_tokens is None else valid_tokens.to(device=codes.device, dtype=torch.bool).contiguous()
+        desc = self.tables_desc()
+        with torch.cuda.device(codes.device):
+            check(_lib.library().lng_lookup_route_chunk(desc, ptr(codes), cdt, b, t, int(route_start), int(route_end),
+                                                        ptr(seg), ptr(val), int(tout) if target_length is not None else 0,
+                                                        ptr(out), _lib.dtype_code(out.dtype), stream_ptr()),
+                  "_lookup_route_chunk")
+        return out
+
+    def _linear(self, x: Tensor, w: Tensor, out_dtype: torch.dtype | None = None) -> Tensor:
+        """y = x . w^T through lng_gemm (tcgen05 for bf16 x bf16, CUDA cores otherwise)."""
+        x = x.contiguous()
+        w = w.contiguous()
+        k = x.shape[-1]
+        m = x.numel() // k
+        n = w.shape[0]
+        out = torch.empty(*x.shape[:-1], n, device=x.device, dtype=out_dtype or x.dtype)
+        with torch.cuda.device(x.device):
+            check(_lib.library().lng_gemm(ptr(x), _lib.dtype_code(x.dtype), k, ptr(w), _lib.dtype_code(w.dtype), k,
+                                          ptr(out), _lib.dtype_code(out.dtype), n, m, n, k, None, 0, stream_ptr()),
+                  "gemm")
+        return out
+
+    def _rms_norm(self, x: Tensor, w: Tensor) -> Tensor:
+        x = x.contiguous()
+        d = x.shape[-1]
+        wf = w.detach().float().contiguous()
+        out = torch.empty_like(x)
+        with torch.cuda.device(x.device):
+            check(_lib.library().lng_rms_norm(ptr(x), _lib.dtype_code(x.dtype), x.numel() // d, d, ptr(wf), self.eps,
+                                              ptr(out), _lib.dtype_code(out.dtype), stream_ptr()), "rms_norm")
+        return out
+
+    def _project_query(self, hidden_states: Tensor) -> Tensor:
+        """``lngram_v2.py:1115-1118``: q_proj(RMSNorm(h)) -> [B, T, QH, HD]."""
+        self._guard()
+        b, t, _ = hidden_states.shape
+        h = _cuda(hidden_states, "hidden_states")
+        q = self._linear(self._rms_norm(h, self.readout_query_norm.weight), self.readout_q_proj.weight)
+        return q.view(b, t, self.readout_num_heads, self.readout_head_dim)
+
+    def _project_memory(self, route_tokens: Tensor) -> tuple[Tensor, Tensor]:
+        """``lngram_v2.py:1120-1131``: RMSNorm(Dt) + kv_proj -> K, V [B, T, KV, R, HD]."""
+        self._guard()
+        rt = _cuda(route_tokens, "route_tokens")
+        kv = self._linear(self._rms_norm(rt, self.readout_memory_norm.weight), self.readout_kv_proj.weight)
+        key, value = kv.split(self.readout_kv_inner_dim, dim=-1)
+        b, t, r, _ = key.shape
+        shape = (b, t, r, self.readout_num_kv_heads, self.readout_head_dim)
+        return key.reshape(shape).permute(0, 1, 3, 2, 4), value.reshape(shape).permute(0, 1, 3, 2, 4)
+
+    def _real_route_probabilities(self, scores: Tensor) -> Tensor:
+        """``lngram_v2.py:1877-1885`` (elementwise; kept for API completeness)."""
+        scores = scores.float()
+        sink = scores.new_tensor(self.readout_sink_logit)
+        m = torch.maximum(scores.amax(dim=-1, keepdim=True), sink)
+        ex = torch.exp(scores - m)
+        return ex / (ex.sum(dim=-1, keepdim=True) + torch.exp(sink - m))
+
+    def _manual_gqa(self, query: Tensor, key: Tensor, value: Tensor) -> Tensor:
+        """``lngram_v2.py:1899-1920`` with explicit K/V: sink attention over routes."""
+        self._guard()
+        b, t = query.shape[:2]
+        q = _cuda(query, "query").contiguous()
+        k, v = key.contiguous(), value.contiguous()
+        r = k.shape[-2]
+        out = torch.empty(b, t, self.readout_num_heads, self.readout_head_dim, device=q.device, dtype=q.dtype)
+        with torch.cuda.device(q.device):
+            check(_lib.library().lng_sink_gqa(ptr(q), ptr(k), ptr(v), _lib.dtype_code(q.dtype), b * t,
+                                              self.readout_num_kv_heads, self.readout_groups, r, self.readout_head_dim,
+                                              self.readout_sink_logit, ptr(out), stream_ptr()), "_manual_gqa")
+        return out
+
+    def _finish(self, head_output: Tensor, segment_ids: Optional[Tensor]) -> Tensor:
+        """``lngram_v2.py:1354-1359``: o_proj then + SiLU(conv(RMSNorm(.)))."""
+        self._guard()
+        b, t = head_output.shape[:2]
+        mixed = self._linear(head_output.reshape(b, t, self.readout_inner_dim), self.readout_o_proj.weight)
+        return self._conv_finish(mixed, segment_ids, None)
+
+    def _conv_finish(self, mixed: Tensor, segment_ids: Optional[Tensor], valid_tokens: Optional[Tensor]) -> Tensor:
+        b, t, _ = mixed.shape
+        out = torch.empty_like(mixed)
+        seg = None if segment_ids is None else segment_ids.to(device=mixed.device, dtype=torch.int64).contiguous()
+        val = None if valid_tokens is None else valid_tokens.to(device=mixed.device, dtype=torch.bool).contiguous()
+        desc = self.readout_desc()
+        with torch.cuda.device(mixed.device):
+            check(_lib.library().lng_conv_finish(desc, ptr(mixed.contiguous()), b, t, ptr(seg), ptr(val), ptr(out),
+                                                 None, stream_ptr()), "conv finish")
+        return out
+
+    def forward(self, hidden_states: Tensor, route_codes_btr: Tensor, q_logits: Optional[Tensor] = None,
+                segment_ids: Optional[Tensor] = None, valid_tokens: Optional[Tensor] = None) -> Tensor:
+        """``lngram_v2.py:1361-1407`` (full and streaming modes compute the same function)."""
+        if hidden_states.dim() != 3:
+            raise ValueError("hidden_states must be [B,T,H]")
+        b, t, hidden = hidden_states.shape
+        if hidden != self.hidden_size:
+            raise ValueError(f"hidden size={hidden}, expected {self.hidden_size}")
+        if tuple(route_codes_btr.shape) != (b, t, self.num_routes):
+            raise ValueError("route_codes_btr has an incompatible shape")
+        if q_logits is not None and tuple(q_logits.shape) != (b, t, self.route_logits_dim):
+            raise ValueError(f"q_logits shape={tuple(q_logits.shape)}, expected {(b, t, self.route_logits_dim)}")
+        self._guard()
+        return self.forward_codes(hidden_states, route_codes_btr, segment_ids, valid_tokens)
+
+    def forward_codes(self, h: Tensor, codes: Optional[Tensor], segment_ids=None, valid_tokens=None, router_x=None,
+                      router_w=None, codes_out: Optional[Tensor] = None, out: Optional[Tensor] = None,
+                      workspace: Optional[Tensor] = None) -> Tensor:
+        """One ``lng_memory_forward`` call: codes (given, or from the fp32 router on ``router_x``),
+        folded query GEMM, fused gather + sink attention, folded output GEMM, conv finish."""
+        h = _cuda(h, "hidden_states")
+        act = self._act()
+        if h.dtype != act:
+            h = h.to(act)
+        h = h.contiguous()
+        b, t, _ = h.shape
+        desc_t = self.tables_desc()
+        desc_r = self.readout_desc(router_w)
+        lib = _lib.library()
+        cptr, cdt = None, 0
+        if codes is not None:
+            codes, cdt = self._codes(codes)
+            cptr = ptr(codes)
+        xptr, xdt = None, 0
+        if router_x is not None:
+            router_x = _cuda(router_x, "router input")
+            if router_x.dtype not in (torch.float32, torch.bfloat16):
+                router_x = router_x.float()
+            router_x = router_x.contiguous()
+            xptr, xdt = ptr(router_x), _lib.dtype_code(router_x.dtype)
+        seg = None if segment_ids is None else segment_ids.to(device=h.device, dtype=torch.int64).contiguous()
+        val = None if valid_tokens is None else valid_tokens.to(device=h.device, dtype=torch.bool).contiguous()
+        if out is None:
+            out = torch.empty_like(h)
+        need = lib.lng_memory_workspace_bytes(desc_t, desc_r, b * t)
+        if workspace is None or workspace.numel() < need:
+            workspace = torch.empty(need, device=h.device, dtype=torch.uint8)
+        with torch.cuda.device(h.device):
+            check(lib.lng_memory_forward(desc_t, desc_r, b, t, ptr(h), xptr, xdt, cptr, cdt, ptr(seg), ptr(val),
+                                         ptr(out), ptr(codes_out), ptr(workspace), workspace.numel(), stream_ptr()),
+                  "memory forward")
+        return out
+
+
+class LngramMemory(nn.Module):
+    """Inference drop-in for the reference wrapper ``ffnmem/memory/wrapper.py:50-125``: owns the
+    router ``d_in -> R*bits`` (evaluated in fp32), quantises, runs the module."""
+
+    def __init__(self, d_model: int, mem_cfg: dict, init_std: float = 0.02, norm_eps: float = 1e-5, ssm_dim: int = 0,
+                 device=None, dtype=None):
+        super().__init__()
+        cfg = dict(APPENDIX_E)
+        cfg.update({k: v for k, v in mem_cfg.items() if k not in WRAPPER_KEYS})
+        self.routes = int(mem_cfg["routes"])
+        self.bits = int(cfg["bits_per_route"])
+        head_dim = int(mem_cfg.get("head_dim", 64))
+        q_heads = int(mem_cfg.get("q_heads", d_model // head_dim))
+        if "ngrams" in cfg:
+            cfg["ngrams"] = tuple(int(n) for n in cfg["ngrams"])
+        for k in ("q_surrogate_enable", "q_surrogate_mode"):
+            cfg.pop(k, None)
+        self.module = RouteNgramMemoryV2(hidden_size=d_model, num_routes=self.routes, memory_dim=int(mem_cfg["mem_dim"]),
+                                         readout_num_heads=q_heads, readout_num_kv_heads=int(mem_cfg.get("kv_heads", 4)),
+                                         readout_head_dim=head_dim, initializer_range=init_std, rmsnorm_eps=norm_eps,
+                                         device=device, dtype=dtype, **cfg)
+        self.router_input = str(mem_cfg.get("router_input", "hidden"))
+        if self.router_input not in ("hidden", "embed2"):
+            raise ValueError(f"router_input {self.router_input!r} is not supported by lngram_b200 (hidden, embed2)")
+        in_dim = d_model if self.router_input == "hidden" else 2 * d_model
+        self.router = nn.Linear(in_dim, self.routes * self.bits, bias=False, device=device, dtype=torch.float32)
+        nn.init.normal_(self.router.weight, mean=0.0, std=float(mem_cfg.get("router_init_std", init_std)))
+        if (mem_cfg.get("token_router") or {}).get("enabled", False) or mem_cfg.get("rank1"):
+            raise ValueError("token_router (SD-A) and rank1 are not part of the lngram_b200 inference path")
+
+    def route_logits(self, h_norm: Tensor) -> Tensor:
+        """fp32 router logits (``wrapper.py:98-101``), materialised only on request."""
+        x = _cuda(h_norm, "router input")
+        x = x.contiguous() if x.dtype in (torch.float32, torch.bfloat16) else x.float().contiguous()
+        w = self.router.weight.detach().float().contiguous()
+        n = x.numel() // x.shape[-1]
+        logits = torch.empty(*x.shape[:-1], w.shape[0], device=x.device, dtype=torch.float32)
+        codes = torch.empty(*x.shape[:-1], self.routes, device=x.device, dtype=torch.uint8)
+        with torch.cuda.device(x.device):
+            check(_lib.library().lng_route_codes(ptr(x), _lib.dtype_code(x.dtype), n, x.shape[-1], x.shape[-1], ptr(w),
+                                                 self.routes, self.bits, ptr(codes), _lib.U8, ptr(logits), stream_ptr()),
+                  "route_logits")
+        return logits
+
+    def route_codes(self, x: Tensor) -> Tensor:
+        """Codes [.., R] (uint8) of the fp32 router without materialising its logits."""
+        x = _cuda(x, "router input")
+        x = x.contiguous() if x.dtype in (torch.float32, torch.bfloat16) else x.float().contiguous()
+        w = self.router.weight.detach().float().contiguous()
+        n = x.numel() // x.shape[-1]
+        codes = torch.empty(*x.shape[:-1], self.routes, device=x.device, dtype=torch.uint8)
+        with torch.cuda.device(x.device):
+            check(_lib.library().lng_route_codes(ptr(x), _lib.dtype_code(x.dtype), n, x.shape[-1], x.shape[-1], ptr(w),
+                                                 self.routes, self.bits, ptr(codes), _lib.U8, None, stream_ptr()),
+                  "route_codes")
+        return codes
+
+    def forward(self, h: Tensor, h_norm: Tensor, router_in: Tensor | None = None, *, codes_out: Tensor | None = None,
+                out: Tensor | None = None, workspace: Tensor | None = None) -> Tensor:
+        """``wrapper.py:103-125`` (eval): one fused C call from router input to memory output."""
+        if self.training and torch.is_grad_enabled():
+            raise RuntimeError("lngram_b200 implements the inference forward only")
+        if self.router_input == "hidden":
+            x = h_norm
+        else:
+            if router_in is None:
+                raise ValueError(f"router_input={self.router_input} needs router_in from the model")
+            x = router_in
+        w = self.router.weight.detach()
+        if w.dtype != torch.float32 or not w.is_contiguous():
+            w = w.float().contiguous()
+        return self.module.forward_codes(h, None, router_x=x, router_w=w, codes_out=codes_out, out=out,
+                                         workspace=workspace)

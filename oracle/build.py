@@ -40,6 +40,19 @@ def build_c_oracle() -> Path:
     return out
 
 
+def load_c_oracle():
+    """ctypes handle of the C oracle with its argument types declared."""
+    import ctypes as C
+
+    lib = C.CDLL(str(build_c_oracle()))
+    lib.oracle_pack_codes.argtypes = [C.c_void_p, C.c_int64, C.c_int64, C.c_int, C.c_void_p]
+    lib.oracle_pack_codes.restype = C.c_int
+    lib.oracle_row_indices.argtypes = [C.c_void_p, C.c_int64, C.c_int64, C.c_int64, C.c_int, C.c_int, C.c_void_p,
+                                       C.c_void_p, C.c_void_p]
+    lib.oracle_row_indices.restype = C.c_int
+    return lib
+
+
 def ref_drafter_path() -> Path:
     return REF_OUT / ("morbius_cpu_drafter" + sysconfig.get_config_var("EXT_SUFFIX"))
 

@@ -150,3 +150,28 @@ def test_drafter_oracle_matches_reference(golden, case):
     # the reference C++ drafter saw the same codes and agreed with RefDrafter
     assert float(g["cpp_code_mismatch"]) < 1e-3
     np.testing.assert_allclose(g["cpp_trace_top_logits"], g["trace_top_logits"], atol=1e-4)
+
+
+def test_c_oracle_matches_numpy_oracle():
+    """The plain-C addressing oracle (used at full BASELINE sizes) equals the numpy restatement."""
+    from oracle.build import load_c_oracle
+
+    lib = load_c_oracle()
+    rng = np.random.default_rng(5)
+    for (B, T, R, order, bits) in [(3, 40, 4, 2, 4), (2, 64, 184, 3, 4), (2, 24, 3, 4, 5), (32, 2048, 184, 3, 4)]:
+        codes = rng.integers(0, 1 << bits, (B, T, R)).astype(np.uint8)
+        seg = np.cumsum(rng.random((B, T)) < 0.05, axis=1).astype(np.int64)
+        valid = (rng.random((B, T)) > 0.1).astype(np.uint8)
+        rows = np.empty((B, T, R), np.int64)
+        lib.oracle_row_indices(codes.ctypes.data, B, T, R, order, bits, seg.ctypes.data, valid.ctypes.data,
+                               rows.ctypes.data)
+        want = np.full((B, T, R), -1, np.int64)
+        if T >= order:
+            mask = om.valid_mask(order, B, T, seg, valid.astype(bool))
+            want[:, order - 1:] = om.row_indices(codes.astype(np.int64), order, bits, 0, R)
+            want[~mask] = -1
+        np.testing.assert_array_equal(rows, want)
+    logits = rng.standard_normal((50, 184 * 4)).astype(np.float32)
+    packed = np.empty((50, 184), np.uint8)
+    lib.oracle_pack_codes(logits.ctypes.data, 50, 184, 4, packed.ctypes.data)
+    np.testing.assert_array_equal(packed, om.quantize_route_logits(logits, 4))

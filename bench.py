@@ -52,51 +52,69 @@ def peaks() -> dict:
 
 # --------------------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region."""
+    """SM clock / throttle-reason sampling (every 200 ms) during the timed region, through NVML in a
+    background thread (the fields of ``nvidia-smi --query-gpu=clocks.sm,clocks.max.sm,
+    clocks_event_reasons.*``).  A separate nvidia-smi process was measured to stall this process's
+    CUDA launches, so it is only the fallback when NVML cannot be loaded."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
 
-    def __init__(self, index: int):
-        self.index = index
+    def __init__(self, index: int, period_s: float = 0.2):
+        self.index, self.period = index, period_s
         self.rows: list = []
-        self.proc = None
+        self.stop = threading.Event()
+        self.t = None
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=subprocess.PIPE,
-                                         stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            import pynvml
+
+            pynvml.nvmlInit()
+            uuid = torch.cuda.get_device_properties(self.index).uuid
+            handle = None
+            for i in range(pynvml.nvmlDeviceGetCount()):
+                h = pynvml.nvmlDeviceGetHandleByIndex(i)
+                u = pynvml.nvmlDeviceGetUUID(h)
+                u = u.decode() if isinstance(u, bytes) else u
+                if str(uuid) in u:
+                    handle = h
+            if handle is None:
+                handle = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.nvml, self.handle = pynvml, handle
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM)
+            self.t = threading.Thread(target=self._run, daemon=True)
             self.t.start()
-        except OSError:
-            self.proc = None
+        except Exception as exc:  # NVML unavailable: leave the record empty and say why
+            self.error = f"{type(exc).__name__}: {exc}"
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) >= 9:
-                self.rows.append(parts)
+    def _run(self):
+        nv = self.nvml
+        while not self.stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                self.rows.append((sm, rs))
+            except Exception:
+                pass
+            self.stop.wait(self.period)
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        self.stop.set()
+        if self.t is not None:
+            self.t.join(timeout=5)
 
     def summary(self) -> dict:
         if not self.rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[5 + i].lower().startswith("active")})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.rows)}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"],
+                    "error": getattr(self, "error", None)}
+        nv = self.nvml
+        reasons = sorted({name for _, rs in self.rows for name, const in self.REASONS if rs & getattr(nv, const)})
+        return {"sm_mhz": statistics.median(float(s) for s, _ in self.rows), "sm_max_mhz": float(self.max_mhz),
+                "reasons": reasons, "samples": len(self.rows), "source": "nvml"}
 
 
 # --------------------------------------------------------------------------- distributed plumbing
@@ -190,28 +208,27 @@ def run_ours(args, rank, world, local) -> dict:
         h, hn = inputs[i % 2]
         mem(h, hn, codes_out=codes, out=out, workspace=ws)
 
-    with torch.no_grad():
+    with torch.no_grad(), ClockSampler(local) as clk:
+        time.sleep(0.5)  # let the sampler start before anything is timed
         for i in range(args.warmup):
             step(i)
         torch.cuda.synchronize()
         lib.device_error(clear=True)
         barrier(world)
         torch.cuda.synchronize()
-        with ClockSampler(local) as clk:
-            t0 = time.perf_counter()
-            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            ev0.record()
-            for i in range(args.steps):
-                step(i)
-            ev1.record()
-            torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record()
+        for i in range(args.steps):
+            step(i)
+        ev1.record()
+        torch.cuda.synchronize()
         ms = ev0.elapsed_time(ev1)
         barrier(world)
         ms_max = max_over_ranks(ms, world)
         # roofline: the dominant kernel (fused gather + sink attention) timed alone, same stream
-        qa = ws[: 0]  # placeholder to keep ws alive
         h, hn = inputs[0]
         att = time_attend(mem, lib, h, codes, ws, args.steps)
+        stages = time_stages(mem, lib, h, hn)
         # e2e through the public API with pinned host buffers
         e2e = time_e2e(mem, inputs, args, world)
         dev_err = lib.device_error(clear=True)
@@ -236,6 +253,7 @@ def run_ours(args, rank, world, local) -> dict:
                      "peak_source": pk["source"], "traffic": traffic, "bytes_per_position": bpp,
                      "ms_per_launch": att["ms"], "launches": att["launches"]},
         "e2e": e2e,
+        "stages_ms": stages,
         "gpu_launches": LAUNCHES_PER_FORWARD * args.steps,
         "clocks": clk.summary(),
     }
@@ -275,6 +293,54 @@ def time_attend(mem, lib, h, codes, ws, steps) -> dict:
     e1.record()
     torch.cuda.synchronize()
     return {"ms": e0.elapsed_time(e1) / n, "launches": n}
+
+
+def time_stages(mem, lib, h, hn, reps: int = 5) -> dict:
+    """CUDA-event time of each stage of one forward, called one C entry point at a time."""
+    m = mem.module
+    M = SB["B"] * SB["T"]
+    dt = m.route_token_dim
+    qd = m.readout_num_heads * dt
+    dev = h.device
+    L = lib.library()
+    s = lib.stream_ptr()
+    f = m.folded()
+    split = mem.router_split()
+    codes = torch.empty(M, SB["routes"], device=dev, dtype=torch.uint8)
+    rs = torch.empty(M, device=dev, dtype=torch.float32)
+    qa = torch.empty(M, qd, device=dev, dtype=torch.bfloat16)
+    u = torch.empty_like(qa)
+    mixed = torch.empty(M, SB["d"], device=dev, dtype=torch.bfloat16)
+    out = torch.empty_like(mixed)
+    desc_t, desc_r = m.tables_desc(), m.readout_desc()
+    stages = {
+        "router_tc": lambda: lib.check(L.lng_route_codes_split(hn.data_ptr(), M, SB["d"], SB["d"], split.data_ptr(),
+                                                               SB["routes"], SB["bits"], codes.data_ptr(), s)),
+        "rms_h": lambda: lib.check(L.lng_rms_rows(h.data_ptr(), lib.BF16, M, SB["d"], m.eps, rs.data_ptr(), s)),
+        "qa_gemm_tc": lambda: lib.check(L.lng_gemm(h.data_ptr(), lib.BF16, SB["d"], f["w_qk"].data_ptr(), lib.BF16,
+                                                   SB["d"], qa.data_ptr(), lib.BF16, qd, M, qd, SB["d"], None, 0, s)),
+        "gather_attend": lambda: lib.check(L.lng_route_attend(desc_t, codes.data_ptr(), lib.U8, SB["B"], SB["T"], 0,
+                                                              None, None, None, 0, SB["routes"], m.readout_num_heads,
+                                                              m.eps, m.readout_sink_logit, qa.data_ptr(),
+                                                              rs.data_ptr(), u.data_ptr(), lib.BF16, 0, None, None,
+                                                              s)),
+        "out_gemm_tc": lambda: lib.check(L.lng_gemm(u.data_ptr(), lib.BF16, qd, f["w_vo"].data_ptr(), lib.BF16, qd,
+                                                    mixed.data_ptr(), lib.BF16, SB["d"], M, SB["d"], qd, None, 0, s)),
+        "conv_finish": lambda: lib.check(L.lng_conv_finish(desc_r, mixed.data_ptr(), SB["B"], SB["T"], None, None,
+                                                           out.data_ptr(), None, s)),
+    }
+    res = {}
+    for name, fn in stages.items():
+        fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        res[name] = round(e0.elapsed_time(e1) / reps, 4)
+    return res
 
 
 def time_e2e(mem, inputs, args, world) -> dict:
@@ -376,8 +442,10 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=("sb_prefill",), default="sb_prefill")
+    ap.add_argument("--batch", type=int, default=SB["B"], help="sequences per GPU (32 = BASELINE; smaller for ncu)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args(argv)
+    SB["B"] = int(args.batch)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     rank, world, local = dist_setup(args.gpus) if args.impl == "ours" else (

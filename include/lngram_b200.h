@@ -71,6 +71,17 @@ int lng_quantize_route_logits(const float* logits, int64_t n, int64_t routes, in
 int lng_route_codes(const void* x, int32_t x_dtype, int64_t n, int64_t in_dim, int64_t x_stride, const float* weight,
                     int64_t routes, int32_t bits, void* codes, int32_t codes_dtype, float* logits, lng_stream_t stream);
 
+/* Split the fp32 router weight W [rows, in_dim] once into bf16 parts W1 | W2 | W3 ([rows, 3*in_dim],
+ * W = W1 + W2 + W3) for the tensor-core router below (a load-time step; no reference counterpart). */
+int lng_router_prepare(const float* weight, int64_t rows, int64_t in_dim, void* w_split, lng_stream_t stream);
+
+/* The router of lng_route_codes on the tcgen05 tensor cores for bf16 inputs x [n, in_dim] (row stride
+ * x_stride): logits = x.W1^T + x.W2^T + x.W3^T (each bf16 product exact, fp32 accumulation) sign-packed
+ * to u8 codes [n, routes] in the GEMM epilogue.  bits in [1, 6], in_dim % 64 == 0, 16-byte rows.
+ * Replaces LngramMemory.route_logits + quantize (ffnmem/memory/wrapper.py:98-101, :106-112). */
+int lng_route_codes_split(const void* x_bf16, int64_t n, int64_t in_dim, int64_t x_stride, const void* w_split,
+                          int64_t routes, int32_t bits, uint8_t* codes, lng_stream_t stream);
+
 /* embed2 router features for token ids (ffnmem/memory/router.py:50-69): for item i with current
  * token cur[i] and previous token prev[i] (-1 = the learned start vector), writes
  * out[i] = concat(RMSNorm(E[prev] or start; prev_w), RMSNorm(E[cur]; cur_w)) in fp32 [n, 2*d].
@@ -91,7 +102,14 @@ typedef struct {
   int32_t bits;        /* bits per route, 1..16 */
   int64_t num_routes;
   int64_t memory_dim;  /* route token width Dt = n_orders * memory_dim */
+  /* Optional per-row sums of squares (fp32 [rows] per order, from lng_table_row_ss): the readout
+   * kernels then read one float per gathered row instead of recomputing the row's RMS. */
+  const float* row_ss[LNG_MAX_ORDERS];
 } lng_tables;
+
+/* row_ss[o][i] = sum_k tables[o][i, k]^2 in fp32 for every row of every order (a load-time step
+ * for lng_route_attend / lng_memory_forward; no reference counterpart). */
+int lng_table_row_ss(const lng_tables* tables, float* const* row_ss, lng_stream_t stream);
 
 /* Route tokens [B, T_out, route_end-route_start, Dt] for codes [B, T, num_routes] (u8 or i32):
  * per order the row r*A^n + sum_k c[t-n+1+k] << (k*bits) (oldest code least significant), zero
@@ -139,6 +157,7 @@ typedef struct {
   const float* conv_bias;  /* [d] or NULL */
   const float* router_w;   /* [R*bits, router_in_dim] fp32, or NULL when codes are supplied */
   int64_t router_in_dim;
+  const void* router_w_split; /* lng_router_prepare output, or NULL (bf16 router inputs then use CUDA cores) */
 } lng_readout;
 
 /* Build w_qk / w_vo (act_dtype) from the reference parameters (all fp32):

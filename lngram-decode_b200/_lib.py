@@ -33,7 +33,7 @@ def dtype_code(t: torch.dtype) -> int:
 class Tables(C.Structure):
     _fields_ = [("n_orders", C.c_int32), ("orders", C.c_int32 * MAX_ORDERS), ("tables", C.c_void_p * MAX_ORDERS),
                 ("table_dtype", C.c_int32), ("bits", C.c_int32), ("num_routes", C.c_int64),
-                ("memory_dim", C.c_int64)]
+                ("memory_dim", C.c_int64), ("row_ss", C.c_void_p * MAX_ORDERS)]
 
 
 class Readout(C.Structure):
@@ -41,7 +41,7 @@ class Readout(C.Structure):
                 ("head_dim", C.c_int32), ("eps", C.c_float), ("sink_logit", C.c_float), ("conv_kernel", C.c_int32),
                 ("conv_dilation", C.c_int32), ("act_dtype", C.c_int32), ("w_qk", C.c_void_p), ("w_vo", C.c_void_p),
                 ("conv_norm", C.c_void_p), ("conv_weight", C.c_void_p), ("conv_bias", C.c_void_p),
-                ("router_w", C.c_void_p), ("router_in_dim", C.c_int64)]
+                ("router_w", C.c_void_p), ("router_in_dim", C.c_int64), ("router_w_split", C.c_void_p)]
 
 
 class Array(C.Structure):
@@ -71,7 +71,10 @@ SIGNATURES = {
     "lng_device_error": (C.c_int, [C.c_int]),
     "lng_quantize_route_logits": (C.c_int, [P, i64, i64, i32, P, i32, P]),
     "lng_route_codes": (C.c_int, [P, i32, i64, i64, i64, P, i64, i32, P, i32, P, P]),
+    "lng_router_prepare": (C.c_int, [P, i64, i64, P, P]),
+    "lng_route_codes_split": (C.c_int, [P, i64, i64, i64, P, i64, i32, P, P]),
     "lng_embed2_features": (C.c_int, [P, P, i64, P, i32, i64, i64, P, P, P, f32, P, P]),
+    "lng_table_row_ss": (C.c_int, [PT, C.POINTER(C.c_void_p), P]),
     "lng_lookup_route_chunk": (C.c_int, [PT, P, i32, i64, i64, i64, i64, P, P, i64, P, i32, P]),
     "lng_lookup_windows": (C.c_int, [PT, P, i32, i64, i64, P, P, i32, P]),
     "lng_fold_readout": (C.c_int, [i64, i64, i32, i32, i32, P, P, P, P, P, P, P, i32, P]),
@@ -118,11 +121,17 @@ def library(require_device: bool = True):
             fn.argtypes = args
         _LIB = lib
     if require_device:
-        if not torch.cuda.is_available():
-            raise RuntimeError("lngram_b200 needs a CUDA device (sm_100a); there is no CPU fallback")
-        if not _LIB.lng_device_ok():
-            raise RuntimeError("lngram_b200 needs a compute-capability 10.x (B200) device")
+        dev = torch.cuda.current_device() if torch.cuda.is_available() else None
+        if dev not in _DEVICE_OK:
+            if dev is None:
+                raise RuntimeError("lngram_b200 needs a CUDA device (sm_100a); there is no CPU fallback")
+            if not _LIB.lng_device_ok():
+                raise RuntimeError("lngram_b200 needs a compute-capability 10.x (B200) device")
+            _DEVICE_OK.add(dev)
     return _LIB
+
+
+_DEVICE_OK: set = set()  # devices already checked (the check queries device properties)
 
 
 def check(status: int, what: str = "") -> None:

@@ -18,6 +18,7 @@ enum DeviceError : unsigned int {
 
 struct TableSet {
   const void* tab[LNG_MAX_ORDERS];
+  const float* ss[LNG_MAX_ORDERS];  // per-row sums of squares, or null
   int order[LNG_MAX_ORDERS];
   int n_orders;
   int bits;
@@ -38,6 +39,76 @@ struct CodeSource {
   int64_t t_offset;      // sequence mode: item t is absolute position t + t_offset (target_length)
   int64_t bstride;       // sequence mode: positions between consecutive batch rows (>= T)
 };
+
+// ---- pipelined form used by the gather kernels: an item's geometry once, then per-route codes.
+constexpr int MAXW = 4;  // longest n-gram window (max order) the pipelined gather supports
+
+struct ItemGeo {
+  int64_t cur;     // codes row of the item's newest slot
+  int avail;       // slots that exist at and before `cur` (capped at MAXW)
+  uint32_t omask;  // bit o set: order o's window is valid for this item
+};
+
+__device__ __forceinline__ ItemGeo item_geometry(const CodeSource& s, const int* orders, int n_orders, int64_t item) {
+  ItemGeo g;
+  g.omask = 0;
+  if (s.window > 0) {
+    const int64_t W = s.window;
+    g.cur = item * W + W - 1;
+    g.avail = int(W < MAXW ? W : MAXW);
+    for (int o = 0; o < n_orders; ++o) {
+      const int n = orders[o];
+      bool ok = W >= n;
+      if (ok && s.seg) ok = s.seg[item * W + W - n] == s.seg[item * W + W - 1];
+      g.omask |= uint32_t(ok) << o;
+    }
+  } else {
+    const int64_t Tout = s.T - s.t_offset;
+    const int64_t b = item / Tout;
+    const int64_t t = item - b * Tout + s.t_offset;
+    const int64_t p = b * s.bstride + t;
+    g.cur = p;
+    g.avail = int(t + 1 < MAXW ? t + 1 : MAXW);
+    const bool tok_ok = !s.valid_tokens || s.valid_tokens[p];
+    for (int o = 0; o < n_orders; ++o) {
+      const int n = orders[o];
+      bool ok = tok_ok && t >= n - 1;
+      if (ok && s.segment_ids) ok = s.segment_ids[p - n + 1] == s.segment_ids[p];
+      g.omask |= uint32_t(ok) << o;
+    }
+  }
+  return g;
+}
+
+// Codes of route r in the item's window, newest first (c[k] = code at slot cur - k); all loads are
+// independent so they overlap, and their first use can be one pipeline step later.
+template <typename CodeT>
+__device__ __forceinline__ void load_window_codes(const CodeSource& s, const ItemGeo& g, int64_t r, bool route_ok,
+                                                  int32_t (&c)[MAXW]) {
+  const CodeT* codes = static_cast<const CodeT*>(s.codes);
+#pragma unroll
+  for (int k = 0; k < MAXW; ++k) c[k] = (route_ok && k < g.avail) ? int32_t(codes[(g.cur - k) * s.R + r]) : 0;
+}
+
+// Table row of order n for window codes c (oldest code least significant), or -1.
+__device__ __forceinline__ int64_t window_row(const int32_t (&c)[MAXW], int order, int bits, int64_t r, bool valid) {
+  if (!valid) return -1;
+  int64_t addr = 0;
+  bool range_ok = true;
+#pragma unroll
+  for (int i = 0; i < MAXW; ++i) {
+    if (i < order) {
+      const int32_t v = c[order - 1 - i];
+      range_ok = range_ok && (v >= 0) && (v < (1 << bits));
+      addr |= int64_t(v) << (i * bits);
+    }
+  }
+  if (!range_ok) {
+    atomicCAS(&g_error_word, 0u, (unsigned int)DEV_ERR_CODE_RANGE);
+    return -1;
+  }
+  return r * (int64_t(1) << (bits * order)) + addr;
+}
 
 template <typename CodeT>
 __device__ __forceinline__ int64_t read_code(const CodeSource& s, int64_t pos_row, int64_t r) {

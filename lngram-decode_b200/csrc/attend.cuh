@@ -210,7 +210,8 @@ struct AttendMmaCfg {
   static constexpr int KT = (DT + 15) / 16;    // k16 steps of the score product
   static constexpr int NTU = DT / 8;           // n8 tiles of the weighted row sum
   static constexpr int ROWB = DT * 2;          // bytes per token row in shared memory
-  static constexpr int STAGE_BYTES = C * ROWB + 32;  // + zero pad read by the last k-step
+  static constexpr int SS_OFF = C * ROWB + 32; // zero pad read by the last k-step, then the rows' sums of squares
+  static constexpr int STAGE_BYTES = SS_OFF + C * 4;
 };
 
 template <typename CodeT, typename T, int DT, int WARPS, int STAGES>
@@ -223,12 +224,11 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
   unsigned char* stage_base = smem_raw + size_t(warp) * STAGES * SB;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw + size_t(WARPS) * STAGES * SB) + warp * STAGES;
 
-  const int64_t nroutes = p.route_end - p.route_start;
-  const int64_t nch = (nroutes + C - 1) / C;
+  const int nch = int((p.route_end - p.route_start + C - 1) / C);
   const int64_t gwarp = int64_t(blockIdx.x) * WARPS + warp;
   const int64_t nwarps = int64_t(gridDim.x) * WARPS;
   const int64_t my_items = gwarp < p.M ? (p.M - 1 - gwarp) / nwarps + 1 : 0;
-  const int64_t jobs = my_items * nch;
+  const int jobs = int(my_items * nch);
   const bool sink_in = !p.partial || p.route_start == 0;
   const int mem_dim = int(p.ts.mem_dim);
 
@@ -241,26 +241,67 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
     if (lane < 8) reinterpret_cast<uint32_t*>(stage_base + s * SB + C * ROWB)[lane] = 0u;
   __syncwarp();
 
-  // issue the gather of job j into its stage: lane = route within the chunk
-  auto issue = [&](int64_t j) {
-    const int s = int(j % STAGES);
-    const int64_t item = gwarp + (j / nch) * nwarps;
-    const int64_t r = p.route_start + (j % nch) * C + lane;
+  // Gather pipeline, lane = route within the chunk.  Job J's codes are loaded (prefetch) one
+  // iteration before its row copies are issued, and copies run STAGES-1 jobs ahead of the math, so
+  // neither the code loads nor the row loads sit on the critical path.
+  int64_t pf_item = gwarp;  // prefetch cursor
+  int pf_chunk = 0;
+  ItemGeo pf_geo{};
+  int32_t pend_c[MAXW];
+  ItemGeo pend_geo{};
+  int pend_chunk = 0;
+  auto prefetch = [&]() {
+    if (pf_chunk == 0) pf_geo = item_geometry(p.src, p.ts.order, p.ts.n_orders, pf_item);
+    pend_geo = pf_geo;
+    pend_chunk = pf_chunk;
+    const int64_t r = p.route_start + int64_t(pf_chunk) * C + lane;
+    load_window_codes<CodeT>(p.src, pf_geo, r, r < p.route_end, pend_c);
+    if (++pf_chunk == nch) {
+      pf_chunk = 0;
+      pf_item += nwarps;
+    }
+  };
+  // The sum of squares of each gathered row (precomputed per table row) is loaded when the row's copy
+  // is issued and written to the stage one iteration later, so its load latency is hidden too; the
+  // lane that wrote it is the lane that reads it.
+  const bool have_ss = p.ts.ss[0] != nullptr;
+  float ss_pend[LNG_MAX_ORDERS];  // raw loaded values: summed only at flush time, after the loads landed
+  int ss_stage = -1;
+  auto flush_ss = [&]() {
+    if (ss_stage >= 0) {
+      float ss = 0.f;
+#pragma unroll
+      for (int o = 0; o < LNG_MAX_ORDERS; ++o)
+        if (o < p.ts.n_orders) ss += ss_pend[o];
+      reinterpret_cast<float*>(stage_base + ss_stage * SB + Cfg::SS_OFF)[lane] = ss;
+    }
+    ss_stage = -1;
+  };
+  auto issue = [&](int s) {
+    flush_ss();
+    const int64_t r = p.route_start + int64_t(pend_chunk) * C + lane;
     unsigned char* row_smem = stage_base + s * SB + lane * ROWB;
     int64_t rows[LNG_MAX_ORDERS];
     uint32_t bytes = 0;
-    for (int o = 0; o < p.ts.n_orders; ++o) {
-      rows[o] = r < p.route_end ? ngram_row<CodeT>(p.src, item, r, p.ts.order[o], p.ts.bits) : -1;
+#pragma unroll
+    for (int o = 0; o < LNG_MAX_ORDERS; ++o) {
+      if (o >= p.ts.n_orders) break;
+      rows[o] = window_row(pend_c, p.ts.order[o], p.ts.bits, r, r < p.route_end && ((pend_geo.omask >> o) & 1u));
+      ss_pend[o] = 0.f;
       if (rows[o] >= 0) {
         bytes += uint32_t(mem_dim * 2);
+        if (have_ss) ss_pend[o] = __ldg(p.ts.ss[o] + rows[o]);
       } else {
         uint4* z = reinterpret_cast<uint4*>(row_smem + o * mem_dim * 2);
         for (int v = 0; v < mem_dim * 2 / 16; ++v) z[v] = make_uint4(0, 0, 0, 0);
       }
     }
+    ss_stage = s;
     fence_proxy_async_smem();
     mbar_arrive_expect_tx(&bars[s], bytes);
-    for (int o = 0; o < p.ts.n_orders; ++o) {
+#pragma unroll
+    for (int o = 0; o < LNG_MAX_ORDERS; ++o) {
+      if (o >= p.ts.n_orders) break;
       if (rows[o] >= 0) {
         const unsigned char* src = static_cast<const unsigned char*>(p.ts.tab[o]) + rows[o] * int64_t(mem_dim) * 2;
         bulk_g2s(row_smem + o * mem_dim * 2, src, uint32_t(mem_dim * 2), &bars[s]);
@@ -268,7 +309,11 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
     }
   };
 
-  for (int64_t j = 0; j < STAGES - 1 && j < jobs; ++j) issue(j);
+  for (int j = 0; j < STAGES - 1 && j < jobs; ++j) {
+    prefetch();
+    issue(j % STAGES);
+  }
+  if (STAGES - 1 < jobs) prefetch();
 
   uint32_t qa_frag[KT][4];
   float uacc[NTU][4];
@@ -276,12 +321,26 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
   float qs = 1.f;
   const int g = lane >> 2, t4 = lane & 3;
   T* tag = nullptr;
+  int64_t item = gwarp - nwarps;  // consume cursor
+  int chunk = nch - 1;
+  int s = STAGES - 1;
+  uint32_t phase = 1;
 
-  for (int64_t j = 0; j < jobs; ++j) {
-    if (j + STAGES - 1 < jobs) issue(j + STAGES - 1);
-    const int s = int(j % STAGES);
-    const int64_t item = gwarp + (j / nch) * nwarps;
-    const int64_t chunk = j % nch;
+  for (int j = 0; j < jobs; ++j) {
+    if (j + STAGES - 1 < jobs) {
+      issue((j + STAGES - 1) % STAGES);
+      if (j + STAGES < jobs) prefetch();
+    } else {
+      flush_ss();
+    }
+    if (++s == STAGES) {
+      s = 0;
+      phase ^= 1u;
+    }
+    if (++chunk == nch) {
+      chunk = 0;
+      item += nwarps;
+    }
     if (chunk == 0) {
       // new item: its folded query as A fragments (rows = heads, k = token dims), zero padded
       const T* qg = static_cast<const T*>(p.qa) + item * int64_t(p.qh) * DT;
@@ -302,14 +361,16 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
       l_r[0] = l_r[1] = 0.f;  // per-thread partial sums; the sink's 1 is added at the end
       qs = p.qscale ? p.qscale[item] : 1.f;
     }
-    const bool landed = mbar_wait_bounded(&bars[s], uint32_t((j / STAGES) & 1), &g_error_word, DEV_ERR_WAIT_TIMEOUT);
+    const bool landed = mbar_wait_bounded(&bars[s], phase, &g_error_word, DEV_ERR_WAIT_TIMEOUT);
     if (!__all_sync(0xffffffffu, landed)) return;
     const unsigned char* st = stage_base + s * SB;
     const uint32_t st_addr = smem_addr(st);
 
     // inverse RMS of this lane's route token (row = lane)
     float rxl;
-    {
+    if (have_ss) {
+      rxl = rsqrtf(reinterpret_cast<const float*>(st + Cfg::SS_OFF)[lane] / float(DT) + p.eps);
+    } else {
       const uint4* rowv = reinterpret_cast<const uint4*>(st + lane * ROWB);
       float ss = 0.f;
 #pragma unroll
@@ -340,20 +401,36 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
 #pragma unroll
-    for (int kt = 0; kt < KT; ++kt) {
+    for (int kt = 0; kt + 1 < KT; kt += 2) {
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt) {
-        // B fragment: rows = routes nt*8..+7, k = kt*16..+15 (two 8x8 matrices)
+        // B fragments of two k16 steps: rows = routes nt*8..+7, k = kt*16..kt*16+31 (four 8x8 matrices)
         const int rrow = nt * 8 + (lane & 7);
-        const int kcol = kt * 16 + ((lane >> 3) & 1) * 8;
+        const int kcol = kt * 16 + (lane >> 3) * 8;
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(st_addr + rrow * ROWB + kcol * 2, b0, b1, b2, b3);
+        mma16816<T>(sacc[nt], qa_frag[kt], b0, b1);
+        mma16816<T>(sacc[nt], qa_frag[kt + 1], b2, b3);
+      }
+    }
+    if (KT & 1) {
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        const int rrow = nt * 8 + (lane & 7);
+        const int kcol = (KT - 1) * 16 + ((lane >> 3) & 1) * 8;
         uint32_t b0, b1;
         ldsm_x2(st_addr + rrow * ROWB + kcol * 2, b0, b1);
-        mma16816<T>(sacc[nt], qa_frag[kt], b0, b1);
+        mma16816<T>(sacc[nt], qa_frag[KT - 1], b0, b1);
       }
     }
 
-    // online softmax update with the sink seed
-    const int64_t rbase = p.route_start + chunk * C;
+    // online softmax update with the sink seed; rxv = this thread's 8 route columns' 1/rms
+    const int64_t rbase = p.route_start + int64_t(chunk) * C;
+    float rxv[4][2];
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int b = 0; b < 2; ++b) rxv[nt][b] = __shfl_sync(0xffffffffu, rxl, nt * 8 + t4 * 2 + b);
     float mx[2] = {m_r[0], m_r[1]};
     float sv[4][4];
 #pragma unroll
@@ -361,8 +438,7 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
         const int col = nt * 8 + t4 * 2 + (h & 1);
-        const float rxc = __shfl_sync(0xffffffffu, rxl, col);
-        float v = sacc[nt][h] * qs * rxc;
+        float v = sacc[nt][h] * (qs * rxv[nt][h & 1]);
         if (rbase + col >= p.route_end) v = -INFINITY;
         sv[nt][h] = v;
         mx[h >> 1] = fmaxf(mx[h >> 1], v);
@@ -376,7 +452,7 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
     float alpha[2];
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
-      alpha[i] = expf(m_r[i] - mx[i]);
+      alpha[i] = __expf(m_r[i] - mx[i]);
       m_r[i] = mx[i];
       l_r[i] *= alpha[i];
     }
@@ -386,11 +462,9 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
       float e[4];
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
-        const int col = nt * 8 + t4 * 2 + (h & 1);
-        const float rxc = __shfl_sync(0xffffffffu, rxl, col);
-        const float ex = expf(sv[nt][h] - m_r[h >> 1]);
+        const float ex = __expf(sv[nt][h] - m_r[h >> 1]);
         l_r[h >> 1] += ex;
-        e[h] = ex * rxc;
+        e[h] = ex * rxv[nt][h & 1];
       }
       pa[nt >> 1][(nt & 1) * 2 + 0] = pack2(e[0], e[1], tag);
       pa[nt >> 1][(nt & 1) * 2 + 1] = pack2(e[2], e[3], tag);

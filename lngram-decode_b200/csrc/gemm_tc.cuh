@@ -1,14 +1,365 @@
-// tcgen05 (5th-generation tensor core) GEMMs for sm_100a: placeholder until the kernels land.
+// tcgen05 GEMMs for sm_100a: C[M, N] = A[M, K] . B[N, K]^T with bf16 operands staged by TMA
+// (128-byte swizzle) into a shared-memory ring, one elected thread issuing tcgen05.mma into a
+// TMEM fp32 accumulator (128 lanes x BN columns), and all four warps reading it back with
+// tcgen05.ld for the epilogue.
+//
+// Two epilogues: MODE 0 stores C (f32 or bf16, optional per-row scale); MODE 1 is the router:
+// logits of 32 routes x `bits` per tile are sign-packed into uint8 codes in registers
+// (ffnmem/memory/lngram_v2.py:74-89), so the fp32 logits never reach memory.  For the router the
+// fp32 weight is split once into three bf16 parts W = W1 + W2 + W3 stored side by side along K
+// and A's k coordinate wraps (a_kperiod): x . W^T = x . W1^T + x . W2^T + x . W3^T with every
+// bf16 x bf16 product exact and fp32 accumulation -- fp32-accurate logits from the tensor cores.
 #pragma once
 
-#include "common.cuh"
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "address.cuh"
 
 namespace lng {
 
-inline int tc_gemm_bf16(const __nv_bfloat16*, int64_t, const __nv_bfloat16*, int64_t, void*, int32_t, int64_t, int64_t,
-                        int64_t, int64_t, const float*, cudaStream_t) {
-  return LNG_ERR_UNSUPPORTED;
+constexpr int TC_BM = 128, TC_BK = 64;
+
+struct TcGemmParams {
+  int64_t M, N, K;       // K = total reduction length seen by B (A wraps with a_kperiod)
+  int64_t a_kperiod;
+  void* C;
+  int64_t ldc;
+  int c_dtype;           // LNG_F32 / LNG_BF16 (MODE 0)
+  const float* rowscale; // MODE 0, may be null
+  int bits;              // MODE 1
+  int64_t routes;        // MODE 1
+  uint8_t* codes;        // MODE 1, [M, routes]
+};
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+      : "memory");
 }
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// K-major operand tile written by TMA with 128-byte swizzle: 8-row groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t umma_desc_sw128(const void* tile) {
+  const uint64_t addr = smem_addr(tile);
+  uint64_t d = 0;
+  d |= (addr >> 4) & 0x3FFFull;        // start address
+  d |= uint64_t(1) << 16;              // leading byte offset (unused for swizzled K-major)
+  d |= uint64_t(1024 >> 4) << 32;      // stride byte offset: 8 rows x 128 B
+  d |= uint64_t(1) << 46;              // descriptor version (sm_100)
+  d |= uint64_t(2) << 61;              // SWIZZLE_128B
+  return d;
+}
+// kind::f16 instruction descriptor: bf16 A/B, fp32 D, both K-major.
+__host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) {
+  return (1u << 4)                     // D format f32
+         | (1u << 7)                   // A format bf16
+         | (1u << 10)                  // B format bf16
+         | (uint32_t(N >> 3) << 17)    // N / 8
+         | (uint32_t(M >> 4) << 24);   // M / 16
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accum)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <int BN>
+struct TcCfg {
+  static constexpr uint32_t A_BYTES = TC_BM * TC_BK * 2;
+  static constexpr uint32_t B_BYTES = BN * TC_BK * 2;
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
+  static constexpr uint32_t TMEM_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+  static constexpr size_t SMEM = size_t(STAGES) * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+template <int BN, int MODE>
+__global__ void __launch_bounds__(128, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b, TcGemmParams p) {
+  using Cfg = TcCfg<BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t tc_smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + size_t(STAGES) * Cfg::STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_bar = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_bar + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t m0 = int64_t(blockIdx.y) * TC_BM, n0 = int64_t(blockIdx.x) * BN;
+  const int KB = int((p.K + TC_BK - 1) / TC_BK);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_bar, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tma_a);
+    tma_prefetch_desc(&tma_b);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                 "r"(Cfg::TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool ok = true;
+
+  if (warp == 0 && lane == 0) {
+    // TMA producer
+    for (int kb = 0; kb < KB && ok; ++kb) {
+      const int s = kb % STAGES;
+      if (kb >= STAGES) ok = mbar_wait_bounded(&empty[s], uint32_t(((kb / STAGES) - 1) & 1), &g_error_word, DEV_ERR_WAIT_TIMEOUT);
+      if (!ok) break;
+      mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+      uint8_t* st = base + size_t(s) * Cfg::STAGE_BYTES;
+      const int32_t ka = int32_t((int64_t(kb) * TC_BK) % p.a_kperiod);
+      tma_load_2d(st, &tma_a, ka, int32_t(m0), &full[s]);
+      tma_load_2d(st + Cfg::A_BYTES, &tma_b, int32_t(kb * TC_BK), int32_t(n0), &full[s]);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // MMA issuer
+    constexpr uint32_t idesc = umma_idesc_bf16(TC_BM, BN);
+    for (int kb = 0; kb < KB && ok; ++kb) {
+      const int s = kb % STAGES;
+      ok = mbar_wait_bounded(&full[s], uint32_t((kb / STAGES) & 1), &g_error_word, DEV_ERR_WAIT_TIMEOUT);
+      if (!ok) break;
+      tc_fence_after();
+      const uint8_t* st = base + size_t(s) * Cfg::STAGE_BYTES;
+      const uint64_t da = umma_desc_sw128(st), db = umma_desc_sw128(st + Cfg::A_BYTES);
+#pragma unroll
+      for (int k = 0; k < TC_BK / 16; ++k) {
+        // advance 16 bf16 = 32 bytes along K inside the swizzle atom (+2 in 16-byte units)
+        umma_bf16(tmem, da + uint64_t(2 * k), db + uint64_t(2 * k), idesc, (kb | k) != 0 ? 1u : 0u);
+      }
+      umma_commit(&empty[s]);
+    }
+    umma_commit(acc_bar);
+  }
+  __syncwarp();
+  // epilogue: warp w owns TMEM lanes 32w..32w+31 = tile rows
+  const bool acc_ok = mbar_wait_bounded(acc_bar, 0u, &g_error_word, DEV_ERR_WAIT_TIMEOUT);
+  __syncwarp();
+  tc_fence_after();
+  const int64_t row = m0 + warp * 32 + lane;
+  const uint32_t tbase = tmem + (uint32_t(warp * 32) << 16);
+  if (__all_sync(0xffffffffu, acc_ok)) {
+    if constexpr (MODE == 0) {
+      const float sc = (p.rowscale && row < p.M) ? p.rowscale[row] : 1.f;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {
+        float v[16];
+        tmem_ld16(tbase + uint32_t(c), v);
+        const int64_t col = n0 + c;
+        if (row >= p.M || col >= p.N) continue;
+        if (p.c_dtype == LNG_F32) {
+          float* dst = static_cast<float*>(p.C) + row * p.ldc + col;
+          if (col + 16 <= p.N) {
+#pragma unroll
+            for (int i = 0; i < 16; i += 4)
+              *reinterpret_cast<float4*>(dst + i) = make_float4(v[i] * sc, v[i + 1] * sc, v[i + 2] * sc, v[i + 3] * sc);
+          } else {
+            for (int i = 0; i < 16 && col + i < p.N; ++i) dst[i] = v[i] * sc;
+          }
+        } else {
+          __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.C) + row * p.ldc + col;
+          if (col + 16 <= p.N) {
+            uint32_t w[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              __nv_bfloat162 b2 = __floats2bfloat162_rn(v[2 * i] * sc, v[2 * i + 1] * sc);
+              w[i] = *reinterpret_cast<uint32_t*>(&b2);
+            }
+            *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+            *reinterpret_cast<uint4*>(dst + 8) = make_uint4(w[4], w[5], w[6], w[7]);
+          } else {
+            for (int i = 0; i < 16 && col + i < p.N; ++i) dst[i] = __float2bfloat16_rn(v[i] * sc);
+          }
+        }
+      }
+    } else {
+      // router: this tile holds routes r0 .. r0+31 (32 * bits logits per row)
+      const int bits = p.bits;
+      const int64_t r0 = n0 / bits;
+      uint32_t packed[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // 32 codes, 4 per word
+      int code = 0, nb = 0, ri = 0;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {
+        float v[16];
+        tmem_ld16(tbase + uint32_t(c), v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          code |= (v[i] > 0.f ? 1 : 0) << nb;
+          if (++nb == bits) {
+            packed[ri >> 2] |= uint32_t(code) << ((ri & 3) * 8);
+            ++ri;
+            code = 0;
+            nb = 0;
+          }
+        }
+      }
+      if (row < p.M) {
+        uint8_t* dst = p.codes + row * p.routes + r0;
+        const int64_t left = p.routes - r0;
+        const int nr = int(left < 32 ? left : 32);
+        if (nr == 32 && (p.routes & 3) == 0 && (r0 & 3) == 0) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) reinterpret_cast<uint32_t*>(dst)[i] = packed[i];
+        } else {
+          for (int i = 0; i < nr; ++i) dst[i] = uint8_t(packed[i >> 2] >> ((i & 3) * 8));
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(Cfg::TMEM_COLS) : "memory");
+  }
+}
+
+// fp32 weight -> [rows, 3*in_dim] bf16 (W1 | W2 | W3) with W = W1 + W2 + W3.
+__global__ void split_bf16x3_kernel(const float* __restrict__ w, int64_t rows, int64_t in_dim,
+                                    __nv_bfloat16* __restrict__ out) {
+  const int64_t total = rows * in_dim;
+  for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < total; e += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = e / in_dim, k = e % in_dim;
+    const float x = w[e];
+    const __nv_bfloat16 a = __float2bfloat16_rn(x);
+    const float r1 = x - __bfloat162float(a);
+    const __nv_bfloat16 b = __float2bfloat16_rn(r1);
+    const float r2 = r1 - __bfloat162float(b);
+    const __nv_bfloat16 c = __float2bfloat16_rn(r2);
+    __nv_bfloat16* o = out + r * 3 * in_dim;
+    o[k] = a;
+    o[in_dim + k] = b;
+    o[2 * in_dim + k] = c;
+  }
+}
+
+// ------------------------------------------------------------------ host side
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
+
+// 2D bf16 tensor map over a row-major [rows, cols] matrix with row stride ld (elements); box 64 x box_rows.
+inline int make_tmap_bf16(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return fail(LNG_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable (driver entry point)");
+  const cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  const cuuint64_t strides[1] = {cuuint64_t(ld) * 2};
+  const cuuint32_t box[2] = {uint32_t(TC_BK), uint32_t(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(LNG_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string(int(r)));
+  return LNG_OK;
+}
+
+template <int BN, int MODE>
+inline int launch_tc_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const TcGemmParams& p, cudaStream_t stream) {
+  auto kern = tc_gemm_kernel<BN, MODE>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(TcCfg<BN>::SMEM));
+  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(tc_gemm_kernel)");
+  dim3 grid(unsigned((p.N + BN - 1) / BN), unsigned((p.M + TC_BM - 1) / TC_BM));
+  kern<<<grid, 128, TcCfg<BN>::SMEM, stream>>>(ta, tb, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_status(e, "tc_gemm_kernel launch");
+  return LNG_OK;
+}
+
+inline bool tc_aligned(const void* p, int64_t ld) {
+  return (reinterpret_cast<uintptr_t>(p) & 15) == 0 && (ld % 8) == 0;
+}
+
+// Plain bf16 GEMM on the tensor cores; LNG_ERR_UNSUPPORTED when the operands do not meet TMA rules.
+inline int tc_gemm_bf16(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int64_t ldb, void* C,
+                        int32_t c_dtype, int64_t ldc, int64_t M, int64_t N, int64_t K, const float* rowscale,
+                        cudaStream_t stream) {
+  if (c_dtype != LNG_F32 && c_dtype != LNG_BF16) return LNG_ERR_UNSUPPORTED;
+  if (!tc_aligned(A, lda) || !tc_aligned(B, ldb) || (reinterpret_cast<uintptr_t>(C) & 15) || (ldc % 8) || K < 16 ||
+      N < 16 || M < 1)
+    return LNG_ERR_UNSUPPORTED;
+  const int BN = (N % 256 == 0) ? 256 : 128;
+  CUtensorMap ta, tb;
+  int st = make_tmap_bf16(&ta, A, M, K, lda, TC_BM);
+  if (st) return st;
+  st = make_tmap_bf16(&tb, B, N, K, ldb, BN);
+  if (st) return st;
+  TcGemmParams p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.a_kperiod = (K + TC_BK - 1) / TC_BK * TC_BK;  // no wrap
+  p.C = C;
+  p.ldc = ldc;
+  p.c_dtype = c_dtype;
+  p.rowscale = rowscale;
+  return BN == 256 ? launch_tc_gemm<256, 0>(ta, tb, p, stream) : launch_tc_gemm<128, 0>(ta, tb, p, stream);
+}
+
+// Router codes on the tensor cores from bf16 inputs and the split weight [routes*bits, 3*in_dim].
+inline int tc_router_split(const __nv_bfloat16* x, int64_t n, int64_t in_dim, int64_t x_stride,
+                           const __nv_bfloat16* w_split, int64_t routes, int32_t bits, uint8_t* codes,
+                           cudaStream_t stream) {
+  if (bits < 1 || bits > 6 || in_dim % TC_BK != 0 || !tc_aligned(x, x_stride) || !tc_aligned(w_split, 3 * in_dim))
+    return LNG_ERR_UNSUPPORTED;
+  const int BN = 32 * bits;
+  CUtensorMap ta, tb;
+  int st = make_tmap_bf16(&ta, x, n, in_dim, x_stride, TC_BM);
+  if (st) return st;
+  st = make_tmap_bf16(&tb, w_split, routes * bits, 3 * in_dim, 3 * in_dim, BN);
+  if (st) return st;
+  TcGemmParams p{};
+  p.M = n;
+  p.N = routes * bits;
+  p.K = 3 * in_dim;
+  p.a_kperiod = in_dim;
+  p.bits = bits;
+  p.routes = routes;
+  p.codes = codes;
+  switch (bits) {
+    case 1: return launch_tc_gemm<32, 1>(ta, tb, p, stream);
+    case 2: return launch_tc_gemm<64, 1>(ta, tb, p, stream);
+    case 3: return launch_tc_gemm<96, 1>(ta, tb, p, stream);
+    case 4: return launch_tc_gemm<128, 1>(ta, tb, p, stream);
+    case 5: return launch_tc_gemm<160, 1>(ta, tb, p, stream);
+    default: return launch_tc_gemm<192, 1>(ta, tb, p, stream);
+  }
+}
+
+// Without a prepared split weight the router stays on the CUDA cores.
 inline int tc_router_codes(const __nv_bfloat16*, int64_t, int64_t, int64_t, const float*, int64_t, int32_t, uint8_t*,
                            cudaStream_t) {
   return LNG_ERR_UNSUPPORTED;

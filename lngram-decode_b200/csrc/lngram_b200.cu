@@ -60,9 +60,12 @@ static int check_tables(const lng_tables* t) {
 
 static TableSet table_set(const lng_tables* t) {
   TableSet ts{};
+  bool all_ss = true;
+  for (int o = 0; o < t->n_orders; ++o) all_ss = all_ss && t->row_ss[o] != nullptr;
   for (int o = 0; o < t->n_orders; ++o) {
     ts.tab[o] = t->tables[o];
     ts.order[o] = t->orders[o];
+    ts.ss[o] = all_ss ? t->row_ss[o] : nullptr;
   }
   ts.n_orders = t->n_orders;
   ts.bits = t->bits;
@@ -71,7 +74,18 @@ static TableSet table_set(const lng_tables* t) {
   return ts;
 }
 
-static int max_order(const lng_tables* t) { return t->orders[t->n_orders - 1]; }
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
 
 }  // namespace lng
 
@@ -82,11 +96,10 @@ extern "C" int lng_abi_version(void) { return 1; }
 extern "C" const char* lng_last_error(void) { return t_last_error.c_str(); }
 
 extern "C" int lng_device_ok(void) {
-  int dev = 0;
+  int dev = 0, major = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 0;
-  cudaDeviceProp prop;
-  if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return 0;
-  return prop.major == 10 ? 1 : 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return 0;
+  return major == 10 ? 1 : 0;
 }
 
 extern "C" int lng_device_error(int clear) {
@@ -144,6 +157,30 @@ extern "C" int lng_route_codes(const void* x, int32_t x_dtype, int64_t n, int64_
   return LNG_OK;
 }
 
+extern "C" int lng_router_prepare(const float* weight, int64_t rows, int64_t in_dim, void* w_split,
+                                  lng_stream_t stream) {
+  LNG_REQUIRE(rows > 0 && in_dim > 0, "bad router shape");
+  LNG_REQUIRE(weight && w_split, "NULL pointer");
+  split_bf16x3_kernel<<<grid_for(rows * in_dim, 256, 16), 256, 0, S(stream)>>>(weight, rows, in_dim,
+                                                                               static_cast<__nv_bfloat16*>(w_split));
+  LNG_LAUNCHED("split_bf16x3_kernel");
+  return LNG_OK;
+}
+
+extern "C" int lng_route_codes_split(const void* x_bf16, int64_t n, int64_t in_dim, int64_t x_stride,
+                                     const void* w_split, int64_t routes, int32_t bits, uint8_t* codes,
+                                     lng_stream_t stream) {
+  LNG_REQUIRE(n >= 0 && in_dim > 0 && routes > 0 && x_stride >= in_dim, "bad router shape");
+  LNG_REQUIRE(bits >= 1 && bits <= 6, "the tensor-core router takes bits_per_route in [1, 6]");
+  LNG_REQUIRE(in_dim % TC_BK == 0, "the tensor-core router needs in_dim % 64 == 0");
+  if (n == 0) return LNG_OK;
+  LNG_REQUIRE(x_bf16 && w_split && codes, "NULL pointer");
+  const int st = tc_router_split(static_cast<const __nv_bfloat16*>(x_bf16), n, in_dim, x_stride,
+                                 static_cast<const __nv_bfloat16*>(w_split), routes, bits, codes, S(stream));
+  if (st == LNG_ERR_UNSUPPORTED) return fail(st, "router operands violate the TMA alignment rules (16-byte rows)");
+  return st;
+}
+
 extern "C" int lng_embed2_features(const int64_t* cur, const int64_t* prev, int64_t n, const void* embedding,
                                    int32_t e_dtype, int64_t vocab, int64_t d, const float* prev_w, const float* cur_w,
                                    const float* start, float eps, float* out, lng_stream_t stream) {
@@ -172,6 +209,32 @@ extern "C" int lng_embed2_features(const int64_t* cur, const int64_t* prev, int6
 }
 
 // ====================================================================== lookup
+extern "C" int lng_table_row_ss(const lng_tables* tables, float* const* row_ss, lng_stream_t stream) {
+  int st = check_tables(tables);
+  if (st) return st;
+  LNG_REQUIRE(row_ss != nullptr, "row_ss is NULL");
+  for (int o = 0; o < tables->n_orders; ++o) {
+    LNG_REQUIRE(row_ss[o] != nullptr, "row_ss pointer is NULL");
+    const int64_t rows = tables->num_routes << (int64_t(tables->bits) * tables->orders[o]);
+    const int g = grid_for(rows * 32, 256, 16);
+    switch (tables->table_dtype) {
+      case LNG_F32:
+        rms_rows_kernel<float, true><<<g, 256, 0, S(stream)>>>(static_cast<const float*>(tables->tables[o]), rows,
+                                                                tables->memory_dim, 0.f, row_ss[o]);
+        break;
+      case LNG_BF16:
+        rms_rows_kernel<__nv_bfloat16, true><<<g, 256, 0, S(stream)>>>(
+            static_cast<const __nv_bfloat16*>(tables->tables[o]), rows, tables->memory_dim, 0.f, row_ss[o]);
+        break;
+      default:
+        rms_rows_kernel<__half, true><<<g, 256, 0, S(stream)>>>(static_cast<const __half*>(tables->tables[o]), rows,
+                                                                 tables->memory_dim, 0.f, row_ss[o]);
+    }
+    LNG_LAUNCHED("rms_rows_kernel (sum of squares)");
+  }
+  return LNG_OK;
+}
+
 template <typename CodeT>
 static int launch_lookup(const lng_tables* t, const CodeSource& src, int64_t M, int64_t rs, int64_t re, void* out,
                          int32_t out_dtype, cudaStream_t stream) {
@@ -237,9 +300,31 @@ extern "C" int lng_lookup_windows(const lng_tables* tables, const void* codes, i
 }
 
 // ====================================================================== attention core
-template <int DT, typename CodeT, typename T>
+// Warps per CTA x shared-memory stages per warp of the gather kernel; LNG_ATTEND_CFG=<warps>x<stages>
+// selects among the compiled shapes (a tuning knob; every shape computes the same result).
+static int attend_cfg() {
+  static int cfg = [] {
+    const char* e = getenv("LNG_ATTEND_CFG");
+    if (!e) return 83;
+    const std::string s(e);
+    if (s == "6x4") return 64;
+    if (s == "4x6") return 46;
+    if (s == "12x2") return 122;
+    return 83;
+  }();
+  return cfg;
+}
+
+template <int DT, typename CodeT, typename T, int WARPS = 8, int STAGES = 3>
 static int launch_attend_mma(const AttendParams& p, cudaStream_t stream) {
-  constexpr int WARPS = 8, STAGES = 3;
+  if constexpr (DT == 136 && WARPS == 8 && STAGES == 3) {
+    switch (attend_cfg()) {
+      case 64: return launch_attend_mma<DT, CodeT, T, 6, 4>(p, stream);
+      case 46: return launch_attend_mma<DT, CodeT, T, 4, 6>(p, stream);
+      case 122: return launch_attend_mma<DT, CodeT, T, 12, 2>(p, stream);
+      default: break;
+    }
+  }
   using Cfg = AttendMmaCfg<DT>;
   const size_t smem = size_t(WARPS) * STAGES * Cfg::STAGE_BYTES + size_t(WARPS) * STAGES * sizeof(uint64_t);
   auto kern = attend_mma_kernel<CodeT, T, DT, WARPS, STAGES>;
@@ -269,7 +354,7 @@ static int attend_impl(const lng_tables* t, const AttendParams& p, int32_t u_dty
   const int64_t Dt = int64_t(t->n_orders) * t->memory_dim;
   // tensor-core path: 16-bit tables, activations of the same type, <= 16 heads, 16-byte rows
   const bool mma_ok = (t->table_dtype == LNG_BF16 || t->table_dtype == LNG_F16) && u_dtype == t->table_dtype &&
-                      p.qh <= 16 && (t->memory_dim % 8) == 0 && !p.partial;
+                      p.qh <= 16 && (t->memory_dim % 8) == 0 && !p.partial && t->orders[t->n_orders - 1] <= MAXW;
   if (mma_ok) {
     bool aligned = (reinterpret_cast<uintptr_t>(p.qa) & 15) == 0 && (reinterpret_cast<uintptr_t>(p.u) & 15) == 0;
     for (int o = 0; o < t->n_orders; ++o) aligned = aligned && (reinterpret_cast<uintptr_t>(t->tables[o]) & 15) == 0;
@@ -438,6 +523,23 @@ static int conv_finish_ws(const lng_readout* ro, const void* mixed, int64_t B, i
   int st = lng_rms_rows(mixed, ro->act_dtype, M, ro->hidden, ro->eps, rs, reinterpret_cast<lng_stream_t>(stream));
   if (st) return st;
   const ConvParams cp = conv_params(ro);
+  const int64_t groups = ro->hidden / 8;
+  if (ro->hidden % 8 == 0 && groups <= 256 && 256 % groups == 0 && ro->conv_kernel <= 8 && M < (int64_t(1) << 31) &&
+      (reinterpret_cast<uintptr_t>(mixed) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(conv_in) & 15) == 0) {
+    const int ppb = 32;
+    const unsigned grid = unsigned(ceil_div(M, ppb));
+    if (ro->act_dtype == LNG_F32)
+      conv_seq_vec_kernel<float, 8><<<grid, 256, 0, stream>>>(cp, static_cast<const float*>(mixed), rs, int(M), int(T),
+                                                               seg, valid, static_cast<float*>(out),
+                                                               static_cast<float*>(conv_in), ppb);
+    else
+      conv_seq_vec_kernel<__nv_bfloat16, 8><<<grid, 256, 0, stream>>>(
+          cp, static_cast<const __nv_bfloat16*>(mixed), rs, int(M), int(T), seg, valid,
+          static_cast<__nv_bfloat16*>(out), static_cast<__nv_bfloat16*>(conv_in), ppb);
+    LNG_LAUNCHED("conv_seq_vec_kernel");
+    return LNG_OK;
+  }
   const int g = grid_for(M * ro->hidden, 256, 16);
   if (ro->act_dtype == LNG_F32)
     conv_seq_kernel<float><<<g, 256, 0, stream>>>(cp, static_cast<const float*>(mixed), rs, B, T, seg, valid,
@@ -607,8 +709,12 @@ extern "C" int lng_memory_forward(const lng_tables* tables, const lng_readout* r
   if (!codes) {
     LNG_REQUIRE(router_x && ro->router_w, "router input and weight are needed when codes are not given");
     uint8_t* c = codes_out ? codes_out : reinterpret_cast<uint8_t*>(ws + L.codes);
-    st = lng_route_codes(router_x, router_x_dtype, M, ro->router_in_dim, ro->router_in_dim, ro->router_w,
-                         tables->num_routes, tables->bits, c, LNG_U8, nullptr, stream);
+    if (router_x_dtype == LNG_BF16 && ro->router_w_split && tables->bits <= 6 && ro->router_in_dim % TC_BK == 0)
+      st = lng_route_codes_split(router_x, M, ro->router_in_dim, ro->router_in_dim, ro->router_w_split,
+                                 tables->num_routes, tables->bits, c, stream);
+    else
+      st = lng_route_codes(router_x, router_x_dtype, M, ro->router_in_dim, ro->router_in_dim, ro->router_w,
+                           tables->num_routes, tables->bits, c, LNG_U8, nullptr, stream);
     if (st) return st;
     codes = c;
     cdt = LNG_U8;

@@ -3,12 +3,14 @@
 // (ffnmem/infer.py:176-182, drafting/tree.py:186-195), the readout fold, and the shard combine.
 #pragma once
 
+#include <type_traits>
+
 #include "address.cuh"
 
 namespace lng {
 
-// rs[i] = 1 / sqrt(mean(x[i]^2) + eps): one warp per row.
-template <typename XT>
+// rs[i] = 1 / sqrt(mean(x[i]^2) + eps) (or, with SUMSQ, the plain sum of squares): one warp per row.
+template <typename XT, bool SUMSQ = false>
 __global__ void rms_rows_kernel(const XT* __restrict__ x, int64_t n, int64_t d, float eps, float* __restrict__ rs) {
   const int lane = threadIdx.x & 31;
   for (int64_t row = (blockIdx.x * int64_t(blockDim.x) + threadIdx.x) >> 5; row < n;
@@ -20,7 +22,7 @@ __global__ void rms_rows_kernel(const XT* __restrict__ x, int64_t n, int64_t d, 
       ss = fmaf(v, v, ss);
     }
     ss = warp_sum(ss);
-    if (lane == 0) rs[row] = rsqrtf(ss / float(d) + eps);
+    if (lane == 0) rs[row] = SUMSQ ? ss : rsqrtf(ss / float(d) + eps);
   }
 }
 
@@ -79,6 +81,99 @@ __global__ void conv_seq_kernel(ConvParams cp, const T* __restrict__ mixed, cons
     if (valid && !valid[pos]) o = 0.f;
     out[e] = from_f32<T>(o);
     if (conv_in) conv_in[e] = from_f32<T>(m * rs[pos] * g);
+  }
+}
+
+// Vectorised sequence-mode conv finish: a thread owns 8 channels (16-byte bf16 / 2 x 16-byte fp32
+// accesses) and walks POS positions; the channel's norm weight, taps and bias stay in registers.
+// Requires d % 8 == 0, k <= 8 and M < 2^31 (checked by the host).
+template <typename T, int KMAX>
+__global__ void __launch_bounds__(256) conv_seq_vec_kernel(ConvParams cp, const T* __restrict__ mixed,
+                                                           const float* __restrict__ rs, int M, int T_,
+                                                           const int64_t* __restrict__ seg,
+                                                           const uint8_t* __restrict__ valid, T* __restrict__ out,
+                                                           T* __restrict__ conv_in, int pos_per_block) {
+  const int groups = int(cp.d / 8);
+  const int grp = threadIdx.x % groups;
+  const int prow = threadIdx.x / groups;
+  const int prows = blockDim.x / groups;
+  const int c0 = grp * 8;
+  float gw[8], wt[KMAX][8], bias[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    gw[i] = cp.norm_w[c0 + i];
+    bias[i] = cp.bias ? cp.bias[c0 + i] : 0.f;
+#pragma unroll
+    for (int tap = 0; tap < KMAX; ++tap) wt[tap][i] = tap < cp.k ? cp.weight[(c0 + i) * cp.k + tap] : 0.f;
+  }
+  const int p_end = min(M, (int(blockIdx.x) + 1) * pos_per_block);
+  for (int pos = int(blockIdx.x) * pos_per_block + prow; pos < p_end; pos += prows) {
+    const int t = pos % T_;
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = bias[i];
+    float self[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int tap = 0; tap < KMAX; ++tap) {
+      if (tap >= cp.k) break;
+      const int lag = (cp.k - 1 - tap) * cp.dil;
+      if (t - lag < 0) continue;
+      const int q = pos - lag;
+      if (seg && seg[q] != seg[pos]) continue;
+      float v[8];
+      if constexpr (std::is_same<T, float>::value) {
+        const float4 a = *reinterpret_cast<const float4*>(mixed + int64_t(q) * cp.d + c0);
+        const float4 b = *reinterpret_cast<const float4*>(mixed + int64_t(q) * cp.d + c0 + 4);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+      } else {
+        const uint4 a = *reinterpret_cast<const uint4*>(mixed + int64_t(q) * cp.d + c0);
+        const uint32_t w4[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          v[2 * i] = __uint_as_float(w4[i] << 16);
+          v[2 * i + 1] = __uint_as_float(w4[i] & 0xffff0000u);
+        }
+      }
+      if (lag == 0) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) self[i] = v[i];
+      }
+      const float r = rs[q];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = fmaf(wt[tap][i], v[i] * r * gw[i], acc[i]);
+    }
+    const bool keep = !valid || valid[pos];
+    float o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = keep ? self[i] + silu_f(acc[i]) : 0.f;
+    if constexpr (std::is_same<T, float>::value) {
+      *reinterpret_cast<float4*>(out + int64_t(pos) * cp.d + c0) = make_float4(o[0], o[1], o[2], o[3]);
+      *reinterpret_cast<float4*>(out + int64_t(pos) * cp.d + c0 + 4) = make_float4(o[4], o[5], o[6], o[7]);
+      if (conv_in) {
+        const float r = rs[pos];
+        *reinterpret_cast<float4*>(conv_in + int64_t(pos) * cp.d + c0) =
+            make_float4(self[0] * r * gw[0], self[1] * r * gw[1], self[2] * r * gw[2], self[3] * r * gw[3]);
+        *reinterpret_cast<float4*>(conv_in + int64_t(pos) * cp.d + c0 + 4) =
+            make_float4(self[4] * r * gw[4], self[5] * r * gw[5], self[6] * r * gw[6], self[7] * r * gw[7]);
+      }
+    } else {
+      uint32_t w4[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        __nv_bfloat162 b2 = __floats2bfloat162_rn(o[2 * i], o[2 * i + 1]);
+        w4[i] = *reinterpret_cast<uint32_t*>(&b2);
+      }
+      *reinterpret_cast<uint4*>(out + int64_t(pos) * cp.d + c0) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+      if (conv_in) {
+        const float r = rs[pos];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          __nv_bfloat162 b2 = __floats2bfloat162_rn(self[2 * i] * r * gw[2 * i], self[2 * i + 1] * r * gw[2 * i + 1]);
+          w4[i] = *reinterpret_cast<uint32_t*>(&b2);
+        }
+        *reinterpret_cast<uint4*>(conv_in + int64_t(pos) * cp.d + c0) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+      }
+    }
   }
 }
 

@@ -161,9 +161,29 @@ class RouteNgramMemoryV2(nn.Module):
             raise ValueError("lngram_b200 runs the readout in fp32 or bf16")
         return dt
 
-    def tables_desc(self, route_tables: dict | None = None) -> _lib.Tables:
+    def row_sumsq(self) -> dict:
+        """Per-row sums of squares of every order table (fp32; cached per table version), read by the
+        fused readout instead of recomputing each gathered row's RMS."""
+        ws = [self.tables[f"ngram_{n}"].weight for n in self.ngrams]
+        key = tuple((w.data_ptr(), w._version, w.dtype, str(w.device)) for w in ws)
+        if getattr(self, "_ss_key", None) == key:
+            return self._ss
+        ss = {n: torch.empty(w.shape[0], device=w.device, dtype=torch.float32) for n, w in zip(self.ngrams, ws)}
+        desc = self.tables_desc(with_ss=False)
+        arr = (_lib.C.c_void_p * _lib.MAX_ORDERS)(*([ss[n].data_ptr() for n in self.ngrams] +
+                                                    [None] * (_lib.MAX_ORDERS - len(self.ngrams))))
+        with torch.cuda.device(ws[0].device):
+            check(_lib.library().lng_table_row_ss(desc, arr, stream_ptr()), "table row sums of squares")
+        self._ss, self._ss_key = ss, key
+        return ss
+
+    def tables_desc(self, route_tables: dict | None = None, with_ss: bool = True) -> _lib.Tables:
         tabs = route_tables or {n: self.tables[f"ngram_{n}"].weight for n in self.ngrams}
+        ss = self.row_sumsq() if (with_ss and route_tables is None) else None
         t = _lib.Tables()
+        if ss is not None:
+            for i, n in enumerate(self.ngrams):
+                t.row_ss[i] = ss[n].data_ptr()
         t.n_orders = len(self.ngrams)
         dts = set()
         for i, n in enumerate(self.ngrams):
@@ -211,7 +231,7 @@ class RouteNgramMemoryV2(nn.Module):
         self._fold_key = key
         return self._fold
 
-    def readout_desc(self, router_w: Tensor | None = None) -> _lib.Readout:
+    def readout_desc(self, router_w: Tensor | None = None, router_w_split: Tensor | None = None) -> _lib.Readout:
         f = self.folded()
         r = _lib.Readout()
         r.hidden = self.hidden_size
@@ -226,6 +246,7 @@ class RouteNgramMemoryV2(nn.Module):
         if router_w is not None:
             r.router_w = ptr(router_w)
             r.router_in_dim = router_w.shape[1]
+        r.router_w_split = ptr(router_w_split)
         return r
 
     # ------------------------------------------------------------------ reference methods
@@ -366,7 +387,7 @@ class RouteNgramMemoryV2(nn.Module):
 
     def forward_codes(self, h: Tensor, codes: Optional[Tensor], segment_ids=None, valid_tokens=None, router_x=None,
                       router_w=None, codes_out: Optional[Tensor] = None, out: Optional[Tensor] = None,
-                      workspace: Optional[Tensor] = None) -> Tensor:
+                      workspace: Optional[Tensor] = None, router_w_split: Optional[Tensor] = None) -> Tensor:
         """One ``lng_memory_forward`` call: codes (given, or from the fp32 router on ``router_x``),
         folded query GEMM, fused gather + sink attention, folded output GEMM, conv finish."""
         h = _cuda(h, "hidden_states")
@@ -376,7 +397,7 @@ class RouteNgramMemoryV2(nn.Module):
         h = h.contiguous()
         b, t, _ = h.shape
         desc_t = self.tables_desc()
-        desc_r = self.readout_desc(router_w)
+        desc_r = self.readout_desc(router_w, router_w_split)
         lib = _lib.library()
         cptr, cdt = None, 0
         if codes is not None:
@@ -447,17 +468,41 @@ class LngramMemory(nn.Module):
                   "route_logits")
         return logits
 
+    def router_split(self) -> Tensor | None:
+        """The router weight as bf16 parts W1 | W2 | W3 for the tensor-core router (cached per weight
+        version); None when the shape does not suit it (bits > 6 or in_dim % 64 != 0)."""
+        w = self.router.weight
+        if self.bits > 6 or w.shape[1] % 64 != 0 or not w.is_cuda:
+            return None
+        key = (w.data_ptr(), w._version, str(w.device))
+        if getattr(self, "_split_key", None) == key:
+            return self._split
+        wf = w.detach().float().contiguous()
+        split = torch.empty(wf.shape[0], 3 * wf.shape[1], device=wf.device, dtype=torch.bfloat16)
+        with torch.cuda.device(wf.device):
+            check(_lib.library().lng_router_prepare(ptr(wf), wf.shape[0], wf.shape[1], ptr(split), stream_ptr()),
+                  "router_prepare")
+        self._split, self._split_key = split, key
+        return split
+
     def route_codes(self, x: Tensor) -> Tensor:
-        """Codes [.., R] (uint8) of the fp32 router without materialising its logits."""
+        """Codes [.., R] (uint8) of the fp32 router without materialising its logits (tensor cores
+        for bf16 inputs, CUDA cores for fp32 inputs)."""
         x = _cuda(x, "router input")
         x = x.contiguous() if x.dtype in (torch.float32, torch.bfloat16) else x.float().contiguous()
-        w = self.router.weight.detach().float().contiguous()
         n = x.numel() // x.shape[-1]
         codes = torch.empty(*x.shape[:-1], self.routes, device=x.device, dtype=torch.uint8)
+        split = self.router_split() if x.dtype == torch.bfloat16 else None
+        lib = _lib.library()
         with torch.cuda.device(x.device):
-            check(_lib.library().lng_route_codes(ptr(x), _lib.dtype_code(x.dtype), n, x.shape[-1], x.shape[-1], ptr(w),
-                                                 self.routes, self.bits, ptr(codes), _lib.U8, None, stream_ptr()),
-                  "route_codes")
+            if split is not None:
+                check(lib.lng_route_codes_split(ptr(x), n, x.shape[-1], x.shape[-1], ptr(split), self.routes,
+                                                self.bits, ptr(codes), stream_ptr()), "route_codes")
+            else:
+                w = self.router.weight.detach().float().contiguous()
+                check(lib.lng_route_codes(ptr(x), _lib.dtype_code(x.dtype), n, x.shape[-1], x.shape[-1], ptr(w),
+                                          self.routes, self.bits, ptr(codes), _lib.U8, None, stream_ptr()),
+                      "route_codes")
         return codes
 
     def forward(self, h: Tensor, h_norm: Tensor, router_in: Tensor | None = None, *, codes_out: Tensor | None = None,
@@ -474,5 +519,6 @@ class LngramMemory(nn.Module):
         w = self.router.weight.detach()
         if w.dtype != torch.float32 or not w.is_contiguous():
             w = w.float().contiguous()
+        split = self.router_split() if x.dtype == torch.bfloat16 else None
         return self.module.forward_codes(h, None, router_x=x, router_w=w, codes_out=codes_out, out=out,
-                                         workspace=workspace)
+                                         workspace=workspace, router_w_split=split)

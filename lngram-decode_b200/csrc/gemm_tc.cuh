@@ -100,7 +100,7 @@ struct TcCfg {
   static constexpr size_t SMEM = size_t(STAGES) * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
 
-template <int BN, int MODE>
+template <int BN, int MODE, int BITS = 1>
 __global__ void __launch_bounds__(128, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b, TcGemmParams p) {
   using Cfg = TcCfg<BN>;
@@ -210,35 +210,34 @@ __global__ void __launch_bounds__(128, 1)
         }
       }
     } else {
-      // router: this tile holds routes r0 .. r0+31 (32 * bits logits per row)
-      const int bits = p.bits;
-      const int64_t r0 = n0 / bits;
-      uint32_t packed[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // 32 codes, 4 per word
-      int code = 0, nb = 0, ri = 0;
-#pragma unroll 1
+      // router: this tile holds routes r0 .. r0+RPT-1 (RPT * BITS logits per row); every index is
+      // static, so the codes are assembled in registers
+      constexpr int RPT = BN / BITS;
+      const int64_t r0 = n0 / BITS;
+      uint32_t packed[(RPT + 3) / 4];
+#pragma unroll
+      for (int i = 0; i < (RPT + 3) / 4; ++i) packed[i] = 0u;
+#pragma unroll
       for (int c = 0; c < BN; c += 16) {
         float v[16];
         tmem_ld16(tbase + uint32_t(c), v);
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          code |= (v[i] > 0.f ? 1 : 0) << nb;
-          if (++nb == bits) {
-            packed[ri >> 2] |= uint32_t(code) << ((ri & 3) * 8);
-            ++ri;
-            code = 0;
-            nb = 0;
-          }
+          const int col = c + i, q = col / BITS, bit = col % BITS;
+          packed[q >> 2] |= uint32_t(v[i] > 0.f ? 1u : 0u) << ((q & 3) * 8 + bit);
         }
       }
       if (row < p.M) {
         uint8_t* dst = p.codes + row * p.routes + r0;
         const int64_t left = p.routes - r0;
-        const int nr = int(left < 32 ? left : 32);
-        if (nr == 32 && (p.routes & 3) == 0 && (r0 & 3) == 0) {
+        const int nr = int(left < RPT ? left : RPT);
+        if (nr == RPT && RPT % 4 == 0 && (p.routes & 3) == 0 && (r0 & 3) == 0) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) reinterpret_cast<uint32_t*>(dst)[i] = packed[i];
+          for (int i = 0; i < RPT / 4; ++i) reinterpret_cast<uint32_t*>(dst)[i] = packed[i];
         } else {
-          for (int i = 0; i < nr; ++i) dst[i] = uint8_t(packed[i >> 2] >> ((i & 3) * 8));
+#pragma unroll
+          for (int i = 0; i < RPT; ++i)
+            if (i < nr) dst[i] = uint8_t(packed[i >> 2] >> ((i & 3) * 8));
         }
       }
     }
@@ -287,9 +286,9 @@ inline int make_tmap_bf16(CUtensorMap* map, const void* ptr, int64_t rows, int64
   return LNG_OK;
 }
 
-template <int BN, int MODE>
+template <int BN, int MODE, int BITS = 1>
 inline int launch_tc_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const TcGemmParams& p, cudaStream_t stream) {
-  auto kern = tc_gemm_kernel<BN, MODE>;
+  auto kern = tc_gemm_kernel<BN, MODE, BITS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(TcCfg<BN>::SMEM));
   if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(tc_gemm_kernel)");
   dim3 grid(unsigned((p.N + BN - 1) / BN), unsigned((p.M + TC_BM - 1) / TC_BM));
@@ -311,7 +310,8 @@ inline int tc_gemm_bf16(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16
   if (!tc_aligned(A, lda) || !tc_aligned(B, ldb) || (reinterpret_cast<uintptr_t>(C) & 15) || (ldc % 8) || K < 16 ||
       N < 16 || M < 1)
     return LNG_ERR_UNSUPPORTED;
-  const int BN = (N % 256 == 0) ? 256 : 128;
+  // 256-column tiles (twice the tensor-pipe efficiency of 128 measured here) unless N <= 128
+  const int BN = N > 128 ? 256 : 128;
   CUtensorMap ta, tb;
   int st = make_tmap_bf16(&ta, A, M, K, lda, TC_BM);
   if (st) return st;
@@ -335,7 +335,7 @@ inline int tc_router_split(const __nv_bfloat16* x, int64_t n, int64_t in_dim, in
                            cudaStream_t stream) {
   if (bits < 1 || bits > 6 || in_dim % TC_BK != 0 || !tc_aligned(x, x_stride) || !tc_aligned(w_split, 3 * in_dim))
     return LNG_ERR_UNSUPPORTED;
-  const int BN = 32 * bits;
+  const int BN = bits <= 4 ? 64 * bits : 32 * bits;  // 64 routes per tile up to 4 bits, else 32
   CUtensorMap ta, tb;
   int st = make_tmap_bf16(&ta, x, n, in_dim, x_stride, TC_BM);
   if (st) return st;
@@ -350,12 +350,12 @@ inline int tc_router_split(const __nv_bfloat16* x, int64_t n, int64_t in_dim, in
   p.routes = routes;
   p.codes = codes;
   switch (bits) {
-    case 1: return launch_tc_gemm<32, 1>(ta, tb, p, stream);
-    case 2: return launch_tc_gemm<64, 1>(ta, tb, p, stream);
-    case 3: return launch_tc_gemm<96, 1>(ta, tb, p, stream);
-    case 4: return launch_tc_gemm<128, 1>(ta, tb, p, stream);
-    case 5: return launch_tc_gemm<160, 1>(ta, tb, p, stream);
-    default: return launch_tc_gemm<192, 1>(ta, tb, p, stream);
+    case 1: return launch_tc_gemm<64, 1, 1>(ta, tb, p, stream);
+    case 2: return launch_tc_gemm<128, 1, 2>(ta, tb, p, stream);
+    case 3: return launch_tc_gemm<192, 1, 3>(ta, tb, p, stream);
+    case 4: return launch_tc_gemm<256, 1, 4>(ta, tb, p, stream);
+    case 5: return launch_tc_gemm<160, 1, 5>(ta, tb, p, stream);
+    default: return launch_tc_gemm<192, 1, 6>(ta, tb, p, stream);
   }
 }
 

@@ -255,6 +255,19 @@ int lng_logits_topk(const float* h, int64_t n, int64_t d, const void* embedding,
                     lng_stream_t stream);
 size_t lng_logits_topk_scratch_bytes(int64_t n, int64_t vocab, int32_t k);
 
+/* lng_logits_topk without any allocation, for callers that cannot allocate device memory where they
+ * draft (inside a captured or replayed CUDA graph, or under an allocator that only serves its own
+ * pools).  No counterpart in the reference: it exists for those callers.  The candidate scratch is
+ * a 4 MiB array inside the library, held by every GPU that loads the library until the process
+ * exits; sizes with n * ceil(vocab / 256) * k * 12 + 256 > 4 MiB are rejected (LNG_ERR_ARGUMENT)
+ * -- e.g. k = 3 at vocab 32000 allows n <= 932.  The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress, with that device current), so make one call on each device
+ * before any stream capture.  All calls share the array and it keeps the last call's contents
+ * (every slot read is first written by the same call); calls that overlap on the GPU -- two streams,
+ * or two threads -- race on it and must be serialised by the caller. */
+int lng_logits_topk_static(const float* h, int64_t n, int64_t d, const void* embedding, int32_t e_dtype,
+                           int64_t vocab, int32_t k, int64_t* ids, float* vals, float* logits, lng_stream_t stream);
+
 /* ------------------------------------------------------------------ drafter (a15) */
 
 /* A GPU drafter with the state machine and API of the reference C++ drafter

@@ -806,4 +806,70 @@ extern "C" int lng_logits_topk(const float* h, int64_t n, int64_t d, const void*
   return LNG_OK;
 }
 
+// ====================================================================== allocation-free top-k
+// Some callers cannot allocate device memory at the point where they draft: code running inside a
+// captured or replayed CUDA graph, or a serving process whose allocator hands out no memory
+// outside its own pools.  For them, lng_logits_topk_static runs the same two kernels as
+// lng_logits_topk with the candidate scratch in this file-scope device array instead of a caller
+// buffer.  The array is part of the library image: every GPU that loads the library holds its
+// 4 MiB until the process exits.
+static constexpr size_t kTopkStaticScratchBytes = size_t(4) << 20;
+static __device__ __align__(256) unsigned char g_topk_static_scratch[kTopkStaticScratchBytes];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_topk_static_mu;
+void* g_topk_static_base[kMaxDevices] = {};  // device address of the array, per device ordinal
+}  // namespace
+
+extern "C" int lng_logits_topk_static(const float* h, int64_t n, int64_t d, const void* embedding, int32_t e_dtype,
+                                      int64_t vocab, int32_t k, int64_t* ids, float* vals, float* logits,
+                                      lng_stream_t stream) {
+  LNG_REQUIRE(n >= 0 && d > 0 && vocab > 0, "bad shape");
+  LNG_REQUIRE(k >= 1 && k <= TK_MAXK, "k must be in [1, 8]");
+  if (n == 0) return LNG_OK;
+  LNG_REQUIRE(h && embedding && ids && vals, "NULL pointer");
+  const size_t need = lng_logits_topk_scratch_bytes(n, vocab, k);
+  if (need > kTopkStaticScratchBytes)
+    return fail(LNG_ERR_ARGUMENT, "lng_logits_topk_static: n * ceil(vocab / 256) * k * 12 bytes (+256) = " +
+                                      std::to_string(need) + " exceeds the 4 MiB static scratch (" +
+                                      std::to_string(kTopkStaticScratchBytes) +
+                                      " bytes); use lng_logits_topk with a caller-provided buffer");
+  int dev = 0;
+  LNG_CUDA(cudaGetDevice(&dev));
+  LNG_REQUIRE(dev >= 0 && dev < kMaxDevices, "device ordinal out of range for the static scratch table");
+  void* base = nullptr;
+  {
+    // first call on a device: resolve the array's device address with that device current
+    std::lock_guard<std::mutex> lock(g_topk_static_mu);
+    if (!g_topk_static_base[dev]) {
+      void* p = nullptr;
+      LNG_CUDA(cudaGetSymbolAddress(&p, g_topk_static_scratch));
+      g_topk_static_base[dev] = p;
+    }
+    base = g_topk_static_base[dev];
+  }
+  const int64_t nch = ceil_div(vocab, TK_VC);
+  const size_t smem = sizeof(float) * (size_t(TK_ROWS) * d + size_t(TK_ROWS) * TK_VC);
+  LNG_REQUIRE(smem <= 227 * 1024, "hidden size too large for the top-k kernel");
+  int64_t* cand_i = static_cast<int64_t*>(base);  // 256-byte aligned: no extra alignment step needed
+  float* cand_v = reinterpret_cast<float*>(cand_i + n * nch * k);
+  dim3 grid(unsigned(nch), unsigned(ceil_div(n, TK_ROWS)));
+#define LNG_TKS(ET)                                                                                        \
+  do {                                                                                                     \
+    auto kern = logits_chunk_topk_kernel<ET>;                                                              \
+    LNG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));          \
+    kern<<<grid, 256, smem, S(stream)>>>(h, n, d, static_cast<const ET*>(embedding), vocab, k, cand_v, cand_i, logits); \
+  } while (0)
+  if (e_dtype == LNG_F32) LNG_TKS(float);
+  else if (e_dtype == LNG_BF16) LNG_TKS(__nv_bfloat16);
+  else if (e_dtype == LNG_F16) LNG_TKS(__half);
+  else return fail(LNG_ERR_ARGUMENT, "embedding dtype must be float");
+#undef LNG_TKS
+  LNG_LAUNCHED("logits_chunk_topk_kernel (static scratch)");
+  topk_merge_kernel<<<unsigned(ceil_div(n * 32, 256)), 256, 0, S(stream)>>>(cand_v, cand_i, n, nch, k, ids, vals);
+  LNG_LAUNCHED("topk_merge_kernel (static scratch)");
+  return LNG_OK;
+}
+
 #include "drafter.cuh"

@@ -7,6 +7,9 @@ behind the C ABI of ``include/lngram_b200.h``.  There is no CPU fallback.
 """
 
 from . import _lib
+from .bundle import Bundle, load_bundle, read_header, write_bundle
+from .drafter import DraftOut, GpuDrafter, make_drafter
 from .memory import LngramMemory, RouteNgramMemoryV2
 
-__all__ = ["LngramMemory", "RouteNgramMemoryV2", "_lib"]
+__all__ = ["Bundle", "DraftOut", "GpuDrafter", "LngramMemory", "RouteNgramMemoryV2", "_lib", "load_bundle",
+           "make_drafter", "read_header", "write_bundle"]

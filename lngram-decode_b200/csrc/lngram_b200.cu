@@ -1,7 +1,9 @@
 // lngram_b200: the C ABI of include/lngram_b200.h (one translation unit, so every kernel shares
 // the device error word and inlines the addressing helpers).
 #include <algorithm>
+#include <cmath>
 #include <cstring>
+#include <memory>
 #include <mutex>
 #include <string>
 #include <vector>

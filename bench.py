@@ -278,7 +278,7 @@ def time_attend(mem, lib, h, codes, ws, steps) -> dict:
     desc = m.tables_desc()
 
     def launch():
-        lib.check(L.lng_route_attend(desc, codes.data_ptr(), lib.U8, SB["B"], SB["T"], 0, None, None, None, 0,
+        lib.check(L.lng_route_attend(desc, codes.data_ptr(), lib.U8, SB["B"], SB["T"], 0, None, None, None, 0, 0,
                                      SB["routes"], m.readout_num_heads, m.eps, m.readout_sink_logit, qa.data_ptr(),
                                      rs.data_ptr(), u.data_ptr(), lib.BF16, 0, None, None, s))
 
@@ -320,7 +320,8 @@ def time_stages(mem, lib, h, hn, reps: int = 5) -> dict:
         "qa_gemm_tc": lambda: lib.check(L.lng_gemm(h.data_ptr(), lib.BF16, SB["d"], f["w_qk"].data_ptr(), lib.BF16,
                                                    SB["d"], qa.data_ptr(), lib.BF16, qd, M, qd, SB["d"], None, 0, s)),
         "gather_attend": lambda: lib.check(L.lng_route_attend(desc_t, codes.data_ptr(), lib.U8, SB["B"], SB["T"], 0,
-                                                              None, None, None, 0, SB["routes"], m.readout_num_heads,
+                                                              None, None, None, 0, 0, SB["routes"],
+                                                              m.readout_num_heads,
                                                               m.eps, m.readout_sink_logit, qa.data_ptr(),
                                                               rs.data_ptr(), u.data_ptr(), lib.BF16, 0, None, None,
                                                               s)),

@@ -172,8 +172,10 @@ int lng_fold_readout(int64_t d, int64_t Dt, int32_t num_heads, int32_t num_kv_he
  *   u[i, q, :] = sum_r p[q, r] rms(tok_r)^-1 tok_r.
  * qa: [M, QH, Dt] (act dtype of `u`); qscale: fp32 [M] or NULL (= 1).
  * Items address their codes in one of two modes:
- *   window == 0: sequence mode, item i = (b, t) of codes [B, T, R] (M = B*T), with the masks of
- *                lng_lookup_route_chunk (segment_ids, valid_tokens may be NULL);
+ *   window == 0: sequence mode, item i = (b, t) of codes [B, T, R] with the masks of
+ *                lng_lookup_route_chunk (segment_ids, valid_tokens may be NULL); with target_length
+ *                > 0 only the last target_length positions of each row are items (M = B*target_length,
+ *                the decode-step view of ffnmem/infer.py:169-174), else M = B*T;
  *   window  > 0: window mode, codes [M, window, R] and seg [M, window] as in lng_lookup_windows.
  * Routes [route_start, route_end) are attended.  partial == 0: u is normalised (head space).
  * partial == 1: the online-softmax state of these routes is written instead -- m [M, QH] and
@@ -182,7 +184,8 @@ int lng_fold_readout(int64_t d, int64_t Dt, int32_t num_heads, int32_t num_kv_he
  * (lngram_v2.py:1944-2070). */
 int lng_route_attend(const lng_tables* tables, const void* codes, int32_t codes_dtype, int64_t B, int64_t T,
                      int64_t window, const int64_t* segment_ids, const uint8_t* valid_tokens, const int32_t* seg,
-                     int64_t route_start, int64_t route_end, int32_t num_heads, float eps, float sink_logit,
+                     int64_t target_length, int64_t route_start, int64_t route_end, int32_t num_heads, float eps,
+                     float sink_logit,
                      const void* qa, const float* qscale, void* u, int32_t u_dtype, int32_t partial, float* m_out,
                      float* l_out, lng_stream_t stream);
 

@@ -13,3 +13,6 @@ from .memory import LngramMemory, RouteNgramMemoryV2
 
 __all__ = ["Bundle", "DraftOut", "GpuDrafter", "LngramMemory", "RouteNgramMemoryV2", "_lib", "load_bundle",
            "make_drafter", "read_header", "write_bundle"]
+from .seams import MemoryCache, memory_step, tree_memory_block, tree_ngram_codes, tree_slots  # noqa: E402
+
+__all__ += ["MemoryCache", "memory_step", "tree_memory_block", "tree_ngram_codes", "tree_slots"]

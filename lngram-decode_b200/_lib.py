@@ -78,8 +78,8 @@ SIGNATURES = {
     "lng_lookup_route_chunk": (C.c_int, [PT, P, i32, i64, i64, i64, i64, P, P, i64, P, i32, P]),
     "lng_lookup_windows": (C.c_int, [PT, P, i32, i64, i64, P, P, i32, P]),
     "lng_fold_readout": (C.c_int, [i64, i64, i32, i32, i32, P, P, P, P, P, P, P, i32, P]),
-    "lng_route_attend": (C.c_int, [PT, P, i32, i64, i64, i64, P, P, P, i64, i64, i32, f32, f32, P, P, P, i32, i32, P,
-                                   P, P]),
+    "lng_route_attend": (C.c_int, [PT, P, i32, i64, i64, i64, P, P, P, i64, i64, i64, i32, f32, f32, P, P, P, i32, i32,
+                                   P, P, P]),
     "lng_sink_gqa": (C.c_int, [P, P, P, i32, i64, i32, i32, i64, i32, f32, P, P]),
     "lng_gemm": (C.c_int, [P, i32, i64, P, i32, i64, P, i32, i64, i64, i64, i64, P, i32, P]),
     "lng_rms_rows": (C.c_int, [P, i32, i64, i64, f32, P, P]),

@@ -401,9 +401,10 @@ static int attend_impl(const lng_tables* t, const AttendParams& p, int32_t u_dty
 
 extern "C" int lng_route_attend(const lng_tables* tables, const void* codes, int32_t codes_dtype, int64_t B, int64_t T,
                                 int64_t window, const int64_t* segment_ids, const uint8_t* valid_tokens,
-                                const int32_t* seg, int64_t route_start, int64_t route_end, int32_t num_heads,
-                                float eps, float sink_logit, const void* qa, const float* qscale, void* u,
-                                int32_t u_dtype, int32_t partial, float* m_out, float* l_out, lng_stream_t stream) {
+                                const int32_t* seg, int64_t target_length, int64_t route_start, int64_t route_end,
+                                int32_t num_heads, float eps, float sink_logit, const void* qa, const float* qscale,
+                                void* u, int32_t u_dtype, int32_t partial, float* m_out, float* l_out,
+                                lng_stream_t stream) {
   int st = check_tables(tables);
   if (st) return st;
   LNG_REQUIRE(codes_dtype == LNG_U8 || codes_dtype == LNG_I32, "codes dtype must be u8 or i32");
@@ -411,13 +412,14 @@ extern "C" int lng_route_attend(const lng_tables* tables, const void* codes, int
   LNG_REQUIRE(0 <= route_start && route_start < route_end && route_end <= tables->num_routes, "bad route range");
   LNG_REQUIRE(u_dtype == LNG_F32 || u_dtype == LNG_BF16 || u_dtype == LNG_F16, "u dtype must be f32, bf16 or f16");
   LNG_REQUIRE(!partial || (u_dtype == LNG_F32 && m_out && l_out), "partial mode needs fp32 u, m_out and l_out");
-  const int64_t M = window > 0 ? B : B * T;
+  const int64_t tout = (window <= 0 && target_length > 0) ? std::min(target_length, T) : T;
+  const int64_t M = window > 0 ? B : B * tout;
   if (M == 0) return LNG_OK;
   LNG_REQUIRE(codes && qa && u, "NULL pointer");
   AttendParams p{};
   p.ts = table_set(tables);
   p.src = CodeSource{codes, window > 0 ? 0 : B, window > 0 ? 0 : T, window, tables->num_routes, segment_ids,
-                     valid_tokens, seg, 0, T};
+                     valid_tokens, seg, window > 0 ? 0 : T - tout, T};
   p.M = M;
   p.route_start = route_start;
   p.route_end = route_end;
@@ -730,7 +732,7 @@ extern "C" int lng_memory_forward(const lng_tables* tables, const lng_readout* r
   if (st) return st;
   // 3. fused gather + sink attention over all routes
   void* u = ws + L.u;
-  st = lng_route_attend(tables, codes, cdt, B, T, 0, segment_ids, valid_tokens, nullptr, 0, tables->num_routes,
+  st = lng_route_attend(tables, codes, cdt, B, T, 0, segment_ids, valid_tokens, nullptr, 0, 0, tables->num_routes,
                         ro->num_heads, ro->eps, ro->sink_logit, qa, rs_h, u, act, 0, nullptr, nullptr, stream);
   if (st) return st;
   // 4. mixed = u . w_vo^T  (= o_proj(head))

@@ -1,0 +1,148 @@
+"""The memory layer's decode and tree-verification seams on the lngram_b200 kernels.
+
+* ``memory_step`` -- ``ffnmem/infer.py:152-182``: the memory output of n new positions after L
+  cached ones: codes over the context [history + new], the fused gather + sink attention on the
+  last n positions, the folded output map, and the short conv over the cached normalised outputs.
+* ``tree_memory_block`` -- the memory part of ``tree_verify_step`` (``drafting/tree.py:165-195``):
+  every node's n-gram window and conv window follow its ancestors, then the cached positions.
+* ``tree_slots`` / ``tree_ngram_codes`` -- ``drafting/tree.py:96-127`` (host-side index building).
+
+``MemoryCache`` holds the memory part of the reference's ``DecodeState`` (``ffnmem/infer.py:65-112``):
+codes [B, max_len, R] and conv inputs [B, max_len, d], indexed by absolute position.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+
+from . import _lib
+from ._lib import check, ptr, stream_ptr
+
+
+class MemoryCache:
+    def __init__(self, m, batch: int, max_len: int, device=None, dtype=None):
+        device = device or m.readout_q_proj.weight.device
+        dtype = dtype or m.readout_q_proj.weight.dtype
+        self.batch, self.max_len, self.length = int(batch), int(max_len), 0
+        self.codes = torch.zeros(batch, max_len, m.num_routes, dtype=torch.uint8, device=device)
+        self.conv_in = torch.zeros(batch, max_len, m.hidden_size, dtype=dtype, device=device)
+
+    def truncate(self, length: int) -> None:
+        if not 0 <= length <= self.length:
+            raise ValueError(f"cannot truncate to {length} (length {self.length})")
+        self.length = length
+
+
+def tree_path(parent, i: int) -> list:
+    """Root .. i along the parent pointers."""
+    out = []
+    while i >= 0:
+        out.append(i)
+        i = parent[i]
+    return out[::-1]
+
+
+def tree_slots(parent, L: int, back: int) -> tuple[Tensor, Tensor]:
+    """For each node the slots of itself and its ``back`` predecessors (oldest first): its ancestors,
+    then the L cached positions before the root; slot L + a is node a.  Returns (idx, ok) [n, back+1]."""
+    n = len(parent)
+    idx = torch.zeros(n, back + 1, dtype=torch.long)
+    ok = torch.zeros(n, back + 1, dtype=torch.bool)
+    for i in range(n):
+        path = tree_path(parent, i)
+        for j in range(back + 1):
+            s = L + path[-1 - j] if j < len(path) else L - (j - len(path) + 1)
+            if s >= 0:
+                idx[i, back - j] = s
+                ok[i, back - j] = True
+    return idx, ok
+
+
+def tree_ngram_codes(parent, codes: Tensor, history: Tensor | None = None, hist: int = 2) -> tuple[Tensor, Tensor]:
+    """Code windows [B, n, hist+1, R] along each node's ancestors then ``history`` (zeros where invalid)
+    and the validity mask [n, hist+1]."""
+    h = 0 if history is None else history.shape[1]
+    allc = codes if history is None else torch.cat((history.to(codes.dtype), codes), 1)
+    idx, ok = tree_slots(parent, h, hist)
+    idx, ok = idx.to(codes.device), ok.to(codes.device)
+    return allc[:, idx] * ok[None, :, :, None].to(codes.dtype), ok
+
+
+def _readout(m, h: Tensor, tables, codes, cdt, B, T, window, seg, target_length):
+    """qa = h . w_qk^T, qscale = 1/rms(h), fused attention, mixed = u . w_vo^T."""
+    lib = _lib.library()
+    f = m.folded()
+    act = m._act()
+    h = h.to(act).contiguous()
+    M = h.numel() // m.hidden_size
+    qd = m.readout_num_heads * m.route_token_dim
+    rs = torch.empty(M, device=h.device, dtype=torch.float32)
+    check(lib.lng_rms_rows(ptr(h), _lib.dtype_code(act), M, m.hidden_size, m.eps, ptr(rs), stream_ptr()), "rms")
+    qa = m._linear(h.view(M, -1), f["w_qk"])
+    u = torch.empty(M, qd, device=h.device, dtype=act)
+    check(lib.lng_route_attend(tables, ptr(codes), cdt, B, T, window, None, None, ptr(seg), target_length, 0,
+                               m.num_routes, m.readout_num_heads, m.eps, m.readout_sink_logit, ptr(qa), ptr(rs),
+                               ptr(u), _lib.dtype_code(act), 0, None, None, stream_ptr()), "route_attend")
+    return m._linear(u, f["w_vo"])
+
+
+def _conv(m, mixed: Tensor, cache: MemoryCache, new_slot: Tensor, slot: Tensor) -> Tensor:
+    out = torch.empty_like(mixed)
+    check(_lib.library().lng_conv_window(m.readout_desc(), ptr(mixed), mixed.shape[0], ptr(cache.conv_in),
+                                         ptr(new_slot), ptr(slot), ptr(out), stream_ptr()), "conv_window")
+    return out
+
+
+@torch.no_grad()
+def memory_step(m, cache: MemoryCache, h: Tensor, codes_new: Tensor, route_codes_ctx: Tensor | None = None) -> Tensor:
+    """``ffnmem/infer.py:152-182``: output [B, n, d] for n new positions after ``cache.length``.  The new
+    codes and conv inputs are written into the cache; ``cache.length`` is left to the caller (the
+    reference's ``decode_step`` advances it after all layers)."""
+    B, n, d = h.shape
+    L = cache.length
+    if L + n > cache.max_len:
+        raise ValueError(f"cache full: {L} + {n} > {cache.max_len}")
+    cache.codes[:, L:L + n] = codes_new.to(torch.uint8)
+    hist = m.route_history_length
+    ctx = cache.codes[:, max(0, L - hist):L + n] if route_codes_ctx is None else route_codes_ctx.to(torch.uint8)
+    ctx = ctx.contiguous()
+    mixed = _readout(m, h, m.tables_desc(), ctx, _lib.U8, B, ctx.shape[1], 0, None, n)
+    k, dil = m.short_conv.kernel_size, m.short_conv.dilation
+    dev = h.device
+    pos = L + torch.arange(n, device=dev)
+    base = (torch.arange(B, device=dev) * cache.max_len)[:, None]
+    new_slot = (base + pos[None, :]).reshape(-1).contiguous()
+    lags = torch.tensor([(k - 1 - tap) * dil for tap in range(k)], device=dev)
+    src = pos[:, None] - lags[None, :]                                    # [n, k]
+    slot = torch.where(src[None] >= 0, base[:, :, None] + src[None], torch.full_like(src[None], -1))
+    out = _conv(m, mixed, cache, new_slot, slot.reshape(B * n, k).contiguous())
+    return out.view(B, n, d)
+
+
+@torch.no_grad()
+def tree_memory_block(m, cache: MemoryCache, h: Tensor, codes: Tensor, parent) -> Tensor:
+    """``drafting/tree.py:178-195``: memory output [B, n, d] of tree nodes ``codes`` [B, n, R] placed
+    after ``cache.length``; writes the nodes' codes and conv inputs at L .. L+n-1 in node order."""
+    B, n, d = h.shape
+    L = cache.length
+    if L + n > cache.max_len:
+        raise ValueError(f"cache full: {L} + {n} > {cache.max_len}")
+    hist = m.route_history_length
+    codes = codes.to(torch.uint8)
+    ctx, valid = tree_ngram_codes(parent, codes, cache.codes[:, max(0, L - hist):L], hist)
+    W = hist + 1
+    seg = valid.to(torch.int32)[None].expand(B, n, W).reshape(B * n, W).contiguous()
+    mixed = _readout(m, h, m.tables_desc(), ctx.reshape(B * n, W, -1).contiguous(), _lib.U8, B * n, 0, W, seg, 0)
+    cache.codes[:, L:L + n] = codes
+    k, dil = m.short_conv.kernel_size, m.short_conv.dilation
+    lp = (k - 1) * dil
+    idx, ok = tree_slots(parent, L, lp)
+    dev = h.device
+    taps = torch.arange(k) * dil                                          # window columns the taps read
+    tslot = torch.where(ok[:, taps], idx[:, taps], torch.full_like(idx[:, taps], -1)).to(dev)  # [n, k]
+    base = (torch.arange(B, device=dev) * cache.max_len)[:, None, None]
+    slot = torch.where(tslot[None] >= 0, base + tslot[None], torch.full_like(tslot[None], -1))
+    new_slot = ((torch.arange(B, device=dev) * cache.max_len)[:, None] + L + torch.arange(n, device=dev)[None])
+    out = _conv(m, mixed, cache, new_slot.reshape(-1).contiguous(), slot.reshape(B * n, k).contiguous())
+    return out.view(B, n, d)

@@ -177,11 +177,11 @@ int lng_fold_readout(int64_t d, int64_t Dt, int32_t num_heads, int32_t num_kv_he
  *                > 0 only the last target_length positions of each row are items (M = B*target_length,
  *                the decode-step view of ffnmem/infer.py:169-174), else M = B*T;
  *   window  > 0: window mode, codes [M, window, R] and seg [M, window] as in lng_lookup_windows.
- * Routes [route_start, route_end) are attended.  partial == 0: u is normalised (head space).
- * partial == 1: the online-softmax state of these routes is written instead -- m [M, QH] and
- * l [M, QH] (fp32; the sink is included only when route_start == 0) and the unnormalised u in
- * fp32 -- so that route shards combine exactly as the streaming readout does
- * (lngram_v2.py:1944-2070). */
+ * Routes [route_start, route_end) are attended.  partial == 0: u is normalised, in the dtype of qa.
+ * partial == 1 or 2: the online-softmax state of these routes is written instead -- m [M, QH] and
+ * l [M, QH] (fp32) and the unnormalised u in fp32 -- with the sink seeded in (1) or left out (2),
+ * so that route shards (one of them with the sink) combine exactly as the streaming readout does
+ * (lngram_v2.py:1944-2070); qa then has the tables' dtype (16-bit tables) or f32. */
 int lng_route_attend(const lng_tables* tables, const void* codes, int32_t codes_dtype, int64_t B, int64_t T,
                      int64_t window, const int64_t* segment_ids, const uint8_t* valid_tokens, const int32_t* seg,
                      int64_t target_length, int64_t route_start, int64_t route_end, int32_t num_heads, float eps,
@@ -246,6 +246,15 @@ int lng_attend_rescale(const float* m_local, const float* m_glob, float* l, floa
                        int64_t Dt, lng_stream_t stream);
 int lng_attend_normalize(const float* l, const float* u, int64_t M, int32_t num_heads, int64_t Dt, void* u_out,
                          int32_t u_dtype, lng_stream_t stream);
+
+/* Head-space form of the same combine, for route shards whose partial values were projected per
+ * head (o = W_v g_m u, [M, QH, HD] fp32): pack [M, QH, HD+1] = (o, l) * exp(m_local - m_glob), ready
+ * for a SUM reduction across shards; lng_attend_unpack then writes head = pack[.., :HD] / pack[.., HD]
+ * (the streaming readout's final division, lngram_v2.py:2066-2070) in f32 or bf16. */
+int lng_attend_pack(const float* m_local, const float* m_glob, const float* l, const float* o, int64_t M,
+                    int32_t num_heads, int32_t head_dim, float* pack, lng_stream_t stream);
+int lng_attend_unpack(const float* pack, int64_t M, int32_t num_heads, int32_t head_dim, void* head, int32_t dtype,
+                      lng_stream_t stream);
 
 /* ------------------------------------------------------------------ draft head (a12) */
 

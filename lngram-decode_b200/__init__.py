@@ -16,3 +16,7 @@ __all__ = ["Bundle", "DraftOut", "GpuDrafter", "LngramMemory", "RouteNgramMemory
 from .seams import MemoryCache, memory_step, tree_memory_block, tree_ngram_codes, tree_slots  # noqa: E402
 
 __all__ += ["MemoryCache", "memory_step", "tree_memory_block", "tree_ngram_codes", "tree_slots"]
+from . import sharded  # noqa: E402
+from .sharded import RouteShardedMemory  # noqa: E402
+
+__all__ += ["RouteShardedMemory", "sharded"]

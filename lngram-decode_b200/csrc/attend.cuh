@@ -53,7 +53,7 @@ __global__ void __launch_bounds__(128) attend_simt_kernel(AttendParams p) {
   float* lrow = mrow + QH;              // [QH]
   float* alpha = lrow + QH;             // [QH]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-  const bool sink_in = !p.partial || p.route_start == 0;
+  const bool sink_in = p.partial != 2;  // partial == 2: a route shard whose state leaves the sink to another
 
   for (int64_t item = blockIdx.x; item < p.M; item += gridDim.x) {
     const float qs = p.qscale ? p.qscale[item] : 1.f;
@@ -229,7 +229,7 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
   const int64_t nwarps = int64_t(gridDim.x) * WARPS;
   const int64_t my_items = gwarp < p.M ? (p.M - 1 - gwarp) / nwarps + 1 : 0;
   const int jobs = int(my_items * nch);
-  const bool sink_in = !p.partial || p.route_start == 0;
+  const bool sink_in = p.partial != 2;  // partial == 2: a route shard whose state leaves the sink to another
   const int mem_dim = int(p.ts.mem_dim);
 
   if (lane == 0) {

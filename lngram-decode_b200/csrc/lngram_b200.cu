@@ -354,9 +354,12 @@ static int dispatch_attend_mma(int64_t Dt, const AttendParams& p, cudaStream_t s
 template <typename CodeT>
 static int attend_impl(const lng_tables* t, const AttendParams& p, int32_t u_dtype, cudaStream_t stream) {
   const int64_t Dt = int64_t(t->n_orders) * t->memory_dim;
-  // tensor-core path: 16-bit tables, activations of the same type, <= 16 heads, 16-byte rows
-  const bool mma_ok = (t->table_dtype == LNG_BF16 || t->table_dtype == LNG_F16) && u_dtype == t->table_dtype &&
-                      p.qh <= 16 && (t->memory_dim % 8) == 0 && !p.partial && t->orders[t->n_orders - 1] <= MAXW;
+  const bool t16 = t->table_dtype == LNG_BF16 || t->table_dtype == LNG_F16;
+  // qa dtype: the activations' in normalised mode; the tables' (16-bit) or f32 in partial mode
+  const int qa_dtype = p.partial ? (t16 ? t->table_dtype : LNG_F32) : u_dtype;
+  // tensor-core path: 16-bit tables, query of the same type, <= 16 heads, 16-byte rows
+  const bool mma_ok = t16 && qa_dtype == t->table_dtype && (p.partial ? u_dtype == LNG_F32 : u_dtype == t->table_dtype) &&
+                      p.qh <= 16 && (t->memory_dim % 8) == 0 && t->orders[t->n_orders - 1] <= MAXW;
   if (mma_ok) {
     bool aligned = (reinterpret_cast<uintptr_t>(p.qa) & 15) == 0 && (reinterpret_cast<uintptr_t>(p.u) & 15) == 0;
     for (int o = 0; o < t->n_orders; ++o) aligned = aligned && (reinterpret_cast<uintptr_t>(t->tables[o]) & 15) == 0;
@@ -371,17 +374,18 @@ static int attend_impl(const lng_tables* t, const AttendParams& p, int32_t u_dty
   const size_t smem = sizeof(float) * (size_t(2 * QH + ATT_C) * Dt + ATT_C + size_t(QH) * ATT_C + 3 * QH);
   LNG_REQUIRE(smem <= 227 * 1024, "route token width too large for the CUDA-core readout");
   const int grid = int(std::min<int64_t>(p.M, int64_t(num_sms()) * 8));
-  const int qdt = p.partial ? t->table_dtype : u_dtype;  // qa dtype follows the activations
-  (void)qdt;
 #define LNG_AT(TT, QT, UT)                                                                                   \
   do {                                                                                                       \
     auto k = attend_simt_kernel<CodeT, TT, QT, UT>;                                                          \
     LNG_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));               \
     k<<<grid, 128, smem, stream>>>(p);                                                                       \
   } while (0)
-  // qa and (normalised) u share the activation dtype `u_dtype`; partial mode writes fp32 u
   const int act = u_dtype;
-  if (t->table_dtype == LNG_F32) {
+  if (p.partial) {  // fp32 state out
+    if (t->table_dtype == LNG_F32) LNG_AT(float, float, float);
+    else if (t->table_dtype == LNG_BF16) LNG_AT(__nv_bfloat16, __nv_bfloat16, float);
+    else LNG_AT(__half, __half, float);
+  } else if (t->table_dtype == LNG_F32) {
     if (act == LNG_F32) LNG_AT(float, float, float);
     else if (act == LNG_BF16) LNG_AT(float, __nv_bfloat16, __nv_bfloat16);
     else return fail(LNG_ERR_ARGUMENT, "unsupported activation dtype");
@@ -411,6 +415,7 @@ extern "C" int lng_route_attend(const lng_tables* tables, const void* codes, int
   LNG_REQUIRE(num_heads >= 1 && num_heads <= 64, "num_heads must be in [1, 64]");
   LNG_REQUIRE(0 <= route_start && route_start < route_end && route_end <= tables->num_routes, "bad route range");
   LNG_REQUIRE(u_dtype == LNG_F32 || u_dtype == LNG_BF16 || u_dtype == LNG_F16, "u dtype must be f32, bf16 or f16");
+  LNG_REQUIRE(partial >= 0 && partial <= 2, "partial must be 0, 1 or 2");
   LNG_REQUIRE(!partial || (u_dtype == LNG_F32 && m_out && l_out), "partial mode needs fp32 u, m_out and l_out");
   const int64_t tout = (window <= 0 && target_length > 0) ? std::min(target_length, T) : T;
   const int64_t M = window > 0 ? B : B * tout;
@@ -767,6 +772,33 @@ extern "C" int lng_attend_normalize(const float* l, const float* u, int64_t M, i
     attend_normalize_kernel<__nv_bfloat16><<<g, 256, 0, S(stream)>>>(l, u, MQ, Dt, static_cast<__nv_bfloat16*>(u_out));
   else return fail(LNG_ERR_ARGUMENT, "u dtype must be f32 or bf16");
   LNG_LAUNCHED("attend_normalize_kernel");
+  return LNG_OK;
+}
+
+extern "C" int lng_attend_pack(const float* m_local, const float* m_glob, const float* l, const float* o, int64_t M,
+                               int32_t num_heads, int32_t head_dim, float* pack, lng_stream_t stream) {
+  LNG_REQUIRE(M >= 0 && num_heads > 0 && head_dim > 0, "bad shape");
+  if (M == 0) return LNG_OK;
+  LNG_REQUIRE(m_local && m_glob && l && o && pack, "NULL pointer");
+  const int64_t MQ = M * num_heads;
+  attend_pack_kernel<<<grid_for(MQ * (head_dim + 1), 256, 16), 256, 0, S(stream)>>>(m_local, m_glob, l, o, MQ,
+                                                                                      head_dim, pack);
+  LNG_LAUNCHED("attend_pack_kernel");
+  return LNG_OK;
+}
+
+extern "C" int lng_attend_unpack(const float* pack, int64_t M, int32_t num_heads, int32_t head_dim, void* head,
+                                 int32_t dtype, lng_stream_t stream) {
+  LNG_REQUIRE(M >= 0 && num_heads > 0 && head_dim > 0, "bad shape");
+  if (M == 0) return LNG_OK;
+  LNG_REQUIRE(pack && head, "NULL pointer");
+  const int64_t MQ = M * num_heads;
+  const int g = grid_for(MQ * head_dim, 256, 16);
+  if (dtype == LNG_F32) attend_unpack_kernel<float><<<g, 256, 0, S(stream)>>>(pack, MQ, head_dim, static_cast<float*>(head));
+  else if (dtype == LNG_BF16)
+    attend_unpack_kernel<__nv_bfloat16><<<g, 256, 0, S(stream)>>>(pack, MQ, head_dim, static_cast<__nv_bfloat16*>(head));
+  else return fail(LNG_ERR_ARGUMENT, "head dtype must be f32 or bf16");
+  LNG_LAUNCHED("attend_unpack_kernel");
   return LNG_OK;
 }
 

@@ -1,0 +1,163 @@
+"""Route-sharded memory layer across GPUs (one process per GPU, NCCL over NVLink).
+
+Each rank holds the table rows of a contiguous block of routes [r0, r1) and the router rows of those
+routes.  A forward over positions [B, T] (hidden states replicated on every rank):
+
+1. codes of the local routes (the router's rows r0*bits .. r1*bits);
+2. the folded query (replicated) and the fused gather + sink attention over the local routes in
+   partial mode: the online-softmax state (m, l, u) of the shard, the sink seeded on rank 0 only;
+3. ``all_reduce(MAX)`` of m, then each rank rescales (l, u) by exp(m_local - m_glob) into one
+   packed buffer [M, QH, Dt + 1];
+4. ``reduce_scatter(SUM)`` of the packed buffer by whole-sequence blocks (B / world sequences per
+   rank), so the short conv needs no halo;
+5. on the local block: u / l, the folded output map, the conv finish -> out [B / world, T, d].
+
+Steps 3-5 are the exact decomposition of the reference's streaming readout over route chunks
+(``ffnmem/memory/lngram_v2.py:1944-2070``: running max, rescaled sums, final division) with one
+chunk per rank.  The two collectives are the only data-path communication.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.distributed as dist
+from torch import Tensor
+
+from . import _lib
+from ._lib import check, ptr, stream_ptr
+from .memory import LngramMemory
+
+
+def route_bounds(routes: int, world: int) -> list[tuple[int, int]]:
+    """Contiguous route blocks, the first ``routes % world`` ranks one route larger."""
+    base, extra = divmod(routes, world)
+    out, start = [], 0
+    for r in range(world):
+        n = base + (1 if r < extra else 0)
+        out.append((start, start + n))
+        start += n
+    return out
+
+
+def all_reduce_max(t: Tensor, group=None) -> Tensor:
+    if dist.is_initialized() and dist.get_world_size(group) > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    return t
+
+
+def reduce_scatter_rows(t: Tensor, group=None) -> Tensor:
+    """SUM over ranks of ``t`` [N, ...]; rank r receives rows r*N/world .. (r+1)*N/world."""
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    if world == 1:
+        return t
+    if t.shape[0] % world:
+        raise ValueError("rows must split evenly across ranks")
+    out = torch.empty((t.shape[0] // world,) + tuple(t.shape[1:]), device=t.device, dtype=t.dtype)
+    dist.reduce_scatter_tensor(out, t.contiguous(), op=dist.ReduceOp.SUM, group=group)
+    return out
+
+
+class RouteShardedMemory:
+    """One rank's share of a route-sharded ``LngramMemory``."""
+
+    def __init__(self, full: LngramMemory, rank: int, world: int, group=None):
+        m = full.module
+        self.rank, self.world, self.group = int(rank), int(world), group
+        self.bounds = route_bounds(m.num_routes, world)
+        self.r0, self.r1 = self.bounds[rank]
+        self.full = full
+        self.R_total = m.num_routes
+        dev = m.readout_q_proj.weight.device
+        # the rank's rows of every order table (route-major layout: contiguous) and of the router
+        self.tables = {}
+        for n in m.ngrams:
+            span = m.alphabet_size ** n
+            self.tables[n] = m.tables[f"ngram_{n}"].weight.detach()[self.r0 * span:self.r1 * span].contiguous()
+        self.router_w = full.router.weight.detach()[self.r0 * full.bits:self.r1 * full.bits].float().contiguous()
+        self.ss = {}
+        self.dev = dev
+
+    def _tables_desc(self):
+        m = self.full.module
+        t = _lib.Tables()
+        t.n_orders = len(m.ngrams)
+        for i, n in enumerate(m.ngrams):
+            t.orders[i] = n
+            t.tables[i] = self.tables[n].data_ptr()
+        t.table_dtype = _lib.dtype_code(self.tables[m.ngrams[0]].dtype)
+        t.bits = m.bits_per_route
+        t.num_routes = self.r1 - self.r0
+        t.memory_dim = m.memory_dim
+        if not self.ss:
+            desc = t
+            self.ss = {n: torch.empty(self.tables[n].shape[0], device=self.dev, dtype=torch.float32) for n in m.ngrams}
+            arr = (_lib.C.c_void_p * _lib.MAX_ORDERS)(*([self.ss[n].data_ptr() for n in m.ngrams] +
+                                                        [None] * (_lib.MAX_ORDERS - len(m.ngrams))))
+            check(_lib.library().lng_table_row_ss(desc, arr, stream_ptr()), "row sums of squares")
+        for i, n in enumerate(m.ngrams):
+            t.row_ss[i] = self.ss[n].data_ptr()
+        return t
+
+    @torch.no_grad()
+    def forward(self, h: Tensor, router_x: Tensor) -> Tensor:
+        """h, router_x [B, T, *] (the same on every rank) -> this rank's block of B / world sequences."""
+        B, T, d = h.shape
+        if B % self.world:
+            raise ValueError("the batch must split into whole sequences per rank")
+        mloc, lloc, u = self.partial(h, router_x)
+        mglob = all_reduce_max(mloc.clone(), self.group)
+        pack = self.pack(mloc, mglob, lloc, u)
+        mine = reduce_scatter_rows(pack.view(B * T, -1), self.group)      # [B*T / world, QH * (Dt + 1)]
+        return self.finish(mine, B // self.world, T)
+
+    def pack(self, mloc: Tensor, mglob: Tensor, lloc: Tensor, u: Tensor) -> Tensor:
+        """(u, l) * exp(m_local - m_glob) packed [M, QH, Dt + 1] for the SUM reduction."""
+        M, QH, Dt = u.shape
+        pack = torch.empty(M, QH, Dt + 1, device=u.device, dtype=torch.float32)
+        check(_lib.library().lng_attend_pack(ptr(mloc), ptr(mglob), ptr(lloc), ptr(u), M, QH, Dt, ptr(pack),
+                                             stream_ptr()), "pack")
+        return pack
+
+    def finish(self, packed: Tensor, Bb: int, T: int) -> Tensor:
+        """Summed packed states of Bb whole sequences -> memory output [Bb, T, d]."""
+        m = self.full.module
+        act = m._act()
+        QH, Dt = m.readout_num_heads, m.route_token_dim
+        Mb = packed.shape[0]
+        ub = torch.empty(Mb, QH * Dt, device=packed.device, dtype=act)
+        check(_lib.library().lng_attend_unpack(ptr(packed.contiguous()), Mb, QH, Dt, ptr(ub), _lib.dtype_code(act),
+                                               stream_ptr()), "unpack")
+        mixed = m._linear(ub, m.folded()["w_vo"])
+        return m._conv_finish(mixed.view(Bb, T, m.hidden_size), None, None)
+
+    @torch.no_grad()
+    def partial(self, h: Tensor, router_x: Tensor) -> tuple[Tensor, Tensor, Tensor]:
+        """This rank's online-softmax state over its routes: m, l [B*T, QH] and u [B*T, QH, Dt] (fp32)."""
+        m = self.full.module
+        lib = _lib.library()
+        s = stream_ptr()
+        act = m._act()
+        B, T, d = h.shape
+        M = B * T
+        Rl = self.r1 - self.r0
+        h = h.to(act).contiguous()
+        x = router_x.contiguous() if router_x.dtype in (torch.float32, torch.bfloat16) else router_x.float()
+        codes = torch.empty(B, T, Rl, device=h.device, dtype=torch.uint8)
+        check(lib.lng_route_codes(ptr(x), _lib.dtype_code(x.dtype), M, x.shape[-1], x.shape[-1], ptr(self.router_w),
+                                  Rl, m.bits_per_route, ptr(codes), _lib.U8, None, s), "route codes")
+        f = m.folded()
+        Dt, QH = m.route_token_dim, m.readout_num_heads
+        rs = torch.empty(M, device=h.device, dtype=torch.float32)
+        check(lib.lng_rms_rows(ptr(h), _lib.dtype_code(act), M, d, m.eps, ptr(rs), s), "rms")
+        tdt = self.tables[m.ngrams[0]].dtype
+        qa = m._linear(h.view(M, d), f["w_qk"].to(tdt) if f["w_qk"].dtype != tdt else f["w_qk"])
+        mloc = torch.empty(M, QH, device=h.device, dtype=torch.float32)
+        lloc = torch.empty_like(mloc)
+        u = torch.empty(M, QH, Dt, device=h.device, dtype=torch.float32)
+        # sink: b0 = log(R_total (1 - mass) / mass) of the whole layer, seeded on rank 0 only
+        check(lib.lng_route_attend(self._tables_desc(), ptr(codes), _lib.U8, B, T, 0, None, None, None, 0, 0, Rl, QH,
+                                   m.eps, m.readout_sink_logit, ptr(qa), ptr(rs), ptr(u), _lib.F32,
+                                   1 if self.rank == 0 else 2, ptr(mloc), ptr(lloc), s), "route_attend partial")
+        return mloc, lloc, u

@@ -58,6 +58,8 @@ def lngram():
 
 @pytest.fixture(scope="session")
 def reference_path():
+    # appended, so this repository's own top-level names (``tests``, ``oracle``) keep precedence
+    # over the reference's packages of the same name
     if str(REFERENCE) not in sys.path:
-        sys.path.insert(0, str(REFERENCE))
+        sys.path.append(str(REFERENCE))
     return REFERENCE

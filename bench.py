@@ -1,18 +1,26 @@
 """Benchmark of the Lngram v2 memory lookup on B200 (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload sb_prefill]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload W]
     python -m torch.distributed.run --nproc-per-node N bench.py --gpus N ...   (N > 1)
 
-Workload ``sb_prefill`` (the metric's configuration): one SB memory layer
-forward over h [32, 2048, 1024] bf16 per GPU, R = 184 routes, 4-bit codes, order 3, table
-[753,664 x 136] bf16, fp32 router [736, 1024], folded readout in bf16.  A step is one
-``LngramMemory.forward`` over the whole batch (router -> codes -> gather + sink attention ->
-output projection -> conv).  Synthetic seeded inputs; inputs (table 205 MB, h + h_norm 268 MB,
-two alternating input sets) are larger than the 126 MB L2.  N GPUs run independent replicas
-(weak scaling, no collective on the data path); the job time is the max over ranks.
+Workloads (synthetic seeded inputs of the shapes the configurations name):
 
-``--impl reference`` times the reference algorithm's CPU restatement (the numpy oracle, all host
-threads) on a bounded sample of the same workload and prints the same metric.
+* ``sb_prefill`` (default; the metric's configuration): one SB memory layer forward over
+  h [32, 2048, 1024] bf16 per GPU, R = 184 routes, 4-bit codes, order 3, table [753,664 x 136]
+  bf16, fp32 router [736, 1024], folded readout in bf16.  A step is one ``LngramMemory.forward``
+  over the whole batch (router -> codes -> gather + sink attention -> output projection -> conv).
+  Inputs (table 205 MB, h + h_norm 268 MB, two alternating input sets) are larger than the 126 MB
+  L2.  N GPUs run independent replicas (weak scaling, no collective on the data path).
+* ``sdb_draft``: the SD-B drafter (182 routes, embed2 token router, vocab 32000); a step drafts
+  4 greedy tokens for each of 64 sequences with 1024-token prefixes (``GpuDrafter.draft_batch``).
+* ``tree_verify``: 64 sequences x a 16-node draft tree after a 1024-position context on the SB
+  layer; a step is the nodes' router codes + ``tree_memory_block``.
+* ``scaled``: the 52 GB scaled table (184 routes x 2**20 rows x 136, 5-bit codes, order 4) over
+  h [64, 4096, 1024]; at N > 1 the routes are sharded across the GPUs (strong scaling).
+
+The job time is the max over ranks of CUDA-event time.  ``--impl reference`` times the reference's
+CPU implementation of the same workload (the reference's C++ drafter for ``sdb_draft``, the numpy
+restatement of the reference forward otherwise) on a bounded sample, on all host threads.
 """
 
 from __future__ import annotations
@@ -231,6 +239,7 @@ def run_ours(args, rank, world, local) -> dict:
         stages = time_stages(mem, lib, h, hn)
         # e2e through the public API with pinned host buffers
         e2e = time_e2e(mem, inputs, args, world)
+        launches = count_launches(lambda: step(0), fallback=LAUNCHES_PER_FORWARD)
         dev_err = lib.device_error(clear=True)
     if dev_err:
         raise RuntimeError(f"device error word {dev_err} after the timed region")
@@ -254,7 +263,7 @@ def run_ours(args, rank, world, local) -> dict:
                      "ms_per_launch": att["ms"], "launches": att["launches"]},
         "e2e": e2e,
         "stages_ms": stages,
-        "gpu_launches": LAUNCHES_PER_FORWARD * args.steps,
+        "gpu_launches": launches["per_step"] * args.steps, "launch_count": launches,
         "clocks": clk.summary(),
     }
     return line
@@ -377,6 +386,47 @@ def time_e2e(mem, inputs, args, world) -> dict:
             "ms_per_step": ms / args.steps}
 
 
+def count_launches(fn, fallback: int) -> dict:
+    """Kernels of this library (namespace ``lng::``) launched by one untimed call of ``fn``, counted from
+    the CUDA activity record of ``torch.profiler``; nothing timed comes from this pass."""
+    try:
+        from torch.profiler import ProfilerActivity, profile
+
+        torch.cuda.synchronize()
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            fn()
+            torch.cuda.synchronize()
+        names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+        ours = [n for n in names if "lng::" in n]
+        return {"per_step": len(ours), "other_kernels_per_step": len([n for n in names if "lng::" not in n
+                                                                     and "emcpy" not in n and "emset" not in n]),
+                "source": "torch.profiler kernel record of one untimed step"}
+    except Exception as exc:  # profiler unavailable: the static count of the launch sites
+        return {"per_step": fallback, "source": f"static count ({type(exc).__name__})"}
+
+
+def timed_steps(step, steps: int, flush: torch.Tensor | None) -> float:
+    """Sum of per-step CUDA-event times (ms); with ``flush``, a buffer larger than L2 is rewritten
+    between steps, outside the timed events."""
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for i, (a, b) in enumerate(evs):
+        if flush is not None:
+            flush.add_(1)
+        a.record()
+        step(i)
+        b.record()
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in evs)
+
+
+def kernel_ms(launch, reps: int, flush: torch.Tensor | None = None) -> float:
+    """Average CUDA-event duration of one call of ``launch`` (after 3 warm-up calls)."""
+    for _ in range(3):
+        launch()
+    torch.cuda.synchronize()
+    return timed_steps(lambda i: launch(), reps, flush) / reps
+
+
 def profiled_traffic(kernel: str, units: int):
     """DRAM bytes per launch of ``kernel`` from the committed ncu summary, scaled to ``units``."""
     p = REPO / "profiles" / "traffic.json"
@@ -386,6 +436,412 @@ def profiled_traffic(kernel: str, units: int):
     if not d:
         return None
     return d["dram_bytes"] * units / d["units"]
+
+
+# --------------------------------------------------------------------------- SD-B drafting
+SDB = dict(nseq=64, plen=1024, gamma=4)
+
+
+def sdb_bundle():
+    """The SD-B drafter bundle: 182 routes, embed2 token router, order 3, 136 dims, vocab 32000,
+    d = 1024, weights N(0, 0.02) (seeded; tables fp32 in the bundle, bf16 on the GPU)."""
+    from tests.golden import cases
+
+    return cases.draft_bundle("sdb")
+
+
+def run_sdb(args, rank, world, local) -> dict:
+    from __graft_entry__ import load_package
+
+    pkg = load_package()
+    lib = pkg._lib
+    dev = torch.device("cuda", local)
+    config, arrays = sdb_bundle()
+    drafter = pkg.GpuDrafter(pkg.Bundle(config, arrays, {}), act_dtype=torch.bfloat16, device=dev)
+    nseq, plen, gamma = SDB["nseq"], SDB["plen"], SDB["gamma"]
+    V, d = int(config["vocab"]), int(config["d_model"])
+    g = torch.Generator(device=dev).manual_seed(300 + rank)
+    prefixes = [torch.randint(0, V, (nseq, plen), device=dev, generator=g) for _ in range(2)]
+    toks = torch.empty(nseq, gamma, device=dev, dtype=torch.int64)
+    flush = torch.zeros(2 * L2_BYTES // 4, device=dev, dtype=torch.float32)
+
+    def step(i):
+        drafter.draft_batch(prefixes[i % 2], gamma, out=toks)
+
+    with torch.no_grad(), ClockSampler(local) as clk:
+        time.sleep(0.5)
+        for i in range(args.warmup):
+            step(i)
+        torch.cuda.synchronize()
+        lib.device_error(clear=True)
+        barrier(world)
+        torch.cuda.synchronize()
+        ms = timed_steps(step, args.steps, flush)
+        barrier(world)
+        ms_max = max_over_ranks(ms, world)
+        # roofline: the draft-head logits + top-1 over the vocabulary (bf16 embedding), timed alone
+        E = torch.from_numpy(np.ascontiguousarray(arrays["embedding"])).to(dev).to(torch.bfloat16)
+        hq = torch.randn(nseq, d, device=dev, generator=g)
+        ids = torch.empty(nseq, 1, device=dev, dtype=torch.int64)
+        vals = torch.empty(nseq, 1, device=dev, dtype=torch.float32)
+        L = lib.library()
+        sb = L.lng_logits_topk_scratch_bytes(nseq, V, 1)
+        scratch = torch.empty(sb, device=dev, dtype=torch.uint8)
+        s = lib.stream_ptr()
+        lk_ms = kernel_ms(lambda: lib.check(L.lng_logits_topk(hq.data_ptr(), nseq, d, E.data_ptr(), lib.BF16, V, 1,
+                                                               ids.data_ptr(), vals.data_ptr(), None,
+                                                               scratch.data_ptr(), sb, s)), max(3, args.steps), flush)
+        # e2e: pinned host prefix in, drafted tokens out, every step
+        hosts = [p.cpu().pin_memory() for p in prefixes]
+        dpre = torch.empty_like(prefixes[0])
+        out_host = torch.empty(nseq, gamma, dtype=torch.int64).pin_memory()
+
+        def e2e_step(i):
+            dpre.copy_(hosts[i % 2], non_blocking=True)
+            drafter.draft_batch(dpre, gamma, out=toks)
+            out_host.copy_(toks, non_blocking=True)
+
+        for i in range(args.warmup):
+            e2e_step(i)
+        torch.cuda.synchronize()
+        barrier(world)
+        e2e_ms = max_over_ranks(timed_steps(e2e_step, args.steps, flush), world)
+        launches = count_launches(lambda: step(0), fallback=0)
+        dev_err = lib.device_error(clear=True)
+    if dev_err:
+        raise RuntimeError(f"device error word {dev_err} after the timed region")
+    pk = peaks()
+    units = nseq * gamma * world * args.steps
+    lk_bytes = V * d * 2 + nseq * d * 4 + nseq * 12
+    achieved = lk_bytes / (lk_ms / 1e3) / 1e9
+    return {
+        "metric": METRIC, "value": units / (ms_max / 1e3), "unit": "draft tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded uniform token prefixes, N(0,0.02) weights)",
+        "config": {"workload": "sdb_draft", "sequences": nseq, "prefix": plen, "gamma": gamma, "vocab": V,
+                   "d_model": d, "routes": int(config["routes"]), "bits": int(config["bits"]),
+                   "ngrams": list(config["ngrams"]), "router": "embed2 (token only)", "sampling": "argmax",
+                   "parallelism": f"replicas{world}",
+                   "l2": "a 252 MB buffer is rewritten between timed steps (outside the step events)"},
+        "roofline": {"bound": "hbm", "kernel": "logits_chunk_topk_kernel (draft-head logits + top-1, bf16 vocab)",
+                     "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+                     "peak_source": pk["source"], "traffic": None, "bytes_per_launch": lk_bytes,
+                     "ms_per_launch": lk_ms, "launches_per_step": gamma},
+        "e2e": {"value": units / (e2e_ms / 1e3), "unit": "draft tokens/s", "h2d_bytes_per_step": nseq * plen * 8,
+                "d2h_bytes_per_step": nseq * gamma * 8, "ms_per_step": e2e_ms / args.steps},
+        "gpu_launches": launches["per_step"] * args.steps, "launch_count": launches,
+        "clocks": clk.summary(),
+    }
+
+
+def cpu_sdb_sample(budget_s: float = 12.0, reps: int | None = None) -> dict:
+    """The reference's C++ drafter (``drafting/cpu/drafter.cpp``, built from the reference sources into
+    ``oracle/_ref``) -- or the oracle restatement when that build is absent -- on SD-B sequences: one
+    drafter per host thread, each holding one committed 1024-token prefix (commit untimed), then
+    ``draft(4)`` + ``truncate`` repeated in parallel on all threads for about ``budget_s`` seconds."""
+    import concurrent.futures as cf
+
+    config, arrays = sdb_bundle()
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    threads = max(1, min(threads, SDB["nseq"]))
+    rng = np.random.default_rng(5)
+    V, plen, gamma = int(config["vocab"]), SDB["plen"], SDB["gamma"]
+    prefixes = rng.integers(0, V, size=(threads, plen))
+    from oracle.build import load_reference_drafter
+
+    ext = load_reference_drafter()
+    if ext is not None:
+        tensors = {k: torch.from_numpy(np.ascontiguousarray(v)) for k, v in arrays.items()}
+        num = {k: float(config[k]) for k in ("d_model", "vocab", "routes", "bits", "mem_dim", "kv_heads", "head_dim",
+                                             "q_heads", "ssm_dim", "sketch_k", "norm_eps", "ssm_eps", "router_eps",
+                                             "draft_eps", "mem_eps", "softmax_scale", "sink_logit")}
+        num.update(shortlist_cap=float(config["shortlist_cap"]), router_ssm=float(config["router_kind"] == "embed2_ssm"),
+                   query_ssm=float(bool(config["query_ssm"])))
+        cores = [ext.Drafter(tensors, num, [int(n) for n in config["ngrams"]], 1) for _ in range(threads)]
+        kind = "reference"
+        draft = lambda c: c.draft(gamma, [], 1, False)  # noqa: E731
+    else:
+        from oracle.drafter import OracleDrafter
+
+        cores = [OracleDrafter(config, arrays) for _ in range(threads)]
+        kind = "port"
+        draft = lambda c: c.draft(gamma, (), 1)  # noqa: E731
+    with cf.ThreadPoolExecutor(threads) as ex:
+        list(ex.map(lambda i: cores[i].commit([int(t) for t in prefixes[i]]), range(threads)))
+        t0 = time.perf_counter()
+        draft(cores[0])
+        cores[0].truncate(plen)
+        one = time.perf_counter() - t0
+        n = reps if reps is not None else max(1, int(budget_s / max(one, 1e-3) / 2))
+
+        def work(i):
+            for _ in range(n):
+                draft(cores[i])
+                cores[i].truncate(plen)
+
+        t0 = time.perf_counter()
+        list(ex.map(work, range(threads)))
+        dt = time.perf_counter() - t0
+    tokens = threads * n * gamma
+    return {"value": tokens / dt, "unit": "draft tokens/s", "cores": threads, "kind": kind,
+            "sample": f"{threads} sequences (1024-token prefixes, one drafter per thread) x {n} drafts of "
+                      f"{gamma} tokens, full-vocabulary argmax"}
+
+
+# --------------------------------------------------------------------------- tree verification (configs[3])
+TREE = dict(nseq=64, ctx=1024)
+
+
+def run_tree(args, rank, world, local) -> dict:
+    from __graft_entry__ import load_package
+    from tests.golden import cases
+
+    pkg = load_package()
+    lib = pkg._lib
+    dev = torch.device("cuda", local)
+    mem = build_sb(pkg, dev, seed=0)
+    m = mem.module
+    parent = cases.TREE_PARENT
+    nseq, ctx, n = TREE["nseq"], TREE["ctx"], len(parent)
+    d = SB["d"]
+    cache = pkg.MemoryCache(m, nseq, ctx + n, device=dev)
+    g = torch.Generator(device=dev).manual_seed(400 + rank)
+
+    def hidden(T):
+        h = torch.randn(nseq, T, d, device=dev, generator=g).to(torch.bfloat16)
+        hf = h.float()
+        return h, (hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + 1e-5)).to(torch.bfloat16)
+
+    with torch.no_grad():
+        hc, hnc = hidden(ctx)                                   # the context, through the prefill seam
+        pkg.memory_step(m, cache, hc, mem.route_codes(hnc))
+        cache.length = ctx
+        del hc, hnc
+        nodes = [hidden(n) for _ in range(2)]
+    flush = torch.zeros(2 * L2_BYTES // 4, device=dev, dtype=torch.float32)
+
+    def step(i):
+        h, hn = nodes[i % 2]
+        pkg.tree_memory_block(m, cache, h, mem.route_codes(hn), parent)
+
+    with torch.no_grad(), ClockSampler(local) as clk:
+        time.sleep(0.5)
+        for i in range(args.warmup):
+            step(i)
+        torch.cuda.synchronize()
+        lib.device_error(clear=True)
+        barrier(world)
+        torch.cuda.synchronize()
+        ms = timed_steps(step, args.steps, flush)
+        barrier(world)
+        ms_max = max_over_ranks(ms, world)
+        # roofline: the fused gather + sink attention over the nodes' tree windows, timed alone
+        att_ms, att_bytes = time_tree_attend(pkg, mem, cache, nodes[0], parent, args.steps, flush)
+        hosts = [(h.cpu().pin_memory(), hn.cpu().pin_memory()) for h, hn in nodes]
+        hd, hnd = torch.empty_like(nodes[0][0]), torch.empty_like(nodes[0][1])
+        out_host = torch.empty(nseq, n, d, dtype=torch.bfloat16).pin_memory()
+
+        def e2e_step(i):
+            h, hn = hosts[i % 2]
+            hd.copy_(h, non_blocking=True)
+            hnd.copy_(hn, non_blocking=True)
+            out_host.copy_(pkg.tree_memory_block(m, cache, hd, mem.route_codes(hnd), parent), non_blocking=True)
+
+        for i in range(args.warmup):
+            e2e_step(i)
+        torch.cuda.synchronize()
+        barrier(world)
+        e2e_ms = max_over_ranks(timed_steps(e2e_step, args.steps, flush), world)
+        launches = count_launches(lambda: step(0), fallback=0)
+        dev_err = lib.device_error(clear=True)
+    if dev_err:
+        raise RuntimeError(f"device error word {dev_err} after the timed region")
+    pk = peaks()
+    units = nseq * n * world * args.steps
+    achieved = att_bytes / (att_ms / 1e3) / 1e9
+    return {
+        "metric": METRIC, "value": units / (ms_max / 1e3), "unit": "tree nodes/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) hidden states, N(0,0.02) tables)",
+        "config": {"workload": "tree_verify", "sequences": nseq, "context": ctx, "nodes": n, "parent": list(parent),
+                   "routes": SB["routes"], "bits": SB["bits"], "ngrams": list(SB["ngrams"]), "mem_dim": SB["mem_dim"],
+                   "step": "router codes of the nodes + tree_memory_block (n-gram and conv windows along ancestors)",
+                   "parallelism": f"replicas{world}",
+                   "l2": "a 252 MB buffer is rewritten between timed steps (outside the step events)"},
+        "roofline": {"bound": "hbm", "kernel": "attend_mma_kernel (tree windows)", "achieved": achieved,
+                     "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+                     "peak_source": pk["source"], "traffic": None, "bytes_per_launch": att_bytes,
+                     "ms_per_launch": att_ms},
+        "e2e": {"value": units / (e2e_ms / 1e3), "unit": "tree nodes/s", "h2d_bytes_per_step": 2 * nseq * n * d * 2,
+                "d2h_bytes_per_step": nseq * n * d * 2, "ms_per_step": e2e_ms / args.steps},
+        "gpu_launches": launches["per_step"] * args.steps, "launch_count": launches,
+        "clocks": clk.summary(),
+    }
+
+
+def time_tree_attend(pkg, mem, cache, node_inputs, parent, steps, flush):
+    """CUDA-event time and algorithmic bytes of lng_route_attend on the tree windows of one step."""
+    m = mem.module
+    lib = pkg._lib
+    L = lib.library()
+    h, hn = node_inputs
+    B, n, d = h.shape
+    hist = m.route_history_length
+    W = hist + 1
+    plan = pkg.seams._tree_plan(parent, cache.length, B, cache.max_len, hist, m.short_conv.kernel_size,
+                                m.short_conv.dilation, h.device)
+    Lc = cache.length
+    codes = mem.route_codes(hn)
+    allc = torch.cat((cache.codes[:, Lc - plan["h0"]:Lc], codes), 1)
+    ctx = (allc[:, plan["gidx"]] * plan["gok"]).reshape(B * n, W, -1).contiguous()
+    f = m.folded()
+    M = B * n
+    qd = m.readout_num_heads * m.route_token_dim
+    rs = torch.empty(M, device=h.device, dtype=torch.float32)
+    s = lib.stream_ptr()
+    lib.check(L.lng_rms_rows(h.data_ptr(), lib.BF16, M, d, m.eps, rs.data_ptr(), s))
+    qa = m._linear(h.reshape(M, d), f["w_qk"])
+    u = torch.empty(M, qd, device=h.device, dtype=torch.bfloat16)
+    desc = m.tables_desc()
+    seg = plan["seg"]
+    ms = kernel_ms(lambda: lib.check(L.lng_route_attend(desc, ctx.data_ptr(), lib.U8, M, 0, W, None, None,
+                                                        seg.data_ptr(), 0, 0, m.num_routes, m.readout_num_heads,
+                                                        m.eps, m.readout_sink_logit, qa.data_ptr(), rs.data_ptr(),
+                                                        u.data_ptr(), lib.BF16, 0, None, None, s)),
+                   max(3, steps), flush)
+    R, Dt = m.num_routes, m.route_token_dim
+    nbytes = M * (R * Dt * 2 + 2 * qd * 2 + W * R + W * 4 + 4)
+    return ms, nbytes
+
+
+# --------------------------------------------------------------------------- scaled route-sharded (configs[4])
+SCALED = dict(B=64, T=4096, d=1024, routes=184, bits=5, ngrams=(4,), mem_dim=136, q_heads=16, kv_heads=4, head_dim=64)
+
+
+def build_scaled_shard(pkg, dev, rank: int, world: int, seed: int = 0):
+    """This rank's block of routes of the scaled layer (tables N(0, 0.02) bf16, filled route chunk by
+    route chunk from a seed per global route, so every world size holds the same table), with the
+    readout weights and router rows seeded identically on every rank."""
+    c = SCALED
+    r0, r1 = pkg.sharded.route_bounds(c["routes"], world)[rank]
+    # the table is created zeroed (no whole-table fp32 init temporary) and filled route by route below
+    mem = pkg.LngramMemory(c["d"], {"routes": r1 - r0, "mem_dim": c["mem_dim"], "kv_heads": c["kv_heads"],
+                                    "q_heads": c["q_heads"], "head_dim": c["head_dim"], "ngrams": list(c["ngrams"]),
+                                    "bits_per_route": c["bits"], "table_init_std_scale": 0.0}, norm_eps=1e-5,
+                           device=dev, dtype=torch.bfloat16).eval()
+    m = mem.module
+    span = (1 << c["bits"]) ** c["ngrams"][0]
+    with torch.no_grad():
+        w = m.tables[f"ngram_{c['ngrams'][0]}"].weight
+        for r in range(r0, r1):
+            g = torch.Generator(device=dev).manual_seed(seed * 100003 + 7919 + r)
+            w[(r - r0) * span:(r - r0 + 1) * span].copy_(
+                (torch.randn(span, c["mem_dim"], device=dev, generator=g) * 0.02).to(torch.bfloat16))
+        g = torch.Generator(device=dev).manual_seed(seed + 2)
+        for name, std in (("readout_q_proj", 0.02), ("readout_kv_proj", 0.02), ("readout_o_proj", 0.006)):
+            p = getattr(m, name).weight
+            p.copy_((torch.randn(p.shape, device=dev, generator=g) * std).to(p.dtype))
+        m.short_conv.conv.weight.copy_((torch.randn(m.short_conv.conv.weight.shape, device=dev, generator=g) * 0.2)
+                                       .to(torch.bfloat16))
+        router = torch.randn(c["routes"] * c["bits"], c["d"], device=dev, generator=g) * 0.02
+        mem.router.weight.copy_(router[r0 * c["bits"]:r1 * c["bits"]])
+    return mem, pkg.RouteShardedMemory(mem, rank, world, routes_total=c["routes"])
+
+
+def run_scaled(args, rank, world, local) -> dict:
+    from __graft_entry__ import load_package
+
+    pkg = load_package()
+    lib = pkg._lib
+    dev = torch.device("cuda", local)
+    c = SCALED
+    B, T, d = c["B"], c["T"], c["d"]
+    mem, shard = build_scaled_shard(pkg, dev, rank, world)
+    g = torch.Generator(device=dev).manual_seed(500)        # the same hidden states on every rank
+    h = torch.randn(B, T, d, device=dev, generator=g).to(torch.bfloat16)
+    hf = h.float()
+    hn = (hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + 1e-5)).to(torch.bfloat16)
+    del hf
+    M = B * T
+    if world == 1:   # the whole table on one GPU: the fused single-GPU forward
+        out = torch.empty(B, T, d, device=dev, dtype=torch.bfloat16)
+        ws = torch.empty(lib.library().lng_memory_workspace_bytes(mem.module.tables_desc(),
+                                                                  mem.module.readout_desc(mem.router.weight), M),
+                         device=dev, dtype=torch.uint8)
+
+        def step(i):
+            mem(h, hn, out=out, workspace=ws)
+    else:
+        def step(i):
+            shard.forward(h, hn)
+
+    with torch.no_grad(), ClockSampler(local) as clk:
+        time.sleep(0.5)
+        for i in range(args.warmup):
+            step(i)
+        torch.cuda.synchronize()
+        lib.device_error(clear=True)
+        barrier(world)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(args.steps):
+            step(i)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        barrier(world)
+        ms_max = max_over_ranks(ms, world)
+        # roofline: the rank's fused gather + sink attention over its routes (partial mode), alone
+        m = mem.module
+        Rl = shard.r1 - shard.r0
+        codes = mem.route_codes(hn)
+        f = m.folded()
+        qd = m.readout_num_heads * m.route_token_dim
+        rs = torch.empty(M, device=dev, dtype=torch.float32)
+        L = lib.library()
+        s = lib.stream_ptr()
+        lib.check(L.lng_rms_rows(h.data_ptr(), lib.BF16, M, d, m.eps, rs.data_ptr(), s))
+        qa = m._linear(h.view(M, d), f["w_qk"])
+        u = torch.empty(M, m.readout_num_heads, m.route_token_dim, device=dev, dtype=torch.float32)
+        ml = torch.empty(M, m.readout_num_heads, device=dev, dtype=torch.float32)
+        ll = torch.empty_like(ml)
+        desc = shard._tables_desc()
+        att_ms = kernel_ms(lambda: lib.check(L.lng_route_attend(desc, codes.data_ptr(), lib.U8, B, T, 0, None, None,
+                                                                None, 0, 0, Rl, m.readout_num_heads, m.eps,
+                                                                shard.sink_logit, qa.data_ptr(), rs.data_ptr(),
+                                                                u.data_ptr(), lib.F32, 1, ml.data_ptr(),
+                                                                ll.data_ptr(), s)), 3)
+        del u, qa
+        launches = count_launches(lambda: step(0), fallback=0)
+        dev_err = lib.device_error(clear=True)
+    if dev_err:
+        raise RuntimeError(f"device error word {dev_err} after the timed region")
+    pk = peaks()
+    Dt = m.route_token_dim
+    att_bytes = M * (Rl * Dt * 2 + qd * 2 + m.readout_num_heads * (Dt + 2) * 4 + Rl)
+    achieved = att_bytes / (att_ms / 1e3) / 1e9
+    table_gb = c["routes"] * (1 << c["bits"]) ** c["ngrams"][0] * c["mem_dim"] * 2 / 1e9
+    return {
+        "metric": METRIC, "value": M * args.steps / (ms_max / 1e3), "unit": "positions/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) hidden states, N(0,0.02) tables)",
+        "config": {"workload": "scaled", "batch": B, "seq_len": T, "d_model": d, "routes": c["routes"],
+                   "routes_per_gpu": Rl, "bits": c["bits"], "ngrams": list(c["ngrams"]), "mem_dim": c["mem_dim"],
+                   "table_gb": round(table_gb, 1),
+                   "parallelism": "route-sharded (NCCL max all-reduce + reduce-scatter by sequence blocks)"
+                   if world > 1 else "single GPU (whole table)",
+                   "l2": f"inputs larger than L2 ({table_gb:.0f} GB table, 1.07 GB h + h_norm)"},
+        "roofline": {"bound": "hbm", "kernel": "attend_mma_kernel (partial mode, this rank's routes)",
+                     "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+                     "peak_source": pk["source"], "traffic": None, "bytes_per_launch": att_bytes,
+                     "ms_per_launch": att_ms},
+        "gpu_launches": launches["per_step"] * args.steps, "launch_count": launches,
+        "clocks": clk.summary(),
+    }
 
 
 # --------------------------------------------------------------------------- CPU baseline / reference arm
@@ -416,24 +872,73 @@ def cpu_sb_sample(budget_s: float = 12.0) -> dict:
             "sample": f"{seqs} x (1 x 2048) SB positions through the numpy oracle forward (fp32, bf16-valued data)"}
 
 
+def cpu_tree_sample(budget_s: float = 12.0, max_seqs: int | None = None) -> dict:
+    """The numpy restatement of the reference's tree-verification memory block (oracle/memory.py
+    ``tree_memory_block``, ``drafting/tree.py:178-195``) with the SB layer: the nodes' router codes and
+    the block for one sequence's 16-node tree after a 1024-position context, repeated for about
+    ``budget_s`` seconds."""
+    from oracle import memory as om
+    from tests.golden import cases
+
+    p = cases.oracle_params("sb_slice")
+    router_w = cases.memory_params("sb_slice")["router.weight"]
+    parent = cases.TREE_PARENT
+    n, d, R = len(parent), SB["d"], SB["routes"]
+    rng = np.random.default_rng(1)
+    hist = p.route_history_length
+    t0 = time.perf_counter()
+    seqs = 0
+    while True:
+        h = cases.bf16_round(rng.standard_normal((1, n, d), dtype=np.float32))
+        x = cases.bf16_round(om.rms_norm(h, None, 1e-5))
+        codes = om.quantize_route_logits(om.route_logits(x, router_w), p.bits)
+        history = rng.integers(0, 1 << p.bits, size=(1, hist, R))
+        conv_cache = rng.standard_normal((1, TREE["ctx"], d), dtype=np.float32)
+        om.tree_memory_block(h, codes, parent, history, conv_cache, TREE["ctx"], p)
+        seqs += 1
+        if time.perf_counter() - t0 >= budget_s or (max_seqs is not None and seqs >= max_seqs):
+            break
+    dt = time.perf_counter() - t0
+    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    return {"value": seqs * n / dt, "unit": "tree nodes/s", "cores": threads, "kind": "port",
+            "sample": f"{seqs} x 16-node trees (1024-position context) through the numpy oracle (fp32)"}
+
+
 def run_reference(args, rank, world) -> dict | None:
+    """The reference algorithm on the host cores (rank 0 only), same metric / unit / config keys."""
     if rank != 0:
         return None
-    per_step = []
-    base = None
+    wl = args.workload
+    if wl == "scaled":
+        return {"impl": "reference", "unavailable": "the scaled table (52 GB) has no bounded CPU sample: the "
+                "reference CPU forward would have to generate and hold the whole table in host memory"}
+    per_step, base = [], None
     for i in range(args.warmup + args.steps):
-        r = cpu_sb_sample(budget_s=0.0)  # one sequence per step
+        if wl == "sb_prefill":
+            r = cpu_sb_sample(budget_s=0.0)                 # one 2048-position sequence per step
+        elif wl == "sdb_draft":
+            r = cpu_sdb_sample(reps=1)                      # one draft of 4 tokens on every thread per step
+        else:
+            r = cpu_tree_sample(budget_s=0.0, max_seqs=1)   # one 16-node tree per step
         if i >= args.warmup:
             per_step.append(r["value"])
         base = r
     value = statistics.mean(per_step)
-    return {"impl": "reference", "metric": METRIC, "value": value, "unit": "positions/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": SB["T"] / value * 1e3,
+    units = {"sb_prefill": SB["T"], "sdb_draft": base["cores"] * SDB["gamma"], "tree_verify": 16}[wl]
+    cfg = {"sb_prefill": {"workload": "sb_prefill", "batch": SB["B"], "seq_len": SB["T"], "routes": SB["routes"]},
+           "sdb_draft": {"workload": "sdb_draft", "sequences": SDB["nseq"], "prefix": SDB["plen"],
+                         "gamma": SDB["gamma"]},
+           "tree_verify": {"workload": "tree_verify", "sequences": TREE["nseq"], "context": TREE["ctx"],
+                           "nodes": 16}}[wl]
+    cfg["sample"] = base["sample"]
+    return {"impl": "reference", "metric": METRIC, "value": value, "unit": base["unit"], "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": units / value * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded)", "config": {"workload": "sb_prefill", "batch": SB["B"], "seq_len": SB["T"],
-                                                     "routes": SB["routes"], "sample": "1 x 2048 positions per step"},
-            "cpu_baseline": dict(base, value=value),
-            "e2e": {"value": value, "unit": "positions/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "data": "synthetic (seeded)", "config": cfg, "cpu_baseline": dict(base, value=value),
+            "e2e": {"value": value, "unit": base["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+RUNNERS = {"sb_prefill": "run_ours", "sdb_draft": "run_sdb", "tree_verify": "run_tree", "scaled": "run_scaled"}
 
 
 def main(argv=None) -> int:
@@ -442,8 +947,9 @@ def main(argv=None) -> int:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("sb_prefill",), default="sb_prefill")
-    ap.add_argument("--batch", type=int, default=SB["B"], help="sequences per GPU (32 = BASELINE; smaller for ncu)")
+    ap.add_argument("--workload", choices=tuple(RUNNERS), default="sb_prefill")
+    ap.add_argument("--batch", type=int, default=SB["B"], help="sb_prefill sequences per GPU (32 = BASELINE; "
+                    "smaller for ncu)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args(argv)
     SB["B"] = int(args.batch)
@@ -456,10 +962,15 @@ def main(argv=None) -> int:
         if line is not None:
             print(json.dumps(line), flush=True)
         return 0
-    line = run_ours(args, rank, world, local)
+    line = globals()[RUNNERS[args.workload]](args, rank, world, local)
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_sb_sample()
+            if args.workload == "sb_prefill":
+                line["cpu_baseline"] = cpu_sb_sample()
+            elif args.workload == "sdb_draft":
+                line["cpu_baseline"] = cpu_sdb_sample()
+            elif args.workload == "tree_verify":
+                line["cpu_baseline"] = cpu_tree_sample()
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist

@@ -581,16 +581,23 @@ extern "C" int lng_drafter_draft_batch(lng_drafter* d, const int64_t* prefix, in
   LNG_REQUIRE(prefix && tokens_out, "NULL pointer");
   std::lock_guard<std::mutex> lk(d->mu);
   const int64_t R = d->R, P = plen + gamma;  // positions per sequence in the working buffers
+  // The drafts' code windows reach back n_max - 1 positions from the last prefix token, and the
+  // embed2 router reads only a position's own and previous token (SSM routers are rejected at
+  // create), so only the last `tail` prefix positions need codes; earlier rows of `codes` are never
+  // read.
+  int64_t n_max = 1;
+  for (int o = 0; o < d->n_orders; ++o) n_max = std::max<int64_t>(n_max, d->orders[o]);
+  const int64_t tail = std::min<int64_t>(plen, n_max);
   ReadoutBufs b;
   void* extra = nullptr;
-  const size_t tok_b = al256(size_t(nseq * (P + 1)) * 8), prev_b = al256(size_t(nseq * std::max<int64_t>(plen, 2)) * 8),
+  const size_t tok_b = al256(size_t(nseq * (P + 1)) * 8), prev_b = al256(size_t(nseq * std::max<int64_t>(2 * tail, 2)) * 8),
                code_b = al256(size_t(nseq * P * R));
-  const int64_t M = std::max<int64_t>(nseq * plen, nseq);
+  const int64_t M = nseq * tail;
   int st = drafter_ws(d, M, 1, &b, tok_b + prev_b + code_b, &extra);
   if (st) return st;
   unsigned char* ex = static_cast<unsigned char*>(extra);
   int64_t* toks = reinterpret_cast<int64_t*>(ex);  // [nseq, P + 1]: toks[s, 0] = -1, toks[s, 1 + p] = token p
-  int64_t* scratch_i = reinterpret_cast<int64_t*>(ex + tok_b);
+  int64_t* scratch_i = reinterpret_cast<int64_t*>(ex + tok_b);  // [2, nseq * tail]: current, previous tokens
   uint8_t* codes = ex + tok_b + prev_b;             // [nseq, P, R]
   cudaStream_t us = reinterpret_cast<cudaStream_t>(stream);
   cudaEvent_t ev;
@@ -601,16 +608,21 @@ extern "C" int lng_drafter_draft_batch(lng_drafter* d, const int64_t* prefix, in
   LNG_CUDA(cudaMemsetAsync(toks, 0xff, size_t(nseq * (P + 1)) * 8, d->stream));
   LNG_CUDA(cudaMemcpy2DAsync(toks + 1, size_t(P + 1) * 8, prefix, size_t(plen) * 8, size_t(plen) * 8, size_t(nseq),
                              cudaMemcpyDeviceToDevice, d->stream));
-  LNG_CUDA(cudaMemcpy2DAsync(scratch_i, size_t(plen) * 8, toks, size_t(P + 1) * 8, size_t(plen) * 8, size_t(nseq),
-                             cudaMemcpyDeviceToDevice, d->stream));
-  // prefix codes [nseq * plen, R] computed densely, then placed with stride P * R
-  uint8_t* dense = reinterpret_cast<uint8_t*>(b.u);  // reuse: nseq*plen*R bytes <= u's size when M = nseq*plen
-  const size_t dense_need = size_t(nseq * plen * R);
+  // tokens of the last `tail` prefix positions (dense [nseq, tail]) and their previous tokens
+  // (toks[s, p] is the token before position p, -1 at p = 0)
+  const int64_t p0 = plen - tail;
+  LNG_CUDA(cudaMemcpy2DAsync(scratch_i, size_t(tail) * 8, prefix + p0, size_t(plen) * 8, size_t(tail) * 8,
+                             size_t(nseq), cudaMemcpyDeviceToDevice, d->stream));
+  LNG_CUDA(cudaMemcpy2DAsync(scratch_i + nseq * tail, size_t(tail) * 8, toks + p0, size_t(P + 1) * 8,
+                             size_t(tail) * 8, size_t(nseq), cudaMemcpyDeviceToDevice, d->stream));
+  // their codes [nseq * tail, R] computed densely, then placed at rows p0 .. plen-1 with stride P * R
+  uint8_t* dense = reinterpret_cast<uint8_t*>(b.u);  // reuse: nseq*tail*R bytes <= u's size (M = nseq*tail)
+  const size_t dense_need = size_t(nseq * tail * R);
   const size_t u_bytes = size_t(M) * d->qh * d->Dt * dtype_size(d->act);
   LNG_REQUIRE(dense_need <= u_bytes, "internal: code staging buffer too small");
-  st = drafter_codes(d, prefix, scratch_i, nseq * plen, b.feat, dense, R);
+  st = drafter_codes(d, scratch_i, scratch_i + nseq * tail, nseq * tail, b.feat, dense, R);
   if (st) return st;
-  LNG_CUDA(cudaMemcpy2DAsync(codes, size_t(P * R), dense, size_t(plen * R), size_t(plen * R), size_t(nseq),
+  LNG_CUDA(cudaMemcpy2DAsync(codes + p0 * R, size_t(P * R), dense, size_t(tail * R), size_t(tail * R), size_t(nseq),
                              cudaMemcpyDeviceToDevice, d->stream));
   for (int64_t g = 0; g < gamma; ++g) {
     const int64_t tpos = plen - 1 + g;  // position of the current token in every sequence

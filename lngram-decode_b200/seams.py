@@ -120,6 +120,35 @@ def memory_step(m, cache: MemoryCache, h: Tensor, codes_new: Tensor, route_codes
     return out.view(B, n, d)
 
 
+_TREE_PLANS: dict = {}
+
+
+def _tree_plan(parent, L: int, B: int, max_len: int, hist: int, k: int, dil: int, device) -> dict:
+    """Index tensors of one tree shape after L cached positions (built once, kept on the device):
+    the n-gram window slots / validity of every node and the conv slots in the flat cache."""
+    key = (tuple(int(x) for x in parent), L, B, max_len, hist, k, dil, str(device))
+    plan = _TREE_PLANS.get(key)
+    if plan is not None:
+        return plan
+    n = len(parent)
+    h0 = min(L, hist)
+    gidx, gok = tree_slots(parent, h0, hist)                              # slots into [history(h0) | nodes]
+    lp = (k - 1) * dil
+    idx, ok = tree_slots(parent, L, lp)
+    taps = torch.arange(k) * dil                                          # window columns the taps read
+    tslot = torch.where(ok[:, taps], idx[:, taps], torch.full_like(idx[:, taps], -1)).to(device)  # [n, k]
+    base = (torch.arange(B, device=device) * max_len)[:, None, None]
+    slot = torch.where(tslot[None] >= 0, base + tslot[None], torch.full_like(tslot[None], -1))
+    new_slot = (torch.arange(B, device=device) * max_len)[:, None] + L + torch.arange(n, device=device)[None]
+    plan = {"h0": h0, "gidx": gidx.to(device), "gok": gok.to(device)[None, :, :, None].to(torch.uint8),
+            "seg": gok.to(torch.int32)[None].expand(B, n, hist + 1).reshape(B * n, hist + 1).contiguous().to(device),
+            "slot": slot.reshape(B * n, k).contiguous(), "new_slot": new_slot.reshape(-1).contiguous()}
+    if len(_TREE_PLANS) > 64:
+        _TREE_PLANS.clear()
+    _TREE_PLANS[key] = plan
+    return plan
+
+
 @torch.no_grad()
 def tree_memory_block(m, cache: MemoryCache, h: Tensor, codes: Tensor, parent) -> Tensor:
     """``drafting/tree.py:178-195``: memory output [B, n, d] of tree nodes ``codes`` [B, n, R] placed
@@ -128,21 +157,17 @@ def tree_memory_block(m, cache: MemoryCache, h: Tensor, codes: Tensor, parent) -
     L = cache.length
     if L + n > cache.max_len:
         raise ValueError(f"cache full: {L} + {n} > {cache.max_len}")
+    if len(parent) != n:
+        raise ValueError(f"parent has {len(parent)} nodes, h has {n}")
     hist = m.route_history_length
-    codes = codes.to(torch.uint8)
-    ctx, valid = tree_ngram_codes(parent, codes, cache.codes[:, max(0, L - hist):L], hist)
-    W = hist + 1
-    seg = valid.to(torch.int32)[None].expand(B, n, W).reshape(B * n, W).contiguous()
-    mixed = _readout(m, h, m.tables_desc(), ctx.reshape(B * n, W, -1).contiguous(), _lib.U8, B * n, 0, W, seg, 0)
-    cache.codes[:, L:L + n] = codes
     k, dil = m.short_conv.kernel_size, m.short_conv.dilation
-    lp = (k - 1) * dil
-    idx, ok = tree_slots(parent, L, lp)
-    dev = h.device
-    taps = torch.arange(k) * dil                                          # window columns the taps read
-    tslot = torch.where(ok[:, taps], idx[:, taps], torch.full_like(idx[:, taps], -1)).to(dev)  # [n, k]
-    base = (torch.arange(B, device=dev) * cache.max_len)[:, None, None]
-    slot = torch.where(tslot[None] >= 0, base + tslot[None], torch.full_like(tslot[None], -1))
-    new_slot = ((torch.arange(B, device=dev) * cache.max_len)[:, None] + L + torch.arange(n, device=dev)[None])
-    out = _conv(m, mixed, cache, new_slot.reshape(-1).contiguous(), slot.reshape(B * n, k).contiguous())
+    plan = _tree_plan(parent, L, B, cache.max_len, hist, k, dil, h.device)
+    codes = codes.to(torch.uint8)
+    allc = torch.cat((cache.codes[:, L - plan["h0"]:L], codes), 1)
+    ctx = allc[:, plan["gidx"]] * plan["gok"]                            # [B, n, hist + 1, R]
+    W = hist + 1
+    mixed = _readout(m, h, m.tables_desc(), ctx.reshape(B * n, W, -1).contiguous(), _lib.U8, B * n, 0, W,
+                     plan["seg"], 0)
+    cache.codes[:, L:L + n] = codes
+    out = _conv(m, mixed, cache, plan["new_slot"], plan["slot"])
     return out.view(B, n, d)

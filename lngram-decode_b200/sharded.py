@@ -62,20 +62,37 @@ def reduce_scatter_rows(t: Tensor, group=None) -> Tensor:
 class RouteShardedMemory:
     """One rank's share of a route-sharded ``LngramMemory``."""
 
-    def __init__(self, full: LngramMemory, rank: int, world: int, group=None):
+    def __init__(self, full: LngramMemory, rank: int, world: int, group=None, routes_total: int | None = None):
+        """``full`` holds every route (its rows of this rank are sliced out), or -- with
+        ``routes_total`` -- only this rank's block of routes already (its sink logit must then be the
+        whole layer's, log(routes_total (1 - mass) / mass))."""
         m = full.module
         self.rank, self.world, self.group = int(rank), int(world), group
-        self.bounds = route_bounds(m.num_routes, world)
+        self.R_total = int(routes_total) if routes_total is not None else m.num_routes
+        self.bounds = route_bounds(self.R_total, world)
         self.r0, self.r1 = self.bounds[rank]
         self.full = full
-        self.R_total = m.num_routes
         dev = m.readout_q_proj.weight.device
+        pre_sliced = routes_total is not None
+        if pre_sliced and m.num_routes != self.r1 - self.r0:
+            raise ValueError(f"the local module holds {m.num_routes} routes, rank {rank} owns {self.r1 - self.r0}")
         # the rank's rows of every order table (route-major layout: contiguous) and of the router
         self.tables = {}
         for n in m.ngrams:
             span = m.alphabet_size ** n
-            self.tables[n] = m.tables[f"ngram_{n}"].weight.detach()[self.r0 * span:self.r1 * span].contiguous()
-        self.router_w = full.router.weight.detach()[self.r0 * full.bits:self.r1 * full.bits].float().contiguous()
+            w = m.tables[f"ngram_{n}"].weight.detach()
+            self.tables[n] = w if pre_sliced else w[self.r0 * span:self.r1 * span].contiguous()
+        rw = full.router.weight.detach()
+        self.router_w = (rw if pre_sliced else rw[self.r0 * full.bits:self.r1 * full.bits]).float().contiguous()
+        self.router_split = None
+        if full.bits <= 6 and self.router_w.shape[1] % 64 == 0:
+            self.router_split = torch.empty(self.router_w.shape[0], 3 * self.router_w.shape[1], device=dev,
+                                            dtype=torch.bfloat16)
+            check(_lib.library().lng_router_prepare(ptr(self.router_w), self.router_w.shape[0], self.router_w.shape[1],
+                                                    ptr(self.router_split), stream_ptr()), "router split")
+        # b0 = log(R (1 - mass) / mass) of the whole layer (the local module's own is of its R_local)
+        mass = m.sink_initial_active_mass
+        self.sink_logit = math.log(self.R_total * (1.0 - mass) / mass)
         self.ss = {}
         self.dev = dev
 
@@ -145,8 +162,13 @@ class RouteShardedMemory:
         h = h.to(act).contiguous()
         x = router_x.contiguous() if router_x.dtype in (torch.float32, torch.bfloat16) else router_x.float()
         codes = torch.empty(B, T, Rl, device=h.device, dtype=torch.uint8)
-        check(lib.lng_route_codes(ptr(x), _lib.dtype_code(x.dtype), M, x.shape[-1], x.shape[-1], ptr(self.router_w),
-                                  Rl, m.bits_per_route, ptr(codes), _lib.U8, None, s), "route codes")
+        if x.dtype == torch.bfloat16 and self.router_split is not None:
+            check(lib.lng_route_codes_split(ptr(x), M, x.shape[-1], x.shape[-1], ptr(self.router_split), Rl,
+                                            m.bits_per_route, ptr(codes), s), "route codes (tensor cores)")
+        else:
+            check(lib.lng_route_codes(ptr(x), _lib.dtype_code(x.dtype), M, x.shape[-1], x.shape[-1],
+                                      ptr(self.router_w), Rl, m.bits_per_route, ptr(codes), _lib.U8, None, s),
+                  "route codes")
         f = m.folded()
         Dt, QH = m.route_token_dim, m.readout_num_heads
         rs = torch.empty(M, device=h.device, dtype=torch.float32)
@@ -158,6 +180,6 @@ class RouteShardedMemory:
         u = torch.empty(M, QH, Dt, device=h.device, dtype=torch.float32)
         # sink: b0 = log(R_total (1 - mass) / mass) of the whole layer, seeded on rank 0 only
         check(lib.lng_route_attend(self._tables_desc(), ptr(codes), _lib.U8, B, T, 0, None, None, None, 0, 0, Rl, QH,
-                                   m.eps, m.readout_sink_logit, ptr(qa), ptr(rs), ptr(u), _lib.F32,
+                                   m.eps, self.sink_logit, ptr(qa), ptr(rs), ptr(u), _lib.F32,
                                    1 if self.rank == 0 else 2, ptr(mloc), ptr(lloc), s), "route_attend partial")
         return mloc, lloc, u

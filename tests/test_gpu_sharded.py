@@ -63,6 +63,47 @@ def test_emulated_shards_sb_shape_bf16(lngram, golden):
     assert_bf16_close(got, g["output_wrapper"], what="8 emulated shards vs reference")
 
 
+def local_shard(lngram, case: str, rank: int, world: int, dtype=torch.float32):
+    """A memory holding only the routes of ``rank`` (tables and router rows sliced from the case's
+    parameters, readout weights whole), wrapped as a pre-sliced route shard."""
+    c = cases.MEMORY_CASES[case]
+    R = c["routes"]
+    r0, r1 = lngram.sharded.route_bounds(R, world)[rank]
+    p = cases.memory_params(case)
+    state = {}
+    for k, v in p.items():
+        if k.startswith("tables.ngram_"):
+            span = (1 << c["bits"]) ** int(k.split("_")[1].split(".")[0])
+            v = v[r0 * span:r1 * span]
+        elif k == "router.weight":
+            v = v[r0 * c["bits"]:r1 * c["bits"]]
+        state[k if k == "router.weight" else "module." + k] = torch.from_numpy(np.ascontiguousarray(v))
+    mem = lngram.LngramMemory(c["d"], {"routes": r1 - r0, "mem_dim": c["mem_dim"], "kv_heads": c["kv_heads"],
+                                       "q_heads": c["q_heads"], "head_dim": c["head_dim"], "ngrams": list(c["ngrams"]),
+                                       "bits_per_route": c["bits"]}, norm_eps=1e-5, device=DEV, dtype=dtype).eval()
+    mem.load_state_dict(state, strict=True)
+    return lngram.RouteShardedMemory(mem, rank, world, routes_total=R)
+
+
+@pytest.mark.parametrize("case,world", [("tiny_multi", 3), ("scaled_slice", 2)])
+def test_pre_sliced_shards_equal_full_forward(lngram, case, world):
+    mem = gpu_memory(lngram, case)
+    inp = cases.memory_inputs(case)
+    h = torch.from_numpy(inp["h"]).to(DEV)
+    x = torch.from_numpy(inp["x"]).to(DEV)
+    shards = [local_shard(lngram, case, r, world) for r in range(world)]
+    with torch.no_grad():
+        want = mem(h, x).cpu().numpy()
+        parts = [s.partial(h, x) for s in shards]
+        mg = parts[0][0].clone()
+        for q in parts[1:]:
+            mg = torch.maximum(mg, q[0])
+        total = sum(s.pack(q[0], mg, q[1], q[2]) for s, q in zip(shards, parts))
+        B, T = h.shape[:2]
+        got = shards[0].finish(total.view(B * T, -1), B, T).cpu().numpy()
+    assert_fp32_close(got, want, what=f"{world} pre-sliced route shards ({case})")
+
+
 def _free_port() -> int:
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))

@@ -12,6 +12,7 @@
 #include "attend.cuh"
 #include "gemm_simt.cuh"
 #include "gemm_tc.cuh"
+#include "logits_tc.cuh"
 #include "lookup.cuh"
 #include "router.cuh"
 #include "rowops.cuh"
@@ -145,6 +146,21 @@ extern "C" int lng_route_codes(const void* x, int32_t x_dtype, int64_t n, int64_
                                    static_cast<uint8_t*>(codes), S(stream));
     if (st != LNG_ERR_UNSUPPORTED) return st;
   }
+  if (ceil_div(n, RT_ROWS) * ceil_div(routes, RT_ROUTES) < 2 * 148 && ceil_div(n, RS_ROWS) < 65536) {
+    // few row tiles: split the features over a cluster instead
+    dim3 grid(unsigned(ceil_div(routes, RS_RPC) * RS_SPLIT), unsigned(ceil_div(n, RS_ROWS)));
+#define LNG_ROUTER_SMALL(XT, CT)                                                                             \
+  router_small_kernel<XT, CT><<<grid, 256, 0, S(stream)>>>(static_cast<const XT*>(x), n, in_dim, x_stride, weight, \
+                                                           routes, bits, static_cast<CT*>(codes), logits)
+    if (x_dtype == LNG_F32) {
+      if (codes_dtype == LNG_U8) LNG_ROUTER_SMALL(float, uint8_t); else LNG_ROUTER_SMALL(float, int32_t);
+    } else {
+      if (codes_dtype == LNG_U8) LNG_ROUTER_SMALL(__nv_bfloat16, uint8_t); else LNG_ROUTER_SMALL(__nv_bfloat16, int32_t);
+    }
+#undef LNG_ROUTER_SMALL
+    LNG_LAUNCHED("router_small_kernel");
+    return LNG_OK;
+  }
   dim3 grid(unsigned(ceil_div(n, RT_ROWS)), unsigned(ceil_div(routes, RT_ROUTES)));
 #define LNG_ROUTER(XT, CT)                                                                                   \
   router_simt_kernel<XT, CT><<<grid, 256, 0, S(stream)>>>(static_cast<const XT*>(x), n, in_dim, x_stride, weight, \
@@ -189,18 +205,18 @@ extern "C" int lng_embed2_features(const int64_t* cur, const int64_t* prev, int6
   LNG_REQUIRE(n >= 0 && vocab > 0 && d > 0, "bad shape");
   if (n == 0) return LNG_OK;
   LNG_REQUIRE(cur && embedding && prev_w && cur_w && start && out, "NULL pointer");
-  const int g = int(ceil_div(n * 32, 256));
+  const int g = int(n < (int64_t(1) << 20) ? n : (int64_t(1) << 20));
   switch (e_dtype) {
     case LNG_F32:
-      embed2_features_kernel<float><<<g, 256, 0, S(stream)>>>(cur, prev, n, static_cast<const float*>(embedding), vocab,
+      embed2_features_kernel<float><<<g, 128, 0, S(stream)>>>(cur, prev, n, static_cast<const float*>(embedding), vocab,
                                                                d, prev_w, cur_w, start, eps, out);
       break;
     case LNG_BF16:
-      embed2_features_kernel<__nv_bfloat16><<<g, 256, 0, S(stream)>>>(
+      embed2_features_kernel<__nv_bfloat16><<<g, 128, 0, S(stream)>>>(
           cur, prev, n, static_cast<const __nv_bfloat16*>(embedding), vocab, d, prev_w, cur_w, start, eps, out);
       break;
     case LNG_F16:
-      embed2_features_kernel<__half><<<g, 256, 0, S(stream)>>>(cur, prev, n, static_cast<const __half*>(embedding),
+      embed2_features_kernel<__half><<<g, 128, 0, S(stream)>>>(cur, prev, n, static_cast<const __half*>(embedding),
                                                                 vocab, d, prev_w, cur_w, start, eps, out);
       break;
     default:
@@ -809,6 +825,55 @@ extern "C" size_t lng_logits_topk_scratch_bytes(int64_t n, int64_t vocab, int32_
   return size_t(n) * nch * k * (sizeof(float) + sizeof(int64_t)) + 256;
 }
 
+namespace {
+// Per-tile candidates [n, ceil(vocab / 256), k] of h . E^T: the tcgen05 kernel for a bf16
+// vocabulary matrix whose shapes meet the TMA rules (d % 64 == 0, 16-byte aligned operands),
+// the CUDA-core kernel otherwise.
+int logits_chunks(const float* h, int64_t n, int64_t d, const void* embedding, int32_t e_dtype, int64_t vocab,
+                  int32_t k, float* cand_v, int64_t* cand_i, float* logits, cudaStream_t stream) {
+  const int64_t nch = ceil_div(vocab, TK_VC);
+  const bool tc = e_dtype == LNG_BF16 && d % TC_BK == 0 && (reinterpret_cast<uintptr_t>(embedding) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(h) & 15) == 0 && vocab < (int64_t(1) << 31);
+  if (tc) {
+    const int bn = n <= 32 ? 32 : n <= 64 ? 64 : 128;
+    CUtensorMap te, th;
+    int st = make_tmap_bf16(&te, embedding, vocab, d, d, LT_BM);
+    if (st) return st;
+    st = make_tmap_f32(&th, h, n, d, d, bn);
+    if (st) return st;
+    dim3 grid(unsigned(ceil_div(n, bn)), unsigned(nch));
+#define LNG_LT(BN)                                                                                          \
+  do {                                                                                                      \
+    auto kern = logits_tc_topk_kernel<BN>;                                                                  \
+    LNG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(LtCfg<BN>::SMEM))); \
+    kern<<<grid, 128, LtCfg<BN>::SMEM, stream>>>(te, th, n, d, vocab, k, cand_v, cand_i, logits);             \
+  } while (0)
+    if (bn == 32) LNG_LT(32);
+    else if (bn == 64) LNG_LT(64);
+    else LNG_LT(128);
+#undef LNG_LT
+    LNG_LAUNCHED("logits_tc_topk_kernel");
+    return LNG_OK;
+  }
+  const size_t smem = sizeof(float) * (size_t(TK_ROWS) * d + size_t(TK_ROWS) * TK_VC);
+  LNG_REQUIRE(smem <= 227 * 1024, "hidden size too large for the top-k kernel");
+  dim3 grid(unsigned(nch), unsigned(ceil_div(n, TK_ROWS)));
+#define LNG_TK(ET)                                                                                         \
+  do {                                                                                                     \
+    auto kern = logits_chunk_topk_kernel<ET>;                                                              \
+    LNG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));          \
+    kern<<<grid, 256, smem, stream>>>(h, n, d, static_cast<const ET*>(embedding), vocab, k, cand_v, cand_i, logits); \
+  } while (0)
+  if (e_dtype == LNG_F32) LNG_TK(float);
+  else if (e_dtype == LNG_BF16) LNG_TK(__nv_bfloat16);
+  else if (e_dtype == LNG_F16) LNG_TK(__half);
+  else return fail(LNG_ERR_ARGUMENT, "embedding dtype must be float");
+#undef LNG_TK
+  LNG_LAUNCHED("logits_chunk_topk_kernel");
+  return LNG_OK;
+}
+}  // namespace
+
 extern "C" int lng_logits_topk(const float* h, int64_t n, int64_t d, const void* embedding, int32_t e_dtype,
                                int64_t vocab, int32_t k, int64_t* ids, float* vals, float* logits, void* scratch,
                                size_t scratch_bytes, lng_stream_t stream) {
@@ -819,24 +884,11 @@ extern "C" int lng_logits_topk(const float* h, int64_t n, int64_t d, const void*
   const int64_t nch = ceil_div(vocab, TK_VC);
   const size_t need = lng_logits_topk_scratch_bytes(n, vocab, k);
   LNG_REQUIRE(scratch && scratch_bytes >= need, "scratch too small (see lng_logits_topk_scratch_bytes)");
-  const size_t smem = sizeof(float) * (size_t(TK_ROWS) * d + size_t(TK_ROWS) * TK_VC);
-  LNG_REQUIRE(smem <= 227 * 1024, "hidden size too large for the top-k kernel");
   uintptr_t base = (reinterpret_cast<uintptr_t>(scratch) + 15) & ~uintptr_t(15);
   int64_t* cand_i = reinterpret_cast<int64_t*>(base);
   float* cand_v = reinterpret_cast<float*>(cand_i + n * nch * k);
-  dim3 grid(unsigned(nch), unsigned(ceil_div(n, TK_ROWS)));
-#define LNG_TK(ET)                                                                                         \
-  do {                                                                                                     \
-    auto kern = logits_chunk_topk_kernel<ET>;                                                              \
-    LNG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));          \
-    kern<<<grid, 256, smem, S(stream)>>>(h, n, d, static_cast<const ET*>(embedding), vocab, k, cand_v, cand_i, logits); \
-  } while (0)
-  if (e_dtype == LNG_F32) LNG_TK(float);
-  else if (e_dtype == LNG_BF16) LNG_TK(__nv_bfloat16);
-  else if (e_dtype == LNG_F16) LNG_TK(__half);
-  else return fail(LNG_ERR_ARGUMENT, "embedding dtype must be float");
-#undef LNG_TK
-  LNG_LAUNCHED("logits_chunk_topk_kernel");
+  int st = logits_chunks(h, n, d, embedding, e_dtype, vocab, k, cand_v, cand_i, logits, S(stream));
+  if (st) return st;
   topk_merge_kernel<<<unsigned(ceil_div(n * 32, 256)), 256, 0, S(stream)>>>(cand_v, cand_i, n, nch, k, ids, vals);
   LNG_LAUNCHED("topk_merge_kernel");
   return LNG_OK;
@@ -886,23 +938,10 @@ extern "C" int lng_logits_topk_static(const float* h, int64_t n, int64_t d, cons
     base = g_topk_static_base[dev];
   }
   const int64_t nch = ceil_div(vocab, TK_VC);
-  const size_t smem = sizeof(float) * (size_t(TK_ROWS) * d + size_t(TK_ROWS) * TK_VC);
-  LNG_REQUIRE(smem <= 227 * 1024, "hidden size too large for the top-k kernel");
   int64_t* cand_i = static_cast<int64_t*>(base);  // 256-byte aligned: no extra alignment step needed
   float* cand_v = reinterpret_cast<float*>(cand_i + n * nch * k);
-  dim3 grid(unsigned(nch), unsigned(ceil_div(n, TK_ROWS)));
-#define LNG_TKS(ET)                                                                                        \
-  do {                                                                                                     \
-    auto kern = logits_chunk_topk_kernel<ET>;                                                              \
-    LNG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));          \
-    kern<<<grid, 256, smem, S(stream)>>>(h, n, d, static_cast<const ET*>(embedding), vocab, k, cand_v, cand_i, logits); \
-  } while (0)
-  if (e_dtype == LNG_F32) LNG_TKS(float);
-  else if (e_dtype == LNG_BF16) LNG_TKS(__nv_bfloat16);
-  else if (e_dtype == LNG_F16) LNG_TKS(__half);
-  else return fail(LNG_ERR_ARGUMENT, "embedding dtype must be float");
-#undef LNG_TKS
-  LNG_LAUNCHED("logits_chunk_topk_kernel (static scratch)");
+  int st = logits_chunks(h, n, d, embedding, e_dtype, vocab, k, cand_v, cand_i, logits, S(stream));
+  if (st) return st;
   topk_merge_kernel<<<unsigned(ceil_div(n * 32, 256)), 256, 0, S(stream)>>>(cand_v, cand_i, n, nch, k, ids, vals);
   LNG_LAUNCHED("topk_merge_kernel (static scratch)");
   return LNG_OK;

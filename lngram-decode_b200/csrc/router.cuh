@@ -4,9 +4,13 @@
 // ffnmem/memory/lngram_v2.py:74-89, :1012-1017 (bit j of route r = logit[r*bits + j] > 0).
 #pragma once
 
+#include <cooperative_groups.h>
+
 #include "address.cuh"
 
 namespace lng {
+
+namespace cg = cooperative_groups;
 
 template <typename CodeOutT>
 __global__ void quantize_logits_kernel(const float* __restrict__ logits, int64_t n, int64_t routes, int bits,
@@ -90,36 +94,129 @@ __global__ void __launch_bounds__(256) router_simt_kernel(const XT* __restrict__
   }
 }
 
-// embed2 router features (ffnmem/memory/router.py:50-69): one warp per item.
-template <typename ET>
-__global__ void embed2_features_kernel(const int64_t* __restrict__ cur, const int64_t* __restrict__ prev, int64_t n,
-                                       const ET* __restrict__ E, int64_t vocab, int64_t d,
-                                       const float* __restrict__ prev_w, const float* __restrict__ cur_w,
-                                       const float* __restrict__ start, float eps, float* __restrict__ out) {
-  const int lane = threadIdx.x & 31;
-  const int64_t warp = (blockIdx.x * int64_t(blockDim.x) + threadIdx.x) >> 5;
-  if (warp >= n) return;
-  const int64_t tc = cur[warp];
-  const int64_t tp = prev ? prev[warp] : -1;
-  if (tc < 0 || tc >= vocab || tp >= vocab) {
-    if (lane == 0) atomicCAS(&g_error_word, 0u, (unsigned int)DEV_ERR_TOKEN_RANGE);
-    return;
+// Small-batch CUDA-core router: a cluster of RS_SPLIT CTAs shares one block of RS_RPC routes (all
+// `bits` logits of each), each CTA summing 1/RS_SPLIT of the input features for RS_ROWS rows; rank 0
+// adds the partial logits of the ranks in rank order through distributed shared memory
+// (deterministic) and packs the codes.  For row counts that leave router_simt_kernel's row tiles
+// too few CTAs to fill the GPU (drafting: one row per sequence).
+constexpr int RS_SPLIT = 8, RS_RPC = 4, RS_ROWS = 64, RS_KC = 64;
+
+template <typename XT, typename CodeOutT>
+__global__ void __cluster_dims__(RS_SPLIT, 1, 1) __launch_bounds__(256)
+    router_small_kernel(const XT* __restrict__ x, int64_t n, int64_t in_dim, int64_t x_stride,
+                        const float* __restrict__ w, int64_t routes, int bits, CodeOutT* __restrict__ codes,
+                        float* __restrict__ logits) {
+  __shared__ float xs[RS_ROWS][RS_KC + 1];
+  __shared__ float ws[RS_RPC * RT_MAXBITS][RS_KC + 1];
+  __shared__ float part[RS_ROWS * RS_RPC * RT_MAXBITS];
+  cg::cluster_group cluster = cg::this_cluster();
+  const unsigned rank = cluster.block_rank();
+  const int r = threadIdx.x >> 2, g = threadIdx.x & 3;  // row within the tile, route within the block
+  const int64_t rb = blockIdx.x / RS_SPLIT;              // route block
+  const int64_t row0 = int64_t(blockIdx.y) * RS_ROWS;
+  const int ncol = RS_RPC * bits;
+  const int64_t col0 = rb * RS_RPC * bits;               // first logit column of the block
+  const int64_t C = routes * bits;
+  const int64_t ks = (in_dim + RS_SPLIT - 1) / RS_SPLIT;
+  const int64_t kbeg = int64_t(rank) * ks, kend = kbeg + ks < in_dim ? kbeg + ks : in_dim;
+  float acc[RT_MAXBITS];
+#pragma unroll
+  for (int j = 0; j < RT_MAXBITS; ++j) acc[j] = 0.f;
+  for (int64_t k0 = kbeg; k0 < kend; k0 += RS_KC) {
+    for (int e = threadIdx.x; e < RS_ROWS * RS_KC; e += blockDim.x) {
+      const int rr = e / RS_KC, kk = e % RS_KC;
+      const int64_t gr = row0 + rr, gk = k0 + kk;
+      xs[rr][kk] = (gr < n && gk < kend) ? to_f32(x[gr * x_stride + gk]) : 0.f;
+    }
+    for (int e = threadIdx.x; e < ncol * RS_KC; e += blockDim.x) {
+      const int c = e / RS_KC, kk = e % RS_KC;
+      const int64_t gc = col0 + c, gk = k0 + kk;
+      ws[c][kk] = (gc < C && gk < kend) ? w[gc * in_dim + gk] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int kk = 0; kk < RS_KC; ++kk) {
+      const float a = xs[r][kk];
+#pragma unroll
+      for (int j = 0; j < RT_MAXBITS; ++j)
+        if (j < bits) acc[j] = fmaf(a, ws[g * bits + j][kk], acc[j]);
+    }
+    __syncthreads();
   }
-  float* o = out + warp * 2 * d;
-  for (int part = 0; part < 2; ++part) {
-    const float* wv = part == 0 ? prev_w : cur_w;
-    const int64_t tok = part == 0 ? tp : tc;
-    float ss = 0.f;
-    for (int64_t j = lane; j < d; j += 32) {
-      const float v = tok >= 0 ? to_f32(E[tok * d + j]) : start[j];
-      ss += v * v;
+#pragma unroll
+  for (int j = 0; j < RT_MAXBITS; ++j)
+    if (j < bits) part[(r * RS_RPC + g) * RT_MAXBITS + j] = acc[j];
+  cluster.sync();
+  if (rank == 0) {
+    float sum[RT_MAXBITS];
+#pragma unroll
+    for (int j = 0; j < RT_MAXBITS; ++j) sum[j] = 0.f;
+    for (unsigned q = 0; q < RS_SPLIT; ++q) {
+      const float* pq = cluster.map_shared_rank(part, q);
+#pragma unroll
+      for (int j = 0; j < RT_MAXBITS; ++j)
+        if (j < bits) sum[j] += pq[(r * RS_RPC + g) * RT_MAXBITS + j];
     }
-    ss = warp_sum(ss);
-    const float rs = rsqrtf(ss / float(d) + eps);
-    for (int64_t j = lane; j < d; j += 32) {
-      const float v = tok >= 0 ? to_f32(E[tok * d + j]) : start[j];
-      o[part * d + j] = v * rs * wv[j];
+    const int64_t gr = row0 + r, route = rb * RS_RPC + g;
+    if (gr < n && route < routes) {
+      int v = 0;
+#pragma unroll
+      for (int j = 0; j < RT_MAXBITS; ++j) {
+        if (j < bits) {
+          v |= (sum[j] > 0.f ? 1 : 0) << j;
+          if (logits) logits[gr * C + route * bits + j] = sum[j];
+        }
+      }
+      codes[gr * routes + route] = static_cast<CodeOutT>(v);
     }
+  }
+  cluster.sync();  // the other ranks' partials stay resident until rank 0 has read them
+}
+
+// embed2 router features (ffnmem/memory/router.py:50-69): one 128-thread CTA per item, the
+// previous and current token rows each RMS-normalised with their own weight.
+template <typename ET>
+__global__ void __launch_bounds__(128) embed2_features_kernel(const int64_t* __restrict__ cur,
+                                                              const int64_t* __restrict__ prev, int64_t n,
+                                                              const ET* __restrict__ E, int64_t vocab, int64_t d,
+                                                              const float* __restrict__ prev_w,
+                                                              const float* __restrict__ cur_w,
+                                                              const float* __restrict__ start, float eps,
+                                                              float* __restrict__ out) {
+  __shared__ float red[2][4];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int64_t item = blockIdx.x; item < n; item += gridDim.x) {
+    const int64_t tc = cur[item];
+    const int64_t tp = prev ? prev[item] : -1;
+    if (tc < 0 || tc >= vocab || tp >= vocab) {
+      if (threadIdx.x == 0) atomicCAS(&g_error_word, 0u, (unsigned int)DEV_ERR_TOKEN_RANGE);
+      continue;
+    }
+    float* o = out + item * 2 * d;
+    float ss[2] = {0.f, 0.f};
+#pragma unroll
+    for (int part = 0; part < 2; ++part) {
+      const int64_t tok = part == 0 ? tp : tc;
+      for (int64_t j = threadIdx.x; j < d; j += blockDim.x) {
+        const float v = tok >= 0 ? to_f32(E[tok * d + j]) : start[j];
+        ss[part] += v * v;
+      }
+      ss[part] = warp_sum(ss[part]);
+      if (lane == 0) red[part][warp] = ss[part];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int part = 0; part < 2; ++part) {
+      const float tot = red[part][0] + red[part][1] + red[part][2] + red[part][3];
+      const float rs = rsqrtf(tot / float(d) + eps);
+      const float* wv = part == 0 ? prev_w : cur_w;
+      const int64_t tok = part == 0 ? tp : tc;
+      for (int64_t j = threadIdx.x; j < d; j += blockDim.x) {
+        const float v = tok >= 0 ? to_f32(E[tok * d + j]) : start[j];
+        o[part * d + j] = v * rs * wv[j];
+      }
+    }
+    __syncthreads();
   }
 }
 

@@ -35,7 +35,8 @@ def run_topk(lngram, h, E, k, want_logits=False):
     return ids, vals, logits
 
 
-@pytest.mark.parametrize("n,d,V,k", [(1, 64, 256, 3), (7, 128, 1000, 8), (64, 1024, 32000, 3), (65, 1024, 32000, 1)])
+@pytest.mark.parametrize("n,d,V,k", [(1, 64, 256, 3), (7, 128, 1000, 8), (64, 1024, 32000, 3), (65, 1024, 32000, 1),
+                                     (33, 192, 515, 2), (300, 256, 3000, 5)])
 @pytest.mark.parametrize("edt", [torch.float32, torch.bfloat16])
 def test_logits_topk_matches_fp32_reference(lngram, n, d, V, k, edt):
     g = torch.Generator(device=DEV).manual_seed(n * 31 + V)
@@ -52,14 +53,16 @@ def test_logits_topk_matches_fp32_reference(lngram, n, d, V, k, edt):
     assert (ids == want_ids).float().mean().item() > 0.99
 
 
-def test_logits_topk_ties_prefer_lower_id(lngram):
-    h = torch.ones(2, 32, device=DEV)
-    E = torch.zeros(600, 32, device=DEV)
+@pytest.mark.parametrize("d,edt", [(32, torch.float32), (64, torch.bfloat16)])
+def test_logits_topk_ties_prefer_lower_id(lngram, d, edt):
+    """Exact ties (CUDA-core kernel for fp32, tensor-core kernel for a bf16 vocabulary)."""
+    h = torch.ones(2, d, device=DEV)
+    E = torch.zeros(600, d, device=DEV, dtype=edt)
     E[[5, 17, 300, 599]] = 1.0          # four exact ties at the top
     E[[2, 400]] = 0.5
     ids, vals, _ = run_topk(lngram, h, E, 6)
     assert ids[0].tolist() == [5, 17, 300, 599, 2, 400]
-    assert vals[0, :4].tolist() == [32.0] * 4
+    assert vals[0, :4].tolist() == [float(d)] * 4
     # fewer than k candidates: -1 / -inf padding, as the reference pads
     ids, vals, _ = run_topk(lngram, h, E[:3], 5)
     assert ids[0].tolist() == [2, 0, 1, -1, -1]

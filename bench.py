@@ -485,7 +485,7 @@ def run_sdb(args, rank, world, local) -> dict:
         ids = torch.empty(nseq, 1, device=dev, dtype=torch.int64)
         vals = torch.empty(nseq, 1, device=dev, dtype=torch.float32)
         L = lib.library()
-        sb = L.lng_logits_topk_scratch_bytes(nseq, V, 1)
+        sb = L.lng_logits_topk_scratch_bytes(nseq, d, V, 1)
         scratch = torch.empty(sb, device=dev, dtype=torch.uint8)
         s = lib.stream_ptr()
         lk_ms = kernel_ms(lambda: lib.check(L.lng_logits_topk(hq.data_ptr(), nseq, d, E.data_ptr(), lib.BF16, V, 1,

@@ -261,18 +261,22 @@ int lng_attend_unpack(const float* pack, int64_t M, int32_t num_heads, int32_t h
 /* Top-k over V logits h[i] . E[v] for n rows without materialising the logits: ids i64 [n, k]
  * (ties -> lower id), vals fp32 [n, k]; logits (fp32 [n, V]) optional.  h fp32 [n, d];
  * E [V, d] f32/bf16/f16.  Replaces F.linear(h, E) + argmax / top-k
- * (ffnmem/memory/draft.py:88-91, drafting/cpu/drafter.cpp:537-556).  k <= 8. */
+ * (ffnmem/memory/draft.py:88-91, drafting/cpu/drafter.cpp:537-556).  k <= 8.  A bf16 E with
+ * d % 64 == 0 runs on the tensor cores with fp32-accurate logits (h split into three bf16 parts
+ * inside `scratch`); other shapes on the CUDA cores.  scratch: lng_logits_topk_scratch_bytes. */
 int lng_logits_topk(const float* h, int64_t n, int64_t d, const void* embedding, int32_t e_dtype, int64_t vocab,
                     int32_t k, int64_t* ids, float* vals, float* logits, void* scratch, size_t scratch_bytes,
                     lng_stream_t stream);
-size_t lng_logits_topk_scratch_bytes(int64_t n, int64_t vocab, int32_t k);
+size_t lng_logits_topk_scratch_bytes(int64_t n, int64_t d, int64_t vocab, int32_t k);
 
 /* lng_logits_topk without any allocation, for callers that cannot allocate device memory where they
  * draft (inside a captured or replayed CUDA graph, or under an allocator that only serves its own
- * pools).  No counterpart in the reference: it exists for those callers.  The candidate scratch is
- * a 4 MiB array inside the library, held by every GPU that loads the library until the process
- * exits; sizes with n * ceil(vocab / 256) * k * 12 + 256 > 4 MiB are rejected (LNG_ERR_ARGUMENT)
- * -- e.g. k = 3 at vocab 32000 allows n <= 932.  The first call on a device looks up the array's
+ * pools).  No counterpart in the reference: it exists for those callers.  The scratch is a 4 MiB
+ * array inside the library, held by every GPU that loads the library until the process exits;
+ * sizes with n * ceil(vocab / 256) * k * 12 (candidates, rounded up to 256) + 256 -- plus
+ * n * d * 6 (the split rows) when the tensor-core path applies -- above 4 MiB are rejected
+ * (LNG_ERR_ARGUMENT): e.g. k = 3 at vocab 32000 allows n <= 932 rows on the CUDA-core path and
+ * n <= 394 at d = 1024 on the tensor-core path.  The first call on a device looks up the array's
  * device address (cudaGetSymbolAddress, with that device current), so make one call on each device
  * before any stream capture.  All calls share the array and it keeps the last call's contents
  * (every slot read is first written by the same call); calls that overlap on the GPU -- two streams,

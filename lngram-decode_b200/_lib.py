@@ -93,7 +93,7 @@ SIGNATURES = {
     "lng_attend_pack": (C.c_int, [P, P, P, P, i64, i32, i32, P, P]),
     "lng_attend_unpack": (C.c_int, [P, i64, i32, i32, P, i32, P]),
     "lng_logits_topk": (C.c_int, [P, i64, i64, P, i32, i64, i32, P, P, P, P, sz, P]),
-    "lng_logits_topk_scratch_bytes": (sz, [i64, i64, i32]),
+    "lng_logits_topk_scratch_bytes": (sz, [i64, i64, i64, i32]),
     "lng_logits_topk_static": (C.c_int, [P, i64, i64, P, i32, i64, i32, P, P, P, P]),
     "lng_drafter_create": (C.c_int, [C.POINTER(DrafterNumbers), C.POINTER(Array), i32, i32, C.POINTER(P)]),
     "lng_drafter_destroy": (None, [P]),

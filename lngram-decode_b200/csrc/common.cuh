@@ -81,6 +81,9 @@ __device__ __forceinline__ float warp_max(float v) {
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
 
 // ------------------------------------------------------------------ mbarrier / bulk copies (sm_90+)
+// Round a byte count up to a multiple of 256 (sub-buffer alignment inside one allocation).
+inline size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
+
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

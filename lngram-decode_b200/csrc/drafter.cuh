@@ -174,15 +174,13 @@ struct ReadoutBufs {
   float* feat;   // [M, 2d]
 };
 
-static size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
-
 static int drafter_ws(lng_drafter* dr, int64_t M, int k, ReadoutBufs* b, size_t extra_bytes, void** extra) {
   const size_t es = size_t(dtype_size(dr->e_dtype)), as = size_t(dtype_size(dr->act));
   const size_t qd = size_t(dr->qh * dr->Dt);
   const size_t sizes[10] = {al256(size_t(M) * dr->d * es), al256(size_t(M) * 4), al256(size_t(M) * qd * as),
                             al256(size_t(M) * qd * as), al256(size_t(M) * dr->d * 4), al256(size_t(M) * dr->d * 4),
                             al256(size_t(M) * k * 8), al256(size_t(M) * k * 4),
-                            al256(lng_logits_topk_scratch_bytes(M, dr->V, k)), al256(size_t(M) * 2 * dr->d * 4)};
+                            al256(lng_logits_topk_scratch_bytes(M, dr->d, dr->V, k)), al256(size_t(M) * 2 * dr->d * 4)};
   size_t total = al256(extra_bytes);
   for (size_t s : sizes) total += s;
   if (total > dr->ws_bytes) {

@@ -819,27 +819,40 @@ extern "C" int lng_attend_unpack(const float* pack, int64_t M, int32_t num_heads
 }
 
 // ====================================================================== logits top-k
-extern "C" size_t lng_logits_topk_scratch_bytes(int64_t n, int64_t vocab, int32_t k) {
-  if (n <= 0 || vocab <= 0 || k <= 0) return 0;
-  const int64_t nch = ceil_div(vocab, TK_VC);
-  return size_t(n) * nch * k * (sizeof(float) + sizeof(int64_t)) + 256;
+namespace {
+size_t topk_cand_bytes(int64_t n, int64_t vocab, int32_t k) {
+  return size_t(n) * ceil_div(vocab, TK_VC) * k * (sizeof(float) + sizeof(int64_t));
+}
+// The tensor-core path applies to a bf16 vocabulary matrix whose shapes meet the TMA rules.
+bool logits_tc_ok(int64_t d, const void* embedding, int32_t e_dtype, int64_t vocab) {
+  return e_dtype == LNG_BF16 && d % TC_BK == 0 && (reinterpret_cast<uintptr_t>(embedding) & 15) == 0 &&
+         vocab < (int64_t(1) << 31);
+}
+size_t split_rows_bytes(int64_t n, int64_t d) { return size_t(n) * 3 * d * sizeof(__nv_bfloat16); }
+}  // namespace
+
+extern "C" size_t lng_logits_topk_scratch_bytes(int64_t n, int64_t d, int64_t vocab, int32_t k) {
+  if (n <= 0 || d <= 0 || vocab <= 0 || k <= 0) return 0;
+  // candidates, then (256-byte aligned) the three bf16 parts of h for the tensor cores
+  return al256(topk_cand_bytes(n, vocab, k) + 256) + split_rows_bytes(n, d) + 256;
 }
 
 namespace {
-// Per-tile candidates [n, ceil(vocab / 256), k] of h . E^T: the tcgen05 kernel for a bf16
-// vocabulary matrix whose shapes meet the TMA rules (d % 64 == 0, 16-byte aligned operands),
-// the CUDA-core kernel otherwise.
+// Per-tile candidates [n, ceil(vocab / 256), k] of h . E^T: the tcgen05 kernel (draft rows split
+// into `split`, 16-byte aligned, n * 3d bf16) when `split` is given and the vocabulary matrix is
+// bf16 with TMA-compatible shapes, the CUDA-core kernel otherwise.
 int logits_chunks(const float* h, int64_t n, int64_t d, const void* embedding, int32_t e_dtype, int64_t vocab,
-                  int32_t k, float* cand_v, int64_t* cand_i, float* logits, cudaStream_t stream) {
+                  int32_t k, float* cand_v, int64_t* cand_i, float* logits, __nv_bfloat16* split,
+                  cudaStream_t stream) {
   const int64_t nch = ceil_div(vocab, TK_VC);
-  const bool tc = e_dtype == LNG_BF16 && d % TC_BK == 0 && (reinterpret_cast<uintptr_t>(embedding) & 15) == 0 &&
-                  (reinterpret_cast<uintptr_t>(h) & 15) == 0 && vocab < (int64_t(1) << 31);
-  if (tc) {
+  if (split && logits_tc_ok(d, embedding, e_dtype, vocab)) {
+    split_rows_bf16x3_kernel<<<grid_for(n * d, 256, 16), 256, 0, stream>>>(h, n, d, split);
+    LNG_LAUNCHED("split_rows_bf16x3_kernel");
     const int bn = n <= 32 ? 32 : n <= 64 ? 64 : 128;
     CUtensorMap te, th;
     int st = make_tmap_bf16(&te, embedding, vocab, d, d, LT_BM);
     if (st) return st;
-    st = make_tmap_f32(&th, h, n, d, d, bn);
+    st = make_tmap_bf16(&th, split, n, 3 * d, 3 * d, bn);
     if (st) return st;
     dim3 grid(unsigned(ceil_div(n, bn)), unsigned(nch));
 #define LNG_LT(BN)                                                                                          \
@@ -882,12 +895,13 @@ extern "C" int lng_logits_topk(const float* h, int64_t n, int64_t d, const void*
   if (n == 0) return LNG_OK;
   LNG_REQUIRE(h && embedding && ids && vals, "NULL pointer");
   const int64_t nch = ceil_div(vocab, TK_VC);
-  const size_t need = lng_logits_topk_scratch_bytes(n, vocab, k);
+  const size_t need = lng_logits_topk_scratch_bytes(n, d, vocab, k);
   LNG_REQUIRE(scratch && scratch_bytes >= need, "scratch too small (see lng_logits_topk_scratch_bytes)");
-  uintptr_t base = (reinterpret_cast<uintptr_t>(scratch) + 15) & ~uintptr_t(15);
+  uintptr_t base = (reinterpret_cast<uintptr_t>(scratch) + 255) & ~uintptr_t(255);
   int64_t* cand_i = reinterpret_cast<int64_t*>(base);
   float* cand_v = reinterpret_cast<float*>(cand_i + n * nch * k);
-  int st = logits_chunks(h, n, d, embedding, e_dtype, vocab, k, cand_v, cand_i, logits, S(stream));
+  auto* split = reinterpret_cast<__nv_bfloat16*>(base + al256(topk_cand_bytes(n, vocab, k)));
+  int st = logits_chunks(h, n, d, embedding, e_dtype, vocab, k, cand_v, cand_i, logits, split, S(stream));
   if (st) return st;
   topk_merge_kernel<<<unsigned(ceil_div(n * 32, 256)), 256, 0, S(stream)>>>(cand_v, cand_i, n, nch, k, ids, vals);
   LNG_LAUNCHED("topk_merge_kernel");
@@ -917,9 +931,13 @@ extern "C" int lng_logits_topk_static(const float* h, int64_t n, int64_t d, cons
   LNG_REQUIRE(k >= 1 && k <= TK_MAXK, "k must be in [1, 8]");
   if (n == 0) return LNG_OK;
   LNG_REQUIRE(h && embedding && ids && vals, "NULL pointer");
-  const size_t need = lng_logits_topk_scratch_bytes(n, vocab, k);
+  // candidates, plus the split draft rows when the tensor-core path applies
+  const bool tc = logits_tc_ok(d, embedding, e_dtype, vocab);
+  const size_t cand = al256(topk_cand_bytes(n, vocab, k));
+  const size_t need = cand + (tc ? split_rows_bytes(n, d) : 0) + 256;
   if (need > kTopkStaticScratchBytes)
-    return fail(LNG_ERR_ARGUMENT, "lng_logits_topk_static: n * ceil(vocab / 256) * k * 12 bytes (+256) = " +
+    return fail(LNG_ERR_ARGUMENT, "lng_logits_topk_static: n * ceil(vocab / 256) * k * 12 bytes" +
+                                      std::string(tc ? " + n * d * 6 bytes (split rows)" : "") + " (+256) = " +
                                       std::to_string(need) + " exceeds the 4 MiB static scratch (" +
                                       std::to_string(kTopkStaticScratchBytes) +
                                       " bytes); use lng_logits_topk with a caller-provided buffer");
@@ -940,7 +958,8 @@ extern "C" int lng_logits_topk_static(const float* h, int64_t n, int64_t d, cons
   const int64_t nch = ceil_div(vocab, TK_VC);
   int64_t* cand_i = static_cast<int64_t*>(base);  // 256-byte aligned: no extra alignment step needed
   float* cand_v = reinterpret_cast<float*>(cand_i + n * nch * k);
-  int st = logits_chunks(h, n, d, embedding, e_dtype, vocab, k, cand_v, cand_i, logits, S(stream));
+  auto* split = tc ? reinterpret_cast<__nv_bfloat16*>(static_cast<unsigned char*>(base) + cand) : nullptr;
+  int st = logits_chunks(h, n, d, embedding, e_dtype, vocab, k, cand_v, cand_i, logits, split, S(stream));
   if (st) return st;
   topk_merge_kernel<<<unsigned(ceil_div(n * 32, 256)), 256, 0, S(stream)>>>(cand_v, cand_i, n, nch, k, ids, vals);
   LNG_LAUNCHED("topk_merge_kernel (static scratch)");

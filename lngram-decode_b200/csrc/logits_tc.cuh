@@ -3,9 +3,9 @@
 // drafting/cpu/drafter.cpp:537-556 ((logit desc, id asc)).
 //
 // One CTA owns 256 vocabulary rows (two 128-lane TMEM accumulators, M side) and BN draft rows
-// (N side).  The vocabulary tile (128-byte swizzle, K-major, 64-element k blocks) and the fp32
-// draft rows of each k block arrive by TMA; two converter warps split the rows into three bf16
-// parts h = h1 + h2 + h3 (each rounding exact to ~2^-24 relative) in the same swizzled layout,
+// (N side).  The fp32 draft rows are split once (split_rows_bf16x3_kernel) into three bf16 parts
+// h = h1 + h2 + h3 (exact to ~2^-24 relative); the vocabulary tile and the three parts of each
+// 64-element k block arrive by TMA (128-byte swizzle, K-major),
 // so logits = E . h1 + E . h2 + E . h3 accumulate in fp32 with every bf16 x bf16 product exact:
 // fp32-accurate logits while the bf16 vocabulary is read from HBM once.  The epilogue reads the
 // accumulators back (tcgen05.ld), takes each draft row's top-k over the tile's 256 entries (warp
@@ -26,22 +26,15 @@ static_assert(LT_BM == TK_VC, "per-tile candidates must use the top-k scratch la
 template <int BN>
 struct LtCfg {
   static constexpr uint32_t A_BYTES = LT_BM * TC_BK * 2;   // 32 KB vocabulary tile per k block
-  static constexpr uint32_t H_BYTES = BN * TC_BK * 4;      // fp32 draft rows of the k block (TMA)
   static constexpr uint32_t B_PART = BN * TC_BK * 2;       // one bf16 part of the draft rows
-  static constexpr uint32_t STAGE_BYTES = A_BYTES + H_BYTES + 3 * B_PART;
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + 3 * B_PART;
   static constexpr int STAGES = (224 * 1024) / STAGE_BYTES > 6 ? 6 : (224 * 1024) / STAGE_BYTES;
   static constexpr uint32_t TMEM_COLS = 2 * BN;
   static constexpr size_t SMEM = size_t(STAGES) * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
   static_assert(STAGES >= 2, "pipeline needs two stages");
-  static_assert(B_PART % 1024 == 0 && A_BYTES % 1024 == 0 && H_BYTES % 1024 == 0,
-                "swizzle atoms must stay 1024-byte aligned");
+  static_assert(B_PART % 1024 == 0 && A_BYTES % 1024 == 0, "swizzle atoms must stay 1024-byte aligned");
   static_assert(SMEM <= 227 * 1024, "shared memory per CTA");
 };
-
-__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
-  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
-  return *reinterpret_cast<uint32_t*>(&v);
-}
 
 // (v, id) strictly after (pv, pid) in (value desc, id asc) order
 __device__ __forceinline__ bool lt_after(float v, int id, float pv, int pid) {
@@ -49,6 +42,25 @@ __device__ __forceinline__ bool lt_after(float v, int id, float pv, int pid) {
 }
 __device__ __forceinline__ bool lt_better(float v, int id, float bv, int bid) {
   return v > bv || (v == bv && id < bid);
+}
+
+// h [n, d] fp32 -> [n, 3d] bf16 rows (h1 | h2 | h3) with h = h1 + h2 + h3: h1 = bf16(h),
+// h2 = bf16(h - h1), h3 = bf16(h - h1 - h2); both differences are exact in fp32.
+__global__ void split_rows_bf16x3_kernel(const float* __restrict__ h, int64_t n, int64_t d,
+                                         __nv_bfloat16* __restrict__ out) {
+  const int64_t total = n * d;
+  for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < total; e += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = e / d, k = e - r * d;
+    const float x = h[e];
+    const __nv_bfloat16 a = __float2bfloat16_rn(x);
+    const float r1 = x - __bfloat162float(a);
+    const __nv_bfloat16 b = __float2bfloat16_rn(r1);
+    const float r2 = r1 - __bfloat162float(b);
+    __nv_bfloat16* o = out + r * 3 * d;
+    o[k] = a;
+    o[d + k] = b;
+    o[2 * d + k] = __float2bfloat16_rn(r2);
+  }
 }
 
 template <int BN>
@@ -60,8 +72,7 @@ __global__ void __launch_bounds__(128, 1)
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t lt_smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(lt_smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* loaded = reinterpret_cast<uint64_t*>(base + size_t(STAGES) * Cfg::STAGE_BYTES);
-  uint64_t* full = loaded + STAGES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + size_t(STAGES) * Cfg::STAGE_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_bar = empty + STAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_bar + 1);
@@ -71,9 +82,8 @@ __global__ void __launch_bounds__(128, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&loaded[s], 1);  // TMA: vocabulary tile + fp32 draft rows
-      mbar_init(&full[s], 2);    // one arrive per converter warp
-      mbar_init(&empty[s], 1);   // MMA commit
+      mbar_init(&full[s], 1);   // TMA: vocabulary tile + the three parts of the draft rows
+      mbar_init(&empty[s], 1);  // MMA commit
     }
     mbar_init(acc_bar, 1);
     fence_mbar_init();
@@ -92,16 +102,19 @@ __global__ void __launch_bounds__(128, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    if (lane == 0) {  // TMA producer: the vocabulary tile and the draft rows of each k block
+    if (lane == 0) {  // TMA producer
       for (int kb = 0; kb < KB; ++kb) {
         const int s = kb % STAGES;
         if (kb >= STAGES &&
             !mbar_wait_bounded(&empty[s], uint32_t(((kb / STAGES) - 1) & 1), &g_error_word, DEV_ERR_WAIT_TIMEOUT))
           break;
         uint8_t* st = base + size_t(s) * Cfg::STAGE_BYTES;
-        mbar_arrive_expect_tx(&loaded[s], Cfg::A_BYTES + Cfg::H_BYTES);
-        tma_load_2d(st, &tma_e, int32_t(kb * TC_BK), int32_t(v0), &loaded[s]);
-        tma_load_2d(st + Cfg::A_BYTES, &tma_h, int32_t(kb * TC_BK), int32_t(r0), &loaded[s]);
+        mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+        tma_load_2d(st, &tma_e, int32_t(kb * TC_BK), int32_t(v0), &full[s]);
+#pragma unroll
+        for (int part = 0; part < 3; ++part)
+          tma_load_2d(st + Cfg::A_BYTES + part * Cfg::B_PART, &tma_h, int32_t(part * d + kb * TC_BK), int32_t(r0),
+                      &full[s]);
       }
     }
   } else if (warp == 1) {
@@ -117,7 +130,7 @@ __global__ void __launch_bounds__(128, 1)
         for (int kk = 0; kk < TC_BK / 16; ++kk) {
 #pragma unroll
           for (int part = 0; part < 3; ++part) {
-            const uint64_t db = umma_desc_sw128(st + Cfg::A_BYTES + Cfg::H_BYTES + part * Cfg::B_PART);
+            const uint64_t db = umma_desc_sw128(st + Cfg::A_BYTES + part * Cfg::B_PART);
             const uint32_t acc = (kb | kk | part) != 0 ? 1u : 0u;
             umma_bf16(tmem, da0 + uint64_t(2 * kk), db + uint64_t(2 * kk), idesc, acc);
             umma_bf16(tmem + uint32_t(BN), da1 + uint64_t(2 * kk), db + uint64_t(2 * kk), idesc, acc);
@@ -126,44 +139,6 @@ __global__ void __launch_bounds__(128, 1)
         umma_commit(&empty[s]);
       }
       umma_commit(acc_bar);
-    }
-  } else {
-    // converters (warps 2, 3): the k block's fp32 draft rows (TMA-staged [BN][64], rows past n are
-    // zero-filled) split into three bf16 parts in the 128-byte-swizzled K-major layout (row r at
-    // r*128 bytes, 16-byte chunk c stored at c ^ (r & 7))
-    const int t = threadIdx.x - 64;
-    for (int kb = 0; kb < KB; ++kb) {
-      const int s = kb % STAGES;
-      const bool ok = mbar_wait_bounded(&loaded[s], uint32_t((kb / STAGES) & 1), &g_error_word, DEV_ERR_WAIT_TIMEOUT);
-      if (!__all_sync(0xffffffffu, ok)) break;
-      uint8_t* st = base + size_t(s) * Cfg::STAGE_BYTES;
-      const float* hs = reinterpret_cast<const float*>(st + Cfg::A_BYTES);
-      uint8_t* bt = st + Cfg::A_BYTES + Cfg::H_BYTES;
-#pragma unroll 4
-      for (int q = t; q < BN * 8; q += 64) {
-        const int r = q >> 3, c = q & 7;
-        const float4 a = *reinterpret_cast<const float4*>(hs + r * TC_BK + c * 8);
-        const float4 b = *reinterpret_cast<const float4*>(hs + r * TC_BK + c * 8 + 4);
-        const float x[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-        uint32_t p1[4], p2[4], p3[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float a1 = __bfloat162float(__float2bfloat16_rn(x[2 * i]));
-          const float b1 = __bfloat162float(__float2bfloat16_rn(x[2 * i + 1]));
-          const float ra = x[2 * i] - a1, rb = x[2 * i + 1] - b1;
-          const float a2 = __bfloat162float(__float2bfloat16_rn(ra)), b2 = __bfloat162float(__float2bfloat16_rn(rb));
-          p1[i] = pack_bf16x2(a1, b1);
-          p2[i] = pack_bf16x2(a2, b2);
-          p3[i] = pack_bf16x2(ra - a2, rb - b2);
-        }
-        const uint32_t off = uint32_t(r) * 128u + (uint32_t(c ^ (r & 7)) << 4);
-        *reinterpret_cast<uint4*>(bt + off) = make_uint4(p1[0], p1[1], p1[2], p1[3]);
-        *reinterpret_cast<uint4*>(bt + Cfg::B_PART + off) = make_uint4(p2[0], p2[1], p2[2], p2[3]);
-        *reinterpret_cast<uint4*>(bt + 2 * Cfg::B_PART + off) = make_uint4(p3[0], p3[1], p3[2], p3[3]);
-      }
-      fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor cores' async proxy
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&full[s]);
     }
   }
   __syncwarp();
@@ -259,22 +234,6 @@ __global__ void __launch_bounds__(128, 1)
       pid = bid;
     }
   }
-}
-
-// 2D fp32 tensor map over a row-major [rows, cols] matrix (row stride ld elements), box
-// TC_BK x box_rows, no swizzle; rows past the end read as zeros.
-inline int make_tmap_f32(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
-  auto enc = tensor_map_encoder();
-  if (!enc) return fail(LNG_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable (driver entry point)");
-  const cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
-  const cuuint64_t strides[1] = {cuuint64_t(ld) * 4};
-  const cuuint32_t box[2] = {uint32_t(TC_BK), uint32_t(box_rows)};
-  const cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(LNG_ERR_CUDA, "cuTensorMapEncodeTiled (f32) failed: " + std::to_string(int(r)));
-  return LNG_OK;
 }
 
 }  // namespace lng

@@ -122,18 +122,39 @@ __global__ void __cluster_dims__(RS_SPLIT, 1, 1) __launch_bounds__(256)
   float acc[RT_MAXBITS];
 #pragma unroll
   for (int j = 0; j < RT_MAXBITS; ++j) acc[j] = 0.f;
-  for (int64_t k0 = kbeg; k0 < kend; k0 += RS_KC) {
-    for (int e = threadIdx.x; e < RS_ROWS * RS_KC; e += blockDim.x) {
-      const int rr = e / RS_KC, kk = e % RS_KC;
+  // the next chunk's x and w are loaded into registers (all loads in flight together) while the
+  // current chunk is multiplied out of shared memory
+  constexpr int XPT = RS_ROWS * RS_KC / 256, WPT = RS_RPC * RT_MAXBITS * RS_KC / 256;
+  float xr[XPT], wr[WPT];
+  auto fetch = [&](int64_t k0) {
+#pragma unroll
+    for (int i = 0; i < XPT; ++i) {
+      const int e = threadIdx.x + i * 256, rr = e / RS_KC, kk = e % RS_KC;
       const int64_t gr = row0 + rr, gk = k0 + kk;
-      xs[rr][kk] = (gr < n && gk < kend) ? to_f32(x[gr * x_stride + gk]) : 0.f;
+      xr[i] = (gr < n && gk < kend) ? to_f32(x[gr * x_stride + gk]) : 0.f;
     }
-    for (int e = threadIdx.x; e < ncol * RS_KC; e += blockDim.x) {
-      const int c = e / RS_KC, kk = e % RS_KC;
+#pragma unroll
+    for (int i = 0; i < WPT; ++i) {
+      const int e = threadIdx.x + i * 256, c = e / RS_KC, kk = e % RS_KC;
       const int64_t gc = col0 + c, gk = k0 + kk;
-      ws[c][kk] = (gc < C && gk < kend) ? w[gc * in_dim + gk] : 0.f;
+      wr[i] = (c < ncol && gc < C && gk < kend) ? w[gc * in_dim + gk] : 0.f;
+    }
+  };
+  if (kbeg < kend) fetch(kbeg);
+  for (int64_t k0 = kbeg; k0 < kend; k0 += RS_KC) {
+    __syncthreads();  // the previous chunk's products are done with the tiles
+#pragma unroll
+    for (int i = 0; i < XPT; ++i) {
+      const int e = threadIdx.x + i * 256;
+      xs[e / RS_KC][e % RS_KC] = xr[i];
+    }
+#pragma unroll
+    for (int i = 0; i < WPT; ++i) {
+      const int e = threadIdx.x + i * 256;
+      ws[e / RS_KC][e % RS_KC] = wr[i];
     }
     __syncthreads();
+    if (k0 + RS_KC < kend) fetch(k0 + RS_KC);
 #pragma unroll 4
     for (int kk = 0; kk < RS_KC; ++kk) {
       const float a = xs[r][kk];
@@ -141,7 +162,6 @@ __global__ void __cluster_dims__(RS_SPLIT, 1, 1) __launch_bounds__(256)
       for (int j = 0; j < RT_MAXBITS; ++j)
         if (j < bits) acc[j] = fmaf(a, ws[g * bits + j][kk], acc[j]);
     }
-    __syncthreads();
   }
 #pragma unroll
   for (int j = 0; j < RT_MAXBITS; ++j)
@@ -197,6 +217,7 @@ __global__ void __launch_bounds__(128) embed2_features_kernel(const int64_t* __r
 #pragma unroll
     for (int part = 0; part < 2; ++part) {
       const int64_t tok = part == 0 ? tp : tc;
+#pragma unroll 8
       for (int64_t j = threadIdx.x; j < d; j += blockDim.x) {
         const float v = tok >= 0 ? to_f32(E[tok * d + j]) : start[j];
         ss[part] += v * v;
@@ -211,6 +232,7 @@ __global__ void __launch_bounds__(128) embed2_features_kernel(const int64_t* __r
       const float rs = rsqrtf(tot / float(d) + eps);
       const float* wv = part == 0 ? prev_w : cur_w;
       const int64_t tok = part == 0 ? tp : tc;
+#pragma unroll 8
       for (int64_t j = threadIdx.x; j < d; j += blockDim.x) {
         const float v = tok >= 0 ? to_f32(E[tok * d + j]) : start[j];
         o[part * d + j] = v * rs * wv[j];

@@ -9,19 +9,49 @@
 
 namespace lng {
 
-// rs[i] = 1 / sqrt(mean(x[i]^2) + eps) (or, with SUMSQ, the plain sum of squares): one warp per row.
-template <typename XT, bool SUMSQ = false>
-__global__ void rms_rows_kernel(const XT* __restrict__ x, int64_t n, int64_t d, float eps, float* __restrict__ rs) {
-  const int lane = threadIdx.x & 31;
-  for (int64_t row = (blockIdx.x * int64_t(blockDim.x) + threadIdx.x) >> 5; row < n;
-       row += (int64_t(gridDim.x) * blockDim.x) >> 5) {
-    const XT* xr = x + row * d;
-    float ss = 0.f;
+// Sixteen bytes of a row as floats (8 bf16 / f16 or 4 f32), from a 16-byte aligned address.
+template <typename XT>
+struct Vec16 {
+  static constexpr int N = 16 / int(sizeof(XT));
+  __device__ __forceinline__ static void load(const XT* p, float (&v)[N]) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(p);
+    const XT* e = reinterpret_cast<const XT*>(&raw);
+#pragma unroll
+    for (int i = 0; i < N; ++i) v[i] = to_f32(e[i]);
+  }
+};
+
+// Sum of squares of one row (warp-cooperative); 16-byte loads when `vec`.
+template <typename XT>
+__device__ __forceinline__ float row_sumsq(const XT* xr, int64_t d, bool vec, int lane) {
+  float ss = 0.f;
+  if (vec) {
+    constexpr int N = Vec16<XT>::N;
+#pragma unroll 4
+    for (int64_t j = int64_t(lane) * N; j < d; j += 32 * N) {
+      float v[N];
+      Vec16<XT>::load(xr + j, v);
+#pragma unroll
+      for (int i = 0; i < N; ++i) ss = fmaf(v[i], v[i], ss);
+    }
+  } else {
+#pragma unroll 8
     for (int64_t j = lane; j < d; j += 32) {
       const float v = to_f32(xr[j]);
       ss = fmaf(v, v, ss);
     }
-    ss = warp_sum(ss);
+  }
+  return warp_sum(ss);
+}
+
+// One warp per row: rs[row] = 1 / sqrt(mean(x^2) + eps) (or the plain sum of squares with SUMSQ).
+template <typename XT, bool SUMSQ = false>
+__global__ void rms_rows_kernel(const XT* __restrict__ x, int64_t n, int64_t d, float eps, float* __restrict__ rs) {
+  const int lane = threadIdx.x & 31;
+  const bool vec = d % Vec16<XT>::N == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+  for (int64_t row = (blockIdx.x * int64_t(blockDim.x) + threadIdx.x) >> 5; row < n;
+       row += (int64_t(gridDim.x) * blockDim.x) >> 5) {
+    const float ss = row_sumsq(x + row * d, d, vec, lane);
     if (lane == 0) rs[row] = SUMSQ ? ss : rsqrtf(ss / float(d) + eps);
   }
 }
@@ -29,17 +59,13 @@ __global__ void rms_rows_kernel(const XT* __restrict__ x, int64_t n, int64_t d, 
 template <typename XT, typename YT>
 __global__ void rms_norm_kernel(const XT* x, int64_t n, int64_t d, const float* __restrict__ w, float eps, YT* y) {
   const int lane = threadIdx.x & 31;
+  const bool vec = d % Vec16<XT>::N == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
   for (int64_t row = (blockIdx.x * int64_t(blockDim.x) + threadIdx.x) >> 5; row < n;
        row += (int64_t(gridDim.x) * blockDim.x) >> 5) {
     const XT* xr = x + row * d;
-    float ss = 0.f;
-    for (int64_t j = lane; j < d; j += 32) {
-      const float v = to_f32(xr[j]);
-      ss = fmaf(v, v, ss);
-    }
-    ss = warp_sum(ss);
-    const float r = rsqrtf(ss / float(d) + eps);
+    const float r = rsqrtf(row_sumsq(xr, d, vec, lane) / float(d) + eps);
     __syncwarp();
+#pragma unroll 8
     for (int64_t j = lane; j < d; j += 32) {
       const float v = to_f32(xr[j]) * r;
       y[row * d + j] = from_f32<YT>(w ? v * w[j] : v);

@@ -27,7 +27,7 @@ def run_topk(lngram, h, E, k, want_logits=False):
     ids = torch.empty(n, k, device=DEV, dtype=torch.int64)
     vals = torch.empty(n, k, device=DEV, dtype=torch.float32)
     logits = torch.empty(n, V, device=DEV, dtype=torch.float32) if want_logits else None
-    need = L.lng_logits_topk_scratch_bytes(n, V, k)
+    need = L.lng_logits_topk_scratch_bytes(n, d, V, k)
     scratch = torch.empty(need, device=DEV, dtype=torch.uint8)
     lib.check(L.lng_logits_topk(h.data_ptr(), n, d, E.data_ptr(), lib.dtype_code(E.dtype), V, k, ids.data_ptr(),
                                 vals.data_ptr(), None if logits is None else logits.data_ptr(), scratch.data_ptr(),

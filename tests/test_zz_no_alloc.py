@@ -23,7 +23,7 @@ def _with_buffer(lib, h, E, k):
     V = E.shape[0]
     ids = torch.empty(n, k, device=DEV, dtype=torch.int64)
     vals = torch.empty(n, k, device=DEV, dtype=torch.float32)
-    need = L.lng_logits_topk_scratch_bytes(n, V, k)
+    need = L.lng_logits_topk_scratch_bytes(n, d, V, k)
     scratch = torch.empty(need, device=DEV, dtype=torch.uint8)
     lib.check(L.lng_logits_topk(h.data_ptr(), n, d, E.data_ptr(), lib.dtype_code(E.dtype), V, k, ids.data_ptr(),
                                 vals.data_ptr(), None, scratch.data_ptr(), need, lib.stream_ptr()))
@@ -69,5 +69,23 @@ def test_static_scratch_rejects_oversized_requests(lngram):
     assert b"exceeds the 4 MiB static scratch" in L.lng_last_error()
     # the largest size that fits is accepted
     lib.check(L.lng_logits_topk_static(h.data_ptr(), 932, 64, E.data_ptr(), lib.F32, 32000, 3, ids.data_ptr(),
+                                       vals.data_ptr(), None, lib.stream_ptr()))
+    torch.cuda.synchronize()
+
+
+def test_static_scratch_tensor_core_limit_includes_split_rows(lngram):
+    """A bf16 vocabulary at d = 1024 takes the tensor-core path, whose split rows share the array:
+    394 rows fit at k = 3, V = 32000, 395 do not."""
+    lib = lngram._lib
+    L = lib.library()
+    h = torch.zeros(395, 1024, device=DEV)
+    E = torch.zeros(32000, 1024, device=DEV, dtype=torch.bfloat16)
+    ids = torch.empty(395, 3, device=DEV, dtype=torch.int64)
+    vals = torch.empty(395, 3, device=DEV, dtype=torch.float32)
+    st = L.lng_logits_topk_static(h.data_ptr(), 395, 1024, E.data_ptr(), lib.BF16, 32000, 3, ids.data_ptr(),
+                                  vals.data_ptr(), None, lib.stream_ptr())
+    assert st == lib.ERR_ARGUMENT
+    assert b"split rows" in L.lng_last_error()
+    lib.check(L.lng_logits_topk_static(h.data_ptr(), 394, 1024, E.data_ptr(), lib.BF16, 32000, 3, ids.data_ptr(),
                                        vals.data_ptr(), None, lib.stream_ptr()))
     torch.cuda.synchronize()

@@ -318,6 +318,7 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
   uint32_t qa_frag[KT][4];
   float uacc[NTU][4];
   float m_r[2], l_r[2];
+  bool running_max = false;
   float qs = 1.f;
   const int g = lane >> 2, t4 = lane & 3;
   T* tag = nullptr;
@@ -359,6 +360,7 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
       for (int nt = 0; nt < NTU; ++nt) uacc[nt][0] = uacc[nt][1] = uacc[nt][2] = uacc[nt][3] = 0.f;
       m_r[0] = m_r[1] = sink_in ? p.sink : -INFINITY;
       l_r[0] = l_r[1] = 0.f;  // per-thread partial sums; the sink's 1 is added at the end
+      running_max = !sink_in;  // without the sink seed there is no fixed offset to start from
       qs = p.qscale ? p.qscale[item] : 1.f;
     }
     const bool landed = mbar_wait_bounded(&bars[s], phase, &g_error_word, DEV_ERR_WAIT_TIMEOUT);
@@ -424,15 +426,20 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
       }
     }
 
-    // online softmax update with the sink seed; rxv = this thread's 8 route columns' 1/rms
+    // softmax update with the sink seed; rxv = this thread's 8 route columns' 1/rms.  The exponent
+    // offset stays the sink logit b0 (m_r's seed) while no score of the item has exceeded b0 + BIG:
+    // p = exp(s - b0) is then finite in the 16-bit P operand and the fp32 sums and the normalised
+    // result is the same, with no per-chunk maximum or rescaling.  From the first chunk with a larger
+    // score (a warp vote), the offset is the running maximum with online rescaling.
+    constexpr float BIG = std::is_same<T, __nv_bfloat16>::value ? 64.f : 4.f;  // f16 P: exp(BIG) * rx < 65504
     const int64_t rbase = p.route_start + int64_t(chunk) * C;
     float rxv[4][2];
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
       for (int b = 0; b < 2; ++b) rxv[nt][b] = __shfl_sync(0xffffffffu, rxl, nt * 8 + t4 * 2 + b);
-    float mx[2] = {m_r[0], m_r[1]};
     float sv[4][4];
+    bool big = false;
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt) {
 #pragma unroll
@@ -441,20 +448,28 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
         float v = sacc[nt][h] * (qs * rxv[nt][h & 1]);
         if (rbase + col >= p.route_end) v = -INFINITY;
         sv[nt][h] = v;
-        mx[h >> 1] = fmaxf(mx[h >> 1], v);
+        big = big || v > p.sink + BIG;
       }
     }
+    running_max = running_max || __any_sync(0xffffffffu, big);
+    float alpha[2] = {1.f, 1.f};
+    if (running_max) {
+      float mx[2] = {m_r[0], m_r[1]};
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 1));
-      mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 2));
-    }
-    float alpha[2];
+      for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      alpha[i] = __expf(m_r[i] - mx[i]);
-      m_r[i] = mx[i];
-      l_r[i] *= alpha[i];
+        for (int h = 0; h < 4; ++h) mx[h >> 1] = fmaxf(mx[h >> 1], sv[nt][h]);
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 1));
+        mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 2));
+      }
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        alpha[i] = __expf(m_r[i] - mx[i]);
+        m_r[i] = mx[i];
+        l_r[i] *= alpha[i];
+      }
     }
     uint32_t pa[2][4];  // P' as A fragments of the two k16 steps
 #pragma unroll
@@ -469,12 +484,14 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
       pa[nt >> 1][(nt & 1) * 2 + 0] = pack2(e[0], e[1], tag);
       pa[nt >> 1][(nt & 1) * 2 + 1] = pack2(e[2], e[3], tag);
     }
+    if (running_max) {
 #pragma unroll
-    for (int nt = 0; nt < NTU; ++nt) {
-      uacc[nt][0] *= alpha[0];
-      uacc[nt][1] *= alpha[0];
-      uacc[nt][2] *= alpha[1];
-      uacc[nt][3] *= alpha[1];
+      for (int nt = 0; nt < NTU; ++nt) {
+        uacc[nt][0] *= alpha[0];
+        uacc[nt][1] *= alpha[0];
+        uacc[nt][2] *= alpha[1];
+        uacc[nt][3] *= alpha[1];
+      }
     }
     // u += P' . tok   (B = tok rows as [k = route][n = dim], loaded transposed)
 #pragma unroll

@@ -10,6 +10,7 @@
 
 #include "address.cuh"
 #include "attend.cuh"
+#include "attend_tc.cuh"
 #include "gemm_simt.cuh"
 #include "gemm_tc.cuh"
 #include "logits_tc.cuh"
@@ -367,12 +368,44 @@ static int dispatch_attend_mma(int64_t Dt, const AttendParams& p, cudaStream_t s
   }
 }
 
+template <typename CodeT, typename T>
+static int launch_attend_tc(const lng_tables* t, const AttendParams& p, cudaStream_t stream) {
+  const int dt = t->table_dtype;
+  const int64_t rows = t->num_routes << (int64_t(t->bits) * t->orders[0]);
+  CUtensorMap tab, tab_tail, qa, qa_tail;
+  int st = make_tmap_16(&tab, dt, t->tables[0], rows, atc::DT, atc::DT, 64, 1, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!st) st = make_tmap_16(&tab_tail, dt, t->tables[0], rows, atc::DT, atc::DT, 16, 1, CU_TENSOR_MAP_SWIZZLE_32B);
+  if (!st) st = make_tmap_16(&qa, dt, p.qa, p.M * p.qh, atc::DT, atc::DT, 64, atc::QN, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!st) st = make_tmap_16(&qa_tail, dt, p.qa, p.M * p.qh, atc::DT, atc::DT, 16, atc::QN, CU_TENSOR_MAP_SWIZZLE_32B);
+  if (st) return st;
+  auto kern = attend_tc_kernel<CodeT, T>;
+  LNG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(atc::SMEM_LAUNCH)));
+  const int grid = int(std::max<int64_t>(1, std::min<int64_t>(p.M, num_sms())));
+  kern<<<grid, atc::THREADS, atc::SMEM_LAUNCH, stream>>>(tab, tab_tail, qa, qa_tail, p);
+  LNG_LAUNCHED("attend_tc_kernel");
+  return LNG_OK;
+}
+
 template <typename CodeT>
 static int attend_impl(const lng_tables* t, const AttendParams& p, int32_t u_dtype, cudaStream_t stream) {
   const int64_t Dt = int64_t(t->n_orders) * t->memory_dim;
   const bool t16 = t->table_dtype == LNG_BF16 || t->table_dtype == LNG_F16;
   // qa dtype: the activations' in normalised mode; the tables' (16-bit) or f32 in partial mode
   const int qa_dtype = p.partial ? (t16 ? t->table_dtype : LNG_F32) : u_dtype;
+  // tcgen05 path (opt-in, LNG_ATTEND_IMPL=tc): 136-dim tokens of 16-bit tables, <= 192 routes, <= 16
+  // heads, normalised output (one order of 136 dims, rows and query rows addressable by 32-bit TMA
+  // coordinates).  It computes the same result as the default warp-per-position kernel, which was
+  // measured faster at the SB shape (more positions in flight per SM); kept for further tuning.
+  static const bool tc_selected = [] {
+    const char* e = getenv("LNG_ATTEND_IMPL");
+    return e && std::string(e) == "tc";
+  }();
+  if (tc_selected && t16 && t->n_orders == 1 && t->memory_dim == atc::DT && p.partial == 0 && u_dtype == t->table_dtype &&
+      p.qh >= 1 && p.qh <= atc::QN && p.route_end - p.route_start <= atc::RP && t->orders[0] <= MAXW &&
+      (t->num_routes << (int64_t(t->bits) * t->orders[0])) < (int64_t(1) << 31) && p.M * p.qh < (int64_t(1) << 31) &&
+      (reinterpret_cast<uintptr_t>(p.qa) & 15) == 0 && (reinterpret_cast<uintptr_t>(t->tables[0]) & 15) == 0)
+    return t->table_dtype == LNG_BF16 ? launch_attend_tc<CodeT, __nv_bfloat16>(t, p, stream)
+                                      : launch_attend_tc<CodeT, __half>(t, p, stream);
   // tensor-core path: 16-bit tables, query of the same type, <= 16 heads, 16-byte rows
   const bool mma_ok = t16 && qa_dtype == t->table_dtype && (p.partial ? u_dtype == LNG_F32 : u_dtype == t->table_dtype) &&
                       p.qh <= 16 && (t->memory_dim % 8) == 0 && t->orders[t->n_orders - 1] <= MAXW;
@@ -538,6 +571,35 @@ static int check_readout(const lng_readout* ro) {
   return LNG_OK;
 }
 
+// Stream-ordered scratch for entry points without a workspace argument, from a memory pool owned by
+// the library (one per device) that keeps freed blocks for reuse instead of returning them to the
+// driver at every synchronisation.
+namespace {
+std::mutex g_pool_mu;
+cudaMemPool_t g_pools[64] = {};
+}  // namespace
+static int scratch_alloc(void** p, size_t bytes, cudaStream_t stream) {
+  int dev = 0;
+  LNG_CUDA(cudaGetDevice(&dev));
+  LNG_REQUIRE(dev >= 0 && dev < 64, "device ordinal out of range for the scratch pool table");
+  cudaMemPool_t pool;
+  {
+    std::lock_guard<std::mutex> lk(g_pool_mu);
+    if (!g_pools[dev]) {
+      cudaMemPoolProps props{};
+      props.allocType = cudaMemAllocationTypePinned;
+      props.location.type = cudaMemLocationTypeDevice;
+      props.location.id = dev;
+      LNG_CUDA(cudaMemPoolCreate(&g_pools[dev], &props));
+      uint64_t keep = ~uint64_t(0);
+      LNG_CUDA(cudaMemPoolSetAttribute(g_pools[dev], cudaMemPoolAttrReleaseThreshold, &keep));
+    }
+    pool = g_pools[dev];
+  }
+  LNG_CUDA(cudaMallocFromPoolAsync(p, bytes, pool, stream));
+  return LNG_OK;
+}
+
 static ConvParams conv_params(const lng_readout* ro) {
   return ConvParams{ro->hidden, ro->conv_kernel, ro->conv_dilation, ro->conv_norm, ro->conv_weight, ro->conv_bias};
 }
@@ -548,6 +610,26 @@ static int conv_finish_ws(const lng_readout* ro, const void* mixed, int64_t B, i
   int st = lng_rms_rows(mixed, ro->act_dtype, M, ro->hidden, ro->eps, rs, reinterpret_cast<lng_stream_t>(stream));
   if (st) return st;
   const ConvParams cp = conv_params(ro);
+  const bool al16 = (reinterpret_cast<uintptr_t>(mixed) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(conv_in) & 15) == 0;
+  const int tile_ch = ro->act_dtype == LNG_F32 ? 128 : 256;
+  if (ro->conv_kernel == 4 && 3 * ro->conv_dilation <= CT_HMAX && ro->hidden % tile_ch == 0 && al16 &&
+      (ro->act_dtype == LNG_F32 || ro->act_dtype == LNG_BF16)) {
+    const size_t smem = size_t(CT_TP + CT_HMAX) * 32 * 16 + size_t(CT_TP + CT_HMAX) * 4;
+    const dim3 grid(unsigned(ceil_div(M, CT_TP)), unsigned(ro->hidden / tile_ch));
+    LNG_CUDA(cudaFuncSetAttribute(conv_tile_kernel<float, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+    LNG_CUDA(cudaFuncSetAttribute(conv_tile_kernel<__nv_bfloat16, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  int(smem)));
+    if (ro->act_dtype == LNG_F32)
+      conv_tile_kernel<float, 4><<<grid, 256, smem, stream>>>(cp, static_cast<const float*>(mixed), rs, M, T, seg, valid,
+                                                              static_cast<float*>(out), static_cast<float*>(conv_in));
+    else
+      conv_tile_kernel<__nv_bfloat16, 4><<<grid, 256, smem, stream>>>(
+          cp, static_cast<const __nv_bfloat16*>(mixed), rs, M, T, seg, valid, static_cast<__nv_bfloat16*>(out),
+          static_cast<__nv_bfloat16*>(conv_in));
+    LNG_LAUNCHED("conv_tile_kernel");
+    return LNG_OK;
+  }
   const int64_t groups = ro->hidden / 8;
   if (ro->hidden % 8 == 0 && groups <= 256 && 256 % groups == 0 && ro->conv_kernel <= 8 && M < (int64_t(1) << 31) &&
       (reinterpret_cast<uintptr_t>(mixed) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
@@ -586,7 +668,8 @@ extern "C" int lng_conv_finish(const lng_readout* ro, const void* mixed, int64_t
   if (B * T == 0) return LNG_OK;
   LNG_REQUIRE(mixed && out && mixed != out, "mixed and out must be distinct non-NULL buffers");
   float* rs = nullptr;
-  LNG_CUDA(cudaMallocAsync(&rs, sizeof(float) * B * T, S(stream)));
+  st = scratch_alloc(reinterpret_cast<void**>(&rs), sizeof(float) * B * T, S(stream));
+  if (st) return st;
   st = conv_finish_ws(ro, mixed, B, T, segment_ids, valid_tokens, out, conv_in, rs, S(stream));
   cudaFreeAsync(rs, S(stream));
   return st;
@@ -599,7 +682,8 @@ extern "C" int lng_conv_window(const lng_readout* ro, const void* mixed, int64_t
   if (n <= 0) return LNG_OK;
   LNG_REQUIRE(mixed && cache && new_slot && slot && out, "NULL pointer");
   float* rs = nullptr;
-  LNG_CUDA(cudaMallocAsync(&rs, sizeof(float) * n, S(stream)));
+  st = scratch_alloc(reinterpret_cast<void**>(&rs), sizeof(float) * n, S(stream));
+  if (st) return st;
   st = lng_rms_rows(mixed, ro->act_dtype, n, ro->hidden, ro->eps, rs, stream);
   if (st) {
     cudaFreeAsync(rs, S(stream));

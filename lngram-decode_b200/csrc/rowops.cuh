@@ -81,6 +81,121 @@ struct ConvParams {
   const float* bias;    // [d] or null
 };
 
+// Sequence-mode conv finish on a shared-memory tile (the form used for whole batches): a CTA takes
+// CT_TP consecutive positions x 512 bytes of channels plus the (k-1)*dil halo positions before
+// them, loaded once with 16-byte coalesced loads; each output position then reads its k taps from
+// shared memory.  Semantics as conv_seq_kernel below (zero left padding, segment mask, valid mask).
+constexpr int CT_TP = 64;    // positions per tile
+constexpr int CT_HMAX = 32;  // largest halo (k-1)*dil the tile holds
+
+template <typename T>
+__device__ __forceinline__ void unpack16(const uint4& w, float (&v)[16 / sizeof(T)]) {
+  if constexpr (std::is_same<T, float>::value) {
+    v[0] = __uint_as_float(w.x); v[1] = __uint_as_float(w.y); v[2] = __uint_as_float(w.z); v[3] = __uint_as_float(w.w);
+  } else {
+    const uint32_t w4[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[2 * i] = __uint_as_float(w4[i] << 16);
+      v[2 * i + 1] = __uint_as_float(w4[i] & 0xffff0000u);
+    }
+  }
+}
+template <typename T>
+__device__ __forceinline__ uint4 pack16(const float (&v)[16 / sizeof(T)]) {
+  if constexpr (std::is_same<T, float>::value) {
+    return make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]), __float_as_uint(v[3]));
+  } else {
+    uint32_t w4[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __nv_bfloat162 b2 = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+      w4[i] = *reinterpret_cast<uint32_t*>(&b2);
+    }
+    return make_uint4(w4[0], w4[1], w4[2], w4[3]);
+  }
+}
+
+template <typename T, int K>
+__global__ void __launch_bounds__(256) conv_tile_kernel(ConvParams cp, const T* __restrict__ mixed,
+                                                        const float* __restrict__ rs, int64_t M, int64_t T_,
+                                                        const int64_t* __restrict__ seg,
+                                                        const uint8_t* __restrict__ valid, T* __restrict__ out,
+                                                        T* __restrict__ conv_in) {
+  constexpr int VEC = 16 / int(sizeof(T));         // channels per 16-byte chunk
+  constexpr int CH = 32 * VEC;                      // channels per tile (512 bytes)
+  constexpr int LOADS = (CT_TP + CT_HMAX) * 32 / 256;
+  extern __shared__ uint4 ct_tile[];                // [rows][32 chunks]
+  float* rsh = reinterpret_cast<float*>(ct_tile + (CT_TP + CT_HMAX) * 32);
+  const int H = (K - 1) * cp.dil;
+  const int rows = CT_TP + H;
+  const int64_t p0 = int64_t(blockIdx.x) * CT_TP, base = p0 - H;
+  const int64_t c0 = int64_t(blockIdx.y) * CH;
+  const int tid = threadIdx.x, lane = tid & 31, pr = tid >> 5;
+  uint4 ld[LOADS];
+#pragma unroll
+  for (int i = 0; i < LOADS; ++i) {  // all loads in flight together, then to shared memory
+    const int e = tid + i * 256, r = e >> 5, ch = e & 31;
+    const int64_t q = base + r;
+    ld[i] = (r < rows && q >= 0 && q < M) ? *reinterpret_cast<const uint4*>(mixed + q * cp.d + c0 + ch * VEC)
+                                          : make_uint4(0, 0, 0, 0);
+  }
+  for (int r = tid; r < rows; r += 256) {
+    const int64_t q = base + r;
+    rsh[r] = (q >= 0 && q < M) ? rs[q] : 0.f;
+  }
+#pragma unroll
+  for (int i = 0; i < LOADS; ++i) {
+    const int e = tid + i * 256;
+    if (e < rows * 32) ct_tile[e] = ld[i];
+  }
+  __syncthreads();
+  const int64_t cc = c0 + lane * VEC;  // this thread's channels
+  float gw[VEC], wt[K][VEC], bias[VEC];
+#pragma unroll
+  for (int j = 0; j < VEC; ++j) {
+    gw[j] = cp.norm_w[cc + j];
+    bias[j] = cp.bias ? cp.bias[cc + j] : 0.f;
+#pragma unroll
+    for (int tap = 0; tap < K; ++tap) wt[tap][j] = cp.weight[(cc + j) * K + tap];
+  }
+  for (int i = pr; i < CT_TP; i += 8) {
+    const int64_t pos = p0 + i;
+    if (pos >= M) break;
+    const int64_t t = pos % T_;
+    float acc[VEC], self[VEC];
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) acc[j] = bias[j];
+#pragma unroll
+    for (int tap = 0; tap < K; ++tap) {
+      const int lag = (K - 1 - tap) * cp.dil;
+      const int r = i + H - lag;
+      float v[VEC];
+      unpack16<T>(ct_tile[r * 32 + lane], v);
+      if (tap == K - 1) {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) self[j] = v[j];
+      }
+      if (t - lag >= 0 && (!seg || seg[pos - lag] == seg[pos])) {
+        const float rq = rsh[r];
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) acc[j] = fmaf(wt[tap][j], v[j] * rq * gw[j], acc[j]);
+      }
+    }
+    const bool keep = !valid || valid[pos];
+    float o[VEC];
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) o[j] = keep ? self[j] + silu_f(acc[j]) : 0.f;
+    *reinterpret_cast<uint4*>(out + pos * cp.d + cc) = pack16<T>(o);
+    if (conv_in) {
+      const float r = rsh[i + H];
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) o[j] = self[j] * r * gw[j];
+      *reinterpret_cast<uint4*>(conv_in + pos * cp.d + cc) = pack16<T>(o);
+    }
+  }
+}
+
 // Sequence-mode conv finish: out[p, c] = mixed[p, c] + SiLU(bias + sum_tap w[c, tap] y[p - lag, c] ok),
 // y = mixed * rs * g (rs precomputed per position), zero left padding, segment mask, valid mask.
 template <typename T>

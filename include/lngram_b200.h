@@ -250,11 +250,12 @@ int lng_attend_normalize(const float* l, const float* u, int64_t M, int32_t num_
 /* Head-space form of the same combine, for route shards whose partial values were projected per
  * head (o = W_v g_m u, [M, QH, HD] fp32): pack [M, QH, HD+1] = (o, l) * exp(m_local - m_glob), ready
  * for a SUM reduction across shards; lng_attend_unpack then writes head = pack[.., :HD] / pack[.., HD]
- * (the streaming readout's final division, lngram_v2.py:2066-2070) in f32 or bf16. */
+ * (the streaming readout's final division, lngram_v2.py:2066-2070) in f32 or bf16.  The pack is f32
+ * or bf16 (pack_dtype; bf16 halves the bytes a reduction moves between GPUs). */
 int lng_attend_pack(const float* m_local, const float* m_glob, const float* l, const float* o, int64_t M,
-                    int32_t num_heads, int32_t head_dim, float* pack, lng_stream_t stream);
-int lng_attend_unpack(const float* pack, int64_t M, int32_t num_heads, int32_t head_dim, void* head, int32_t dtype,
-                      lng_stream_t stream);
+                    int32_t num_heads, int32_t head_dim, void* pack, int32_t pack_dtype, lng_stream_t stream);
+int lng_attend_unpack(const void* pack, int32_t pack_dtype, int64_t M, int32_t num_heads, int32_t head_dim, void* head,
+                      int32_t dtype, lng_stream_t stream);
 
 /* ------------------------------------------------------------------ draft head (a12) */
 

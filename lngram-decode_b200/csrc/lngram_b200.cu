@@ -876,28 +876,40 @@ extern "C" int lng_attend_normalize(const float* l, const float* u, int64_t M, i
 }
 
 extern "C" int lng_attend_pack(const float* m_local, const float* m_glob, const float* l, const float* o, int64_t M,
-                               int32_t num_heads, int32_t head_dim, float* pack, lng_stream_t stream) {
+                               int32_t num_heads, int32_t head_dim, void* pack, int32_t pack_dtype, lng_stream_t stream) {
   LNG_REQUIRE(M >= 0 && num_heads > 0 && head_dim > 0, "bad shape");
   if (M == 0) return LNG_OK;
   LNG_REQUIRE(m_local && m_glob && l && o && pack, "NULL pointer");
   const int64_t MQ = M * num_heads;
-  attend_pack_kernel<<<grid_for(MQ * (head_dim + 1), 256, 16), 256, 0, S(stream)>>>(m_local, m_glob, l, o, MQ,
-                                                                                      head_dim, pack);
+  const int g = grid_for(MQ * (head_dim + 1), 256, 16);
+  if (pack_dtype == LNG_F32)
+    attend_pack_kernel<float><<<g, 256, 0, S(stream)>>>(m_local, m_glob, l, o, MQ, head_dim, static_cast<float*>(pack));
+  else if (pack_dtype == LNG_BF16)
+    attend_pack_kernel<__nv_bfloat16><<<g, 256, 0, S(stream)>>>(m_local, m_glob, l, o, MQ, head_dim,
+                                                                static_cast<__nv_bfloat16*>(pack));
+  else
+    return fail(LNG_ERR_ARGUMENT, "pack dtype must be f32 or bf16");
   LNG_LAUNCHED("attend_pack_kernel");
   return LNG_OK;
 }
 
-extern "C" int lng_attend_unpack(const float* pack, int64_t M, int32_t num_heads, int32_t head_dim, void* head,
-                                 int32_t dtype, lng_stream_t stream) {
+extern "C" int lng_attend_unpack(const void* pack, int32_t pack_dtype, int64_t M, int32_t num_heads, int32_t head_dim,
+                                 void* head, int32_t dtype, lng_stream_t stream) {
   LNG_REQUIRE(M >= 0 && num_heads > 0 && head_dim > 0, "bad shape");
   if (M == 0) return LNG_OK;
   LNG_REQUIRE(pack && head, "NULL pointer");
+  LNG_REQUIRE(pack_dtype == LNG_F32 || pack_dtype == LNG_BF16, "pack dtype must be f32 or bf16");
+  LNG_REQUIRE(dtype == LNG_F32 || dtype == LNG_BF16, "head dtype must be f32 or bf16");
   const int64_t MQ = M * num_heads;
   const int g = grid_for(MQ * head_dim, 256, 16);
-  if (dtype == LNG_F32) attend_unpack_kernel<float><<<g, 256, 0, S(stream)>>>(pack, MQ, head_dim, static_cast<float*>(head));
-  else if (dtype == LNG_BF16)
-    attend_unpack_kernel<__nv_bfloat16><<<g, 256, 0, S(stream)>>>(pack, MQ, head_dim, static_cast<__nv_bfloat16*>(head));
-  else return fail(LNG_ERR_ARGUMENT, "head dtype must be f32 or bf16");
+#define LNG_UNPACK(PT, OT) \
+  attend_unpack_kernel<PT, OT><<<g, 256, 0, S(stream)>>>(static_cast<const PT*>(pack), MQ, head_dim, static_cast<OT*>(head))
+  if (pack_dtype == LNG_F32) {
+    if (dtype == LNG_F32) LNG_UNPACK(float, float); else LNG_UNPACK(float, __nv_bfloat16);
+  } else {
+    if (dtype == LNG_F32) LNG_UNPACK(__nv_bfloat16, float); else LNG_UNPACK(__nv_bfloat16, __nv_bfloat16);
+  }
+#undef LNG_UNPACK
   LNG_LAUNCHED("attend_unpack_kernel");
   return LNG_OK;
 }

@@ -395,26 +395,27 @@ __global__ void attend_rescale_kernel(const float* __restrict__ m, const float* 
 
 // Route-shard combine in head space: pack[i, q, :HD] = o[i, q, :] * s, pack[i, q, HD] = l[i, q] * s
 // with s = exp(m_local - m_glob) (the streaming update of lngram_v2.py:1922-1942 across shards).
+template <typename PT>
 __global__ void attend_pack_kernel(const float* __restrict__ m, const float* __restrict__ mg,
                                    const float* __restrict__ l, const float* __restrict__ o, int64_t MQ, int HD,
-                                   float* __restrict__ pack) {
+                                   PT* __restrict__ pack) {
   const int64_t total = MQ * (HD + 1);
   for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < total; e += int64_t(gridDim.x) * blockDim.x) {
     const int64_t iq = e / (HD + 1);
     const int j = int(e % (HD + 1));
     const float s = expf(m[iq] - mg[iq]);
-    pack[e] = (j < HD ? o[iq * HD + j] : l[iq]) * s;
+    pack[e] = from_f32<PT>((j < HD ? o[iq * HD + j] : l[iq]) * s);
   }
 }
 
 // head[i, q, :] = pack[i, q, :HD] / pack[i, q, HD]  (the final division of lngram_v2.py:2066-2070)
-template <typename OT>
-__global__ void attend_unpack_kernel(const float* __restrict__ pack, int64_t MQ, int HD, OT* __restrict__ head) {
+template <typename PT, typename OT>
+__global__ void attend_unpack_kernel(const PT* __restrict__ pack, int64_t MQ, int HD, OT* __restrict__ head) {
   const int64_t total = MQ * HD;
   for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < total; e += int64_t(gridDim.x) * blockDim.x) {
     const int64_t iq = e / HD;
     const int j = int(e % HD);
-    head[e] = from_f32<OT>(pack[iq * (HD + 1) + j] / fmaxf(pack[iq * (HD + 1) + HD], 1.17549435e-38f));
+    head[e] = from_f32<OT>(to_f32(pack[iq * (HD + 1) + j]) / fmaxf(to_f32(pack[iq * (HD + 1) + HD]), 1.17549435e-38f));
   }
 }
 

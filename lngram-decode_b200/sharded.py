@@ -8,8 +8,8 @@ routes.  A forward over positions [B, T] (hidden states replicated on every rank
    partial mode: the online-softmax state (m, l, u) of the shard, the sink seeded on rank 0 only;
 3. ``all_reduce(MAX)`` of m, then each rank rescales (l, u) by exp(m_local - m_glob) into one
    packed buffer [M, QH, Dt + 1];
-4. ``reduce_scatter(SUM)`` of the packed buffer by whole-sequence blocks (B / world sequences per
-   rank), so the short conv needs no halo;
+4. ``reduce_scatter(SUM)`` of the packed buffer (bf16 for bf16 layers) by whole-sequence blocks
+   (B / world sequences per rank), so the short conv needs no halo;
 5. on the local block: u / l, the folded output map, the conv finish -> out [B / world, T, d].
 
 Steps 3-5 are the exact decomposition of the reference's streaming readout over route chunks
@@ -90,6 +90,7 @@ class RouteShardedMemory:
                                             dtype=torch.bfloat16)
             check(_lib.library().lng_router_prepare(ptr(self.router_w), self.router_w.shape[0], self.router_w.shape[1],
                                                     ptr(self.router_split), stream_ptr()), "router split")
+        self.pack_dtype = torch.bfloat16 if m._act() == torch.bfloat16 else torch.float32
         # b0 = log(R (1 - mass) / mass) of the whole layer (the local module's own is of its R_local)
         mass = m.sink_initial_active_mass
         self.sink_logit = math.log(self.R_total * (1.0 - mass) / mass)
@@ -118,23 +119,47 @@ class RouteShardedMemory:
         return t
 
     @torch.no_grad()
-    def forward(self, h: Tensor, router_x: Tensor) -> Tensor:
-        """h, router_x [B, T, *] (the same on every rank) -> this rank's block of B / world sequences."""
+    def forward(self, h: Tensor, router_x: Tensor, chunks: int = 1) -> Tensor:
+        """h, router_x [B, T, *] (the same on every rank) -> this rank's B / world sequences.
+
+        With ``chunks`` > 1 the batch is processed in that many groups of whole sequences, and each
+        group's reduce-scatter runs on NCCL's stream while the next group is gathered; the rank then
+        returns the r-th block of every group, in group order (chunks = 1: the r-th block of B)."""
         B, T, d = h.shape
-        if B % self.world:
-            raise ValueError("the batch must split into whole sequences per rank")
-        mloc, lloc, u = self.partial(h, router_x)
-        mglob = all_reduce_max(mloc.clone(), self.group)
-        pack = self.pack(mloc, mglob, lloc, u)
-        mine = reduce_scatter_rows(pack.view(B * T, -1), self.group)      # [B*T / world, QH * (Dt + 1)]
-        return self.finish(mine, B // self.world, T)
+        if B % (self.world * chunks):
+            raise ValueError("the batch must split into whole sequences per rank and chunk")
+        Bc = B // chunks
+        outs, pending = [], None
+        for c in range(chunks):
+            hc, xc = h[c * Bc:(c + 1) * Bc], router_x[c * Bc:(c + 1) * Bc]
+            mloc, lloc, u = self.partial(hc, xc)
+            mglob = all_reduce_max(mloc.clone(), self.group)
+            pack = self.pack(mloc, mglob, lloc, u).view(Bc * T, -1)
+            del mloc, lloc, u
+            if self.world > 1 and dist.is_initialized():
+                mine = torch.empty((Bc * T // self.world, pack.shape[1]), device=pack.device, dtype=pack.dtype)
+                work = dist.reduce_scatter_tensor(mine, pack, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
+            else:
+                mine, work = pack, None
+            if pending is not None:
+                outs.append(self._finish_pending(pending, T))
+            pending = (work, mine, pack)  # the pack stays referenced until its reduction is done
+        outs.append(self._finish_pending(pending, T))
+        return outs[0] if len(outs) == 1 else torch.cat(outs, 0)
+
+    def _finish_pending(self, pending, T: int) -> Tensor:
+        work, mine, _pack = pending
+        if work is not None:
+            work.wait()  # the current stream waits for the reduction
+        return self.finish(mine, mine.shape[0] // T, T)
 
     def pack(self, mloc: Tensor, mglob: Tensor, lloc: Tensor, u: Tensor) -> Tensor:
-        """(u, l) * exp(m_local - m_glob) packed [M, QH, Dt + 1] for the SUM reduction."""
+        """(u, l) * exp(m_local - m_glob) packed [M, QH, Dt + 1] for the SUM reduction, in the pack
+        dtype (bf16 for bf16 layers: half the bytes on NVLink; fp32 otherwise)."""
         M, QH, Dt = u.shape
-        pack = torch.empty(M, QH, Dt + 1, device=u.device, dtype=torch.float32)
+        pack = torch.empty(M, QH, Dt + 1, device=u.device, dtype=self.pack_dtype)
         check(_lib.library().lng_attend_pack(ptr(mloc), ptr(mglob), ptr(lloc), ptr(u), M, QH, Dt, ptr(pack),
-                                             stream_ptr()), "pack")
+                                             _lib.dtype_code(self.pack_dtype), stream_ptr()), "pack")
         return pack
 
     def finish(self, packed: Tensor, Bb: int, T: int) -> Tensor:
@@ -144,8 +169,9 @@ class RouteShardedMemory:
         QH, Dt = m.readout_num_heads, m.route_token_dim
         Mb = packed.shape[0]
         ub = torch.empty(Mb, QH * Dt, device=packed.device, dtype=act)
-        check(_lib.library().lng_attend_unpack(ptr(packed.contiguous()), Mb, QH, Dt, ptr(ub), _lib.dtype_code(act),
-                                               stream_ptr()), "unpack")
+        packed = packed.contiguous()
+        check(_lib.library().lng_attend_unpack(ptr(packed), _lib.dtype_code(packed.dtype), Mb, QH, Dt, ptr(ub),
+                                               _lib.dtype_code(act), stream_ptr()), "unpack")
         mixed = m._linear(ub, m.folded()["w_vo"])
         return m._conv_finish(mixed.view(Bb, T, m.hidden_size), None, None)
 

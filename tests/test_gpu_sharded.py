@@ -4,7 +4,7 @@
   only), combined through the pack / unpack kernels, equals the unsharded forward (fp32: 1e-5;
   bf16 SB shape: 1e-2).
 * Two GPUs (skipped with fewer): one process per GPU over NCCL; every rank's block of sequences
-  equals the single-GPU forward of those sequences.
+  equals the single-GPU forward of those sequences, also with two overlapped sequence groups.
 """
 
 from __future__ import annotations
@@ -136,13 +136,21 @@ def _rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
         inp = cases.memory_inputs("tiny")
         h = torch.from_numpy(inp["h"]).to(DEV)
         x = torch.from_numpy(inp["x"]).to(DEV)
+        shard = lngram.RouteShardedMemory(mem, rank, world)
         with torch.no_grad():
-            out = lngram.RouteShardedMemory(mem, rank, world).forward(h, x)
+            out = shard.forward(h, x)
             full = mem(h, x)
+            # two overlapped sequence groups over 4 sequences: rank r gets sequence r of each group
+            h4 = torch.cat((h, h.flip(1)), 0)
+            x4 = torch.cat((x, x.flip(1)), 0)
+            out4 = shard.forward(h4, x4, chunks=2)
+            full4 = mem(h4, x4)
         torch.cuda.synchronize()
         B = h.shape[0]
         blk = slice(rank * B // world, (rank + 1) * B // world)
         np.save(os.path.join(out_dir, f"rank{rank}.npy"), np.stack([out.cpu().numpy(), full[blk].cpu().numpy()]))
+        np.save(os.path.join(out_dir, f"rank{rank}_chunks.npy"),
+                np.stack([out4.cpu().numpy(), full4[[rank, 2 + rank]].cpu().numpy()]))
     finally:
         dist.destroy_process_group()
 
@@ -154,3 +162,5 @@ def test_two_gpu_route_sharded_forward(tmp_path):
     for r in range(2):
         got, want = np.load(tmp_path / f"rank{r}.npy")
         assert_fp32_close(got, want, what=f"rank {r} block")
+        got, want = np.load(tmp_path / f"rank{r}_chunks.npy")
+        assert_fp32_close(got, want, what=f"rank {r} blocks of two overlapped groups")

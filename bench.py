@@ -524,9 +524,10 @@ def run_sdb(args, rank, world, local) -> dict:
                    "ngrams": list(config["ngrams"]), "router": "embed2 (token only)", "sampling": "argmax",
                    "parallelism": f"replicas{world}",
                    "l2": "a 252 MB buffer is rewritten between timed steps (outside the step events)"},
-        "roofline": {"bound": "hbm", "kernel": "logits_chunk_topk_kernel (draft-head logits + top-1, bf16 vocab)",
+        "roofline": {"bound": "hbm", "kernel": "logits_tc_topk_kernel (draft-head logits + top-1 on tcgen05, bf16 vocab)",
                      "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
-                     "peak_source": pk["source"], "traffic": None, "bytes_per_launch": lk_bytes,
+                     "peak_source": pk["source"], "traffic": profiled_traffic("logits_tc", nseq),
+                     "bytes_per_launch": lk_bytes,
                      "ms_per_launch": lk_ms, "launches_per_step": gamma},
         "e2e": {"value": units / (e2e_ms / 1e3), "unit": "draft tokens/s", "h2d_bytes_per_step": nseq * plen * 8,
                 "d2h_bytes_per_step": nseq * gamma * 8, "ms_per_step": e2e_ms / args.steps},

@@ -78,7 +78,9 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+// SiLU with the fast exponential and divide (a few ulp, far inside the fp32 / bf16 output bars);
+// for x -> -inf the divisor overflows and the quotient is 0, the function's limit.
+__device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 // ------------------------------------------------------------------ mbarrier / bulk copies (sm_90+)
 // Round a byte count up to a multiple of 256 (sub-buffer alignment inside one allocation).

@@ -96,12 +96,18 @@ struct TcCfg {
   static constexpr uint32_t B_BYTES = BN * TC_BK * 2;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
-  static constexpr uint32_t TMEM_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+  // two accumulators (tile i and tile i + 1) of BN columns each, allocated as a power of two
+  static constexpr uint32_t TMEM_COLS = 2 * BN <= 32 ? 32 : 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
   static constexpr size_t SMEM = size_t(STAGES) * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
 
+// Persistent GEMM: one CTA per SM walks the output tiles (m-major, so neighbouring CTAs share A
+// rows in L2).  Warp 0 issues the TMA loads, warp 1 the MMAs into one of two TMEM accumulators,
+// warps 2-5 (one per TMEM lane quadrant) run the epilogue of tile i while the MMAs of tile i + 1
+// proceed.  All waits are bounded; an expired wait records DEV_ERR_WAIT_TIMEOUT and every role
+// leaves its loop.
 template <int BN, int MODE, int BITS = 1>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(192, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b, TcGemmParams p) {
   using Cfg = TcCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
@@ -109,18 +115,31 @@ __global__ void __launch_bounds__(128, 1)
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(base + size_t(STAGES) * Cfg::STAGE_BYTES);
   uint64_t* empty = full + STAGES;
-  uint64_t* acc_bar = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_bar + 1);
+  uint64_t* acc_full = empty + STAGES;   // [2] MMA commit: accumulator ready
+  uint64_t* acc_empty = acc_full + 2;    // [2] 128 epilogue arrivals: accumulator drained
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile uint32_t* abort_flag = tmem_slot + 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t m0 = int64_t(blockIdx.y) * TC_BM, n0 = int64_t(blockIdx.x) * BN;
+  const int64_t n_tiles = (p.N + BN - 1) / BN, m_tiles = (p.M + TC_BM - 1) / TC_BM;
+  const int64_t tiles = n_tiles * m_tiles;
   const int KB = int((p.K + TC_BK - 1) / TC_BK);
+  auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
+    if (*abort_flag) return false;
+    if (mbar_wait_bounded(bar, parity, &g_error_word, DEV_ERR_WAIT_TIMEOUT)) return true;
+    *abort_flag = 1u;
+    return false;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(acc_bar, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 128);
+    }
+    *abort_flag = 0u;
     fence_mbar_init();
     tma_prefetch_desc(&tma_a);
     tma_prefetch_desc(&tma_b);
@@ -135,111 +154,139 @@ __global__ void __launch_bounds__(128, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  bool ok = true;
 
-  if (warp == 0 && lane == 0) {
-    // TMA producer
-    for (int kb = 0; kb < KB && ok; ++kb) {
-      const int s = kb % STAGES;
-      if (kb >= STAGES) ok = mbar_wait_bounded(&empty[s], uint32_t(((kb / STAGES) - 1) & 1), &g_error_word, DEV_ERR_WAIT_TIMEOUT);
-      if (!ok) break;
-      mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
-      uint8_t* st = base + size_t(s) * Cfg::STAGE_BYTES;
-      const int32_t ka = int32_t((int64_t(kb) * TC_BK) % p.a_kperiod);
-      tma_load_2d(st, &tma_a, ka, int32_t(m0), &full[s]);
-      tma_load_2d(st + Cfg::A_BYTES, &tma_b, int32_t(kb * TC_BK), int32_t(n0), &full[s]);
+  if (warp == 0) {
+    if (lane == 0) {  // TMA producer over all tiles of this CTA
+      uint32_t it = 0;
+      for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+        const int64_t m0 = (t / n_tiles) * TC_BM, n0 = (t % n_tiles) * BN;
+        bool ok = true;
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s = int(it % STAGES);
+          if (it >= uint32_t(STAGES) && !wait(&empty[s], ((it / STAGES) - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+          uint8_t* st = base + size_t(s) * Cfg::STAGE_BYTES;
+          const int32_t ka = int32_t((int64_t(kb) * TC_BK) % p.a_kperiod);
+          tma_load_2d(st, &tma_a, ka, int32_t(m0), &full[s]);
+          tma_load_2d(st + Cfg::A_BYTES, &tma_b, int32_t(kb * TC_BK), int32_t(n0), &full[s]);
+        }
+        if (!ok) break;
+      }
     }
-  } else if (warp == 1 && lane == 0) {
-    // MMA issuer
-    constexpr uint32_t idesc = umma_idesc_bf16(TC_BM, BN);
-    for (int kb = 0; kb < KB && ok; ++kb) {
-      const int s = kb % STAGES;
-      ok = mbar_wait_bounded(&full[s], uint32_t((kb / STAGES) & 1), &g_error_word, DEV_ERR_WAIT_TIMEOUT);
-      if (!ok) break;
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer
+      constexpr uint32_t idesc = umma_idesc_bf16(TC_BM, BN);
+      uint32_t it = 0, ti = 0;
+      for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++ti) {
+        const uint32_t ab = ti & 1;
+        if (ti >= 2 && !wait(&acc_empty[ab], ((ti >> 1) - 1) & 1)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + ab * uint32_t(BN);
+        bool ok = true;
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s = int(it % STAGES);
+          if (!wait(&full[s], (it / STAGES) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint8_t* st = base + size_t(s) * Cfg::STAGE_BYTES;
+          const uint64_t da = umma_desc_sw128(st), db = umma_desc_sw128(st + Cfg::A_BYTES);
+#pragma unroll
+          for (int k = 0; k < TC_BK / 16; ++k)
+            // advance 16 bf16 = 32 bytes along K inside the swizzle atom (+2 in 16-byte units)
+            umma_bf16(d, da + uint64_t(2 * k), db + uint64_t(2 * k), idesc, (kb | k) != 0 ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[ab]);
+      }
+    }
+  } else {
+    // epilogue warps 2-5: warp w drains TMEM lanes 32 (w % 4) .. +31 = tile rows
+    const int q = warp & 3;
+    uint32_t ti = 0;
+    for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++ti) {
+      const uint32_t ab = ti & 1;
+      const int64_t m0 = (t / n_tiles) * TC_BM, n0 = (t % n_tiles) * BN;
+      const bool acc_ok = wait(&acc_full[ab], (ti >> 1) & 1);
+      __syncwarp();
       tc_fence_after();
-      const uint8_t* st = base + size_t(s) * Cfg::STAGE_BYTES;
-      const uint64_t da = umma_desc_sw128(st), db = umma_desc_sw128(st + Cfg::A_BYTES);
-#pragma unroll
-      for (int k = 0; k < TC_BK / 16; ++k) {
-        // advance 16 bf16 = 32 bytes along K inside the swizzle atom (+2 in 16-byte units)
-        umma_bf16(tmem, da + uint64_t(2 * k), db + uint64_t(2 * k), idesc, (kb | k) != 0 ? 1u : 0u);
-      }
-      umma_commit(&empty[s]);
-    }
-    umma_commit(acc_bar);
-  }
-  __syncwarp();
-  // epilogue: warp w owns TMEM lanes 32w..32w+31 = tile rows
-  const bool acc_ok = mbar_wait_bounded(acc_bar, 0u, &g_error_word, DEV_ERR_WAIT_TIMEOUT);
-  __syncwarp();
-  tc_fence_after();
-  const int64_t row = m0 + warp * 32 + lane;
-  const uint32_t tbase = tmem + (uint32_t(warp * 32) << 16);
-  if (__all_sync(0xffffffffu, acc_ok)) {
-    if constexpr (MODE == 0) {
-      const float sc = (p.rowscale && row < p.M) ? p.rowscale[row] : 1.f;
+      const int64_t row = m0 + q * 32 + lane;
+      const uint32_t tbase = tmem + (uint32_t(q * 32) << 16) + ab * uint32_t(BN);
+      if (__all_sync(0xffffffffu, acc_ok)) {
+        if constexpr (MODE == 0) {
+          const float sc = (p.rowscale && row < p.M) ? p.rowscale[row] : 1.f;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
-        float v[16];
-        tmem_ld16(tbase + uint32_t(c), v);
-        const int64_t col = n0 + c;
-        if (row >= p.M || col >= p.N) continue;
-        if (p.c_dtype == LNG_F32) {
-          float* dst = static_cast<float*>(p.C) + row * p.ldc + col;
-          if (col + 16 <= p.N) {
+          for (int c = 0; c < BN; c += 16) {
+            float v[16];
+            tmem_ld16(tbase + uint32_t(c), v);
+            const int64_t col = n0 + c;
+            if (row >= p.M || col >= p.N) continue;
+            if (p.c_dtype == LNG_F32) {
+              float* dst = static_cast<float*>(p.C) + row * p.ldc + col;
+              if (col + 16 <= p.N) {
 #pragma unroll
-            for (int i = 0; i < 16; i += 4)
-              *reinterpret_cast<float4*>(dst + i) = make_float4(v[i] * sc, v[i + 1] * sc, v[i + 2] * sc, v[i + 3] * sc);
-          } else {
-            for (int i = 0; i < 16 && col + i < p.N; ++i) dst[i] = v[i] * sc;
-          }
-        } else {
-          __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.C) + row * p.ldc + col;
-          if (col + 16 <= p.N) {
-            uint32_t w[8];
+                for (int i = 0; i < 16; i += 4)
+                  *reinterpret_cast<float4*>(dst + i) =
+                      make_float4(v[i] * sc, v[i + 1] * sc, v[i + 2] * sc, v[i + 3] * sc);
+              } else {
+                for (int i = 0; i < 16 && col + i < p.N; ++i) dst[i] = v[i] * sc;
+              }
+            } else {
+              __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.C) + row * p.ldc + col;
+              if (col + 16 <= p.N) {
+                uint32_t w[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              __nv_bfloat162 b2 = __floats2bfloat162_rn(v[2 * i] * sc, v[2 * i + 1] * sc);
-              w[i] = *reinterpret_cast<uint32_t*>(&b2);
+                for (int i = 0; i < 8; ++i) {
+                  __nv_bfloat162 b2 = __floats2bfloat162_rn(v[2 * i] * sc, v[2 * i + 1] * sc);
+                  w[i] = *reinterpret_cast<uint32_t*>(&b2);
+                }
+                *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+                *reinterpret_cast<uint4*>(dst + 8) = make_uint4(w[4], w[5], w[6], w[7]);
+              } else {
+                for (int i = 0; i < 16 && col + i < p.N; ++i) dst[i] = __float2bfloat16_rn(v[i] * sc);
+              }
             }
-            *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
-            *reinterpret_cast<uint4*>(dst + 8) = make_uint4(w[4], w[5], w[6], w[7]);
-          } else {
-            for (int i = 0; i < 16 && col + i < p.N; ++i) dst[i] = __float2bfloat16_rn(v[i] * sc);
+          }
+        } else {
+          // router: this tile holds routes r0 .. r0+RPT-1 (RPT * BITS logits per row); every index is
+          // static, so the codes are assembled in registers
+          constexpr int RPT = BN / BITS;
+          const int64_t r0 = n0 / BITS;
+          uint32_t packed[(RPT + 3) / 4];
+#pragma unroll
+          for (int i = 0; i < (RPT + 3) / 4; ++i) packed[i] = 0u;
+#pragma unroll
+          for (int c = 0; c < BN; c += 16) {
+            float v[16];
+            tmem_ld16(tbase + uint32_t(c), v);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int col = c + i, qq = col / BITS, bit = col % BITS;
+              packed[qq >> 2] |= uint32_t(v[i] > 0.f ? 1u : 0u) << ((qq & 3) * 8 + bit);
+            }
+          }
+          if (row < p.M) {
+            uint8_t* dst = p.codes + row * p.routes + r0;
+            const int64_t left = p.routes - r0;
+            const int nr = int(left < RPT ? left : RPT);
+            if (nr == RPT && RPT % 4 == 0 && (p.routes & 3) == 0 && (r0 & 3) == 0) {
+#pragma unroll
+              for (int i = 0; i < RPT / 4; ++i) reinterpret_cast<uint32_t*>(dst)[i] = packed[i];
+            } else {
+#pragma unroll
+              for (int i = 0; i < RPT; ++i)
+                if (i < nr) dst[i] = uint8_t(packed[i >> 2] >> ((i & 3) * 8));
+            }
           }
         }
       }
-    } else {
-      // router: this tile holds routes r0 .. r0+RPT-1 (RPT * BITS logits per row); every index is
-      // static, so the codes are assembled in registers
-      constexpr int RPT = BN / BITS;
-      const int64_t r0 = n0 / BITS;
-      uint32_t packed[(RPT + 3) / 4];
-#pragma unroll
-      for (int i = 0; i < (RPT + 3) / 4; ++i) packed[i] = 0u;
-#pragma unroll
-      for (int c = 0; c < BN; c += 16) {
-        float v[16];
-        tmem_ld16(tbase + uint32_t(c), v);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int col = c + i, q = col / BITS, bit = col % BITS;
-          packed[q >> 2] |= uint32_t(v[i] > 0.f ? 1u : 0u) << ((q & 3) * 8 + bit);
-        }
-      }
-      if (row < p.M) {
-        uint8_t* dst = p.codes + row * p.routes + r0;
-        const int64_t left = p.routes - r0;
-        const int nr = int(left < RPT ? left : RPT);
-        if (nr == RPT && RPT % 4 == 0 && (p.routes & 3) == 0 && (r0 & 3) == 0) {
-#pragma unroll
-          for (int i = 0; i < RPT / 4; ++i) reinterpret_cast<uint32_t*>(dst)[i] = packed[i];
-        } else {
-#pragma unroll
-          for (int i = 0; i < RPT; ++i)
-            if (i < nr) dst[i] = uint8_t(packed[i >> 2] >> ((i & 3) * 8));
-        }
-      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[ab]);
     }
   }
   tc_fence_before();
@@ -291,8 +338,9 @@ inline int launch_tc_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const Tc
   auto kern = tc_gemm_kernel<BN, MODE, BITS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(TcCfg<BN>::SMEM));
   if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(tc_gemm_kernel)");
-  dim3 grid(unsigned((p.N + BN - 1) / BN), unsigned((p.M + TC_BM - 1) / TC_BM));
-  kern<<<grid, 128, TcCfg<BN>::SMEM, stream>>>(ta, tb, p);
+  const int64_t tiles = ((p.N + BN - 1) / BN) * ((p.M + TC_BM - 1) / TC_BM);
+  const int grid = int(tiles < num_sms() ? tiles : num_sms());
+  kern<<<grid, 192, TcCfg<BN>::SMEM, stream>>>(ta, tb, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_status(e, "tc_gemm_kernel launch");
   return LNG_OK;

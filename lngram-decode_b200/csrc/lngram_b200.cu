@@ -614,6 +614,7 @@ static int conv_finish_ws(const lng_readout* ro, const void* mixed, int64_t B, i
                     (reinterpret_cast<uintptr_t>(conv_in) & 15) == 0;
   const int tile_ch = ro->act_dtype == LNG_F32 ? 128 : 256;
   if (ro->conv_kernel == 4 && 3 * ro->conv_dilation <= CT_HMAX && ro->hidden % tile_ch == 0 && al16 &&
+      M < (int64_t(1) << 31) &&
       (ro->act_dtype == LNG_F32 || ro->act_dtype == LNG_BF16)) {
     const size_t smem = size_t(CT_TP + CT_HMAX) * 32 * 16 + size_t(CT_TP + CT_HMAX) * 4;
     const dim3 grid(unsigned(ceil_div(M, CT_TP)), unsigned(ro->hidden / tile_ch));
@@ -621,10 +622,10 @@ static int conv_finish_ws(const lng_readout* ro, const void* mixed, int64_t B, i
     LNG_CUDA(cudaFuncSetAttribute(conv_tile_kernel<__nv_bfloat16, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   int(smem)));
     if (ro->act_dtype == LNG_F32)
-      conv_tile_kernel<float, 4><<<grid, 256, smem, stream>>>(cp, static_cast<const float*>(mixed), rs, M, T, seg, valid,
+      conv_tile_kernel<float, 4><<<grid, 128, smem, stream>>>(cp, static_cast<const float*>(mixed), rs, M, T, seg, valid,
                                                               static_cast<float*>(out), static_cast<float*>(conv_in));
     else
-      conv_tile_kernel<__nv_bfloat16, 4><<<grid, 256, smem, stream>>>(
+      conv_tile_kernel<__nv_bfloat16, 4><<<grid, 128, smem, stream>>>(
           cp, static_cast<const __nv_bfloat16*>(mixed), rs, M, T, seg, valid, static_cast<__nv_bfloat16*>(out),
           static_cast<__nv_bfloat16*>(conv_in));
     LNG_LAUNCHED("conv_tile_kernel");

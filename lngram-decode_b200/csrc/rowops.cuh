@@ -81,11 +81,13 @@ struct ConvParams {
   const float* bias;    // [d] or null
 };
 
-// Sequence-mode conv finish on a shared-memory tile (the form used for whole batches): a CTA takes
-// CT_TP consecutive positions x 512 bytes of channels plus the (k-1)*dil halo positions before
-// them, loaded once with 16-byte coalesced loads; each output position then reads its k taps from
-// shared memory.  Semantics as conv_seq_kernel below (zero left padding, segment mask, valid mask).
-constexpr int CT_TP = 64;    // positions per tile
+// Sequence-mode conv finish on a shared-memory tile (the form used for whole batches): a 128-thread
+// CTA takes CT_TP consecutive positions x 512 bytes of channels plus the (k-1)*dil halo positions
+// before them, copied once into shared memory with 16-byte cp.async (no register staging, so six
+// CTAs fit an SM and their loads overlap each other's math); each output position then reads its k
+// taps from shared memory.  Semantics as conv_seq_kernel below (zero left padding, segment mask,
+// valid mask).
+constexpr int CT_TP = 32;    // positions per tile
 constexpr int CT_HMAX = 32;  // largest halo (k-1)*dil the tile holds
 
 template <typename T>
@@ -117,39 +119,36 @@ __device__ __forceinline__ uint4 pack16(const float (&v)[16 / sizeof(T)]) {
 }
 
 template <typename T, int K>
-__global__ void __launch_bounds__(256) conv_tile_kernel(ConvParams cp, const T* __restrict__ mixed,
+__global__ void __launch_bounds__(128) conv_tile_kernel(ConvParams cp, const T* __restrict__ mixed,
                                                         const float* __restrict__ rs, int64_t M, int64_t T_,
                                                         const int64_t* __restrict__ seg,
                                                         const uint8_t* __restrict__ valid, T* __restrict__ out,
                                                         T* __restrict__ conv_in) {
-  constexpr int VEC = 16 / int(sizeof(T));         // channels per 16-byte chunk
-  constexpr int CH = 32 * VEC;                      // channels per tile (512 bytes)
-  constexpr int LOADS = (CT_TP + CT_HMAX) * 32 / 256;
-  extern __shared__ uint4 ct_tile[];                // [rows][32 chunks]
+  constexpr int VEC = 16 / int(sizeof(T));  // channels per 16-byte chunk
+  constexpr int CH = 32 * VEC;               // channels per tile (512 bytes)
+  extern __shared__ uint4 ct_tile[];         // [rows][32 chunks]
   float* rsh = reinterpret_cast<float*>(ct_tile + (CT_TP + CT_HMAX) * 32);
   const int H = (K - 1) * cp.dil;
   const int rows = CT_TP + H;
   const int64_t p0 = int64_t(blockIdx.x) * CT_TP, base = p0 - H;
   const int64_t c0 = int64_t(blockIdx.y) * CH;
   const int tid = threadIdx.x, lane = tid & 31, pr = tid >> 5;
-  uint4 ld[LOADS];
-#pragma unroll
-  for (int i = 0; i < LOADS; ++i) {  // all loads in flight together, then to shared memory
-    const int e = tid + i * 256, r = e >> 5, ch = e & 31;
+  const uint32_t tile_s = static_cast<uint32_t>(__cvta_generic_to_shared(ct_tile));
+  for (int e = tid; e < rows * 32; e += 128) {
+    const int r = e >> 5, ch = e & 31;
     const int64_t q = base + r;
-    ld[i] = (r < rows && q >= 0 && q < M) ? *reinterpret_cast<const uint4*>(mixed + q * cp.d + c0 + ch * VEC)
-                                          : make_uint4(0, 0, 0, 0);
+    const bool in = q >= 0 && q < M;
+    const T* src = mixed + (in ? q * cp.d + c0 + ch * VEC : 0);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(tile_s + uint32_t(e) * 16u), "l"(src),
+                 "r"(in ? 16u : 0u)
+                 : "memory");
   }
-  for (int r = tid; r < rows; r += 256) {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  for (int r = tid; r < rows; r += 128) {
     const int64_t q = base + r;
     rsh[r] = (q >= 0 && q < M) ? rs[q] : 0.f;
   }
-#pragma unroll
-  for (int i = 0; i < LOADS; ++i) {
-    const int e = tid + i * 256;
-    if (e < rows * 32) ct_tile[e] = ld[i];
-  }
-  __syncthreads();
+  // per-channel parameters, with the norm weight folded into the taps
   const int64_t cc = c0 + lane * VEC;  // this thread's channels
   float gw[VEC], wt[K][VEC], bias[VEC];
 #pragma unroll
@@ -157,12 +156,15 @@ __global__ void __launch_bounds__(256) conv_tile_kernel(ConvParams cp, const T* 
     gw[j] = cp.norm_w[cc + j];
     bias[j] = cp.bias ? cp.bias[cc + j] : 0.f;
 #pragma unroll
-    for (int tap = 0; tap < K; ++tap) wt[tap][j] = cp.weight[(cc + j) * K + tap];
+    for (int tap = 0; tap < K; ++tap) wt[tap][j] = cp.weight[(cc + j) * K + tap] * gw[j];
   }
-  for (int i = pr; i < CT_TP; i += 8) {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
+  const uint32_t Tu = uint32_t(T_);  // M < 2^31 (checked by the host): 32-bit position arithmetic
+  for (int i = pr; i < CT_TP; i += 4) {
     const int64_t pos = p0 + i;
     if (pos >= M) break;
-    const int64_t t = pos % T_;
+    const int t = int(uint32_t(pos) % Tu);
     float acc[VEC], self[VEC];
 #pragma unroll
     for (int j = 0; j < VEC; ++j) acc[j] = bias[j];
@@ -179,7 +181,7 @@ __global__ void __launch_bounds__(256) conv_tile_kernel(ConvParams cp, const T* 
       if (t - lag >= 0 && (!seg || seg[pos - lag] == seg[pos])) {
         const float rq = rsh[r];
 #pragma unroll
-        for (int j = 0; j < VEC; ++j) acc[j] = fmaf(wt[tap][j], v[j] * rq * gw[j], acc[j]);
+        for (int j = 0; j < VEC; ++j) acc[j] = fmaf(wt[tap][j], v[j] * rq, acc[j]);
       }
     }
     const bool keep = !valid || valid[pos];

@@ -30,6 +30,16 @@ struct TcGemmParams {
   int bits;              // MODE 1
   int64_t routes;        // MODE 1
   uint8_t* codes;        // MODE 1, [M, routes]
+  // Operand parts (npairs > 0): the reduction runs over npairs products A_part . B_part^T, each
+  // part_k long; k block kb reads A at x = a_part[kb / pkb] * part_k + (kb % pkb) * 64 and B at
+  // b_part[..] likewise (pkb = part_k / 64).  K is then npairs * part_k.
+  int npairs;
+  int a_part[8], b_part[8];
+  int64_t part_k;
+  // Split-K (splits > 1, MODE 0): the k blocks are divided into `splits` ranges and range s writes
+  // its partial product to C + s * split_stride (fp32).
+  int splits;
+  int64_t split_stride;
 };
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, uint64_t* bar) {
@@ -121,8 +131,19 @@ __global__ void __launch_bounds__(192, 1)
   volatile uint32_t* abort_flag = tmem_slot + 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t n_tiles = (p.N + BN - 1) / BN, m_tiles = (p.M + TC_BM - 1) / TC_BM;
-  const int64_t tiles = n_tiles * m_tiles;
+  const int splits = p.splits > 1 ? p.splits : 1;
+  const int64_t mn_tiles = n_tiles * m_tiles, tiles = mn_tiles * splits;
   const int KB = int((p.K + TC_BK - 1) / TC_BK);
+  const int pkb = p.npairs > 0 ? int(p.part_k / TC_BK) : 1;
+  // tile t -> (split, m, n) and its k-block range
+  auto tile_of = [&](int64_t t, int64_t& m0, int64_t& n0, int& kb0, int& kb1, int& sp) {
+    sp = int(t / mn_tiles);
+    const int64_t r = t - int64_t(sp) * mn_tiles;
+    m0 = (r / n_tiles) * TC_BM;
+    n0 = (r % n_tiles) * BN;
+    kb0 = int(int64_t(KB) * sp / splits);
+    kb1 = int(int64_t(KB) * (sp + 1) / splits);
+  };
   auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
     if (*abort_flag) return false;
     if (mbar_wait_bounded(bar, parity, &g_error_word, DEV_ERR_WAIT_TIMEOUT)) return true;
@@ -159,9 +180,11 @@ __global__ void __launch_bounds__(192, 1)
     if (lane == 0) {  // TMA producer over all tiles of this CTA
       uint32_t it = 0;
       for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
-        const int64_t m0 = (t / n_tiles) * TC_BM, n0 = (t % n_tiles) * BN;
+        int64_t m0, n0;
+        int kb0, kb1, sp;
+        tile_of(t, m0, n0, kb0, kb1, sp);
         bool ok = true;
-        for (int kb = 0; kb < KB; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = int(it % STAGES);
           if (it >= uint32_t(STAGES) && !wait(&empty[s], ((it / STAGES) - 1) & 1)) {
             ok = false;
@@ -169,9 +192,17 @@ __global__ void __launch_bounds__(192, 1)
           }
           mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
           uint8_t* st = base + size_t(s) * Cfg::STAGE_BYTES;
-          const int32_t ka = int32_t((int64_t(kb) * TC_BK) % p.a_kperiod);
+          int32_t ka, kbx;
+          if (p.npairs > 0) {
+            const int pr = kb / pkb, kk = (kb - pr * pkb) * TC_BK;
+            ka = int32_t(p.a_part[pr] * p.part_k + kk);
+            kbx = int32_t(p.b_part[pr] * p.part_k + kk);
+          } else {
+            ka = int32_t((int64_t(kb) * TC_BK) % p.a_kperiod);
+            kbx = int32_t(kb * TC_BK);
+          }
           tma_load_2d(st, &tma_a, ka, int32_t(m0), &full[s]);
-          tma_load_2d(st + Cfg::A_BYTES, &tma_b, int32_t(kb * TC_BK), int32_t(n0), &full[s]);
+          tma_load_2d(st + Cfg::A_BYTES, &tma_b, kbx, int32_t(n0), &full[s]);
         }
         if (!ok) break;
       }
@@ -182,11 +213,14 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t it = 0, ti = 0;
       for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++ti) {
         const uint32_t ab = ti & 1;
+        int64_t m0, n0;
+        int kb0, kb1, sp;
+        tile_of(t, m0, n0, kb0, kb1, sp);
         if (ti >= 2 && !wait(&acc_empty[ab], ((ti >> 1) - 1) & 1)) break;
         tc_fence_after();
         const uint32_t d = tmem + ab * uint32_t(BN);
         bool ok = true;
-        for (int kb = 0; kb < KB; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = int(it % STAGES);
           if (!wait(&full[s], (it / STAGES) & 1)) {
             ok = false;
@@ -198,7 +232,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int k = 0; k < TC_BK / 16; ++k)
             // advance 16 bf16 = 32 bytes along K inside the swizzle atom (+2 in 16-byte units)
-            umma_bf16(d, da + uint64_t(2 * k), db + uint64_t(2 * k), idesc, (kb | k) != 0 ? 1u : 0u);
+            umma_bf16(d, da + uint64_t(2 * k), db + uint64_t(2 * k), idesc, (kb != kb0 || k != 0) ? 1u : 0u);
           umma_commit(&empty[s]);
         }
         if (!ok) break;
@@ -211,7 +245,9 @@ __global__ void __launch_bounds__(192, 1)
     uint32_t ti = 0;
     for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++ti) {
       const uint32_t ab = ti & 1;
-      const int64_t m0 = (t / n_tiles) * TC_BM, n0 = (t % n_tiles) * BN;
+      int64_t m0, n0;
+      int kb0, kb1, sp;
+      tile_of(t, m0, n0, kb0, kb1, sp);
       const bool acc_ok = wait(&acc_full[ab], (ti >> 1) & 1);
       __syncwarp();
       tc_fence_after();
@@ -227,7 +263,7 @@ __global__ void __launch_bounds__(192, 1)
             const int64_t col = n0 + c;
             if (row >= p.M || col >= p.N) continue;
             if (p.c_dtype == LNG_F32) {
-              float* dst = static_cast<float*>(p.C) + row * p.ldc + col;
+              float* dst = static_cast<float*>(p.C) + int64_t(sp) * p.split_stride + row * p.ldc + col;
               if (col + 16 <= p.N) {
 #pragma unroll
                 for (int i = 0; i < 16; i += 4)
@@ -335,10 +371,14 @@ inline int make_tmap_bf16(CUtensorMap* map, const void* ptr, int64_t rows, int64
 
 template <int BN, int MODE, int BITS = 1>
 inline int launch_tc_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const TcGemmParams& p, cudaStream_t stream) {
+  // the MODE 0 epilogue stores 16-byte vectors: rows and split slices must keep that alignment
+  if (MODE == 0 && ((reinterpret_cast<uintptr_t>(p.C) & 15) || p.ldc % (p.c_dtype == LNG_F32 ? 4 : 8) ||
+                    p.split_stride % (p.c_dtype == LNG_F32 ? 4 : 8)))
+    return fail(LNG_ERR_ARGUMENT, "tc_gemm: output base / row stride not 16-byte aligned");
   auto kern = tc_gemm_kernel<BN, MODE, BITS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(TcCfg<BN>::SMEM));
   if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(tc_gemm_kernel)");
-  const int64_t tiles = ((p.N + BN - 1) / BN) * ((p.M + TC_BM - 1) / TC_BM);
+  const int64_t tiles = ((p.N + BN - 1) / BN) * ((p.M + TC_BM - 1) / TC_BM) * (p.splits > 1 ? p.splits : 1);
   const int grid = int(tiles < num_sms() ? tiles : num_sms());
   kern<<<grid, 192, TcCfg<BN>::SMEM, stream>>>(ta, tb, p);
   e = cudaGetLastError();

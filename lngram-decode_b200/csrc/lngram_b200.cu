@@ -19,6 +19,8 @@
 #include "rowops.cuh"
 #include "topk.cuh"
 
+static int scratch_alloc(void** p, size_t bytes, cudaStream_t stream);
+
 namespace lng {
 
 static thread_local std::string t_last_error;
@@ -133,6 +135,96 @@ extern "C" int lng_quantize_route_logits(const float* logits, int64_t n, int64_t
   return LNG_OK;
 }
 
+namespace lng {
+// Sign-packed codes from split-K partial logits [splits, routes * bits, ldp >= n] (split order sum).
+template <typename CodeT>
+__global__ void router_reduce_pack_kernel(const float* __restrict__ part, int splits, int64_t n, int64_t ldp,
+                                          int64_t routes, int bits, CodeT* __restrict__ codes,
+                                          float* __restrict__ logits) {
+  const int64_t total = n * routes;
+  const int64_t cols = routes * bits;
+  for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < total; e += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t row = e % n, r = e / n;  // consecutive threads: consecutive rows (coalesced partial reads)
+    int v = 0;
+    for (int j = 0; j < bits; ++j) {
+      float acc = 0.f;
+      for (int sp = 0; sp < splits; ++sp) acc += part[(int64_t(sp) * cols + r * bits + j) * ldp + row];
+      v |= (acc > 0.f ? 1 : 0) << j;
+      if (logits) logits[row * cols + r * bits + j] = acc;
+    }
+    codes[row * routes + r] = static_cast<CodeT>(v);
+  }
+}
+
+// fp32 router for few rows on the tensor cores: x = x1 + x2 + x3 and W = W1 + W2 + W3 split into
+// bf16 parts (each exact to ~2^-24 relative), logits^T = sum of the six products x_i . W_j^T with
+// i + j <= 4 (the dropped ones are below 2^-24 of |x| |W|), as one split-K GEMM with the logit
+// columns as M (so few rows still fill the GPU), partial sums reduced in a fixed order.
+// Scratch (x parts, W parts, partials) comes from the library pool and is released on `stream`.
+static int tc_router_small_f32(const float* x, int64_t n, int64_t in_dim, int64_t x_stride, const float* w,
+                               int64_t routes, int32_t bits, void* codes, int codes_i32, float* logits,
+                              cudaStream_t stream) {
+  if (in_dim % TC_BK != 0 || x_stride != in_dim || n < 1 || n > 256 || (reinterpret_cast<uintptr_t>(x) & 15))
+    return LNG_ERR_UNSUPPORTED;
+  const int64_t cols = routes * bits;
+  const int64_t m_tiles = (cols + TC_BM - 1) / TC_BM;
+  const int npairs = 6;
+  const int64_t KB = npairs * (in_dim / TC_BK);
+  int splits = int((num_sms() + m_tiles - 1) / m_tiles);
+  if (splits > KB) splits = int(KB);
+  const int BN = n <= 64 ? 64 : n <= 128 ? 128 : 256;
+  const int64_t ldp = (n + 3) & ~int64_t(3);  // partial rows padded so the epilogue's 16-byte stores stay aligned
+  const size_t xs_b = al256(size_t(n) * 3 * in_dim * 2), ws_b = al256(size_t(cols) * 3 * in_dim * 2),
+               ps_b = al256(size_t(splits) * cols * ldp * 4);
+  void* scratch = nullptr;
+  int st = scratch_alloc(&scratch, xs_b + ws_b + ps_b, stream);
+  if (st) return st;
+  auto* xs = static_cast<__nv_bfloat16*>(scratch);
+  auto* ws = reinterpret_cast<__nv_bfloat16*>(static_cast<unsigned char*>(scratch) + xs_b);
+  auto* ps = reinterpret_cast<float*>(static_cast<unsigned char*>(scratch) + xs_b + ws_b);
+  split_rows_bf16x3_kernel<<<grid_for(n * in_dim, 256, 16), 256, 0, stream>>>(x, n, in_dim, xs);
+  split_bf16x3_kernel<<<grid_for(cols * in_dim, 256, 16), 256, 0, stream>>>(w, cols, in_dim, ws);
+  CUtensorMap ta, tb;
+  st = make_tmap_bf16(&ta, ws, cols, 3 * in_dim, 3 * in_dim, TC_BM);
+  if (!st) st = make_tmap_bf16(&tb, xs, n, 3 * in_dim, 3 * in_dim, BN);
+  if (!st) {
+    TcGemmParams p{};
+    p.M = cols;
+    p.N = n;
+    p.K = npairs * in_dim;
+    p.a_kperiod = p.K;
+    p.C = ps;
+    p.ldc = ldp;
+    p.c_dtype = LNG_F32;
+    p.npairs = npairs;
+    const int ap[6] = {0, 1, 2, 0, 1, 0}, bp[6] = {0, 0, 0, 1, 1, 2};  // (W_j, x_i)
+    for (int i = 0; i < npairs; ++i) {
+      p.a_part[i] = ap[i];
+      p.b_part[i] = bp[i];
+    }
+    p.part_k = in_dim;
+    p.splits = splits;
+    p.split_stride = cols * ldp;
+    st = BN == 64 ? launch_tc_gemm<64, 0>(ta, tb, p, stream)
+                  : BN == 128 ? launch_tc_gemm<128, 0>(ta, tb, p, stream) : launch_tc_gemm<256, 0>(ta, tb, p, stream);
+  }
+  if (!st) {
+    const int g = grid_for(n * routes, 256, 8);
+    if (codes_i32)
+      router_reduce_pack_kernel<int32_t><<<g, 256, 0, stream>>>(ps, splits, n, ldp, routes, bits,
+                                                                static_cast<int32_t*>(codes), logits);
+    else
+      router_reduce_pack_kernel<uint8_t><<<g, 256, 0, stream>>>(ps, splits, n, ldp, routes, bits,
+                                                                static_cast<uint8_t*>(codes), logits);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) st = cuda_status(e, "router_reduce_pack_kernel");
+  }
+  cudaFreeAsync(scratch, stream);
+  return st;
+}
+
+}  // namespace lng
+
 extern "C" int lng_route_codes(const void* x, int32_t x_dtype, int64_t n, int64_t in_dim, int64_t x_stride,
                                const float* weight, int64_t routes, int32_t bits, void* codes, int32_t codes_dtype,
                                float* logits, lng_stream_t stream) {
@@ -145,6 +237,12 @@ extern "C" int lng_route_codes(const void* x, int32_t x_dtype, int64_t n, int64_
   if (x_dtype == LNG_BF16 && codes_dtype == LNG_U8 && logits == nullptr) {
     const int st = tc_router_codes(static_cast<const __nv_bfloat16*>(x), n, in_dim, x_stride, weight, routes, bits,
                                    static_cast<uint8_t*>(codes), S(stream));
+    if (st != LNG_ERR_UNSUPPORTED) return st;
+  }
+  if (x_dtype == LNG_F32 && n <= 256) {
+    // few fp32 rows: six bf16 split products on the tensor cores, split-K over the GPU
+    const int st = tc_router_small_f32(static_cast<const float*>(x), n, in_dim, x_stride, weight, routes, bits, codes,
+                                       codes_dtype == LNG_I32, logits, S(stream));
     if (st != LNG_ERR_UNSUPPORTED) return st;
   }
   if (ceil_div(n, RT_ROWS) * ceil_div(routes, RT_ROUTES) < 2 * 148 && ceil_div(n, RS_ROWS) < 65536) {

@@ -818,6 +818,7 @@ def run_scaled(args, rank, world, local) -> dict:
                                                                 u.data_ptr(), lib.F32, 1, ml.data_ptr(),
                                                                 ll.data_ptr(), s)), 3)
         del u, qa
+        phases = time_scaled_phases(pkg, shard, h, hn, world) if world > 1 else None
         launches = count_launches(lambda: step(0), fallback=0)
         dev_err = lib.device_error(clear=True)
     if dev_err:
@@ -843,8 +844,40 @@ def run_scaled(args, rank, world, local) -> dict:
                      "peak_source": pk["source"], "traffic": None, "bytes_per_launch": att_bytes,
                      "ms_per_launch": att_ms},
         "gpu_launches": launches["per_step"] * args.steps, "launch_count": launches,
+        "phases_ms": phases,
         "clocks": clk.summary(),
     }
+
+
+def time_scaled_phases(pkg, shard, h, hn, world) -> dict:
+    """Max-over-ranks CUDA-event time of each phase of the route-sharded forward on one sequence group,
+    run back to back without overlap, scaled to the whole batch (the step overlaps the exchange)."""
+    B, T = h.shape[:2]
+    Bc = B // SCALED_CHUNKS
+    hc, xc = h[:Bc], hn[:Bc]
+    m = shard.full.module
+    res = {}
+
+    def tm(name, fn):
+        fn()
+        torch.cuda.synchronize()
+        barrier(world)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        out = fn()
+        b.record()
+        torch.cuda.synchronize()
+        res[name] = round(max_over_ranks(a.elapsed_time(b), world) * SCALED_CHUNKS, 3)
+        return out
+
+    f = m.folded()
+    tm("query_gemm (replicated)", lambda: m._linear(hc.reshape(Bc * T, -1), f["w_qk"]))
+    mloc, lloc, u = tm("partial (codes + rms + query gemm + gather)", lambda: shard.partial(hc, xc))
+    mg = tm("all_reduce_max", lambda: pkg.sharded.all_reduce_max(mloc.clone()))
+    pack = tm("pack", lambda: shard.pack(mloc, mg, lloc, u))
+    mine = tm("reduce_scatter", lambda: pkg.sharded.reduce_scatter_rows(pack.view(Bc * T, -1)))
+    tm("finish (unpack + output gemm + conv)", lambda: shard.finish(mine, Bc // world, T))
+    return res
 
 
 # --------------------------------------------------------------------------- CPU baseline / reference arm

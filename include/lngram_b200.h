@@ -181,7 +181,11 @@ int lng_fold_readout(int64_t d, int64_t Dt, int32_t num_heads, int32_t num_kv_he
  * partial == 1 or 2: the online-softmax state of these routes is written instead -- m [M, QH] and
  * l [M, QH] (fp32) and the unnormalised u in fp32 -- with the sink seeded in (1) or left out (2),
  * so that route shards (one of them with the sink) combine exactly as the streaming readout does
- * (lngram_v2.py:1944-2070); qa then has the tables' dtype (16-bit tables) or f32. */
+ * (lngram_v2.py:1944-2070); qa then has the tables' dtype (16-bit tables) or f32.
+ * partial == 3 or 4 (16-bit tables): the same state as 1 / 2, written as the bf16 pack
+ * [M, QH, Dt + 1] = (u, l) of lng_attend_pack plus m [M, QH]; the tensor-core kernel starts every
+ * shard from the offset b0, so after the max all-reduce of m the packs of all shards usually share
+ * one scale (lng_attend_pack_rescale fixes the rows that do not) and sum directly. */
 int lng_route_attend(const lng_tables* tables, const void* codes, int32_t codes_dtype, int64_t B, int64_t T,
                      int64_t window, const int64_t* segment_ids, const uint8_t* valid_tokens, const int32_t* seg,
                      int64_t target_length, int64_t route_start, int64_t route_end, int32_t num_heads, float eps,
@@ -256,6 +260,10 @@ int lng_attend_pack(const float* m_local, const float* m_glob, const float* l, c
                     int32_t num_heads, int32_t head_dim, void* pack, int32_t pack_dtype, lng_stream_t stream);
 int lng_attend_unpack(const void* pack, int32_t pack_dtype, int64_t M, int32_t num_heads, int32_t head_dim, void* head,
                       int32_t dtype, lng_stream_t stream);
+/* pack[i, q, :] *= exp(m_local[i, q] - m_glob[i, q]) for the rows where the two differ (packs written
+ * by lng_route_attend partial 3 / 4), in place. */
+int lng_attend_pack_rescale(const float* m_local, const float* m_glob, int64_t M, int32_t num_heads, int32_t head_dim,
+                            void* pack, int32_t pack_dtype, lng_stream_t stream);
 
 /* ------------------------------------------------------------------ draft head (a12) */
 

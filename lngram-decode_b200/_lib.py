@@ -92,6 +92,7 @@ SIGNATURES = {
     "lng_attend_normalize": (C.c_int, [P, P, i64, i32, i64, P, i32, P]),
     "lng_attend_pack": (C.c_int, [P, P, P, P, i64, i32, i32, P, i32, P]),
     "lng_attend_unpack": (C.c_int, [P, i32, i64, i32, i32, P, i32, P]),
+    "lng_attend_pack_rescale": (C.c_int, [P, P, i64, i32, i32, P, i32, P]),
     "lng_logits_topk": (C.c_int, [P, i64, i64, P, i32, i64, i32, P, P, P, P, sz, P]),
     "lng_logits_topk_scratch_bytes": (sz, [i64, i64, i64, i32]),
     "lng_logits_topk_static": (C.c_int, [P, i64, i64, P, i32, i64, i32, P, P, P, P]),

@@ -229,7 +229,8 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
   const int64_t nwarps = int64_t(gridDim.x) * WARPS;
   const int64_t my_items = gwarp < p.M ? (p.M - 1 - gwarp) / nwarps + 1 : 0;
   const int jobs = int(my_items * nch);
-  const bool sink_in = p.partial != 2;  // partial == 2: a route shard whose state leaves the sink to another
+  // partial 2 / 4: a route shard whose state leaves the sink to another shard
+  const bool sink_in = p.partial != 2 && p.partial != 4;
   const int mem_dim = int(p.ts.mem_dim);
 
   if (lane == 0) {
@@ -358,9 +359,11 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
       }
 #pragma unroll
       for (int nt = 0; nt < NTU; ++nt) uacc[nt][0] = uacc[nt][1] = uacc[nt][2] = uacc[nt][3] = 0.f;
-      m_r[0] = m_r[1] = sink_in ? p.sink : -INFINITY;
+      // every mode starts from the offset b0 (shards without the sink too, so that all shards'
+      // states share one scale and combine without rescaling unless a score exceeded b0 + BIG)
+      m_r[0] = m_r[1] = p.sink;
       l_r[0] = l_r[1] = 0.f;  // per-thread partial sums; the sink's 1 is added at the end
-      running_max = !sink_in;  // without the sink seed there is no fixed offset to start from
+      running_max = false;
       qs = p.qscale ? p.qscale[item] : 1.f;
     }
     const bool landed = mbar_wait_bounded(&bars[s], phase, &g_error_word, DEV_ERR_WAIT_TIMEOUT);
@@ -527,7 +530,19 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
       for (int i = 0; i < 2; ++i) {
         const int row = g + i * 8;
         if (row >= p.qh) continue;
-        if (p.partial) {
+        if (p.partial >= 3) {
+          // packed state (u, l) in bf16 [M, QH, DT + 1], ready for a SUM reduction across shards
+          __nv_bfloat16* po = static_cast<__nv_bfloat16*>(p.u) + (item * int64_t(p.qh) + row) * (DT + 1);
+#pragma unroll
+          for (int nt = 0; nt < NTU; ++nt) {
+            po[nt * 8 + t4 * 2] = __float2bfloat16_rn(uacc[nt][i * 2]);
+            po[nt * 8 + t4 * 2 + 1] = __float2bfloat16_rn(uacc[nt][i * 2 + 1]);
+          }
+          if (t4 == 0) {
+            po[DT] = __float2bfloat16_rn(l[i]);
+            p.m_out[item * p.qh + row] = m_r[i];
+          }
+        } else if (p.partial) {
           float* uo = static_cast<float*>(p.u) + obase + row * DT;
 #pragma unroll
           for (int nt = 0; nt < NTU; ++nt) {

@@ -505,7 +505,9 @@ static int attend_impl(const lng_tables* t, const AttendParams& p, int32_t u_dty
     return t->table_dtype == LNG_BF16 ? launch_attend_tc<CodeT, __nv_bfloat16>(t, p, stream)
                                       : launch_attend_tc<CodeT, __half>(t, p, stream);
   // tensor-core path: 16-bit tables, query of the same type, <= 16 heads, 16-byte rows
-  const bool mma_ok = t16 && qa_dtype == t->table_dtype && (p.partial ? u_dtype == LNG_F32 : u_dtype == t->table_dtype) &&
+  const bool mma_ok = t16 && qa_dtype == t->table_dtype &&
+                      (p.partial >= 3 ? u_dtype == LNG_BF16
+                                      : (p.partial ? u_dtype == LNG_F32 : u_dtype == t->table_dtype)) &&
                       p.qh <= 16 && (t->memory_dim % 8) == 0 && t->orders[t->n_orders - 1] <= MAXW;
   if (mma_ok) {
     bool aligned = (reinterpret_cast<uintptr_t>(p.qa) & 15) == 0 && (reinterpret_cast<uintptr_t>(p.u) & 15) == 0;
@@ -516,6 +518,7 @@ static int attend_impl(const lng_tables* t, const AttendParams& p, int32_t u_dty
       if (st != LNG_ERR_UNSUPPORTED) return st;
     }
   }
+  if (p.partial >= 3) return fail(LNG_ERR_UNSUPPORTED, "packed shard states need 16-bit tables and the tensor-core kernel");
   // CUDA-core path (fp32 tables / activations, partial shard states, any width)
   const int QH = p.qh;
   const size_t smem = sizeof(float) * (size_t(2 * QH + ATT_C) * Dt + ATT_C + size_t(QH) * ATT_C + 3 * QH);
@@ -562,8 +565,10 @@ extern "C" int lng_route_attend(const lng_tables* tables, const void* codes, int
   LNG_REQUIRE(num_heads >= 1 && num_heads <= 64, "num_heads must be in [1, 64]");
   LNG_REQUIRE(0 <= route_start && route_start < route_end && route_end <= tables->num_routes, "bad route range");
   LNG_REQUIRE(u_dtype == LNG_F32 || u_dtype == LNG_BF16 || u_dtype == LNG_F16, "u dtype must be f32, bf16 or f16");
-  LNG_REQUIRE(partial >= 0 && partial <= 2, "partial must be 0, 1 or 2");
-  LNG_REQUIRE(!partial || (u_dtype == LNG_F32 && m_out && l_out), "partial mode needs fp32 u, m_out and l_out");
+  LNG_REQUIRE(partial >= 0 && partial <= 4, "partial must be 0 .. 4");
+  LNG_REQUIRE(!(partial == 1 || partial == 2) || (u_dtype == LNG_F32 && m_out && l_out),
+              "partial modes 1 / 2 need fp32 u, m_out and l_out");
+  LNG_REQUIRE(partial < 3 || (u_dtype == LNG_BF16 && m_out), "partial modes 3 / 4 need a bf16 pack and m_out");
   const int64_t tout = (window <= 0 && target_length > 0) ? std::min(target_length, T) : T;
   const int64_t M = window > 0 ? B : B * tout;
   if (M == 0) return LNG_OK;
@@ -1010,6 +1015,24 @@ extern "C" int lng_attend_unpack(const void* pack, int32_t pack_dtype, int64_t M
   }
 #undef LNG_UNPACK
   LNG_LAUNCHED("attend_unpack_kernel");
+  return LNG_OK;
+}
+
+extern "C" int lng_attend_pack_rescale(const float* m_local, const float* m_glob, int64_t M, int32_t num_heads,
+                                       int32_t head_dim, void* pack, int32_t pack_dtype, lng_stream_t stream) {
+  LNG_REQUIRE(M >= 0 && num_heads > 0 && head_dim > 0, "bad shape");
+  if (M == 0) return LNG_OK;
+  LNG_REQUIRE(m_local && m_glob && pack, "NULL pointer");
+  const int64_t MQ = M * num_heads;
+  const int g = grid_for(MQ, 256, 16);
+  if (pack_dtype == LNG_F32)
+    attend_pack_rescale_kernel<float><<<g, 256, 0, S(stream)>>>(m_local, m_glob, MQ, head_dim, static_cast<float*>(pack));
+  else if (pack_dtype == LNG_BF16)
+    attend_pack_rescale_kernel<__nv_bfloat16><<<g, 256, 0, S(stream)>>>(m_local, m_glob, MQ, head_dim,
+                                                                        static_cast<__nv_bfloat16*>(pack));
+  else
+    return fail(LNG_ERR_ARGUMENT, "pack dtype must be f32 or bf16");
+  LNG_LAUNCHED("attend_pack_rescale_kernel");
   return LNG_OK;
 }
 

@@ -410,6 +410,20 @@ __global__ void attend_pack_kernel(const float* __restrict__ m, const float* __r
   }
 }
 
+// pack[i, q, :] *= exp(m_local - m_glob) where the two differ (shards share the offset b0 unless a
+// score exceeded it by a margin, so usually no row is touched).
+template <typename PT>
+__global__ void attend_pack_rescale_kernel(const float* __restrict__ m, const float* __restrict__ mg, int64_t MQ,
+                                           int HD, PT* __restrict__ pack) {
+  for (int64_t iq = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; iq < MQ; iq += int64_t(gridDim.x) * blockDim.x) {
+    const float a = m[iq], b = mg[iq];
+    if (a == b) continue;
+    const float sc = expf(a - b);
+    PT* row = pack + iq * (HD + 1);
+    for (int j = 0; j <= HD; ++j) row[j] = from_f32<PT>(to_f32(row[j]) * sc);
+  }
+}
+
 // head[i, q, :] = pack[i, q, :HD] / pack[i, q, HD]  (the final division of lngram_v2.py:2066-2070)
 template <typename PT, typename OT>
 __global__ void attend_unpack_kernel(const PT* __restrict__ pack, int64_t MQ, int HD, OT* __restrict__ head) {

@@ -6,8 +6,10 @@ routes.  A forward over positions [B, T] (hidden states replicated on every rank
 1. codes of the local routes (the router's rows r0*bits .. r1*bits);
 2. the folded query (replicated) and the fused gather + sink attention over the local routes in
    partial mode: the online-softmax state (m, l, u) of the shard, the sink seeded on rank 0 only;
-3. ``all_reduce(MAX)`` of m, then each rank rescales (l, u) by exp(m_local - m_glob) into one
-   packed buffer [M, QH, Dt + 1];
+   for 16-bit tables and bf16 activations the kernel writes (u, l) directly as one bf16 pack
+   [M, QH, Dt + 1], every shard offset by the sink logit b0;
+3. ``all_reduce(MAX)`` of m, then each rank rescales (l, u) by exp(m_local - m_glob) -- for
+   kernel-written packs only the rows whose offset differs from the maximum;
 4. ``reduce_scatter(SUM)`` of the packed buffer (bf16 for bf16 layers) by whole-sequence blocks
    (B / world sequences per rank), so the short conv needs no halo;
 5. on the local block: u / l, the folded output map, the conv finish -> out [B / world, T, d].
@@ -91,6 +93,9 @@ class RouteShardedMemory:
             check(_lib.library().lng_router_prepare(ptr(self.router_w), self.router_w.shape[0], self.router_w.shape[1],
                                                     ptr(self.router_split), stream_ptr()), "router split")
         self.pack_dtype = torch.bfloat16 if m._act() == torch.bfloat16 else torch.float32
+        # 16-bit tables + bf16 activations: the attention kernel writes the bf16 pack itself
+        self.packed = self.pack_dtype == torch.bfloat16 and self.tables[m.ngrams[0]].dtype in (torch.bfloat16,
+                                                                                              torch.float16)
         # b0 = log(R (1 - mass) / mass) of the whole layer (the local module's own is of its R_local)
         mass = m.sink_initial_active_mass
         self.sink_logit = math.log(self.R_total * (1.0 - mass) / mass)
@@ -132,10 +137,17 @@ class RouteShardedMemory:
         outs, pending = [], None
         for c in range(chunks):
             hc, xc = h[c * Bc:(c + 1) * Bc], router_x[c * Bc:(c + 1) * Bc]
-            mloc, lloc, u = self.partial(hc, xc)
-            mglob = all_reduce_max(mloc.clone(), self.group)
-            pack = self.pack(mloc, mglob, lloc, u).view(Bc * T, -1)
-            del mloc, lloc, u
+            if self.packed:
+                mloc, pack = self.partial_packed(hc, xc)
+                mglob = all_reduce_max(mloc.clone(), self.group)
+                self.rescale(mloc, mglob, pack)
+                pack = pack.view(Bc * T, -1)
+                del mloc, mglob
+            else:
+                mloc, lloc, u = self.partial(hc, xc)
+                mglob = all_reduce_max(mloc.clone(), self.group)
+                pack = self.pack(mloc, mglob, lloc, u).view(Bc * T, -1)
+                del mloc, lloc, u
             if self.world > 1 and dist.is_initialized():
                 mine = torch.empty((Bc * T // self.world, pack.shape[1]), device=pack.device, dtype=pack.dtype)
                 work = dist.reduce_scatter_tensor(mine, pack, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
@@ -175,9 +187,29 @@ class RouteShardedMemory:
         mixed = m._linear(ub, m.folded()["w_vo"])
         return m._conv_finish(mixed.view(Bb, T, m.hidden_size), None, None)
 
+    def rescale(self, mloc: Tensor, mglob: Tensor, pack: Tensor) -> None:
+        """Rows of a kernel-written pack whose offset differs from the global maximum, rescaled in place."""
+        M, QH, Dt1 = pack.shape
+        check(_lib.library().lng_attend_pack_rescale(ptr(mloc), ptr(mglob), M, QH, Dt1 - 1, ptr(pack),
+                                                     _lib.dtype_code(pack.dtype), stream_ptr()), "pack rescale")
+
     @torch.no_grad()
-    def partial(self, h: Tensor, router_x: Tensor) -> tuple[Tensor, Tensor, Tensor]:
-        """This rank's online-softmax state over its routes: m, l [B*T, QH] and u [B*T, QH, Dt] (fp32)."""
+    def partial_packed(self, h: Tensor, router_x: Tensor) -> tuple[Tensor, Tensor]:
+        """This rank's state as the bf16 pack [B*T, QH, Dt + 1] = (u, l) and m [B*T, QH], written by the
+        attention kernel (partial mode 3 with the sink on rank 0, 4 elsewhere)."""
+        m = self.full.module
+        codes, qa, rs, (B, T, M) = self._query(h, router_x)
+        Dt, QH = m.route_token_dim, m.readout_num_heads
+        mloc = torch.empty(M, QH, device=h.device, dtype=torch.float32)
+        pack = torch.empty(M, QH, Dt + 1, device=h.device, dtype=torch.bfloat16)
+        check(_lib.library().lng_route_attend(self._tables_desc(), ptr(codes), _lib.U8, B, T, 0, None, None, None, 0, 0,
+                                              self.r1 - self.r0, QH, m.eps, self.sink_logit, ptr(qa), ptr(rs),
+                                              ptr(pack), _lib.BF16, 3 if self.rank == 0 else 4, ptr(mloc), None,
+                                              stream_ptr()), "route_attend packed")
+        return mloc, pack
+
+    def _query(self, h: Tensor, router_x: Tensor):
+        """Codes of the local routes, 1/rms(h) and the folded query, shared by both state forms."""
         m = self.full.module
         lib = _lib.library()
         s = stream_ptr()
@@ -196,16 +228,24 @@ class RouteShardedMemory:
                                       ptr(self.router_w), Rl, m.bits_per_route, ptr(codes), _lib.U8, None, s),
                   "route codes")
         f = m.folded()
-        Dt, QH = m.route_token_dim, m.readout_num_heads
         rs = torch.empty(M, device=h.device, dtype=torch.float32)
         check(lib.lng_rms_rows(ptr(h), _lib.dtype_code(act), M, d, m.eps, ptr(rs), s), "rms")
         tdt = self.tables[m.ngrams[0]].dtype
         qa = m._linear(h.view(M, d), f["w_qk"].to(tdt) if f["w_qk"].dtype != tdt else f["w_qk"])
+        return codes, qa, rs, (B, T, M)
+
+    @torch.no_grad()
+    def partial(self, h: Tensor, router_x: Tensor) -> tuple[Tensor, Tensor, Tensor]:
+        """This rank's online-softmax state over its routes: m, l [B*T, QH] and u [B*T, QH, Dt] (fp32)."""
+        m = self.full.module
+        codes, qa, rs, (B, T, M) = self._query(h, router_x)
+        Dt, QH = m.route_token_dim, m.readout_num_heads
         mloc = torch.empty(M, QH, device=h.device, dtype=torch.float32)
         lloc = torch.empty_like(mloc)
         u = torch.empty(M, QH, Dt, device=h.device, dtype=torch.float32)
         # sink: b0 = log(R_total (1 - mass) / mass) of the whole layer, seeded on rank 0 only
-        check(lib.lng_route_attend(self._tables_desc(), ptr(codes), _lib.U8, B, T, 0, None, None, None, 0, 0, Rl, QH,
-                                   m.eps, self.sink_logit, ptr(qa), ptr(rs), ptr(u), _lib.F32,
-                                   1 if self.rank == 0 else 2, ptr(mloc), ptr(lloc), s), "route_attend partial")
+        check(_lib.library().lng_route_attend(self._tables_desc(), ptr(codes), _lib.U8, B, T, 0, None, None, None, 0, 0,
+                                              self.r1 - self.r0, QH, m.eps, self.sink_logit, ptr(qa), ptr(rs), ptr(u),
+                                              _lib.F32, 1 if self.rank == 0 else 2, ptr(mloc), ptr(lloc),
+                                              stream_ptr()), "route_attend partial")
         return mloc, lloc, u

@@ -63,6 +63,28 @@ def test_emulated_shards_sb_shape_bf16(lngram, golden):
     assert_bf16_close(got, g["output_wrapper"], what="8 emulated shards vs reference")
 
 
+def test_emulated_packed_shards_sb_shape_bf16(lngram, golden):
+    """Kernel-written bf16 packs (partial modes 3 / 4), rescaled to the global maximum and summed."""
+    g = golden("memory_sb_slice")
+    mem = gpu_memory(lngram, "sb_slice", dtype=torch.bfloat16)
+    inp = cases.memory_inputs("sb_slice")
+    h = torch.from_numpy(inp["h"]).to(DEV).to(torch.bfloat16)
+    x = torch.from_numpy(inp["x"]).to(DEV)
+    shards = [lngram.RouteShardedMemory(mem, r, 8) for r in range(8)]
+    assert all(s.packed for s in shards)
+    with torch.no_grad():
+        parts = [s.partial_packed(h, x) for s in shards]
+        mg = parts[0][0].clone()
+        for q in parts[1:]:
+            mg = torch.maximum(mg, q[0])
+        for s, q in zip(shards, parts):
+            s.rescale(q[0], mg, q[1])
+        total = sum(q[1].float() for q in parts).to(torch.bfloat16)
+        B, T = h.shape[:2]
+        got = shards[0].finish(total.view(B * T, -1), B, T).float().cpu().numpy()
+    assert_bf16_close(got, g["output_wrapper"], what="8 emulated packed shards vs reference")
+
+
 def local_shard(lngram, case: str, rank: int, world: int, dtype=torch.float32):
     """A memory holding only the routes of ``rank`` (tables and router rows sliced from the case's
     parameters, readout weights whole), wrapped as a pre-sliced route shard."""

@@ -872,9 +872,14 @@ def time_scaled_phases(pkg, shard, h, hn, world) -> dict:
 
     f = m.folded()
     tm("query_gemm (replicated)", lambda: m._linear(hc.reshape(Bc * T, -1), f["w_qk"]))
-    mloc, lloc, u = tm("partial (codes + rms + query gemm + gather)", lambda: shard.partial(hc, xc))
-    mg = tm("all_reduce_max", lambda: pkg.sharded.all_reduce_max(mloc.clone()))
-    pack = tm("pack", lambda: shard.pack(mloc, mg, lloc, u))
+    if shard.packed:
+        mloc, pack = tm("partial (codes + rms + query gemm + gather -> bf16 pack)", lambda: shard.partial_packed(hc, xc))
+        mg = tm("all_reduce_max", lambda: pkg.sharded.all_reduce_max(mloc.clone(), shard.group_m))
+        tm("rescale", lambda: shard.rescale(mloc, mg, pack))
+    else:
+        mloc, lloc, u = tm("partial (codes + rms + query gemm + gather)", lambda: shard.partial(hc, xc))
+        mg = tm("all_reduce_max", lambda: pkg.sharded.all_reduce_max(mloc.clone()))
+        pack = tm("pack", lambda: shard.pack(mloc, mg, lloc, u))
     mine = tm("reduce_scatter", lambda: pkg.sharded.reduce_scatter_rows(pack.view(Bc * T, -1)))
     tm("finish (unpack + output gemm + conv)", lambda: shard.finish(mine, Bc // world, T))
     return res

@@ -99,6 +99,13 @@ class RouteShardedMemory:
         # b0 = log(R (1 - mass) / mass) of the whole layer (the local module's own is of its R_local)
         mass = m.sink_initial_active_mass
         self.sink_logit = math.log(self.R_total * (1.0 - mass) / mass)
+        # the max all-reduce runs on its own communicator, so it does not queue behind the previous
+        # group's reduce-scatter (collectives of one communicator run in order on one stream);
+        # created collectively, so every rank constructs its shard at the same point
+        self.group_m = None
+        if dist.is_initialized() and dist.get_world_size(group) > 1:
+            ranks = dist.get_process_group_ranks(group) if group is not None else list(range(dist.get_world_size()))
+            self.group_m = dist.new_group(ranks)
         self.ss = {}
         self.dev = dev
 
@@ -139,7 +146,7 @@ class RouteShardedMemory:
             hc, xc = h[c * Bc:(c + 1) * Bc], router_x[c * Bc:(c + 1) * Bc]
             if self.packed:
                 mloc, pack = self.partial_packed(hc, xc)
-                mglob = all_reduce_max(mloc.clone(), self.group)
+                mglob = all_reduce_max(mloc.clone(), self.group_m if self.group_m is not None else self.group)
                 self.rescale(mloc, mglob, pack)
                 pack = pack.view(Bc * T, -1)
                 del mloc, mglob

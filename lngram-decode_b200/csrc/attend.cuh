@@ -33,6 +33,7 @@ struct AttendParams {
   int partial;
   float* m_out;
   float* l_out;
+  int rows32;      // every table row index fits int32 (the tensor-core gather's cooperative copies)
 };
 
 // ------------------------------------------------------------------ generic CUDA-core version
@@ -139,8 +140,10 @@ __global__ void __launch_bounds__(128) attend_simt_kernel(AttendParams p) {
 }
 
 // ------------------------------------------------------------------ tensor-core version (bf16 / f16)
-// One warp per item; routes in chunks of 32 streamed through a per-warp ring of shared-memory
-// stages by bulk (TMA-engine) copies, one 16-byte-aligned row copy per (route, order).  Scores
+// One warp per item; routes in chunks of 32 streamed through a per-warp ring of two shared-memory
+// stages: the rows of a single-order table by the warp's own 16-byte cp.async copies, multi-order
+// tokens by one bulk (TMA-engine) copy per (route, order) row; the item's folded query arrives by
+// one bulk copy with its first chunk.  Scores
 // (16 x 32 per chunk) and the weighted row sum (16 x Dt) are mma.sync m16n8k16 products with fp32
 // accumulation: the per-item products are 16 x 32 x Dt, below the 64-row minimum of a tcgen05 MMA,
 // and every item has its own B operand, so the warp-level MMA is the fitting unit here.
@@ -204,14 +207,27 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+__device__ __forceinline__ float ex2_approx(float x) {  // 2^x (PTX ex2.approx.ftz.f32)
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 template <int DT>
 struct AttendMmaCfg {
-  static constexpr int C = 32;                 // routes per chunk (= lanes: one route per lane)
-  static constexpr int KT = (DT + 15) / 16;    // k16 steps of the score product
-  static constexpr int NTU = DT / 8;           // n8 tiles of the weighted row sum
-  static constexpr int ROWB = DT * 2;          // bytes per token row in shared memory
-  static constexpr int SS_OFF = C * ROWB + 32; // zero pad read by the last k-step, then the rows' sums of squares
-  static constexpr int STAGE_BYTES = SS_OFF + C * 4;
+  static constexpr int C = 32;                   // routes per chunk (= lanes: one route per lane)
+  static constexpr int KT = (DT + 15) / 16;      // k16 steps of the score product
+  static constexpr int NTU = DT / 8;             // n8 tiles of the weighted row sum
+  static constexpr int ROWB = DT * 2;            // bytes per token row in shared memory
+  static constexpr int SS_OFF = C * ROWB + 32;   // zero pad read by the last k-step, then the rows' sums of squares
+  static constexpr int QS_OFF = SS_OFF + C * 4;  // the item's query scale (stages holding an item's first chunk)
+  static constexpr int QA_OFF = QS_OFF + 16;     // the item's folded query [16 heads][DT] (same stages)
+  static constexpr int STAGES = 2;
+  static constexpr int STAGE_BYTES = QA_OFF + 16 * ROWB;
+  // warps per CTA: as many as 227 KB of shared memory holds, at most 8 (register file: ~250 per thread)
+  static constexpr int FIT = (227 * 1024) / (STAGES * (STAGE_BYTES + 8));
+  static constexpr int WARPS = FIT < 8 ? FIT : 8;
+  static_assert(FIT >= 1, "route token too wide for the tensor-core gather");
 };
 
 template <typename CodeT, typename T, int DT, int WARPS, int STAGES>
@@ -244,17 +260,22 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
 
   // Gather pipeline, lane = route within the chunk.  Job J's codes are loaded (prefetch) one
   // iteration before its row copies are issued, and copies run STAGES-1 jobs ahead of the math, so
-  // neither the code loads nor the row loads sit on the critical path.
+  // neither the code loads nor the row loads sit on the critical path.  The stage of an item's
+  // first chunk also receives the item's folded query (one bulk copy) and its query scale.
   int64_t pf_item = gwarp;  // prefetch cursor
   int pf_chunk = 0;
   ItemGeo pf_geo{};
   int32_t pend_c[MAXW];
   ItemGeo pend_geo{};
   int pend_chunk = 0;
+  int64_t pend_item = 0;
+  float pend_qs = 1.f;
   auto prefetch = [&]() {
     if (pf_chunk == 0) pf_geo = item_geometry(p.src, p.ts.order, p.ts.n_orders, pf_item);
     pend_geo = pf_geo;
     pend_chunk = pf_chunk;
+    pend_item = pf_item;
+    if (pf_chunk == 0) pend_qs = p.qscale ? __ldg(p.qscale + pf_item) : 1.f;
     const int64_t r = p.route_start + int64_t(pf_chunk) * C + lane;
     load_window_codes<CodeT>(p.src, pf_geo, r, r < p.route_end, pend_c);
     if (++pf_chunk == nch) {
@@ -278,6 +299,13 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
     }
     ss_stage = -1;
   };
+  const uint32_t qa_bytes = uint32_t(p.qh) * DT * 2;
+  // Single-order tables: the chunk's 32 rows are copied cooperatively by the whole warp with 16-byte
+  // cp.async copies (load/store path, about two rows per warp instruction).  One bulk copy (TMA
+  // engine) per row measured slower: the engine's per-copy cost, not HBM, bounded the row rate.
+  // Multi-order tokens keep one bulk copy per (route, order) row.
+  const bool coop = p.ts.n_orders == 1 && p.rows32;
+  const bool bulk_lane = !coop;
   auto issue = [&](int s) {
     flush_ss();
     const int64_t r = p.route_start + int64_t(pend_chunk) * C + lane;
@@ -290,20 +318,47 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
       rows[o] = window_row(pend_c, p.ts.order[o], p.ts.bits, r, r < p.route_end && ((pend_geo.omask >> o) & 1u));
       ss_pend[o] = 0.f;
       if (rows[o] >= 0) {
-        bytes += uint32_t(mem_dim * 2);
+        if (bulk_lane) bytes += uint32_t(mem_dim * 2);
         if (have_ss) ss_pend[o] = __ldg(p.ts.ss[o] + rows[o]);
-      } else {
+      } else if (bulk_lane) {
         uint4* z = reinterpret_cast<uint4*>(row_smem + o * mem_dim * 2);
         for (int v = 0; v < mem_dim * 2 / 16; ++v) z[v] = make_uint4(0, 0, 0, 0);
       }
     }
     ss_stage = s;
+    if (coop) {
+      // piece f of the C x (DT / 8) 16-byte pieces: row f / (DT / 8), piece f % (DT / 8); the row
+      // index comes from the lane that computed it; invalid rows are zero-filled (source size 0)
+      constexpr int PPR = DT / 8, NP = C * PPR;
+      const int32_t myrow = int32_t(rows[0]);
+      const unsigned char* tb = static_cast<const unsigned char*>(p.ts.tab[0]);
+      const uint32_t dst0 = smem_addr(stage_base + s * SB);
+#pragma unroll
+      for (int i = 0; i < (NP + 31) / 32; ++i) {
+        const int f = i * 32 + lane;
+        const int fq = f < NP ? f : NP - 1;
+        const int q = fq / PPR, pc = fq - q * PPR;
+        const int32_t rq = __shfl_sync(0xffffffffu, myrow, q);
+        if (NP % 32 == 0 || f < NP)
+          cp_async16(dst0 + uint32_t(q * ROWB + pc * 16), tb + int64_t(rq < 0 ? 0 : rq) * ROWB + pc * 16,
+                     rq < 0 ? 0u : 16u);
+      }
+      cp_async_mbar_arrive(&bars[s]);
+    }
+    const bool first = pend_chunk == 0 && lane == 0;
+    if (first) {
+      reinterpret_cast<float*>(stage_base + s * SB + Cfg::QS_OFF)[0] = pend_qs;
+      bytes += qa_bytes;
+    }
     fence_proxy_async_smem();
     mbar_arrive_expect_tx(&bars[s], bytes);
+    if (first)
+      bulk_g2s(stage_base + s * SB + Cfg::QA_OFF,
+               static_cast<const unsigned char*>(p.qa) + pend_item * int64_t(qa_bytes), qa_bytes, &bars[s]);
 #pragma unroll
     for (int o = 0; o < LNG_MAX_ORDERS; ++o) {
       if (o >= p.ts.n_orders) break;
-      if (rows[o] >= 0) {
+      if (rows[o] >= 0 && bulk_lane) {
         const unsigned char* src = static_cast<const unsigned char*>(p.ts.tab[o]) + rows[o] * int64_t(mem_dim) * 2;
         bulk_g2s(row_smem + o * mem_dim * 2, src, uint32_t(mem_dim * 2), &bars[s]);
       }
@@ -318,15 +373,17 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
 
   uint32_t qa_frag[KT][4];
   float uacc[NTU][4];
-  float m_r[2], l_r[2];
+  float m_r[2], l_r[2];  // running offset (log2 units) and per-thread partial sums
   bool running_max = false;
-  float qs = 1.f;
+  float qsl = 1.f;  // query scale x log2(e)
   const int g = lane >> 2, t4 = lane & 3;
   T* tag = nullptr;
   int64_t item = gwarp - nwarps;  // consume cursor
   int chunk = nch - 1;
   int s = STAGES - 1;
   uint32_t phase = 1;
+  constexpr float LOG2E = 1.4426950408889634f;
+  const float sink2 = p.sink * LOG2E;
 
   for (int j = 0; j < jobs; ++j) {
     if (j + STAGES - 1 < jobs) {
@@ -343,33 +400,40 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
       chunk = 0;
       item += nwarps;
     }
-    if (chunk == 0) {
-      // new item: its folded query as A fragments (rows = heads, k = token dims), zero padded
-      const T* qg = static_cast<const T*>(p.qa) + item * int64_t(p.qh) * DT;
-#pragma unroll
-      for (int kt = 0; kt < KT; ++kt) {
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          const int row = g + ((h & 1) ? 8 : 0);
-          const int col = kt * 16 + t4 * 2 + ((h & 2) ? 8 : 0);
-          uint32_t v = 0u;
-          if (row < p.qh && col < DT) v = *reinterpret_cast<const uint32_t*>(qg + row * DT + col);
-          qa_frag[kt][h] = v;
-        }
-      }
-#pragma unroll
-      for (int nt = 0; nt < NTU; ++nt) uacc[nt][0] = uacc[nt][1] = uacc[nt][2] = uacc[nt][3] = 0.f;
-      // every mode starts from the offset b0 (shards without the sink too, so that all shards'
-      // states share one scale and combine without rescaling unless a score exceeded b0 + BIG)
-      m_r[0] = m_r[1] = p.sink;
-      l_r[0] = l_r[1] = 0.f;  // per-thread partial sums; the sink's 1 is added at the end
-      running_max = false;
-      qs = p.qscale ? p.qscale[item] : 1.f;
-    }
     const bool landed = mbar_wait_bounded(&bars[s], phase, &g_error_word, DEV_ERR_WAIT_TIMEOUT);
     if (!__all_sync(0xffffffffu, landed)) return;
     const unsigned char* st = stage_base + s * SB;
     const uint32_t st_addr = smem_addr(st);
+    if (chunk == 0) {
+      // new item: its folded query as A fragments (rows = heads, k = token dims) from the stage,
+      // rows >= qh and k >= DT zeroed
+      const uint32_t qa_addr = st_addr + Cfg::QA_OFF + ((lane & 7) + ((lane >> 3) & 1) * 8) * ROWB;
+#pragma unroll
+      for (int kt = 0; kt < KT; ++kt) {
+        if (kt == KT - 1 && (DT % 16) != 0) {
+          ldsm_x2(qa_addr + kt * 32, qa_frag[kt][0], qa_frag[kt][1]);
+          qa_frag[kt][2] = qa_frag[kt][3] = 0u;
+        } else {
+          ldsm_x4(qa_addr + kt * 32 + (lane >> 4) * 16, qa_frag[kt][0], qa_frag[kt][1], qa_frag[kt][2],
+                  qa_frag[kt][3]);
+        }
+      }
+      if (p.qh < 16) {
+#pragma unroll
+        for (int kt = 0; kt < KT; ++kt) {
+          if (g >= p.qh) qa_frag[kt][0] = qa_frag[kt][2] = 0u;
+          if (g + 8 >= p.qh) qa_frag[kt][1] = qa_frag[kt][3] = 0u;
+        }
+      }
+      qsl = reinterpret_cast<const float*>(st + Cfg::QS_OFF)[0] * LOG2E;
+#pragma unroll
+      for (int nt = 0; nt < NTU; ++nt) uacc[nt][0] = uacc[nt][1] = uacc[nt][2] = uacc[nt][3] = 0.f;
+      // every mode starts from the offset b0 (shards without the sink too, so that all shards'
+      // states share one scale and combine without rescaling unless a score exceeded b0 + BIG)
+      m_r[0] = m_r[1] = sink2;
+      l_r[0] = l_r[1] = 0.f;  // the sink's 1 is added at the end
+      running_max = false;
+    }
 
     // inverse RMS of this lane's route token (row = lane)
     float rxl;
@@ -407,16 +471,17 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
     for (int nt = 0; nt < 4; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
 #pragma unroll
     for (int kt = 0; kt + 1 < KT; kt += 2) {
+      // B fragments of two k16 steps for all four route tiles first, then the products one k-step at
+      // a time across the tiles (four independent accumulators between dependent products)
+      uint32_t bf[4][4];
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt) {
-        // B fragments of two k16 steps: rows = routes nt*8..+7, k = kt*16..kt*16+31 (four 8x8 matrices)
-        const int rrow = nt * 8 + (lane & 7);
-        const int kcol = kt * 16 + (lane >> 3) * 8;
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(st_addr + rrow * ROWB + kcol * 2, b0, b1, b2, b3);
-        mma16816<T>(sacc[nt], qa_frag[kt], b0, b1);
-        mma16816<T>(sacc[nt], qa_frag[kt + 1], b2, b3);
-      }
+      for (int nt = 0; nt < 4; ++nt)
+        ldsm_x4(st_addr + (nt * 8 + (lane & 7)) * ROWB + (kt * 16 + (lane >> 3) * 8) * 2, bf[nt][0], bf[nt][1],
+                bf[nt][2], bf[nt][3]);
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) mma16816<T>(sacc[nt], qa_frag[kt], bf[nt][0], bf[nt][1]);
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) mma16816<T>(sacc[nt], qa_frag[kt + 1], bf[nt][2], bf[nt][3]);
     }
     if (KT & 1) {
 #pragma unroll
@@ -429,12 +494,14 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
       }
     }
 
-    // softmax update with the sink seed; rxv = this thread's 8 route columns' 1/rms.  The exponent
-    // offset stays the sink logit b0 (m_r's seed) while no score of the item has exceeded b0 + BIG:
-    // p = exp(s - b0) is then finite in the 16-bit P operand and the fp32 sums and the normalised
-    // result is the same, with no per-chunk maximum or rescaling.  From the first chunk with a larger
-    // score (a warp vote), the offset is the running maximum with online rescaling.
+    // softmax update in log2 units with the sink seed; rxv = this thread's 8 route columns' 1/rms.
+    // The exponent offset stays the sink logit b0 (m_r's seed) while no score of the item has
+    // exceeded b0 + BIG: p = 2^(s - b0) is then finite in the 16-bit P operand and the fp32 sums and
+    // the normalised result is the same, with no per-chunk maximum or rescaling.  From the first
+    // chunk with a larger score (a warp vote), the offset is the running maximum with online
+    // rescaling.
     constexpr float BIG = std::is_same<T, __nv_bfloat16>::value ? 64.f : 4.f;  // f16 P: exp(BIG) * rx < 65504
+    const float big2 = sink2 + BIG * LOG2E;
     const int64_t rbase = p.route_start + int64_t(chunk) * C;
     float rxv[4][2];
 #pragma unroll
@@ -446,14 +513,23 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt) {
 #pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        const int col = nt * 8 + t4 * 2 + (h & 1);
-        float v = sacc[nt][h] * (qs * rxv[nt][h & 1]);
-        if (rbase + col >= p.route_end) v = -INFINITY;
-        sv[nt][h] = v;
-        big = big || v > p.sink + BIG;
+      for (int b = 0; b < 2; ++b) {
+        const float c = qsl * rxv[nt][b];
+        sv[nt][b] = sacc[nt][b] * c;
+        sv[nt][b + 2] = sacc[nt][b + 2] * c;
       }
     }
+    if (rbase + C > p.route_end) {  // the item's last chunk is ragged: routes past the end take no part
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int h = 0; h < 4; ++h)
+          if (rbase + nt * 8 + t4 * 2 + (h & 1) >= p.route_end) sv[nt][h] = -INFINITY;
+    }
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int h = 0; h < 4; ++h) big = big || sv[nt][h] > big2;
     running_max = running_max || __any_sync(0xffffffffu, big);
     float alpha[2] = {1.f, 1.f};
     if (running_max) {
@@ -469,7 +545,7 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
       }
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
-        alpha[i] = __expf(m_r[i] - mx[i]);
+        alpha[i] = ex2_approx(m_r[i] - mx[i]);
         m_r[i] = mx[i];
         l_r[i] *= alpha[i];
       }
@@ -480,7 +556,7 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
       float e[4];
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
-        const float ex = __expf(sv[nt][h] - m_r[h >> 1]);
+        const float ex = ex2_approx(sv[nt][h] - m_r[h >> 1]);
         l_r[h >> 1] += ex;
         e[h] = ex * rxv[nt][h & 1];
       }
@@ -517,13 +593,14 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
     __syncwarp();
 
     if (chunk == nch - 1) {
+      constexpr float LN2 = 0.6931471805599453f;
       float l[2];
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
         l[i] = l_r[i];
         l[i] += __shfl_xor_sync(0xffffffffu, l[i], 1);
         l[i] += __shfl_xor_sync(0xffffffffu, l[i], 2);
-        if (sink_in) l[i] += expf(p.sink - m_r[i]);  // the sink's seed 1, rescaled to the final max
+        if (sink_in) l[i] += ex2_approx(sink2 - m_r[i]);  // the sink's seed 1, rescaled to the final offset
       }
       const int64_t obase = item * int64_t(p.qh) * DT;
 #pragma unroll
@@ -540,7 +617,7 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
           }
           if (t4 == 0) {
             po[DT] = __float2bfloat16_rn(l[i]);
-            p.m_out[item * p.qh + row] = m_r[i];
+            p.m_out[item * p.qh + row] = m_r[i] * LN2;
           }
         } else if (p.partial) {
           float* uo = static_cast<float*>(p.u) + obase + row * DT;
@@ -549,7 +626,7 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
             *reinterpret_cast<float2*>(uo + nt * 8 + t4 * 2) = make_float2(uacc[nt][i * 2], uacc[nt][i * 2 + 1]);
           }
           if (t4 == 0) {
-            p.m_out[item * p.qh + row] = m_r[i];
+            p.m_out[item * p.qh + row] = m_r[i] * LN2;
             p.l_out[item * p.qh + row] = l[i];
           }
         } else {

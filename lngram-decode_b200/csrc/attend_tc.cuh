@@ -72,13 +72,6 @@ __device__ __forceinline__ bool group_bar_or(int g, bool pred) {
       : "memory");
   return out != 0;
 }
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
-}
-__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t* bar) {
-  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // tcgen05.ld of 16 columns of this warp's 32 TMEM lanes without waiting, and the wait that makes
 // the registers valid: it names them as operands, so no use can be scheduled above it.

@@ -417,32 +417,12 @@ extern "C" int lng_lookup_windows(const lng_tables* tables, const void* codes, i
 }
 
 // ====================================================================== attention core
-// Warps per CTA x shared-memory stages per warp of the gather kernel; LNG_ATTEND_CFG=<warps>x<stages>
-// selects among the compiled shapes (a tuning knob; every shape computes the same result).
-static int attend_cfg() {
-  static int cfg = [] {
-    const char* e = getenv("LNG_ATTEND_CFG");
-    if (!e) return 83;
-    const std::string s(e);
-    if (s == "6x4") return 64;
-    if (s == "4x6") return 46;
-    if (s == "12x2") return 122;
-    return 83;
-  }();
-  return cfg;
-}
-
-template <int DT, typename CodeT, typename T, int WARPS = 8, int STAGES = 3>
+// Warps per CTA and shared-memory stages per warp of the gather kernel come from the token width
+// (AttendMmaCfg): two stages per warp, as many warps (at most 8) as the shared memory holds.
+template <int DT, typename CodeT, typename T>
 static int launch_attend_mma(const AttendParams& p, cudaStream_t stream) {
-  if constexpr (DT == 136 && WARPS == 8 && STAGES == 3) {
-    switch (attend_cfg()) {
-      case 64: return launch_attend_mma<DT, CodeT, T, 6, 4>(p, stream);
-      case 46: return launch_attend_mma<DT, CodeT, T, 4, 6>(p, stream);
-      case 122: return launch_attend_mma<DT, CodeT, T, 12, 2>(p, stream);
-      default: break;
-    }
-  }
   using Cfg = AttendMmaCfg<DT>;
+  constexpr int WARPS = Cfg::WARPS, STAGES = Cfg::STAGES;
   const size_t smem = size_t(WARPS) * STAGES * Cfg::STAGE_BYTES + size_t(WARPS) * STAGES * sizeof(uint64_t);
   auto kern = attend_mma_kernel<CodeT, T, DT, WARPS, STAGES>;
   LNG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
@@ -510,11 +490,15 @@ static int attend_impl(const lng_tables* t, const AttendParams& p, int32_t u_dty
                                       : (p.partial ? u_dtype == LNG_F32 : u_dtype == t->table_dtype)) &&
                       p.qh <= 16 && (t->memory_dim % 8) == 0 && t->orders[t->n_orders - 1] <= MAXW;
   if (mma_ok) {
+    AttendParams q = p;
+    q.rows32 = 1;
+    for (int o = 0; o < t->n_orders; ++o)
+      q.rows32 = q.rows32 && (t->num_routes << (int64_t(t->bits) * t->orders[o])) < (int64_t(1) << 31);
     bool aligned = (reinterpret_cast<uintptr_t>(p.qa) & 15) == 0 && (reinterpret_cast<uintptr_t>(p.u) & 15) == 0;
     for (int o = 0; o < t->n_orders; ++o) aligned = aligned && (reinterpret_cast<uintptr_t>(t->tables[o]) & 15) == 0;
     if (aligned) {
-      const int st = t->table_dtype == LNG_BF16 ? dispatch_attend_mma<CodeT, __nv_bfloat16>(Dt, p, stream)
-                                                : dispatch_attend_mma<CodeT, __half>(Dt, p, stream);
+      const int st = t->table_dtype == LNG_BF16 ? dispatch_attend_mma<CodeT, __nv_bfloat16>(Dt, q, stream)
+                                                : dispatch_attend_mma<CodeT, __half>(Dt, q, stream);
       if (st != LNG_ERR_UNSUPPORTED) return st;
     }
   }
@@ -715,23 +699,20 @@ static int conv_finish_ws(const lng_readout* ro, const void* mixed, int64_t B, i
   const ConvParams cp = conv_params(ro);
   const bool al16 = (reinterpret_cast<uintptr_t>(mixed) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
                     (reinterpret_cast<uintptr_t>(conv_in) & 15) == 0;
-  const int tile_ch = ro->act_dtype == LNG_F32 ? 128 : 256;
-  if (ro->conv_kernel == 4 && 3 * ro->conv_dilation <= CT_HMAX && ro->hidden % tile_ch == 0 && al16 &&
-      M < (int64_t(1) << 31) &&
-      (ro->act_dtype == LNG_F32 || ro->act_dtype == LNG_BF16)) {
-    const size_t smem = size_t(CT_TP + CT_HMAX) * 32 * 16 + size_t(CT_TP + CT_HMAX) * 4;
-    const dim3 grid(unsigned(ceil_div(M, CT_TP)), unsigned(ro->hidden / tile_ch));
-    LNG_CUDA(cudaFuncSetAttribute(conv_tile_kernel<float, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-    LNG_CUDA(cudaFuncSetAttribute(conv_tile_kernel<__nv_bfloat16, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  int(smem)));
+  if (ro->conv_kernel == 4 && ro->conv_dilation <= 1024 && al16 && M < (int64_t(1) << 31) - (int64_t(1) << 20) &&
+      ro->hidden % (ro->act_dtype == LNG_F32 ? 4 : 8) == 0 && (ro->act_dtype == LNG_F32 || ro->act_dtype == LNG_BF16)) {
+    const int64_t chunks = ro->hidden / (ro->act_dtype == LNG_F32 ? 4 : 8);
+    const int64_t run = int64_t(CS_RUN) * ro->conv_dilation;
+    const dim3 grid(unsigned(ceil_div(M, run)), unsigned(ro->conv_dilation), unsigned(ceil_div(chunks, 128)));
     if (ro->act_dtype == LNG_F32)
-      conv_tile_kernel<float, 4><<<grid, 128, smem, stream>>>(cp, static_cast<const float*>(mixed), rs, M, T, seg, valid,
-                                                              static_cast<float*>(out), static_cast<float*>(conv_in));
+      conv_stream_kernel<float, 4><<<grid, 128, 0, stream>>>(cp, static_cast<const float*>(mixed), rs, int(M), int(T),
+                                                             seg, valid, static_cast<float*>(out),
+                                                             static_cast<float*>(conv_in));
     else
-      conv_tile_kernel<__nv_bfloat16, 4><<<grid, 128, smem, stream>>>(
-          cp, static_cast<const __nv_bfloat16*>(mixed), rs, M, T, seg, valid, static_cast<__nv_bfloat16*>(out),
-          static_cast<__nv_bfloat16*>(conv_in));
-    LNG_LAUNCHED("conv_tile_kernel");
+      conv_stream_kernel<__nv_bfloat16, 4><<<grid, 128, 0, stream>>>(
+          cp, static_cast<const __nv_bfloat16*>(mixed), rs, int(M), int(T), seg, valid,
+          static_cast<__nv_bfloat16*>(out), static_cast<__nv_bfloat16*>(conv_in));
+    LNG_LAUNCHED("conv_stream_kernel");
     return LNG_OK;
   }
   const int64_t groups = ro->hidden / 8;

@@ -81,37 +81,67 @@ struct ConvParams {
   const float* bias;    // [d] or null
 };
 
-// Sequence-mode conv finish on a shared-memory tile (the form used for whole batches): a 128-thread
-// CTA takes CT_TP consecutive positions x 512 bytes of channels plus the (k-1)*dil halo positions
-// before them, copied once into shared memory with 16-byte cp.async (no register staging, so six
-// CTAs fit an SM and their loads overlap each other's math); each output position then reads its k
-// taps from shared memory.  Semantics as conv_seq_kernel below (zero left padding, segment mask,
-// valid mask).
-constexpr int CT_TP = 32;    // positions per tile
-constexpr int CT_HMAX = 32;  // largest halo (k-1)*dil the tile holds
+// Sequence-mode conv finish as position streams (the form used for whole batches): a thread owns
+// 16 bytes of channels and one stream of positions p0 + res + j * dil (j < CS_RUN) of its CTA's run,
+// so the k taps of every output are the stream's own last k inputs, held in registers.  Every input
+// row is read once (plus a (k-1)-row halo per stream) with 16-byte loads straight from global
+// memory (a warp reads 512 contiguous bytes of one position), CS_PF rows ahead of their use; the
+// arithmetic runs on channel pairs with the packed fp32 instructions (f32x2) and no shared memory.
+// Semantics as conv_seq_kernel below (zero left padding, segment mask, valid mask).  For bf16
+// activations SiLU(x) = h + h tanh(h), h = x / 2 (one hardware tanh, relative error about 2^-11,
+// below the bf16 output's resolution); fp32 activations use x / (1 + e^-x).
+constexpr int CS_RUN = 32;  // positions per stream
+constexpr int CS_PF = 4;    // rows loaded ahead
+
+__device__ __forceinline__ uint64_t f2_bits(float2 a) { return *reinterpret_cast<uint64_t*>(&a); }
+__device__ __forceinline__ float2 f2_from(uint64_t b) { return *reinterpret_cast<float2*>(&b); }
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {  // a * b + c, two lanes of fp32
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
+  return f2_from(d);
+}
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return f2_from(d);
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return f2_from(d);
+}
+__device__ __forceinline__ float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 template <typename T>
-__device__ __forceinline__ void unpack16(const uint4& w, float (&v)[16 / sizeof(T)]) {
+__device__ __forceinline__ uint4 ld_nc16(const T* p) {
+  return __ldg(reinterpret_cast<const uint4*>(p));
+}
+// 16 bytes of activations as channel pairs
+template <typename T>
+__device__ __forceinline__ void unpack_pairs(const uint4& w, float2 (&v)[8 / sizeof(T)]) {
   if constexpr (std::is_same<T, float>::value) {
-    v[0] = __uint_as_float(w.x); v[1] = __uint_as_float(w.y); v[2] = __uint_as_float(w.z); v[3] = __uint_as_float(w.w);
+    v[0] = make_float2(__uint_as_float(w.x), __uint_as_float(w.y));
+    v[1] = make_float2(__uint_as_float(w.z), __uint_as_float(w.w));
   } else {
     const uint32_t w4[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      v[2 * i] = __uint_as_float(w4[i] << 16);
-      v[2 * i + 1] = __uint_as_float(w4[i] & 0xffff0000u);
-    }
+    for (int i = 0; i < 4; ++i) v[i] = make_float2(__uint_as_float(w4[i] << 16), __uint_as_float(w4[i] & 0xffff0000u));
   }
 }
 template <typename T>
-__device__ __forceinline__ uint4 pack16(const float (&v)[16 / sizeof(T)]) {
+__device__ __forceinline__ uint4 pack_pairs(const float2 (&v)[8 / sizeof(T)]) {
   if constexpr (std::is_same<T, float>::value) {
-    return make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]), __float_as_uint(v[3]));
+    return make_uint4(__float_as_uint(v[0].x), __float_as_uint(v[0].y), __float_as_uint(v[1].x),
+                      __float_as_uint(v[1].y));
   } else {
     uint32_t w4[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      __nv_bfloat162 b2 = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+      __nv_bfloat162 b2 = __floats2bfloat162_rn(v[i].x, v[i].y);
       w4[i] = *reinterpret_cast<uint32_t*>(&b2);
     }
     return make_uint4(w4[0], w4[1], w4[2], w4[3]);
@@ -119,82 +149,117 @@ __device__ __forceinline__ uint4 pack16(const float (&v)[16 / sizeof(T)]) {
 }
 
 template <typename T, int K>
-__global__ void __launch_bounds__(128) conv_tile_kernel(ConvParams cp, const T* __restrict__ mixed,
-                                                        const float* __restrict__ rs, int64_t M, int64_t T_,
-                                                        const int64_t* __restrict__ seg,
-                                                        const uint8_t* __restrict__ valid, T* __restrict__ out,
-                                                        T* __restrict__ conv_in) {
-  constexpr int VEC = 16 / int(sizeof(T));  // channels per 16-byte chunk
-  constexpr int CH = 32 * VEC;               // channels per tile (512 bytes)
-  extern __shared__ uint4 ct_tile[];         // [rows][32 chunks]
-  float* rsh = reinterpret_cast<float*>(ct_tile + (CT_TP + CT_HMAX) * 32);
-  const int H = (K - 1) * cp.dil;
-  const int rows = CT_TP + H;
-  const int64_t p0 = int64_t(blockIdx.x) * CT_TP, base = p0 - H;
-  const int64_t c0 = int64_t(blockIdx.y) * CH;
-  const int tid = threadIdx.x, lane = tid & 31, pr = tid >> 5;
-  const uint32_t tile_s = static_cast<uint32_t>(__cvta_generic_to_shared(ct_tile));
-  for (int e = tid; e < rows * 32; e += 128) {
-    const int r = e >> 5, ch = e & 31;
-    const int64_t q = base + r;
-    const bool in = q >= 0 && q < M;
-    const T* src = mixed + (in ? q * cp.d + c0 + ch * VEC : 0);
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(tile_s + uint32_t(e) * 16u), "l"(src),
-                 "r"(in ? 16u : 0u)
-                 : "memory");
-  }
-  asm volatile("cp.async.commit_group;" ::: "memory");
-  for (int r = tid; r < rows; r += 128) {
-    const int64_t q = base + r;
-    rsh[r] = (q >= 0 && q < M) ? rs[q] : 0.f;
-  }
+__global__ void __launch_bounds__(128) conv_stream_kernel(ConvParams cp, const T* __restrict__ mixed,
+                                                          const float* __restrict__ rs, int M, int T_,
+                                                          const int64_t* __restrict__ seg,
+                                                          const uint8_t* __restrict__ valid, T* __restrict__ out,
+                                                          T* __restrict__ conv_in) {
+  constexpr int NP = 8 / int(sizeof(T));  // channel pairs per 16 bytes
+  constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
+  const int chunks = int(cp.d / (2 * NP));
+  const int c = int(blockIdx.z) * 128 + int(threadIdx.x);
+  if (c >= chunks) return;
+  const int dil = cp.dil;
+  const int p_first = int(blockIdx.x) * CS_RUN * dil + int(blockIdx.y);
+  const int64_t cc = int64_t(c) * 2 * NP;
+  const int64_t step = int64_t(dil) * cp.d;  // elements between consecutive positions of the stream
   // per-channel parameters, with the norm weight folded into the taps
-  const int64_t cc = c0 + lane * VEC;  // this thread's channels
-  float gw[VEC], wt[K][VEC], bias[VEC];
+  float2 gw[NP], wt[K][NP], bias[NP];
 #pragma unroll
-  for (int j = 0; j < VEC; ++j) {
-    gw[j] = cp.norm_w[cc + j];
-    bias[j] = cp.bias ? cp.bias[cc + j] : 0.f;
+  for (int i = 0; i < NP; ++i) {
+    gw[i] = make_float2(__ldg(cp.norm_w + cc + 2 * i), __ldg(cp.norm_w + cc + 2 * i + 1));
+    bias[i] = cp.bias ? make_float2(__ldg(cp.bias + cc + 2 * i), __ldg(cp.bias + cc + 2 * i + 1)) : make_float2(0.f, 0.f);
 #pragma unroll
-    for (int tap = 0; tap < K; ++tap) wt[tap][j] = cp.weight[(cc + j) * K + tap] * gw[j];
+    for (int tap = 0; tap < K; ++tap)
+      wt[tap][i] = make_float2(__ldg(cp.weight + (cc + 2 * i) * K + tap) * gw[i].x,
+                               __ldg(cp.weight + (cc + 2 * i + 1) * K + tap) * gw[i].y);
   }
-  asm volatile("cp.async.wait_all;" ::: "memory");
-  __syncthreads();
-  const uint32_t Tu = uint32_t(T_);  // M < 2^31 (checked by the host): 32-bit position arithmetic
-  for (int i = pr; i < CT_TP; i += 4) {
-    const int64_t pos = p0 + i;
+  // the stream's previous K-1 normalised inputs (oldest first); rows before position 0 are zero
+  float2 win[K - 1][NP];
+#pragma unroll
+  for (int h = 0; h < K - 1; ++h) {
+    const int q = p_first - (K - 1 - h) * dil;
+    float2 v[NP];
+    unpack_pairs<T>(q >= 0 ? ld_nc16(mixed + int64_t(q) * cp.d + cc) : make_uint4(0, 0, 0, 0), v);
+    const float rq = q >= 0 ? __ldg(rs + q) : 0.f;
+#pragma unroll
+    for (int i = 0; i < NP; ++i) win[h][i] = fmul2(v[i], make_float2(rq, rq));
+  }
+  const T* src = mixed + int64_t(p_first) * cp.d + cc;  // row of position p_first
+  uint4 ring[CS_PF];
+  float rring[CS_PF];
+#pragma unroll
+  for (int i = 0; i < CS_PF; ++i) {
+    const int q = p_first + i * dil;
+    ring[i] = q < M ? ld_nc16(src + i * step) : make_uint4(0, 0, 0, 0);
+    rring[i] = q < M ? __ldg(rs + q) : 0.f;
+  }
+  T* dst = out + int64_t(p_first) * cp.d + cc;
+  int t = p_first % T_;
+#pragma unroll
+  for (int j = 0; j < CS_RUN; ++j) {
+    const int pos = p_first + j * dil;
     if (pos >= M) break;
-    const int t = int(uint32_t(pos) % Tu);
-    float acc[VEC], self[VEC];
+    float2 v[NP];
+    unpack_pairs<T>(ring[j % CS_PF], v);
+    const float rq = rring[j % CS_PF];
+    if (j + CS_PF < CS_RUN) {
+      const int q = pos + CS_PF * dil;
+      ring[j % CS_PF] = q < M ? ld_nc16(src + (j + CS_PF) * step) : make_uint4(0, 0, 0, 0);
+      rring[j % CS_PF] = q < M ? __ldg(rs + q) : 0.f;
+    }
+    float2 y[NP], acc[NP];
 #pragma unroll
-    for (int j = 0; j < VEC; ++j) acc[j] = bias[j];
+    for (int i = 0; i < NP; ++i) y[i] = fmul2(v[i], make_float2(rq, rq));
+    if (!seg && t >= (K - 1) * dil) {  // every tap inside the sequence (uniform across the CTA)
 #pragma unroll
-    for (int tap = 0; tap < K; ++tap) {
-      const int lag = (K - 1 - tap) * cp.dil;
-      const int r = i + H - lag;
-      float v[VEC];
-      unpack16<T>(ct_tile[r * 32 + lane], v);
-      if (tap == K - 1) {
+      for (int i = 0; i < NP; ++i) {
+        acc[i] = bias[i];
 #pragma unroll
-        for (int j = 0; j < VEC; ++j) self[j] = v[j];
+        for (int tap = 0; tap < K - 1; ++tap) acc[i] = ffma2(wt[tap][i], win[tap][i], acc[i]);
+        acc[i] = ffma2(wt[K - 1][i], y[i], acc[i]);
       }
-      if (t - lag >= 0 && (!seg || seg[pos - lag] == seg[pos])) {
-        const float rq = rsh[r];
+    } else {
+      const int64_t sp = seg ? seg[pos] : 0;
 #pragma unroll
-        for (int j = 0; j < VEC; ++j) acc[j] = fmaf(wt[tap][j], v[j] * rq, acc[j]);
+      for (int i = 0; i < NP; ++i) acc[i] = bias[i];
+#pragma unroll
+      for (int tap = 0; tap < K; ++tap) {
+        const int lag = (K - 1 - tap) * dil;
+        if (t - lag >= 0 && (!seg || seg[pos - lag] == sp)) {
+#pragma unroll
+          for (int i = 0; i < NP; ++i) acc[i] = ffma2(wt[tap][i], tap == K - 1 ? y[i] : win[tap][i], acc[i]);
+        }
       }
     }
-    const bool keep = !valid || valid[pos];
-    float o[VEC];
+    float2 o[NP];
 #pragma unroll
-    for (int j = 0; j < VEC; ++j) o[j] = keep ? self[j] + silu_f(acc[j]) : 0.f;
-    *reinterpret_cast<uint4*>(out + pos * cp.d + cc) = pack16<T>(o);
+    for (int i = 0; i < NP; ++i) {
+      if constexpr (BF) {
+        const float2 h = fmul2(acc[i], make_float2(0.5f, 0.5f));
+        o[i] = fadd2(v[i], ffma2(h, make_float2(tanh_approx(h.x), tanh_approx(h.y)), h));
+      } else {
+        o[i] = make_float2(v[i].x + silu_f(acc[i].x), v[i].y + silu_f(acc[i].y));
+      }
+    }
+    if (valid && !valid[pos]) {
+#pragma unroll
+      for (int i = 0; i < NP; ++i) o[i] = make_float2(0.f, 0.f);
+    }
+    *reinterpret_cast<uint4*>(dst + j * step) = pack_pairs<T>(o);
     if (conv_in) {
-      const float r = rsh[i + H];
 #pragma unroll
-      for (int j = 0; j < VEC; ++j) o[j] = self[j] * r * gw[j];
-      *reinterpret_cast<uint4*>(conv_in + pos * cp.d + cc) = pack16<T>(o);
+      for (int i = 0; i < NP; ++i) o[i] = fmul2(y[i], gw[i]);
+      *reinterpret_cast<uint4*>(conv_in + int64_t(pos) * cp.d + cc) = pack_pairs<T>(o);
     }
+#pragma unroll
+    for (int h = 0; h + 1 < K - 1; ++h)
+#pragma unroll
+      for (int i = 0; i < NP; ++i) win[h][i] = win[h + 1][i];
+#pragma unroll
+    for (int i = 0; i < NP; ++i) win[K - 2][i] = y[i];
+    t += dil;
+    while (t >= T_) t -= T_;
   }
 }
 

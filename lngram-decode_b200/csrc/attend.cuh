@@ -327,22 +327,26 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
     }
     ss_stage = s;
     if (coop) {
-      // piece f of the C x (DT / 8) 16-byte pieces: row f / (DT / 8), piece f % (DT / 8); the row
-      // index comes from the lane that computed it; invalid rows are zero-filled (source size 0)
-      constexpr int PPR = DT / 8, NP = C * PPR;
+      // 16-byte pieces: G lanes per row copy pieces 0..G-1 of 32 / G rows per instruction (the row
+      // index comes from the lane that computed it); each lane copies the pieces G..DT/8-1 of its own
+      // row; invalid rows are zero-filled (source size 0)
+      constexpr int PPR = DT / 8;
+      constexpr int G = PPR >= 16 ? 16 : (PPR >= 8 ? 8 : (PPR >= 4 ? 4 : (PPR >= 2 ? 2 : 1)));
+      constexpr int RPI = 32 / G;
       const int32_t myrow = int32_t(rows[0]);
-      const unsigned char* tb = static_cast<const unsigned char*>(p.ts.tab[0]);
-      const uint32_t dst0 = smem_addr(stage_base + s * SB);
+      const unsigned char* tbl = static_cast<const unsigned char*>(p.ts.tab[0]) + (lane % G) * 16;
+      const uint32_t dst_l = smem_addr(stage_base + s * SB) + uint32_t((lane / G) * ROWB + (lane % G) * 16);
 #pragma unroll
-      for (int i = 0; i < (NP + 31) / 32; ++i) {
-        const int f = i * 32 + lane;
-        const int fq = f < NP ? f : NP - 1;
-        const int q = fq / PPR, pc = fq - q * PPR;
-        const int32_t rq = __shfl_sync(0xffffffffu, myrow, q);
-        if (NP % 32 == 0 || f < NP)
-          cp_async16(dst0 + uint32_t(q * ROWB + pc * 16), tb + int64_t(rq < 0 ? 0 : rq) * ROWB + pc * 16,
-                     rq < 0 ? 0u : 16u);
+      for (int i = 0; i < C / RPI; ++i) {
+        const int32_t rq = __shfl_sync(0xffffffffu, myrow, i * RPI + lane / G);
+        cp_async16(dst_l + uint32_t(i * RPI * ROWB), tbl + uint64_t(uint32_t(rq < 0 ? 0 : rq)) * ROWB,
+                   rq < 0 ? 0u : 16u);
       }
+      const uint32_t dst_own = smem_addr(row_smem);
+      const unsigned char* src_own = static_cast<const unsigned char*>(p.ts.tab[0]) +
+                                     uint64_t(uint32_t(myrow < 0 ? 0 : myrow)) * ROWB;
+#pragma unroll
+      for (int pc = G; pc < PPR; ++pc) cp_async16(dst_own + pc * 16, src_own + pc * 16, myrow < 0 ? 0u : 16u);
       cp_async_mbar_arrive(&bars[s]);
     }
     const bool first = pend_chunk == 0 && lane == 0;

@@ -332,6 +332,275 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// ------------------------------------------------------------------ two-SM form (cta_group::2)
+// A cluster of two CTAs on two SMs computes 256 x BN output tiles with M = 256 MMAs issued by the
+// first CTA of the pair (the leader): each CTA stages its own 128 rows of A and half of the BN rows
+// of B (TMA, 128-byte swizzle), so every SM loads 2/3 of the operand bytes the one-CTA form loads
+// per FLOP (the one-CTA GEMM is bounded by L2->SM operand traffic at these shapes).  Each CTA's TMEM
+// holds its 128 rows x BN fp32 accumulator, twice (tile i and tile i + 1).
+//   * both CTAs' TMA loads complete on the leader's full[s] barrier (.cta_group::2 loads), whose
+//     expected bytes the leader's producer posts for the pair;
+//   * the leader's MMA commits free a stage in both CTAs (tcgen05.commit multicast to empty[s]) and
+//     mark an accumulator ready in both (acc_full);
+//   * all 256 epilogue threads of the pair arrive on the leader's acc_empty before the accumulator is
+//     reused (the second CTA's threads remotely).
+// Waits are bounded as in the one-CTA form; both CTAs meet at cluster barriers after set-up and
+// before the TMEM is released.
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of this CTA's shared variable `p` as seen in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t mapa_shared(const void* p, uint32_t rank) {
+  uint32_t a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_addr(p)), "r"(rank));
+  return a;
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void cluster_sync_all() {  // every thread of both CTAs (warps converged)
+  __syncwarp();
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int32_t x, int32_t y,
+                                                 uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster)
+      : "memory");
+}
+__device__ __forceinline__ void umma_bf16_pair(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accum)
+      : "memory");
+}
+// arrive (once the MMAs issued so far complete) on the barrier at this offset in both CTAs
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}" ::"r"(
+          smem_addr(bar))
+      : "memory");
+}
+
+template <int BN>
+struct Tc2Cfg {
+  static constexpr int BM = 256;  // rows per pair tile (128 per CTA)
+  static constexpr uint32_t A_BYTES = TC_BM * TC_BK * 2;
+  static constexpr uint32_t B_BYTES = (BN / 2) * TC_BK * 2;
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
+  static constexpr uint32_t TMEM_COLS = TcCfg<BN>::TMEM_COLS;
+  static constexpr size_t SMEM = size_t(STAGES) * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static_assert((BN / 2) % 8 == 0 && BN % 16 == 0 && BN <= 256, "pair tile width");
+};
+
+template <int BN, int MODE, int BITS = 1>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+    tc_gemm2_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                    TcGemmParams p) {
+  using Cfg = Tc2Cfg<BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t tc_smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + size_t(STAGES) * Cfg::STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;  // [2] (both CTAs) leader's MMA commit: accumulator ready
+  uint64_t* acc_empty = acc_full + 2;   // [2] (leader) 256 epilogue arrivals: accumulator drained
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile uint32_t* abort_flag = tmem_slot + 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int64_t pair = blockIdx.x >> 1, npair = gridDim.x >> 1;
+  const int64_t n_tiles = (p.N + BN - 1) / BN, m_tiles = (p.M + Cfg::BM - 1) / Cfg::BM;
+  const int64_t tiles = n_tiles * m_tiles;
+  const int KB = int((p.K + TC_BK - 1) / TC_BK);
+  auto tile_of = [&](int64_t t, int64_t& m0, int64_t& n0) {
+    m0 = (t / n_tiles) * Cfg::BM;
+    n0 = (t % n_tiles) * BN;
+  };
+  auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
+    if (*abort_flag) return false;
+    if (mbar_wait_bounded(bar, parity, &g_error_word, DEV_ERR_WAIT_TIMEOUT)) return true;
+    *abort_flag = 1u;
+    return false;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 256);
+    }
+    *abort_flag = 0u;
+    fence_mbar_init();
+    tma_prefetch_desc(&tma_a);
+    tma_prefetch_desc(&tma_b);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                 "r"(Cfg::TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers initialised and TMEM allocated in both CTAs
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {  // TMA producer: this CTA's A rows and B half, completing on the leader's barrier
+      uint32_t it = 0;
+      const uint32_t full_l0 = mapa_shared(&full[0], 0);
+      for (int64_t t = pair; t < tiles; t += npair) {
+        int64_t m0, n0;
+        tile_of(t, m0, n0);
+        bool ok = true;
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s = int(it % STAGES);
+          if (it >= uint32_t(STAGES) && !wait(&empty[s], ((it / STAGES) - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          if (leader) mbar_arrive_expect_tx(&full[s], 2 * Cfg::STAGE_BYTES);
+          uint8_t* st = base + size_t(s) * Cfg::STAGE_BYTES;
+          const int32_t ka = int32_t((int64_t(kb) * TC_BK) % p.a_kperiod), kbx = int32_t(kb * TC_BK);
+          const uint32_t fb = full_l0 + uint32_t(s) * 8u;
+          tma_load_2d_pair(st, &tma_a, ka, int32_t(m0 + int64_t(rank) * TC_BM), fb);
+          tma_load_2d_pair(st + Cfg::A_BYTES, &tma_b, kbx, int32_t(n0 + int64_t(rank) * (BN / 2)), fb);
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {  // MMA issuer for the pair
+      constexpr uint32_t idesc = umma_idesc_bf16(Cfg::BM, BN);
+      uint32_t it = 0, ti = 0;
+      for (int64_t t = pair; t < tiles; t += npair, ++ti) {
+        const uint32_t ab = ti & 1;
+        if (ti >= 2 && !wait(&acc_empty[ab], ((ti >> 1) - 1) & 1)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + ab * uint32_t(BN);
+        bool ok = true;
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s = int(it % STAGES);
+          if (!wait(&full[s], (it / STAGES) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint8_t* st = base + size_t(s) * Cfg::STAGE_BYTES;
+          const uint64_t da = umma_desc_sw128(st), db = umma_desc_sw128(st + Cfg::A_BYTES);
+#pragma unroll
+          for (int k = 0; k < TC_BK / 16; ++k)
+            umma_bf16_pair(d, da + uint64_t(2 * k), db + uint64_t(2 * k), idesc, (kb != 0 || k != 0) ? 1u : 0u);
+          umma_commit_pair(&empty[s]);
+        }
+        if (!ok) break;
+        umma_commit_pair(&acc_full[ab]);
+      }
+    }
+  } else {
+    // epilogue warps 2-5 of each CTA: TMEM lanes 32 (w % 4) .. +31 = this CTA's tile rows
+    const int q = warp & 3;
+    const uint32_t acc_empty_l0 = mapa_shared(&acc_empty[0], 0);
+    uint32_t ti = 0;
+    for (int64_t t = pair; t < tiles; t += npair, ++ti) {
+      const uint32_t ab = ti & 1;
+      int64_t m0, n0;
+      tile_of(t, m0, n0);
+      const bool acc_ok = wait(&acc_full[ab], (ti >> 1) & 1);
+      __syncwarp();
+      tc_fence_after();
+      const int64_t row = m0 + int64_t(rank) * TC_BM + q * 32 + lane;
+      const uint32_t tbase = tmem + (uint32_t(q * 32) << 16) + ab * uint32_t(BN);
+      if (__all_sync(0xffffffffu, acc_ok)) {
+        if constexpr (MODE == 0) {
+          const float sc = (p.rowscale && row < p.M) ? p.rowscale[row] : 1.f;
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 16) {
+            float v[16];
+            tmem_ld16(tbase + uint32_t(c), v);
+            const int64_t col = n0 + c;
+            if (row >= p.M || col >= p.N) continue;
+            if (p.c_dtype == LNG_F32) {
+              float* dst = static_cast<float*>(p.C) + row * p.ldc + col;
+              if (col + 16 <= p.N) {
+#pragma unroll
+                for (int i = 0; i < 16; i += 4)
+                  *reinterpret_cast<float4*>(dst + i) =
+                      make_float4(v[i] * sc, v[i + 1] * sc, v[i + 2] * sc, v[i + 3] * sc);
+              } else {
+                for (int i = 0; i < 16 && col + i < p.N; ++i) dst[i] = v[i] * sc;
+              }
+            } else {
+              __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.C) + row * p.ldc + col;
+              if (col + 16 <= p.N) {
+                uint32_t w[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  __nv_bfloat162 b2 = __floats2bfloat162_rn(v[2 * i] * sc, v[2 * i + 1] * sc);
+                  w[i] = *reinterpret_cast<uint32_t*>(&b2);
+                }
+                *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+                *reinterpret_cast<uint4*>(dst + 8) = make_uint4(w[4], w[5], w[6], w[7]);
+              } else {
+                for (int i = 0; i < 16 && col + i < p.N; ++i) dst[i] = __float2bfloat16_rn(v[i] * sc);
+              }
+            }
+          }
+        } else {
+          constexpr int RPT = BN / BITS;
+          const int64_t r0 = n0 / BITS;
+          uint32_t packed[(RPT + 3) / 4];
+#pragma unroll
+          for (int i = 0; i < (RPT + 3) / 4; ++i) packed[i] = 0u;
+#pragma unroll
+          for (int c = 0; c < BN; c += 16) {
+            float v[16];
+            tmem_ld16(tbase + uint32_t(c), v);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int col = c + i, qq = col / BITS, bit = col % BITS;
+              packed[qq >> 2] |= uint32_t(v[i] > 0.f ? 1u : 0u) << ((qq & 3) * 8 + bit);
+            }
+          }
+          if (row < p.M) {
+            uint8_t* dst = p.codes + row * p.routes + r0;
+            const int64_t left = p.routes - r0;
+            const int nr = int(left < RPT ? left : RPT);
+            if (nr == RPT && RPT % 4 == 0 && (p.routes & 3) == 0 && (r0 & 3) == 0) {
+#pragma unroll
+              for (int i = 0; i < RPT / 4; ++i) reinterpret_cast<uint32_t*>(dst)[i] = packed[i];
+            } else {
+#pragma unroll
+              for (int i = 0; i < RPT; ++i)
+                if (i < nr) dst[i] = uint8_t(packed[i >> 2] >> ((i & 3) * 8));
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive_cluster(acc_empty_l0 + ab * 8u);
+    }
+  }
+  tc_fence_before();
+  cluster_sync_all();  // every MMA of the pair retired and read before the TMEM is released
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(Cfg::TMEM_COLS) : "memory");
+  }
+}
+
 // fp32 weight -> [rows, 3*in_dim] bf16 (W1 | W2 | W3) with W = W1 + W2 + W3.
 __global__ void split_bf16x3_kernel(const float* __restrict__ w, int64_t rows, int64_t in_dim,
                                     __nv_bfloat16* __restrict__ out) {
@@ -386,6 +655,27 @@ inline int launch_tc_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const Tc
   return LNG_OK;
 }
 
+// The two-SM form for large row counts (at least one 256-row tile per SM pair); npairs / splits
+// are not supported by it.
+template <int BN, int MODE, int BITS = 1>
+inline int launch_tc_gemm2(const CUtensorMap& ta, const CUtensorMap& tb, const TcGemmParams& p, cudaStream_t stream) {
+  if (MODE == 0 && ((reinterpret_cast<uintptr_t>(p.C) & 15) || p.ldc % (p.c_dtype == LNG_F32 ? 4 : 8)))
+    return fail(LNG_ERR_ARGUMENT, "tc_gemm: output base / row stride not 16-byte aligned");
+  auto kern = tc_gemm2_kernel<BN, MODE, BITS>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Tc2Cfg<BN>::SMEM));
+  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(tc_gemm2_kernel)");
+  const int64_t tiles = ((p.N + BN - 1) / BN) * ((p.M + Tc2Cfg<BN>::BM - 1) / Tc2Cfg<BN>::BM);
+  const int64_t pairs = tiles < num_sms() / 2 ? tiles : num_sms() / 2;
+  kern<<<int(2 * pairs), 192, Tc2Cfg<BN>::SMEM, stream>>>(ta, tb, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_status(e, "tc_gemm2_kernel launch");
+  return LNG_OK;
+}
+#ifndef TC_PAIR_MIN_M
+#define TC_PAIR_MIN_M 8192
+#endif
+constexpr int64_t TC2_MIN_M = TC_PAIR_MIN_M;  // rows from which the two-SM form is used
+
 inline bool tc_aligned(const void* p, int64_t ld) {
   return (reinterpret_cast<uintptr_t>(p) & 15) == 0 && (ld % 8) == 0;
 }
@@ -400,10 +690,11 @@ inline int tc_gemm_bf16(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16
     return LNG_ERR_UNSUPPORTED;
   // 256-column tiles (twice the tensor-pipe efficiency of 128 measured here) unless N <= 128
   const int BN = N > 128 ? 256 : 128;
+  const bool pair = M >= TC2_MIN_M;
   CUtensorMap ta, tb;
   int st = make_tmap_bf16(&ta, A, M, K, lda, TC_BM);
   if (st) return st;
-  st = make_tmap_bf16(&tb, B, N, K, ldb, BN);
+  st = make_tmap_bf16(&tb, B, N, K, ldb, pair ? BN / 2 : BN);
   if (st) return st;
   TcGemmParams p{};
   p.M = M;
@@ -414,6 +705,7 @@ inline int tc_gemm_bf16(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16
   p.ldc = ldc;
   p.c_dtype = c_dtype;
   p.rowscale = rowscale;
+  if (pair) return BN == 256 ? launch_tc_gemm2<256, 0>(ta, tb, p, stream) : launch_tc_gemm2<128, 0>(ta, tb, p, stream);
   return BN == 256 ? launch_tc_gemm<256, 0>(ta, tb, p, stream) : launch_tc_gemm<128, 0>(ta, tb, p, stream);
 }
 
@@ -424,10 +716,11 @@ inline int tc_router_split(const __nv_bfloat16* x, int64_t n, int64_t in_dim, in
   if (bits < 1 || bits > 6 || in_dim % TC_BK != 0 || !tc_aligned(x, x_stride) || !tc_aligned(w_split, 3 * in_dim))
     return LNG_ERR_UNSUPPORTED;
   const int BN = bits <= 4 ? 64 * bits : 32 * bits;  // 64 routes per tile up to 4 bits, else 32
+  const bool pair = n >= TC2_MIN_M;
   CUtensorMap ta, tb;
   int st = make_tmap_bf16(&ta, x, n, in_dim, x_stride, TC_BM);
   if (st) return st;
-  st = make_tmap_bf16(&tb, w_split, routes * bits, 3 * in_dim, 3 * in_dim, BN);
+  st = make_tmap_bf16(&tb, w_split, routes * bits, 3 * in_dim, 3 * in_dim, pair ? BN / 2 : BN);
   if (st) return st;
   TcGemmParams p{};
   p.M = n;
@@ -437,6 +730,16 @@ inline int tc_router_split(const __nv_bfloat16* x, int64_t n, int64_t in_dim, in
   p.bits = bits;
   p.routes = routes;
   p.codes = codes;
+  if (pair) {
+    switch (bits) {
+      case 1: return launch_tc_gemm2<64, 1, 1>(ta, tb, p, stream);
+      case 2: return launch_tc_gemm2<128, 1, 2>(ta, tb, p, stream);
+      case 3: return launch_tc_gemm2<192, 1, 3>(ta, tb, p, stream);
+      case 4: return launch_tc_gemm2<256, 1, 4>(ta, tb, p, stream);
+      case 5: return launch_tc_gemm2<160, 1, 5>(ta, tb, p, stream);
+      default: return launch_tc_gemm2<192, 1, 6>(ta, tb, p, stream);
+    }
+  }
   switch (bits) {
     case 1: return launch_tc_gemm<64, 1, 1>(ta, tb, p, stream);
     case 2: return launch_tc_gemm<128, 1, 2>(ta, tb, p, stream);

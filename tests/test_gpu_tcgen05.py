@@ -31,7 +31,9 @@ def gemm(lngram, a, b, out_dtype, rowscale=None):
 
 
 @pytest.mark.parametrize("m,n,k", [(128, 256, 64), (256, 128, 1024), (65536 // 16, 2176, 1024), (300, 1024, 2176),
-                                   (129, 136, 72), (1, 16, 16), (777, 520, 200)])
+                                   (129, 136, 72), (1, 16, 16), (777, 520, 200),
+                                   # two-SM (cta_group::2) form: 256-row pair tiles, ragged rows / columns
+                                   (8192 + 77, 2176, 1024), (8704, 1024, 2176), (9000, 100, 64)])
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
 def test_tc_gemm_matches_fp32_reference(lngram, m, n, k, out_dtype):
     g = torch.Generator(device=DEV).manual_seed(m * 7 + n)
@@ -55,13 +57,15 @@ def test_tc_gemm_rowscale_and_strided_operands(lngram):
     torch.testing.assert_close(got, want, rtol=1e-5, atol=1e-5 * want.abs().max().item())
 
 
-@pytest.mark.parametrize("bits,routes,in_dim", [(4, 184, 1024), (5, 184, 1024), (4, 182, 2048), (4, 8, 128),
-                                                (3, 40, 64)])
-def test_tc_router_codes_fp32_accurate(lngram, bits, routes, in_dim):
+@pytest.mark.parametrize("bits,routes,in_dim,n", [(4, 184, 1024, 4099), (5, 184, 1024, 4099), (4, 182, 2048, 4099),
+                                                  (4, 8, 128, 4099), (3, 40, 64, 4099),
+                                                  # two-SM form (from 8192 rows)
+                                                  (4, 184, 1024, 8192 + 5), (5, 184, 1024, 8192 + 300),
+                                                  (3, 40, 64, 8192 + 1)])
+def test_tc_router_codes_fp32_accurate(lngram, bits, routes, in_dim, n):
     """bf16 inputs x fp32 router weight through the bf16x3 split: codes agree with the fp32 sign
     everywhere the fp32 logit is not within 1e-5 of zero."""
     lib = lngram._lib
-    n = 4099
     g = torch.Generator(device=DEV).manual_seed(bits * 1000 + routes)
     x = torch.randn(n, in_dim, device=DEV, generator=g).to(torch.bfloat16)
     w = torch.randn(routes * bits, in_dim, device=DEV, generator=g) * 0.02

@@ -395,11 +395,38 @@ struct Tc2Cfg {
   static constexpr uint32_t A_BYTES = TC_BM * TC_BK * 2;
   static constexpr uint32_t B_BYTES = (BN / 2) * TC_BK * 2;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
+  // epilogue staging: one 32-row x 128-byte buffer per epilogue warp (swizzled 16-byte chunks)
+  static constexpr uint32_t EPI_BYTES = 4 * 4096;
+  static constexpr int FIT = int((227 * 1024 - EPI_BYTES - 1024 - 256) / STAGE_BYTES);
+  static constexpr int STAGES = FIT > 8 ? 8 : FIT;
   static constexpr uint32_t TMEM_COLS = TcCfg<BN>::TMEM_COLS;
-  static constexpr size_t SMEM = size_t(STAGES) * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr size_t SMEM = size_t(STAGES) * STAGE_BYTES + EPI_BYTES + 1024 /*align*/ + 256 /*barriers*/;
   static_assert((BN / 2) % 8 == 0 && BN % 16 == 0 && BN <= 256, "pair tile width");
+  static_assert(STAGES >= 3, "pair pipeline depth");
 };
+
+// 32 TMEM columns of this warp's 32 lanes; tmem_wait32 makes the registers valid (it names them as
+// operands, so no use can be scheduled above it).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait32(uint32_t (&r)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]),
+                 "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]),
+                 "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]),
+                 "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
 
 template <int BN, int MODE, int BITS = 1>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
@@ -409,7 +436,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t tc_smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(base + size_t(STAGES) * Cfg::STAGE_BYTES);
+  uint8_t* epi = base + size_t(STAGES) * Cfg::STAGE_BYTES;  // epilogue staging buffers
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi + Cfg::EPI_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;  // [2] (both CTAs) leader's MMA commit: accumulator ready
   uint64_t* acc_empty = acc_full + 2;   // [2] (leader) 256 epilogue arrivals: accumulator drained
@@ -526,38 +554,66 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       const uint32_t tbase = tmem + (uint32_t(q * 32) << 16) + ab * uint32_t(BN);
       if (__all_sync(0xffffffffu, acc_ok)) {
         if constexpr (MODE == 0) {
+          // 128-byte column chunks (64 bf16 / 32 f32) of this warp's 32 rows: TMEM -> registers (row
+          // per lane) -> this warp's staging buffer (16-byte pieces swizzled by row) -> read back four
+          // rows per instruction, so each global store writes whole 128-byte row segments
           const float sc = (p.rowscale && row < p.M) ? p.rowscale[row] : 1.f;
+          const bool f32 = p.c_dtype == LNG_F32;
+          const int CW = f32 ? 32 : 64;
+          const int esz = f32 ? 4 : 2;
+          const int64_t y0 = m0 + int64_t(rank) * TC_BM + q * 32;
+          uint8_t* buf = epi + q * 4096;
 #pragma unroll 1
-          for (int c = 0; c < BN; c += 16) {
-            float v[16];
-            tmem_ld16(tbase + uint32_t(c), v);
-            const int64_t col = n0 + c;
-            if (row >= p.M || col >= p.N) continue;
-            if (p.c_dtype == LNG_F32) {
-              float* dst = static_cast<float*>(p.C) + row * p.ldc + col;
-              if (col + 16 <= p.N) {
+          for (int c = 0; c < BN; c += CW) {
+            uint32_t r0[32], r1[32];
+            tmem_ld32(tbase + uint32_t(c), r0);
+            if (!f32) tmem_ld32(tbase + uint32_t(c) + 32u, r1);
+            tmem_wait32(r0);
+            if (!f32) tmem_wait32(r1);
+            uint4* rowp = reinterpret_cast<uint4*>(buf + lane * 128);
+            if (f32) {
 #pragma unroll
-                for (int i = 0; i < 16; i += 4)
-                  *reinterpret_cast<float4*>(dst + i) =
-                      make_float4(v[i] * sc, v[i + 1] * sc, v[i + 2] * sc, v[i + 3] * sc);
-              } else {
-                for (int i = 0; i < 16 && col + i < p.N; ++i) dst[i] = v[i] * sc;
-              }
+              for (int j = 0; j < 8; ++j)
+                rowp[j ^ (lane & 7)] = make_uint4(__float_as_uint(__uint_as_float(r0[4 * j]) * sc),
+                                                  __float_as_uint(__uint_as_float(r0[4 * j + 1]) * sc),
+                                                  __float_as_uint(__uint_as_float(r0[4 * j + 2]) * sc),
+                                                  __float_as_uint(__uint_as_float(r0[4 * j + 3]) * sc));
             } else {
-              __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.C) + row * p.ldc + col;
-              if (col + 16 <= p.N) {
-                uint32_t w[8];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                  __nv_bfloat162 b2 = __floats2bfloat162_rn(v[2 * i] * sc, v[2 * i + 1] * sc);
+              for (int j = 0; j < 8; ++j) {
+                const uint32_t(&rr)[32] = j < 4 ? r0 : r1;
+                const int b = (j & 3) * 8;
+                uint32_t w[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(rr[b + 2 * i]) * sc,
+                                                            __uint_as_float(rr[b + 2 * i + 1]) * sc);
                   w[i] = *reinterpret_cast<uint32_t*>(&b2);
                 }
-                *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
-                *reinterpret_cast<uint4*>(dst + 8) = make_uint4(w[4], w[5], w[6], w[7]);
-              } else {
-                for (int i = 0; i < 16 && col + i < p.N; ++i) dst[i] = __float2bfloat16_rn(v[i] * sc);
+                rowp[j ^ (lane & 7)] = make_uint4(w[0], w[1], w[2], w[3]);
               }
             }
+            __syncwarp();
+            const int j = lane & 7;                  // this lane's 16-byte piece of a row
+            const int64_t col = n0 + c + j * (16 / esz);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int rr = i * 4 + (lane >> 3);      // row within the warp's 32
+              const int64_t grow = y0 + rr;
+              const uint4 v = *reinterpret_cast<const uint4*>(buf + rr * 128 + ((j ^ (rr & 7)) * 16));
+              if (grow >= p.M || col >= p.N) continue;
+              uint8_t* dst = static_cast<uint8_t*>(p.C) + (grow * p.ldc + col) * esz;
+              if (col + 16 / esz <= p.N) {
+                *reinterpret_cast<uint4*>(dst) = v;
+              } else {  // ragged last columns
+                const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+                for (int e = 0; e < 16 / esz && col + e < p.N; ++e) {
+                  if (f32) reinterpret_cast<uint32_t*>(dst)[e] = vv[e];
+                  else reinterpret_cast<uint16_t*>(dst)[e] = uint16_t(vv[e >> 1] >> ((e & 1) * 16));
+                }
+              }
+            }
+            __syncwarp();
           }
         } else {
           constexpr int RPT = BN / BITS;

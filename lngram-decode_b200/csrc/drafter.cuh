@@ -56,6 +56,7 @@ struct lng_drafter {
   void* tab[LNG_MAX_ORDERS] = {};
   float* ss[LNG_MAX_ORDERS] = {};
   float *router_w = nullptr, *prev_norm = nullptr, *cur_norm = nullptr, *start = nullptr;
+  __nv_bfloat16* router_w_split = nullptr;  // router weight as bf16 parts W1 | W2 | W3 (made once)
   float *out_norm = nullptr;
   void *w_qk = nullptr, *w_vo = nullptr;
   std::vector<void*> owned;
@@ -219,11 +220,11 @@ static int drafter_codes(lng_drafter* dr, const int64_t* cur, const int64_t* pre
                                dr->start, dr->router_eps, feat, s);
   if (st) return st;
   if (codes_stride == dr->R)
-    return lng_route_codes(feat, LNG_F32, M, 2 * dr->d, 2 * dr->d, dr->router_w, dr->R, int32_t(dr->bits), codes_out,
-                           LNG_U8, nullptr, s);
+    return route_codes_presplit(feat, M, 2 * dr->d, dr->router_w, dr->router_w_split, dr->R, int32_t(dr->bits),
+                                codes_out, dr->stream);
   for (int64_t i = 0; i < M; ++i) {  // strided destination (batched drafting): one row at a time
-    st = lng_route_codes(feat + i * 2 * dr->d, LNG_F32, 1, 2 * dr->d, 2 * dr->d, dr->router_w, dr->R,
-                         int32_t(dr->bits), codes_out + i * codes_stride, LNG_U8, nullptr, s);
+    st = route_codes_presplit(feat + i * 2 * dr->d, 1, 2 * dr->d, dr->router_w, dr->router_w_split, dr->R,
+                              int32_t(dr->bits), codes_out + i * codes_stride, dr->stream);
     if (st) return st;
   }
   return LNG_OK;
@@ -331,6 +332,16 @@ extern "C" int lng_drafter_create(const lng_drafter_numbers* num, const lng_arra
   if ((st = upload_f32(D, find_array(arrays, n_arrays, "mem_norm"), D->Dt, &mem_norm))) return st;
   if ((st = upload_f32(D, find_array(arrays, n_arrays, "kv_proj"), 2 * KH * D->Dt, &kv_proj))) return st;
   if ((st = upload_f32(D, find_array(arrays, n_arrays, "router"), D->R * D->bits * 2 * D->d, &D->router_w))) return st;
+  {  // the router weight's bf16x3 split, used by every small-batch code computation of this drafter
+    const int64_t rows = D->R * D->bits, in_dim = 2 * D->d;
+    void* wsp = nullptr;
+    LNG_CUDA(cudaMalloc(&wsp, size_t(rows) * 3 * in_dim * sizeof(__nv_bfloat16)));
+    D->owned.push_back(wsp);
+    D->router_w_split = static_cast<__nv_bfloat16*>(wsp);
+    split_bf16x3_kernel<<<grid_for(rows * in_dim, 256, 16), 256>>>(D->router_w, rows, in_dim, D->router_w_split);
+    LNG_CUDA(cudaGetLastError());
+    LNG_LAUNCHED("split_bf16x3_kernel");
+  }
   if ((st = upload_f32(D, find_array(arrays, n_arrays, "router_prev_norm"), D->d, &D->prev_norm))) return st;
   if ((st = upload_f32(D, find_array(arrays, n_arrays, "router_cur_norm"), D->d, &D->cur_norm))) return st;
   if ((st = upload_f32(D, find_array(arrays, n_arrays, "router_start"), D->d, &D->start))) return st;
@@ -641,8 +652,8 @@ extern "C" int lng_drafter_draft_batch(lng_drafter* d, const int64_t* prefix, in
       st = lng_embed2_features(b.ids, scratch_i + nseq, nseq, d->E, d->e_dtype, d->V, d->d, d->prev_norm,
                                d->cur_norm, d->start, d->router_eps, b.feat, reinterpret_cast<lng_stream_t>(d->stream));
       if (st) return st;
-      st = lng_route_codes(b.feat, LNG_F32, nseq, 2 * d->d, 2 * d->d, d->router_w, R, int32_t(d->bits), dense, LNG_U8,
-                           nullptr, reinterpret_cast<lng_stream_t>(d->stream));
+      st = route_codes_presplit(b.feat, nseq, 2 * d->d, d->router_w, d->router_w_split, R, int32_t(d->bits), dense,
+                                d->stream);
       if (st) return st;
       LNG_CUDA(cudaMemcpy2DAsync(codes + (tpos + 1) * R, size_t(P * R), dense, size_t(R), size_t(R), size_t(nseq),
                                  cudaMemcpyDeviceToDevice, d->stream));

@@ -137,22 +137,43 @@ extern "C" int lng_quantize_route_logits(const float* logits, int64_t n, int64_t
 
 namespace lng {
 // Sign-packed codes from split-K partial logits [splits, routes * bits, ldp >= n] (split order sum).
+// Split-K reduce + sign pack of the small-batch router.  A 256-thread CTA owns 32 rows x RB routes
+// (CB = RB * bits logit columns): thread (c, row) sums the `splits` partials of one logit in a fixed
+// order (consecutive threads read consecutive rows of a partial), the logits meet in shared
+// memory, and thread (route, row) packs that route's sign bits.
 template <typename CodeT>
-__global__ void router_reduce_pack_kernel(const float* __restrict__ part, int splits, int64_t n, int64_t ldp,
-                                          int64_t routes, int bits, CodeT* __restrict__ codes,
-                                          float* __restrict__ logits) {
-  const int64_t total = n * routes;
+__global__ void __launch_bounds__(256) router_reduce_pack_kernel(const float* __restrict__ part, int splits, int64_t n,
+                                                                 int64_t ldp, int64_t routes, int bits,
+                                                                 CodeT* __restrict__ codes, float* __restrict__ logits) {
+  __shared__ float lg[8][32];
+  const int rb = bits <= 8 ? 8 / bits : 1;  // routes per CTA
+  const int cb = rb * bits;                 // logit columns per CTA (<= 8)
   const int64_t cols = routes * bits;
-  for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < total; e += int64_t(gridDim.x) * blockDim.x) {
-    const int64_t row = e % n, r = e / n;  // consecutive threads: consecutive rows (coalesced partial reads)
-    int v = 0;
-    for (int j = 0; j < bits; ++j) {
-      float acc = 0.f;
-      for (int sp = 0; sp < splits; ++sp) acc += part[(int64_t(sp) * cols + r * bits + j) * ldp + row];
-      v |= (acc > 0.f ? 1 : 0) << j;
-      if (logits) logits[row * cols + r * bits + j] = acc;
+  const int64_t row0 = int64_t(blockIdx.x) * 32, r0 = int64_t(blockIdx.y) * rb;
+  const int t = threadIdx.x, row = t & 31, c = t >> 5;
+  const int64_t grow = row0 + row, col = r0 * bits + c;
+  if (c < cb && grow < n && col < cols) {
+    const float* pp = part + col * ldp + grow;
+    const int64_t sstride = cols * ldp;
+    float acc = 0.f;
+    int sp = 0;
+    for (; sp + 4 <= splits; sp += 4) {  // four independent loads in flight, summed in split order
+      const float v0 = pp[(sp + 0) * sstride], v1 = pp[(sp + 1) * sstride];
+      const float v2 = pp[(sp + 2) * sstride], v3 = pp[(sp + 3) * sstride];
+      acc += v0;
+      acc += v1;
+      acc += v2;
+      acc += v3;
     }
-    codes[row * routes + r] = static_cast<CodeT>(v);
+    for (; sp < splits; ++sp) acc += pp[sp * sstride];
+    lg[c][row] = acc;
+    if (logits) logits[grow * cols + col] = acc;
+  }
+  __syncthreads();
+  if (c < rb && grow < n && r0 + c < routes) {
+    int v = 0;
+    for (int j = 0; j < bits; ++j) v |= (lg[c * bits + j][row] > 0.f ? 1 : 0) << j;
+    codes[grow * routes + r0 + c] = static_cast<CodeT>(v);
   }
 }
 
@@ -163,7 +184,7 @@ __global__ void router_reduce_pack_kernel(const float* __restrict__ part, int sp
 // Scratch (x parts, W parts, partials) comes from the library pool and is released on `stream`.
 static int tc_router_small_f32(const float* x, int64_t n, int64_t in_dim, int64_t x_stride, const float* w,
                                int64_t routes, int32_t bits, void* codes, int codes_i32, float* logits,
-                              cudaStream_t stream) {
+                               cudaStream_t stream, const __nv_bfloat16* w_split = nullptr) {
   if (in_dim % TC_BK != 0 || x_stride != in_dim || n < 1 || n > 256 || (reinterpret_cast<uintptr_t>(x) & 15))
     return LNG_ERR_UNSUPPORTED;
   const int64_t cols = routes * bits;
@@ -174,16 +195,17 @@ static int tc_router_small_f32(const float* x, int64_t n, int64_t in_dim, int64_
   if (splits > KB) splits = int(KB);
   const int BN = n <= 64 ? 64 : n <= 128 ? 128 : 256;
   const int64_t ldp = (n + 3) & ~int64_t(3);  // partial rows padded so the epilogue's 16-byte stores stay aligned
-  const size_t xs_b = al256(size_t(n) * 3 * in_dim * 2), ws_b = al256(size_t(cols) * 3 * in_dim * 2),
+  const size_t xs_b = al256(size_t(n) * 3 * in_dim * 2), ws_b = w_split ? 0 : al256(size_t(cols) * 3 * in_dim * 2),
                ps_b = al256(size_t(splits) * cols * ldp * 4);
   void* scratch = nullptr;
   int st = scratch_alloc(&scratch, xs_b + ws_b + ps_b, stream);
   if (st) return st;
   auto* xs = static_cast<__nv_bfloat16*>(scratch);
-  auto* ws = reinterpret_cast<__nv_bfloat16*>(static_cast<unsigned char*>(scratch) + xs_b);
+  auto* ws = w_split ? const_cast<__nv_bfloat16*>(w_split)
+                     : reinterpret_cast<__nv_bfloat16*>(static_cast<unsigned char*>(scratch) + xs_b);
   auto* ps = reinterpret_cast<float*>(static_cast<unsigned char*>(scratch) + xs_b + ws_b);
   split_rows_bf16x3_kernel<<<grid_for(n * in_dim, 256, 16), 256, 0, stream>>>(x, n, in_dim, xs);
-  split_bf16x3_kernel<<<grid_for(cols * in_dim, 256, 16), 256, 0, stream>>>(w, cols, in_dim, ws);
+  if (!w_split) split_bf16x3_kernel<<<grid_for(cols * in_dim, 256, 16), 256, 0, stream>>>(w, cols, in_dim, ws);
   CUtensorMap ta, tb;
   st = make_tmap_bf16(&ta, ws, cols, 3 * in_dim, 3 * in_dim, TC_BM);
   if (!st) st = make_tmap_bf16(&tb, xs, n, 3 * in_dim, 3 * in_dim, BN);
@@ -209,7 +231,8 @@ static int tc_router_small_f32(const float* x, int64_t n, int64_t in_dim, int64_
                   : BN == 128 ? launch_tc_gemm<128, 0>(ta, tb, p, stream) : launch_tc_gemm<256, 0>(ta, tb, p, stream);
   }
   if (!st) {
-    const int g = grid_for(n * routes, 256, 8);
+    const int rb = bits <= 8 ? 8 / bits : 1;
+    const dim3 g(unsigned(ceil_div(n, 32)), unsigned(ceil_div(routes, rb)));
     if (codes_i32)
       router_reduce_pack_kernel<int32_t><<<g, 256, 0, stream>>>(ps, splits, n, ldp, routes, bits,
                                                                 static_cast<int32_t*>(codes), logits);
@@ -223,6 +246,21 @@ static int tc_router_small_f32(const float* x, int64_t n, int64_t in_dim, int64_
   return st;
 }
 
+}  // namespace lng
+
+namespace lng {
+// Router codes of fp32 rows given the weight and its bf16x3 split (made once by the owner of a
+// fixed weight, e.g. the drafter): the small-batch tensor-core path skips the per-call split.
+static int route_codes_presplit(const float* x, int64_t n, int64_t in_dim, const float* w,
+                                const __nv_bfloat16* w_split, int64_t routes, int32_t bits, uint8_t* codes,
+                                cudaStream_t stream) {
+  if (n >= 1 && n <= 256 && w_split) {
+    const int st = tc_router_small_f32(x, n, in_dim, in_dim, w, routes, bits, codes, 0, nullptr, stream, w_split);
+    if (st != LNG_ERR_UNSUPPORTED) return st;
+  }
+  return lng_route_codes(x, LNG_F32, n, in_dim, in_dim, w, routes, bits, codes, LNG_U8, nullptr,
+                         reinterpret_cast<lng_stream_t>(stream));
+}
 }  // namespace lng
 
 extern "C" int lng_route_codes(const void* x, int32_t x_dtype, int64_t n, int64_t in_dim, int64_t x_stride,
@@ -634,6 +672,26 @@ extern "C" int lng_rms_norm(const void* x, int32_t x_dtype, int64_t n, int64_t d
   LNG_REQUIRE(n >= 0 && d > 0, "bad shape");
   if (n == 0) return LNG_OK;
   LNG_REQUIRE(x && y, "NULL pointer");
+  const int xsz = x_dtype == LNG_F32 ? 4 : 2;
+  const int64_t vec_elems = 32 * (16 / xsz);
+  if (d % vec_elems == 0 && d / vec_elems <= RN_NV && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    // rows that fit in registers: one read of x
+    const int nv = int(d / vec_elems);
+    const unsigned gr = unsigned(ceil_div(n, 8));
+#define LNG_RNR(XT, YT) \
+  rms_norm_reg_kernel<XT, YT><<<gr, 256, 0, S(stream)>>>(static_cast<const XT*>(x), n, d, nv, w, eps, static_cast<YT*>(y))
+    bool done = true;
+    if (x_dtype == LNG_F32 && y_dtype == LNG_F32) LNG_RNR(float, float);
+    else if (x_dtype == LNG_BF16 && y_dtype == LNG_BF16) LNG_RNR(__nv_bfloat16, __nv_bfloat16);
+    else if (x_dtype == LNG_BF16 && y_dtype == LNG_F32) LNG_RNR(__nv_bfloat16, float);
+    else if (x_dtype == LNG_F32 && y_dtype == LNG_BF16) LNG_RNR(float, __nv_bfloat16);
+    else done = false;
+#undef LNG_RNR
+    if (done) {
+      LNG_LAUNCHED("rms_norm_reg_kernel");
+      return LNG_OK;
+    }
+  }
   const int g = grid_for(n * 32, 256, 16);
 #define LNG_RN(XT, YT) rms_norm_kernel<XT, YT><<<g, 256, 0, S(stream)>>>(static_cast<const XT*>(x), n, d, w, eps, static_cast<YT*>(y))
   if (x_dtype == LNG_F32 && y_dtype == LNG_F32) LNG_RN(float, float);

@@ -73,6 +73,39 @@ __global__ void rms_norm_kernel(const XT* x, int64_t n, int64_t d, const float* 
   }
 }
 
+// RMSNorm of rows short enough to stay in registers (d = 32 lanes x nv vectors x 16 bytes,
+// nv <= RN_NV): one warp per row reads the row once, reduces, and writes the scaled row.
+constexpr int RN_NV = 16;
+template <typename XT, typename YT>
+__global__ void __launch_bounds__(256) rms_norm_reg_kernel(const XT* __restrict__ x, int64_t n, int64_t d, int nv,
+                                                           const float* __restrict__ w, float eps, YT* __restrict__ y) {
+  constexpr int N = Vec16<XT>::N;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (row >= n) return;
+  const XT* xr = x + row * d;
+  float v[RN_NV][N];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < RN_NV; ++i) {
+    if (i < nv) {
+      Vec16<XT>::load(xr + (int64_t(i) * 32 + lane) * N, v[i]);
+#pragma unroll
+      for (int k = 0; k < N; ++k) ss = fmaf(v[i][k], v[i][k], ss);
+    }
+  }
+  const float r = rsqrtf(warp_sum(ss) / float(d) + eps);
+  YT* yr = y + row * d;
+#pragma unroll
+  for (int i = 0; i < RN_NV; ++i) {
+    if (i < nv) {
+      const int64_t j0 = (int64_t(i) * 32 + lane) * N;
+#pragma unroll
+      for (int k = 0; k < N; ++k) yr[j0 + k] = from_f32<YT>(w ? v[i][k] * r * w[j0 + k] : v[i][k] * r);
+    }
+  }
+}
+
 struct ConvParams {
   int64_t d;
   int k, dil;

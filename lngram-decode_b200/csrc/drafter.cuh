@@ -35,6 +35,17 @@ __global__ void copy_i64_kernel(const int64_t* __restrict__ src, int64_t* __rest
   if (i < n) dst[i * dst_stride] = src[i * src_stride];
 }
 
+// The drafted tokens of one step: ids[s] -> toks[s * ts] and out[s * os] (one launch for both).
+__global__ void store_draft_kernel(const int64_t* __restrict__ ids, int64_t n, int64_t* __restrict__ toks,
+                                   int64_t ts, int64_t* __restrict__ out, int64_t os) {
+  const int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x;
+  if (i < n) {
+    const int64_t v = ids[i];
+    toks[i * ts] = v;
+    out[i * os] = v;
+  }
+}
+
 __global__ void f32_to_bf16_kernel(const float* __restrict__ in, int64_t n, __nv_bfloat16* __restrict__ out) {
   for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < n; e += int64_t(gridDim.x) * blockDim.x)
     out[e] = __float2bfloat16_rn(in[e]);
@@ -642,14 +653,13 @@ extern "C" int lng_drafter_draft_batch(lng_drafter* d, const int64_t* prefix, in
     st = drafter_readout(d, scratch_i, nseq, src, 1, b, nullptr);
     if (st) return st;
     // next tokens -> toks[s, 2 + tpos] and tokens_out[s, g]
-    copy_i64_kernel<<<unsigned(ceil_div(nseq, 128)), 128, 0, d->stream>>>(b.ids, toks + 2 + tpos, nseq, 1, P + 1);
-    copy_i64_kernel<<<unsigned(ceil_div(nseq, 128)), 128, 0, d->stream>>>(b.ids, tokens_out + g, nseq, 1, gamma);
-    LNG_LAUNCHED("copy_i64_kernel");
+    store_draft_kernel<<<unsigned(ceil_div(nseq, 128)), 128, 0, d->stream>>>(b.ids, nseq, toks + 2 + tpos, P + 1,
+                                                                             tokens_out + g, gamma);
+    LNG_LAUNCHED("store_draft_kernel");
     if (g + 1 < gamma) {
-      // codes of the drafted tokens at position tpos + 1 (strided rows of the code buffer)
-      copy_i64_kernel<<<unsigned(ceil_div(nseq, 128)), 128, 0, d->stream>>>(toks + 1 + tpos, scratch_i + nseq, nseq,
-                                                                            P + 1, 1);
-      st = lng_embed2_features(b.ids, scratch_i + nseq, nseq, d->E, d->e_dtype, d->V, d->d, d->prev_norm,
+      // codes of the drafted tokens at position tpos + 1 (strided rows of the code buffer); their
+      // previous tokens are this step's current tokens, still in scratch_i
+      st = lng_embed2_features(b.ids, scratch_i, nseq, d->E, d->e_dtype, d->V, d->d, d->prev_norm,
                                d->cur_norm, d->start, d->router_eps, b.feat, reinterpret_cast<lng_stream_t>(d->stream));
       if (st) return st;
       st = route_codes_presplit(b.feat, nseq, 2 * d->d, d->router_w, d->router_w_split, R, int32_t(d->bits), dense,

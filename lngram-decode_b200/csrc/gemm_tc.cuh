@@ -744,7 +744,8 @@ inline int tc_gemm_bf16(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16
   if (!tc_aligned(A, lda) || !tc_aligned(B, ldb) || (reinterpret_cast<uintptr_t>(C) & 15) || (ldc % 8) || K < 16 ||
       N < 16 || M < 1)
     return LNG_ERR_UNSUPPORTED;
-  // 256-column tiles (twice the tensor-pipe efficiency of 128 measured here) unless N <= 128
+  // 256-column tiles (twice the tensor-pipe efficiency of 128 measured here) unless N <= 128; 128 for
+  // few rows was also measured and was slower (each CTA still streams all of K)
   const int BN = N > 128 ? 256 : 128;
   const bool pair = M >= TC2_MIN_M;
   CUtensorMap ta, tb;
@@ -771,8 +772,12 @@ inline int tc_router_split(const __nv_bfloat16* x, int64_t n, int64_t in_dim, in
                            cudaStream_t stream) {
   if (bits < 1 || bits > 6 || in_dim % TC_BK != 0 || !tc_aligned(x, x_stride) || !tc_aligned(w_split, 3 * in_dim))
     return LNG_ERR_UNSUPPORTED;
-  const int BN = bits <= 4 ? 64 * bits : 32 * bits;  // 64 routes per tile up to 4 bits, else 32
   const bool pair = n >= TC2_MIN_M;
+  // 64 routes per tile up to 4 bits, else 32; 16 when the row tiles are so few that wider tiles
+  // would leave most SMs idle (measured 2-3 % faster on the 1,024-node tree step)
+  int BN = bits <= 4 ? 64 * bits : 32 * bits;
+  const bool narrow = !pair && ((n + TC_BM - 1) / TC_BM) * ((routes * bits + BN - 1) / BN) < num_sms() / 2;
+  if (narrow) BN = 16 * bits;
   CUtensorMap ta, tb;
   int st = make_tmap_bf16(&ta, x, n, in_dim, x_stride, TC_BM);
   if (st) return st;
@@ -794,6 +799,16 @@ inline int tc_router_split(const __nv_bfloat16* x, int64_t n, int64_t in_dim, in
       case 4: return launch_tc_gemm2<256, 1, 4>(ta, tb, p, stream);
       case 5: return launch_tc_gemm2<160, 1, 5>(ta, tb, p, stream);
       default: return launch_tc_gemm2<192, 1, 6>(ta, tb, p, stream);
+    }
+  }
+  if (narrow) {
+    switch (bits) {
+      case 1: return launch_tc_gemm<16, 1, 1>(ta, tb, p, stream);
+      case 2: return launch_tc_gemm<32, 1, 2>(ta, tb, p, stream);
+      case 3: return launch_tc_gemm<48, 1, 3>(ta, tb, p, stream);
+      case 4: return launch_tc_gemm<64, 1, 4>(ta, tb, p, stream);
+      case 5: return launch_tc_gemm<80, 1, 5>(ta, tb, p, stream);
+      default: return launch_tc_gemm<96, 1, 6>(ta, tb, p, stream);
     }
   }
   switch (bits) {

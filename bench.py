@@ -989,7 +989,7 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=tuple(RUNNERS), default="sb_prefill")
-    ap.add_argument("--batch", type=int, default=SB["B"], help="sb_prefill sequences per GPU (32 = BASELINE; "
+    ap.add_argument("--batch", type=int, default=SB["B"], help="sb_prefill sequences per GPU (32 = the SB configuration; "
                     "smaller for ncu)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args(argv)

@@ -286,8 +286,9 @@ size_t lng_logits_topk_scratch_bytes(int64_t n, int64_t d, int64_t vocab, int32_
  * n * d * 6 (the split rows) when the tensor-core path applies -- above 4 MiB are rejected
  * (LNG_ERR_ARGUMENT): e.g. k = 3 at vocab 32000 allows n <= 932 rows on the CUDA-core path and
  * n <= 394 at d = 1024 on the tensor-core path.  The first call on a device looks up the array's
- * device address (cudaGetSymbolAddress, with that device current), so make one call on each device
- * before any stream capture.  All calls share the array and it keeps the last call's contents
+ * device address (cudaGetSymbolAddress, with that device current) and keeps it for the life of the
+ * device's context (a cudaDeviceReset invalidates it), so make one call on each device before any
+ * stream capture.  All calls share the array and it keeps the last call's contents
  * (every slot read is first written by the same call); calls that overlap on the GPU -- two streams,
  * or two threads -- race on it and must be serialised by the caller. */
 int lng_logits_topk_static(const float* h, int64_t n, int64_t d, const void* embedding, int32_t e_dtype,

@@ -13,9 +13,9 @@ from .memory import LngramMemory, RouteNgramMemoryV2
 
 __all__ = ["Bundle", "DraftOut", "GpuDrafter", "LngramMemory", "RouteNgramMemoryV2", "_lib", "load_bundle",
            "make_drafter", "read_header", "write_bundle"]
-from .seams import MemoryCache, memory_step, tree_memory_block, tree_ngram_codes, tree_slots  # noqa: E402
+from .seams import MemoryCache, ancestor_table, memory_step, tree_memory_block, tree_ngram_codes, tree_slots  # noqa: E402
 
-__all__ += ["MemoryCache", "memory_step", "tree_memory_block", "tree_ngram_codes", "tree_slots"]
+__all__ += ["MemoryCache", "ancestor_table", "memory_step", "tree_memory_block", "tree_ngram_codes", "tree_slots"]
 from . import sharded  # noqa: E402
 from .sharded import RouteShardedMemory  # noqa: E402
 

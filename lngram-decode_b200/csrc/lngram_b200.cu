@@ -10,7 +10,6 @@
 
 #include "address.cuh"
 #include "attend.cuh"
-#include "attend_tc.cuh"
 #include "gemm_simt.cuh"
 #include "gemm_tc.cuh"
 #include "logits_tc.cuh"
@@ -484,44 +483,12 @@ static int dispatch_attend_mma(int64_t Dt, const AttendParams& p, cudaStream_t s
   }
 }
 
-template <typename CodeT, typename T>
-static int launch_attend_tc(const lng_tables* t, const AttendParams& p, cudaStream_t stream) {
-  const int dt = t->table_dtype;
-  const int64_t rows = t->num_routes << (int64_t(t->bits) * t->orders[0]);
-  CUtensorMap tab, tab_tail, qa, qa_tail;
-  int st = make_tmap_16(&tab, dt, t->tables[0], rows, atc::DT, atc::DT, 64, 1, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (!st) st = make_tmap_16(&tab_tail, dt, t->tables[0], rows, atc::DT, atc::DT, 16, 1, CU_TENSOR_MAP_SWIZZLE_32B);
-  if (!st) st = make_tmap_16(&qa, dt, p.qa, p.M * p.qh, atc::DT, atc::DT, 64, atc::QN, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (!st) st = make_tmap_16(&qa_tail, dt, p.qa, p.M * p.qh, atc::DT, atc::DT, 16, atc::QN, CU_TENSOR_MAP_SWIZZLE_32B);
-  if (st) return st;
-  auto kern = attend_tc_kernel<CodeT, T>;
-  LNG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(atc::SMEM_LAUNCH)));
-  const int grid = int(std::max<int64_t>(1, std::min<int64_t>(p.M, num_sms())));
-  kern<<<grid, atc::THREADS, atc::SMEM_LAUNCH, stream>>>(tab, tab_tail, qa, qa_tail, p);
-  LNG_LAUNCHED("attend_tc_kernel");
-  return LNG_OK;
-}
-
 template <typename CodeT>
 static int attend_impl(const lng_tables* t, const AttendParams& p, int32_t u_dtype, cudaStream_t stream) {
   const int64_t Dt = int64_t(t->n_orders) * t->memory_dim;
   const bool t16 = t->table_dtype == LNG_BF16 || t->table_dtype == LNG_F16;
   // qa dtype: the activations' in normalised mode; the tables' (16-bit) or f32 in partial mode
   const int qa_dtype = p.partial ? (t16 ? t->table_dtype : LNG_F32) : u_dtype;
-  // tcgen05 path (opt-in, LNG_ATTEND_IMPL=tc): 136-dim tokens of 16-bit tables, <= 192 routes, <= 16
-  // heads, normalised output (one order of 136 dims, rows and query rows addressable by 32-bit TMA
-  // coordinates).  It computes the same result as the default warp-per-position kernel, which was
-  // measured faster at the SB shape (more positions in flight per SM); kept for further tuning.
-  static const bool tc_selected = [] {
-    const char* e = getenv("LNG_ATTEND_IMPL");
-    return e && std::string(e) == "tc";
-  }();
-  if (tc_selected && t16 && t->n_orders == 1 && t->memory_dim == atc::DT && p.partial == 0 && u_dtype == t->table_dtype &&
-      p.qh >= 1 && p.qh <= atc::QN && p.route_end - p.route_start <= atc::RP && t->orders[0] <= MAXW &&
-      (t->num_routes << (int64_t(t->bits) * t->orders[0])) < (int64_t(1) << 31) && p.M * p.qh < (int64_t(1) << 31) &&
-      (reinterpret_cast<uintptr_t>(p.qa) & 15) == 0 && (reinterpret_cast<uintptr_t>(t->tables[0]) & 15) == 0)
-    return t->table_dtype == LNG_BF16 ? launch_attend_tc<CodeT, __nv_bfloat16>(t, p, stream)
-                                      : launch_attend_tc<CodeT, __half>(t, p, stream);
   // tensor-core path: 16-bit tables, query of the same type, <= 16 heads, 16-byte rows
   const bool mma_ok = t16 && qa_dtype == t->table_dtype &&
                       (p.partial >= 3 ? u_dtype == LNG_BF16

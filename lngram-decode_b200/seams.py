@@ -5,7 +5,8 @@
   last n positions, the folded output map, and the short conv over the cached normalised outputs.
 * ``tree_memory_block`` -- the memory part of ``tree_verify_step`` (``drafting/tree.py:165-195``):
   every node's n-gram window and conv window follow its ancestors, then the cached positions.
-* ``tree_slots`` / ``tree_ngram_codes`` -- ``drafting/tree.py:96-127`` (host-side index building).
+* ``tree_slots`` / ``tree_ngram_codes`` -- the node windows of ``drafting/tree.py:96-127``, built from a
+  device-side ancestor table (``ancestor_table``).
 
 ``MemoryCache`` holds the memory part of the reference's ``DecodeState`` (``ffnmem/infer.py:65-112``):
 codes [B, max_len, R] and conv inputs [B, max_len, d], indexed by absolute position.
@@ -34,39 +35,43 @@ class MemoryCache:
         self.length = length
 
 
-def tree_path(parent, i: int) -> list:
-    """Root .. i along the parent pointers."""
-    out = []
-    while i >= 0:
-        out.append(i)
-        i = parent[i]
-    return out[::-1]
+def ancestor_table(parent, depth: int, device=None) -> tuple[Tensor, Tensor]:
+    """(anc, level) of a draft tree: anc[j, i] = the j-th ancestor of node i (anc[0] = i, -1 above
+    the root) for j <= depth, and level[i] = the node's distance from the root.  Built on the device
+    by repeated gathers through the parent array (one gather per level), not per node."""
+    par = torch.as_tensor([int(x) for x in parent], dtype=torch.long, device=device)
+    n = par.numel()
+    cur = torch.arange(n, dtype=torch.long, device=device)
+    rows = [cur]
+    for _ in range(max(depth, n - 1)):     # a path is at most n nodes long
+        cur = torch.where(cur >= 0, par[cur.clamp_min(0)], cur)
+        rows.append(cur)
+    chain = torch.stack(rows)                                         # [max(depth, n - 1) + 1, n]
+    level = (chain >= 0).sum(0) - 1
+    anc = chain[:depth + 1]
+    return anc, level
 
 
-def tree_slots(parent, L: int, back: int) -> tuple[Tensor, Tensor]:
-    """For each node the slots of itself and its ``back`` predecessors (oldest first): its ancestors,
-    then the L cached positions before the root; slot L + a is node a.  Returns (idx, ok) [n, back+1]."""
-    n = len(parent)
-    idx = torch.zeros(n, back + 1, dtype=torch.long)
-    ok = torch.zeros(n, back + 1, dtype=torch.bool)
-    for i in range(n):
-        path = tree_path(parent, i)
-        for j in range(back + 1):
-            s = L + path[-1 - j] if j < len(path) else L - (j - len(path) + 1)
-            if s >= 0:
-                idx[i, back - j] = s
-                ok[i, back - j] = True
-    return idx, ok
+def tree_slots(parent, L: int, back: int, device=None) -> tuple[Tensor, Tensor]:
+    """Slots [n, back + 1] (oldest first) of every node and its ``back`` predecessors: first the
+    node's ancestors (node a sits at slot L + a), then, past the root, the cached positions L - 1,
+    L - 2, ...; ``ok`` is False for slots before position 0.  The reading order of the reference's
+    ``drafting/tree.py:96-127`` (a node's window follows its ancestor path, then the history)."""
+    anc, level = ancestor_table(parent, back, device)
+    j = torch.arange(back + 1, device=anc.device)[:, None]            # steps back from the node
+    # j <= level: ancestor j of the node; beyond the root: cached position L - (j - level)
+    slot = torch.where(j <= level[None], L + anc, L - (j - level[None]))
+    ok = slot >= 0
+    return slot.clamp_min(0).flip(0).t().contiguous(), ok.flip(0).t().contiguous()
 
 
 def tree_ngram_codes(parent, codes: Tensor, history: Tensor | None = None, hist: int = 2) -> tuple[Tensor, Tensor]:
-    """Code windows [B, n, hist+1, R] along each node's ancestors then ``history`` (zeros where invalid)
-    and the validity mask [n, hist+1]."""
+    """Code windows [B, n, hist+1, R] of the tree nodes ``codes`` [B, n, R] after ``history``
+    [B, h, R] (zeros where a slot precedes position 0), and the slot validity [n, hist+1]."""
     h = 0 if history is None else history.shape[1]
-    allc = codes if history is None else torch.cat((history.to(codes.dtype), codes), 1)
-    idx, ok = tree_slots(parent, h, hist)
-    idx, ok = idx.to(codes.device), ok.to(codes.device)
-    return allc[:, idx] * ok[None, :, :, None].to(codes.dtype), ok
+    seq = codes if history is None else torch.cat((history.to(codes.dtype), codes), 1)
+    idx, ok = tree_slots(parent, h, hist, codes.device)
+    return seq[:, idx] * ok[None, :, :, None].to(codes.dtype), ok
 
 
 def _readout(m, h: Tensor, tables, codes, cdt, B, T, window, seg, target_length):
@@ -132,16 +137,16 @@ def _tree_plan(parent, L: int, B: int, max_len: int, hist: int, k: int, dil: int
         return plan
     n = len(parent)
     h0 = min(L, hist)
-    gidx, gok = tree_slots(parent, h0, hist)                              # slots into [history(h0) | nodes]
+    gidx, gok = tree_slots(parent, h0, hist, device)                      # slots into [history(h0) | nodes]
     lp = (k - 1) * dil
-    idx, ok = tree_slots(parent, L, lp)
-    taps = torch.arange(k) * dil                                          # window columns the taps read
-    tslot = torch.where(ok[:, taps], idx[:, taps], torch.full_like(idx[:, taps], -1)).to(device)  # [n, k]
+    idx, ok = tree_slots(parent, L, lp, device)
+    taps = torch.arange(k, device=device) * dil                           # window columns the taps read
+    tslot = torch.where(ok[:, taps], idx[:, taps], torch.full_like(idx[:, taps], -1))  # [n, k]
     base = (torch.arange(B, device=device) * max_len)[:, None, None]
     slot = torch.where(tslot[None] >= 0, base + tslot[None], torch.full_like(tslot[None], -1))
     new_slot = (torch.arange(B, device=device) * max_len)[:, None] + L + torch.arange(n, device=device)[None]
-    plan = {"h0": h0, "gidx": gidx.to(device), "gok": gok.to(device)[None, :, :, None].to(torch.uint8),
-            "seg": gok.to(torch.int32)[None].expand(B, n, hist + 1).reshape(B * n, hist + 1).contiguous().to(device),
+    plan = {"h0": h0, "gidx": gidx, "gok": gok[None, :, :, None].to(torch.uint8),
+            "seg": gok.to(torch.int32)[None].expand(B, n, hist + 1).reshape(B * n, hist + 1).contiguous(),
             "slot": slot.reshape(B * n, k).contiguous(), "new_slot": new_slot.reshape(-1).contiguous()}
     if len(_TREE_PLANS) > 64:
         _TREE_PLANS.clear()

@@ -24,7 +24,8 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 BUILD = HERE / "_build"
 REF_OUT = HERE / "_ref"
-DEFAULT_REFERENCE = Path(os.environ.get("LNGRAM_REFERENCE", "/root/reference"))
+# the reference checkout: LNGRAM_REFERENCE, else a directory named "reference" beside this repository
+DEFAULT_REFERENCE = Path(os.environ.get("LNGRAM_REFERENCE") or (HERE.parent.parent / "reference"))
 
 
 def _run(cmd: list) -> None:

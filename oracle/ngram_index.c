@@ -6,7 +6,7 @@
  *   ffnmem/memory/lngram_v2.py:314-325   _aligned_ngram_address (oldest code least significant)
  *   ffnmem/memory/lngram_v2.py:1027-1045 _valid_mask (t >= n-1, same segment, valid last token)
  *   ffnmem/memory/lngram_v2.py:1075-1084 route offsets r * A^n
- * so that tests can check the CUDA path bit-exactly at full BASELINE sizes in seconds.
+ * so that tests can check the CUDA path bit-exactly at the full benchmark sizes in seconds.
  * Only tests/ and bench.py's CPU-baseline leg load the built library.
  */
 #include <stdint.h>

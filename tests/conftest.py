@@ -2,7 +2,8 @@
 
 ``-m gpu`` tests need a B200 and the built CUDA library; everything else runs on the CPU.
 Tests marked ``reference`` import the reference checkout (read-only) when it is present
-(``LNGRAM_REFERENCE``, default ``/root/reference``) and are skipped when it is not.
+(``LNGRAM_REFERENCE``, else a checkout named ``reference`` beside this repository) and are
+skipped when it is not.
 """
 
 from __future__ import annotations
@@ -16,7 +17,8 @@ import pytest
 
 REPO = Path(__file__).resolve().parents[1]
 GOLDEN = REPO / "tests" / "golden"
-REFERENCE = Path(os.environ.get("LNGRAM_REFERENCE", "/root/reference"))
+# the reference checkout: LNGRAM_REFERENCE, else a directory named "reference" beside this repository
+REFERENCE = Path(os.environ.get("LNGRAM_REFERENCE") or (REPO.parent / "reference"))
 if str(REPO) not in sys.path:
     sys.path.insert(0, str(REPO))
 

@@ -3,7 +3,7 @@
 Everything is generated with ``numpy.random.default_rng`` (PCG64: identical on every host),
 so the fixtures in this folder store only small inputs and the reference's outputs; the
 large arrays (tables, embeddings) are regenerated from the seeds at test time.  Seed
-convention (SURVEY-style): 0 token ids, 1 hidden states, 2 tables, 3 router, 4 projections,
+convention: 0 token ids, 1 hidden states, 2 tables, 3 router, 4 projections,
 5 norms / conv / start vectors.  Generated in fp32 and, for bf16 cases, rounded to
 bf16-representable values (round to nearest even), as the reference initialises in fp32
 and casts (``ffnmem/memory/lngram_v2.py:20-33``).
@@ -36,17 +36,17 @@ def _normal(seed: int, shape, std: float, stream: int = 0) -> np.ndarray:
 
 # --------------------------------------------------------------------------- memory layer
 MEMORY_CASES = {
-    # BASELINE configs[0] (tiny_cpu): router fed by E[x] directly; R=8, 4 bits, n=3, 32 dims.
+    # The tiny_cpu configuration: router fed by E[x] directly; R=8, 4 bits, n=3, 32 dims.
     "tiny": dict(d=128, routes=8, bits=4, ngrams=(3,), mem_dim=32, q_heads=4, kv_heads=2, head_dim=32,
                  B=2, T=64, vocab=32000, router="embedding", bf16=False),
     # The reference's own tiny memory (configs/tiny_cpu.yaml): orders (2, 3), with packed
     # segments and left padding, and the streaming route-chunk mode.
     "tiny_multi": dict(d=64, routes=4, bits=4, ngrams=(2, 3), mem_dim=16, q_heads=4, kv_heads=2, head_dim=16,
                        B=3, T=40, router="hidden", bf16=False, segments=True, valid=True, stream_chunk=3),
-    # SB memory shape (BASELINE configs[1]) on a short slice, bf16-valued data.
+    # SB memory shape on a short slice, bf16-valued data.
     "sb_slice": dict(d=1024, routes=184, bits=4, ngrams=(3,), mem_dim=136, q_heads=16, kv_heads=4, head_dim=64,
                      B=1, T=48, router="hidden", bf16=True, o_std=0.006),
-    # Scaled-table addressing (BASELINE configs[4]): 5-bit codes, 4-gram windows, 2**20 rows per route.
+    # Scaled-table addressing: 5-bit codes, 4-gram windows, 2**20 rows per route.
     "scaled_slice": dict(d=64, routes=3, bits=5, ngrams=(4,), mem_dim=8, q_heads=4, kv_heads=2, head_dim=16,
                          B=2, T=24, router="hidden", bf16=False),
 }
@@ -126,7 +126,7 @@ def oracle_params(case: str, params: dict | None = None):
 
 # --------------------------------------------------------------------------- drafter bundles
 DRAFT_CASES = {
-    # SD-B shape (BASELINE configs[2]): embed2 router over 182 routes, full-vocab scoring.
+    # SD-B shape: embed2 router over 182 routes, full-vocab scoring.
     "sdb": dict(d=1024, vocab=32000, routes=182, bits=4, ngrams=(3,), mem_dim=136, kv_heads=4, head_dim=64,
                 q_heads=4, table_dtype="fp32", bf16=True, w_o_std=0.02),
     # Reference-sized tiny drafter (configs/tiny_cpu_sd.yaml with embed2): orders (2, 3), fp16 tables.
@@ -194,7 +194,7 @@ def random_sketch(config: dict, k: int = 4, seed: int = 0, empty_frac: float = 0
 
 
 # --------------------------------------------------------------------------- tree / decode seams
-# BASELINE configs[3] default parent array: root + 4 children + 11 grandchildren.
+# Default tree parent array: root + 4 children + 11 grandchildren.
 TREE_PARENT = (-1, 0, 0, 0, 0, 1, 1, 1, 2, 2, 2, 3, 3, 3, 4, 4)
 # The reference's tree KAT (``tests/test_live_tree.py:15``).
 KAT_PARENT = (-1, 0, 1, 0, 3, 1)

@@ -220,7 +220,7 @@ def write_draft_case(case: str, n_trace: int, with_cpp: bool) -> None:
 
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__)
-    ap.add_argument("--reference", default=os.environ.get("LNGRAM_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("LNGRAM_REFERENCE") or str(HERE.parents[2] / "reference"))
     ap.add_argument("--only", nargs="*", default=None)
     args = ap.parse_args(argv)
     sys.path.insert(0, args.reference)

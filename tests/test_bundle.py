@@ -34,6 +34,7 @@ def test_interchange_with_reference_format(lngram, reference_path, tmp_path):
     from drafting.export_drafter import write_bundle as ref_write
 
     config, arrays = cases.draft_bundle("tiny")
+    arrays = dict(arrays, **cases.random_sketch(config))       # uint16 ids / uint32 counts / int32 fallback too
     p1 = ref_write(tmp_path / "ref.bin", config, arrays, {"s": 1})
     ours = lngram.load_bundle(p1)
     p2 = lngram.write_bundle(tmp_path / "ours.bin", config, arrays, {"s": 1})

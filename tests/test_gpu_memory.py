@@ -176,7 +176,7 @@ def _sb_tables(dtype=torch.bfloat16, rows=184 * 4096, dim=136, seed=2):
 
 
 def test_sb_full_size_lookup_rows_exact(lngram):
-    """BASELINE SB size (32 x 2048 x 184): gathered rows are exact copies of the addressed rows."""
+    """Full SB size (32 x 2048 x 184): gathered rows are exact copies of the addressed rows."""
     from oracle.build import load_c_oracle
 
     lib_c = load_c_oracle()

@@ -153,7 +153,7 @@ def test_drafter_oracle_matches_reference(golden, case):
 
 
 def test_c_oracle_matches_numpy_oracle():
-    """The plain-C addressing oracle (used at full BASELINE sizes) equals the numpy restatement."""
+    """The plain-C addressing oracle (used at the full benchmark sizes) equals the numpy restatement."""
     from oracle.build import load_c_oracle
 
     lib = load_c_oracle()

@@ -10,17 +10,25 @@ Workloads (synthetic seeded inputs of the shapes the configurations name):
   bf16, fp32 router [736, 1024], folded readout in bf16.  A step is one ``LngramMemory.forward``
   over the whole batch (router -> codes -> gather + sink attention -> output projection -> conv).
   Inputs (table 205 MB, h + h_norm 268 MB, two alternating input sets) are larger than the 126 MB
-  L2.  N GPUs run independent replicas (weak scaling, no collective on the data path).
+  L2.  N GPUs run independent replicas (weak scaling, no collective on the data path).  ``e2e`` is
+  the same forward through ``LngramMemory.forward_host``: pinned host h in, h_norm = attn_norm(h)
+  on the device, output out, the copies overlapped with the forward by sequence groups.
+  Unless ``--no-extras``, the default line also carries ``workloads``: the three other workloads
+  below, each measured on its own configuration (at most 10 steps) in the same run.
 * ``sdb_draft``: the SD-B drafter (182 routes, embed2 token router, vocab 32000); a step drafts
   4 greedy tokens for each of 64 sequences with 1024-token prefixes (``GpuDrafter.draft_batch``).
 * ``tree_verify``: 64 sequences x a 16-node draft tree after a 1024-position context on the SB
   layer; a step is the nodes' router codes + ``tree_memory_block``.
-* ``scaled``: the 52 GB scaled table (184 routes x 2**20 rows x 136, 5-bit codes, order 4) over
-  h [64, 4096, 1024]; at N > 1 the routes are sharded across the GPUs (strong scaling).
+* ``scaled`` (``route_sharded`` in ``workloads``): the 52 GB scaled table (184 routes x 2**20 rows x
+  136, 5-bit codes, order 4) over h [64, 4096, 1024]; at N > 1 the routes are sharded across the
+  GPUs (strong scaling), with per-phase times and the NCCL bytes of a rank.
 
 The job time is the max over ranks of CUDA-event time.  ``--impl reference`` times the reference's
-CPU implementation of the same workload (the reference's C++ drafter for ``sdb_draft``, the numpy
-restatement of the reference forward otherwise) on a bounded sample, on all host threads.
+CPU implementation of the same workload on a bounded sample, on all host threads: the reference's
+own C++ drafter (built from its sources) for ``sdb_draft``; for ``sb_prefill`` / ``tree_verify``
+a torch-CPU restatement of the reference forward (``oracle/torch_port.py``: the reference's own
+operator sequence, measured at the reference's speed with identical outputs), because the
+reference's Python does not travel to the GPU box.
 """
 
 from __future__ import annotations
@@ -178,23 +186,58 @@ def build_sb(pkg, dev, seed: int = 0):
         m.short_conv.conv.weight.copy_((torch.randn(m.short_conv.conv.weight.shape, device=dev, generator=g) * 0.2)
                                        .to(torch.bfloat16))
         mem.router.weight.copy_(torch.randn(mem.router.weight.shape, device=dev, generator=g) * 0.02)
+        # the block's attn_norm weight (bf16 model): h_norm = attn_norm(h) is the router input
+        mem.attn_norm_weight = (1.0 + 0.1 * torch.randn(c["d"], device=dev, generator=g)).to(torch.bfloat16)
     return mem
 
 
-def sb_inputs(dev, seed: int):
+def sb_inputs(pkg, mem, dev, seed: int):
+    """h [B, T, d] bf16 N(0, 1) and h_norm = attn_norm(h) (the block norm, ``ffnmem/model.py:114``)."""
     g = torch.Generator(device=dev).manual_seed(seed)
     h = torch.randn(SB["B"], SB["T"], SB["d"], device=dev, generator=g).to(torch.bfloat16)
-    hf = h.float()
-    hn = (hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + 1e-5)).to(torch.bfloat16)
-    return h, hn
+    return h, pkg.rms_norm(h, mem.attn_norm_weight, 1e-5)
+
+
+def layer_bytes_per_position() -> int:
+    """Algorithmic bytes of the memory lookup per position (the survey's measurement rule): the R rows
+    of every order (bf16) + the hidden state in + the output out (d bf16 each) = 54,144 B at SB."""
+    c = SB
+    dt = len(c["ngrams"]) * c["mem_dim"]
+    return c["routes"] * dt * 2 + 2 * c["d"] * 2
 
 
 def attend_bytes_per_position() -> int:
-    """Algorithmic bytes of the gather + sink-attention kernel per position: the R rows of every
-    order (bf16), the folded query and the output (QH x Dt bf16 each), the R codes (u8)."""
+    """Bytes the gather + sink-attention kernel itself moves per position: the R rows of every order
+    (bf16), the folded query and the output (QH x Dt bf16 each), the R codes (u8) = 58,936 B at SB."""
     c = SB
     dt = len(c["ngrams"]) * c["mem_dim"]
     return c["routes"] * dt * 2 + 2 * c["q_heads"] * dt * 2 + c["routes"]
+
+
+def sb_config(world: int) -> dict:
+    return {"workload": "sb_prefill", "batch": SB["B"], "seq_len": SB["T"], "d_model": SB["d"],
+            "routes": SB["routes"], "bits": SB["bits"], "ngrams": list(SB["ngrams"]), "mem_dim": SB["mem_dim"],
+            "readout": "q16/kv4/hd64", "parallelism": f"replicas{world}",
+            "l2": "inputs larger than L2 (205 MB table, 2 x 268 MB alternating h/h_norm sets)"}
+
+
+def sdb_config(config: dict, world: int) -> dict:
+    return {"workload": "sdb_draft", "sequences": SDB["nseq"], "prefix": SDB["plen"], "gamma": SDB["gamma"],
+            "vocab": int(config["vocab"]), "d_model": int(config["d_model"]), "routes": int(config["routes"]),
+            "bits": int(config["bits"]), "ngrams": list(config["ngrams"]), "router": "embed2 (token only)",
+            "sampling": "argmax", "parallelism": f"replicas{world}",
+            "l2": "a 252 MB buffer is rewritten between timed steps (outside the step events)"}
+
+
+def tree_config(world: int) -> dict:
+    from tests.golden import cases
+
+    return {"workload": "tree_verify", "sequences": TREE["nseq"], "context": TREE["ctx"],
+            "nodes": len(cases.TREE_PARENT), "parent": list(cases.TREE_PARENT), "routes": SB["routes"],
+            "bits": SB["bits"], "ngrams": list(SB["ngrams"]), "mem_dim": SB["mem_dim"],
+            "step": "router codes of the nodes + tree_memory_block (n-gram and conv windows along ancestors)",
+            "parallelism": f"replicas{world}",
+            "l2": "a 252 MB buffer is rewritten between timed steps (outside the step events)"}
 
 
 def run_ours(args, rank, world, local) -> dict:
@@ -204,7 +247,7 @@ def run_ours(args, rank, world, local) -> dict:
     lib = pkg._lib
     dev = torch.device("cuda", local)
     mem = build_sb(pkg, dev, seed=0)
-    inputs = [sb_inputs(dev, 100 + rank * 10 + i) for i in range(2)]
+    inputs = [sb_inputs(pkg, mem, dev, 100 + rank * 10 + i) for i in range(2)]
     M = SB["B"] * SB["T"]
     out = torch.empty(SB["B"], SB["T"], SB["d"], device=dev, dtype=torch.bfloat16)
     codes = torch.empty(SB["B"], SB["T"], SB["routes"], device=dev, dtype=torch.uint8)
@@ -246,20 +289,21 @@ def run_ours(args, rank, world, local) -> dict:
     pk = peaks()
     units = M * world * args.steps
     value = units / (ms_max / 1e3)
-    bpp = attend_bytes_per_position()
+    bpp = layer_bytes_per_position()
     achieved = bpp * M / (att["ms"] / 1e3) / 1e9
+    kio = attend_bytes_per_position()
     traffic = profiled_traffic("attend_mma", M)
     line = {
         "metric": METRIC, "value": value, "unit": "positions/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) hidden states, N(0,0.02) tables)",
-        "config": {"workload": "sb_prefill", "batch": SB["B"], "seq_len": SB["T"], "d_model": SB["d"],
-                   "routes": SB["routes"], "bits": SB["bits"], "ngrams": list(SB["ngrams"]), "mem_dim": SB["mem_dim"],
-                   "readout": "q16/kv4/hd64 folded", "parallelism": f"replicas{world}",
-                   "l2": "inputs larger than L2 (205 MB table, 2 x 268 MB alternating h/h_norm sets)"},
+        "config": sb_config(world),
         "roofline": {"bound": "hbm", "kernel": "attend_mma_kernel (fused gather + sink attention)",
                      "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
                      "peak_source": pk["source"], "traffic": traffic, "bytes_per_position": bpp,
+                     "bytes_rule": "R x Dt x 2 (rows) + 2 x d x 2 (hidden in, output out)",
+                     "kernel_io_bytes_per_position": kio,
+                     "achieved_kernel_io": kio * M / (att["ms"] / 1e3) / 1e9,
                      "ms_per_launch": att["ms"], "launches": att["launches"]},
         "e2e": e2e,
         "stages_ms": stages,
@@ -353,21 +397,20 @@ def time_stages(mem, lib, h, hn, reps: int = 5) -> dict:
     return res
 
 
+E2E_GROUPS = 8
+
+
 def time_e2e(mem, inputs, args, world) -> dict:
-    """Same metric through LngramMemory.forward with pinned HOST inputs/outputs: H2D of h and
-    h_norm, the forward, D2H of the output, every step."""
-    dev = inputs[0][0].device
-    hosts = [(h.cpu().pin_memory(), hn.cpu().pin_memory()) for h, hn in inputs]
+    """Same metric through the public host-memory call ``LngramMemory.forward_host``: every step copies
+    that step's pinned host h in, makes h_norm = attn_norm(h) on the device, runs the forward and copies
+    the output back to pinned host memory, in E2E_GROUPS groups of sequences pipelined over three streams
+    (copy in / forward / copy out overlap)."""
+    hosts = [h.cpu().pin_memory() for h, _ in inputs]
     out_host = torch.empty(SB["B"], SB["T"], SB["d"], dtype=torch.bfloat16).pin_memory()
-    hd = torch.empty_like(inputs[0][0])
-    hnd = torch.empty_like(inputs[0][1])
 
     def step(i):
-        h, hn = hosts[i % 2]
-        hd.copy_(h, non_blocking=True)
-        hnd.copy_(hn, non_blocking=True)
-        out = mem(hd, hnd)
-        out_host.copy_(out, non_blocking=True)
+        mem.forward_host(hosts[i % 2], norm_weight=mem.attn_norm_weight, norm_eps=1e-5, out=out_host,
+                         groups=E2E_GROUPS, synchronize=False)
 
     for i in range(args.warmup):
         step(i)
@@ -382,8 +425,10 @@ def time_e2e(mem, inputs, args, world) -> dict:
     ms = max_over_ranks(e0.elapsed_time(e1), world)
     M = SB["B"] * SB["T"]
     return {"value": M * world * args.steps / (ms / 1e3), "unit": "positions/s",
-            "h2d_bytes_per_step": 2 * hd.numel() * 2, "d2h_bytes_per_step": out_host.numel() * 2,
-            "ms_per_step": ms / args.steps}
+            "h2d_bytes_per_step": hosts[0].numel() * 2, "d2h_bytes_per_step": out_host.numel() * 2,
+            "ms_per_step": ms / args.steps,
+            "call": f"LngramMemory.forward_host(h, norm_weight=attn_norm.weight, groups={E2E_GROUPS}): h in, "
+                    "h_norm on the device, output out; copies overlapped with the forward"}
 
 
 def count_launches(fn, fallback: int) -> dict:
@@ -519,11 +564,7 @@ def run_sdb(args, rank, world, local) -> dict:
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded uniform token prefixes, N(0,0.02) weights)",
-        "config": {"workload": "sdb_draft", "sequences": nseq, "prefix": plen, "gamma": gamma, "vocab": V,
-                   "d_model": d, "routes": int(config["routes"]), "bits": int(config["bits"]),
-                   "ngrams": list(config["ngrams"]), "router": "embed2 (token only)", "sampling": "argmax",
-                   "parallelism": f"replicas{world}",
-                   "l2": "a 252 MB buffer is rewritten between timed steps (outside the step events)"},
+        "config": sdb_config(config, world),
         "roofline": {"bound": "hbm", "kernel": "logits_tc_topk_kernel (draft-head logits + top-1 on tcgen05, bf16 vocab)",
                      "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
                      "peak_source": pk["source"], "traffic": profiled_traffic("logits_tc", nseq),
@@ -585,9 +626,9 @@ def cpu_sdb_sample(budget_s: float = 12.0, reps: int | None = None) -> dict:
         list(ex.map(work, range(threads)))
         dt = time.perf_counter() - t0
     tokens = threads * n * gamma
-    return {"value": tokens / dt, "unit": "draft tokens/s", "cores": threads, "kind": kind,
-            "sample": f"{threads} sequences (1024-token prefixes, one drafter per thread) x {n} drafts of "
-                      f"{gamma} tokens, full-vocabulary argmax"}
+    return dict({"value": tokens / dt, "unit": "draft tokens/s", "cores": threads, "kind": kind,
+                 "sample": f"{threads} sequences (1024-token prefixes, one drafter per thread) x {n} drafts of "
+                           f"{gamma} tokens, full-vocabulary argmax"}, **host_cpu())
 
 
 # --------------------------------------------------------------------------- tree verification
@@ -666,11 +707,7 @@ def run_tree(args, rank, world, local) -> dict:
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) hidden states, N(0,0.02) tables)",
-        "config": {"workload": "tree_verify", "sequences": nseq, "context": ctx, "nodes": n, "parent": list(parent),
-                   "routes": SB["routes"], "bits": SB["bits"], "ngrams": list(SB["ngrams"]), "mem_dim": SB["mem_dim"],
-                   "step": "router codes of the nodes + tree_memory_block (n-gram and conv windows along ancestors)",
-                   "parallelism": f"replicas{world}",
-                   "l2": "a 252 MB buffer is rewritten between timed steps (outside the step events)"},
+        "config": tree_config(world),
         "roofline": {"bound": "hbm", "kernel": "attend_mma_kernel (tree windows)", "achieved": achieved,
                      "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
                      "peak_source": pk["source"], "traffic": None, "bytes_per_launch": att_bytes,
@@ -845,6 +882,10 @@ def run_scaled(args, rank, world, local) -> dict:
                      "ms_per_launch": att_ms},
         "gpu_launches": launches["per_step"] * args.steps, "launch_count": launches,
         "phases_ms": phases,
+        "nccl_bytes_per_rank": None if world == 1 else {
+            "all_reduce_max_fp32": M * m.readout_num_heads * 4,
+            "reduce_scatter_sent_bf16": int(M * m.readout_num_heads * (Dt + 1) * 2 * (world - 1) / world),
+            "note": "per forward; each of the SCALED_CHUNKS groups moves its share"},
         "clocks": clk.summary(),
     }
 
@@ -886,63 +927,97 @@ def time_scaled_phases(pkg, shard, h, hn, world) -> dict:
 
 
 # --------------------------------------------------------------------------- CPU baseline / reference arm
-def cpu_sb_sample(budget_s: float = 12.0) -> dict:
-    """The numpy restatement of the reference forward (oracle/memory.py) on whole SB sequences
-    (B = 1 x T = 2048) until ``budget_s`` seconds have passed (at least one sequence)."""
-    from oracle import memory as om
+def host_cpu() -> dict:
+    """The host's CPU model, core count and the threads torch uses (recorded beside every CPU figure)."""
+    model = None
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return {"cpu_model": model, "os_cpu_count": os.cpu_count(), "torch_threads": torch.get_num_threads()}
+
+
+def _port_threads() -> int:
+    n = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    torch.set_num_threads(max(1, n))
+    return torch.get_num_threads()
+
+
+PORT_NOTE = ("torch-CPU restatement of the reference forward (oracle/torch_port.py): the same operator kinds "
+             "as the reference's own torch forward, measured at its speed on the same cores with identical outputs")
+
+
+_PORT_PARAMS: dict = {}
+
+
+def _sb_port_params():
+    """The SB layer's parameters for the torch-CPU port (made once per process)."""
+    if "sb" not in _PORT_PARAMS:
+        from oracle import torch_port as tp
+        from tests.golden import cases
+
+        _PORT_PARAMS["sb"] = tp.from_state(cases.memory_params("sb_slice"), cases.MEMORY_CASES["sb_slice"])
+    return _PORT_PARAMS["sb"]
+
+
+def cpu_sb_sample(budget_s: float = 12.0, max_seqs: int = 4) -> dict:
+    """The reference memory-layer forward (torch CPU port) on whole SB sequences (B = 1 x T = 2048) until
+    ``budget_s`` seconds have passed (at least one sequence, at most ``max_seqs``)."""
+    from oracle import torch_port as tp
     from tests.golden import cases
 
     c = SB
-    p = cases.oracle_params("sb_slice")
-    rng = np.random.default_rng(0)
-    router_w = cases.memory_params("sb_slice")["router.weight"]
-    n_pos = 0
+    threads = _port_threads()
+    p = _sb_port_params()
+    w = 1.0 + 0.1 * torch.randn(c["d"], generator=torch.Generator().manual_seed(7))
+    g = torch.Generator().manual_seed(0)
+    n_pos, seqs = 0, 0
     t0 = time.perf_counter()
-    seqs = 0
     while True:
-        h = cases.bf16_round(rng.standard_normal((1, c["T"], c["d"]), dtype=np.float32))
-        x = cases.bf16_round(om.rms_norm(h, None, 1e-5))
-        om.lngram_memory_forward(h, x, router_w, p)
+        h = torch.randn(1, c["T"], c["d"], generator=g).to(torch.bfloat16).float()
+        hn = h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + 1e-5) * w       # attn_norm (fp32 model)
+        tp.lngram_forward(h, hn, p)
         n_pos += c["T"]
         seqs += 1
-        if time.perf_counter() - t0 >= budget_s or seqs >= 4:
+        if time.perf_counter() - t0 >= budget_s or seqs >= max_seqs:
             break
     dt = time.perf_counter() - t0
-    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
-    return {"value": n_pos / dt, "unit": "positions/s", "cores": threads, "kind": "port",
-            "sample": f"{seqs} x (1 x 2048) SB positions through the numpy oracle forward (fp32, bf16-valued data)"}
+    return dict({"value": n_pos / dt, "unit": "positions/s", "cores": threads, "kind": "port",
+                 "sample": f"{seqs} x (1 x 2048) SB positions through the reference forward, fp32 ({PORT_NOTE})"},
+                **host_cpu())
 
 
 def cpu_tree_sample(budget_s: float = 12.0, max_seqs: int | None = None) -> dict:
-    """The numpy restatement of the reference's tree-verification memory block (oracle/memory.py
-    ``tree_memory_block``, ``drafting/tree.py:178-195``) with the SB layer: the nodes' router codes and
-    the block for one sequence's 16-node tree after a 1024-position context, repeated for about
-    ``budget_s`` seconds."""
-    from oracle import memory as om
+    """The reference tree-verification memory block (``drafting/tree.py:178-195``, torch CPU port) with the
+    SB layer: the nodes' router codes and the block for one sequence's 16-node tree after a 1024-position
+    context, repeated for about ``budget_s`` seconds."""
+    from oracle import torch_port as tp
     from tests.golden import cases
 
-    p = cases.oracle_params("sb_slice")
-    router_w = cases.memory_params("sb_slice")["router.weight"]
+    threads = _port_threads()
+    p = _sb_port_params()
     parent = cases.TREE_PARENT
     n, d, R = len(parent), SB["d"], SB["routes"]
-    rng = np.random.default_rng(1)
-    hist = p.route_history_length
+    g = torch.Generator().manual_seed(1)
+    hist, lp = max(SB["ngrams"]) - 1, 3 * max(SB["ngrams"])
     t0 = time.perf_counter()
     seqs = 0
     while True:
-        h = cases.bf16_round(rng.standard_normal((1, n, d), dtype=np.float32))
-        x = cases.bf16_round(om.rms_norm(h, None, 1e-5))
-        codes = om.quantize_route_logits(om.route_logits(x, router_w), p.bits)
-        history = rng.integers(0, 1 << p.bits, size=(1, hist, R))
-        conv_cache = rng.standard_normal((1, TREE["ctx"], d), dtype=np.float32)
-        om.tree_memory_block(h, codes, parent, history, conv_cache, TREE["ctx"], p)
+        h = torch.randn(1, n, d, generator=g).to(torch.bfloat16).float()
+        x = h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + 1e-5)
+        history = torch.randint(0, 1 << SB["bits"], (1, hist, R), generator=g)
+        conv_cache = torch.randn(1, lp, d, generator=g)
+        tp.tree_block(h, x, parent, history, conv_cache, p)
         seqs += 1
         if time.perf_counter() - t0 >= budget_s or (max_seqs is not None and seqs >= max_seqs):
             break
     dt = time.perf_counter() - t0
-    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
-    return {"value": seqs * n / dt, "unit": "tree nodes/s", "cores": threads, "kind": "port",
-            "sample": f"{seqs} x 16-node trees (1024-position context) through the numpy oracle (fp32)"}
+    return dict({"value": seqs * n / dt, "unit": "tree nodes/s", "cores": threads, "kind": "port",
+                 "sample": f"{seqs} x 16-node trees (1024-position context) through the reference tree block, "
+                           f"fp32 ({PORT_NOTE})"}, **host_cpu())
 
 
 def run_reference(args, rank, world) -> dict | None:
@@ -966,12 +1041,8 @@ def run_reference(args, rank, world) -> dict | None:
         base = r
     value = statistics.mean(per_step)
     units = {"sb_prefill": SB["T"], "sdb_draft": base["cores"] * SDB["gamma"], "tree_verify": 16}[wl]
-    cfg = {"sb_prefill": {"workload": "sb_prefill", "batch": SB["B"], "seq_len": SB["T"], "routes": SB["routes"]},
-           "sdb_draft": {"workload": "sdb_draft", "sequences": SDB["nseq"], "prefix": SDB["plen"],
-                         "gamma": SDB["gamma"]},
-           "tree_verify": {"workload": "tree_verify", "sequences": TREE["nseq"], "context": TREE["ctx"],
-                           "nodes": 16}}[wl]
-    cfg["sample"] = base["sample"]
+    cfg = {"sb_prefill": lambda: sb_config(world), "sdb_draft": lambda: sdb_config(sdb_bundle()[0], world),
+           "tree_verify": lambda: tree_config(world)}[wl]()
     return {"impl": "reference", "metric": METRIC, "value": value, "unit": base["unit"], "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": units / value * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
@@ -980,6 +1051,13 @@ def run_reference(args, rank, world) -> dict | None:
 
 
 RUNNERS = {"sb_prefill": "run_ours", "sdb_draft": "run_sdb", "tree_verify": "run_tree", "scaled": "run_scaled"}
+SUB_KEYS = ("value", "unit", "ms_per_step", "steps", "warmup", "scaling", "config", "roofline", "e2e", "cpu_baseline",
+            "gpu_launches", "phases_ms", "nccl_bytes_per_rank", "clocks")
+
+
+def summarize(res: dict) -> dict:
+    """The keys of one workload's line that go into the default line's ``workloads`` sub-object."""
+    return {k: res[k] for k in SUB_KEYS if k in res}
 
 
 def main(argv=None) -> int:
@@ -992,6 +1070,8 @@ def main(argv=None) -> int:
     ap.add_argument("--batch", type=int, default=SB["B"], help="sb_prefill sequences per GPU (32 = the SB configuration; "
                     "smaller for ncu)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="sb_prefill only: skip the SD-B / tree / scaled "
+                    "sub-objects of the default line")
     args = ap.parse_args(argv)
     SB["B"] = int(args.batch)
     if args.warmup < 3:
@@ -1004,14 +1084,21 @@ def main(argv=None) -> int:
             print(json.dumps(line), flush=True)
         return 0
     line = globals()[RUNNERS[args.workload]](args, rank, world, local)
+    cpu_arms = {"sb_prefill": cpu_sb_sample, "sdb_draft": cpu_sdb_sample, "tree_verify": cpu_tree_sample}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload in cpu_arms:
+        line["cpu_baseline"] = cpu_arms[args.workload]()
+    if args.workload == "sb_prefill" and not args.no_extras:
+        # the other parts of the metric, each on its own configuration, in the same JSON line
+        sub = argparse.Namespace(**vars(args))
+        sub.steps, sub.warmup = min(args.steps, 10), max(3, min(args.warmup, 3))
+        line["workloads"] = {}
+        for wl in ("sdb_draft", "tree_verify", "scaled"):
+            torch.cuda.empty_cache()
+            res = globals()[RUNNERS[wl]](sub, rank, world, local)
+            if rank == 0 and world == 1 and not args.no_cpu_baseline and wl in cpu_arms:
+                res["cpu_baseline"] = cpu_arms[wl](budget_s=6.0)
+            line["workloads"]["route_sharded" if wl == "scaled" else wl] = summarize(res)
     if rank == 0:
-        if world == 1 and not args.no_cpu_baseline:
-            if args.workload == "sb_prefill":
-                line["cpu_baseline"] = cpu_sb_sample()
-            elif args.workload == "sdb_draft":
-                line["cpu_baseline"] = cpu_sdb_sample()
-            elif args.workload == "tree_verify":
-                line["cpu_baseline"] = cpu_tree_sample()
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist

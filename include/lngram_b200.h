@@ -214,6 +214,14 @@ int lng_rms_rows(const void* x, int32_t x_dtype, int64_t n, int64_t d, float eps
 int lng_rms_norm(const void* x, int32_t x_dtype, int64_t n, int64_t d, const float* w, float eps, void* y,
                  int32_t y_dtype, lng_stream_t stream);
 
+/* The model block's RMSNorm with its rounding rule (ffnmem/model.py:39-48, the attn_norm that makes the
+ * router input h_norm at ffnmem/model.py:114): y = cast_y(cast_x(x * rsqrt(mean(x^2) + eps)) * w), the
+ * normalised row rounded to x's dtype BEFORE the weight multiply.  The reference's output dtype is the
+ * promotion of x's and w's (bf16 x with an fp32 weight gives fp32 y; with a bf16 weight, bf16 y); y_dtype
+ * selects it.  x f32 / bf16 / f16; w f32 / bf16 [d] or NULL (= 1); y may not alias x. */
+int lng_rms_norm_model(const void* x, int32_t x_dtype, int64_t n, int64_t d, const void* w, int32_t w_dtype,
+                       float eps, void* y, int32_t y_dtype, lng_stream_t stream);
+
 /* The short-conv finish of the readout (lngram_v2.py:1354-1359, :207-286), sequence mode:
  * out[b, t] = mixed[b, t] + SiLU(bias + sum_tap w[:, tap] * RMSNorm(mixed)[b, t - lag(tap)] * same_segment)
  * with lag(tap) = (k-1-tap)*dilation and zero left padding, then * valid_tokens[b, t].

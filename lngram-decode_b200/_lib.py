@@ -83,6 +83,7 @@ SIGNATURES = {
     "lng_sink_gqa": (C.c_int, [P, P, P, i32, i64, i32, i32, i64, i32, f32, P, P]),
     "lng_gemm": (C.c_int, [P, i32, i64, P, i32, i64, P, i32, i64, i64, i64, i64, P, i32, P]),
     "lng_rms_rows": (C.c_int, [P, i32, i64, i64, f32, P, P]),
+    "lng_rms_norm_model": (C.c_int, [P, i32, i64, i64, P, i32, f32, P, i32, P]),
     "lng_rms_norm": (C.c_int, [P, i32, i64, i64, P, f32, P, i32, P]),
     "lng_conv_finish": (C.c_int, [PR, P, i64, i64, P, P, P, P, P]),
     "lng_conv_window": (C.c_int, [PR, P, i64, P, P, P, P, P]),

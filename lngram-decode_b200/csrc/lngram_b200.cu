@@ -673,6 +673,29 @@ extern "C" int lng_rms_norm(const void* x, int32_t x_dtype, int64_t n, int64_t d
   return LNG_OK;
 }
 
+extern "C" int lng_rms_norm_model(const void* x, int32_t x_dtype, int64_t n, int64_t d, const void* w,
+                                  int32_t w_dtype, float eps, void* y, int32_t y_dtype, lng_stream_t stream) {
+  LNG_REQUIRE(n >= 0 && d > 0, "bad shape");
+  LNG_REQUIRE(x_dtype == LNG_F32 || x_dtype == LNG_BF16 || x_dtype == LNG_F16, "x dtype must be f32, bf16 or f16");
+  LNG_REQUIRE(!w || w_dtype == LNG_F32 || w_dtype == LNG_BF16, "weight dtype must be f32 or bf16");
+  LNG_REQUIRE(y_dtype == LNG_F32 || y_dtype == LNG_BF16 || y_dtype == LNG_F16, "y dtype must be f32, bf16 or f16");
+  if (n == 0) return LNG_OK;
+  LNG_REQUIRE(x && y, "NULL pointer");
+  const int64_t xsz = x_dtype == LNG_F32 ? 4 : 2;
+  const int64_t vec_elems = 32 * (16 / xsz);
+  const bool reg = d % vec_elems == 0 && d / vec_elems <= RN_NV && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+  const int nv = reg ? int(d / vec_elems) : 0;
+  const unsigned gr = unsigned(ceil_div(n, 8));
+  const int wb = w && w_dtype == LNG_BF16;
+#define LNG_RM(XT) rms_norm_model_kernel<XT><<<gr, 256, 0, S(stream)>>>(static_cast<const XT*>(x), n, d, nv, w, wb, eps, y, y_dtype)
+  if (x_dtype == LNG_F32) LNG_RM(float);
+  else if (x_dtype == LNG_BF16) LNG_RM(__nv_bfloat16);
+  else LNG_RM(__half);
+#undef LNG_RM
+  LNG_LAUNCHED("rms_norm_model_kernel");
+  return LNG_OK;
+}
+
 static int check_readout(const lng_readout* ro) {
   LNG_REQUIRE(ro != nullptr, "readout descriptor is NULL");
   LNG_REQUIRE(ro->hidden > 0 && ro->num_heads > 0 && ro->num_kv_heads > 0 && ro->head_dim > 0, "bad readout shape");

@@ -106,6 +106,60 @@ __global__ void __launch_bounds__(256) rms_norm_reg_kernel(const XT* __restrict_
   }
 }
 
+// RMSNorm with the rounding order of the model's block norm (ffnmem/model.py:39-48):
+//   y = cast_y( cast_x(x * rsqrt(mean(x^2) + eps)) * w )
+// i.e. the normalised row is rounded to x's own dtype first and only then multiplied by the
+// weight (w fp32 or bf16, or none); one warp per row, the row kept in registers when it fits
+// (nv > 0, 16-byte vectors) and re-read from global memory otherwise.
+template <typename XT>
+__device__ __forceinline__ float round_to(float v) {
+  return to_f32(from_f32<XT>(v));
+}
+
+template <typename XT>
+__global__ void __launch_bounds__(256) rms_norm_model_kernel(const XT* __restrict__ x, int64_t n, int64_t d, int nv,
+                                                             const void* __restrict__ w, int w_bf16, float eps,
+                                                             void* __restrict__ y, int y_dtype) {
+  constexpr int N = Vec16<XT>::N;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (row >= n) return;
+  const XT* xr = x + row * d;
+  auto weight = [&](int64_t j) -> float {
+    if (!w) return 1.f;
+    return w_bf16 ? to_f32(static_cast<const __nv_bfloat16*>(w)[j]) : static_cast<const float*>(w)[j];
+  };
+  auto store = [&](int64_t j, float v) {
+    if (y_dtype == LNG_F32) static_cast<float*>(y)[row * d + j] = v;
+    else if (y_dtype == LNG_BF16) static_cast<__nv_bfloat16*>(y)[row * d + j] = __float2bfloat16_rn(v);
+    else static_cast<__half*>(y)[row * d + j] = __float2half_rn(v);
+  };
+  if (nv > 0) {
+    float v[RN_NV][N];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < RN_NV; ++i) {
+      if (i < nv) {
+        Vec16<XT>::load(xr + (int64_t(i) * 32 + lane) * N, v[i]);
+#pragma unroll
+        for (int k = 0; k < N; ++k) ss = fmaf(v[i][k], v[i][k], ss);
+      }
+    }
+    const float r = rsqrtf(warp_sum(ss) / float(d) + eps);
+#pragma unroll
+    for (int i = 0; i < RN_NV; ++i) {
+      if (i < nv) {
+        const int64_t j0 = (int64_t(i) * 32 + lane) * N;
+#pragma unroll
+        for (int k = 0; k < N; ++k) store(j0 + k, round_to<XT>(v[i][k] * r) * weight(j0 + k));
+      }
+    }
+  } else {
+    const float r = rsqrtf(row_sumsq(xr, d, false, lane) / float(d) + eps);
+    for (int64_t j = lane; j < d; j += 32) store(j, round_to<XT>(to_f32(xr[j]) * r) * weight(j));
+  }
+}
+
 struct ConvParams {
   int64_t d;
   int k, dil;

@@ -69,6 +69,26 @@ def _cuda(t: Tensor, what: str) -> Tensor:
     return t
 
 
+def rms_norm(x: Tensor, weight: Tensor | None, eps: float) -> Tensor:
+    """The model block's RMSNorm (``ffnmem/model.py:39-48``), e.g. the ``attn_norm`` whose output is the
+    memory router's input (``ffnmem/model.py:114``): the row is normalised in fp32, rounded to x's dtype,
+    then multiplied by ``weight``; the result has the promoted dtype of x and the weight, as in torch."""
+    x = _cuda(x, "x").contiguous()
+    if weight is not None:
+        weight = weight.detach().to(x.device).contiguous()
+        if weight.dtype not in (torch.float32, torch.bfloat16):
+            weight = weight.float()
+    out_dt = x.dtype if weight is None else torch.promote_types(x.dtype, weight.dtype)
+    d = x.shape[-1]
+    y = torch.empty(x.shape, device=x.device, dtype=out_dt)
+    with torch.cuda.device(x.device):
+        check(_lib.library().lng_rms_norm_model(ptr(x), _lib.dtype_code(x.dtype), x.numel() // d, d, ptr(weight),
+                                                _lib.dtype_code(weight.dtype) if weight is not None else 0,
+                                                float(eps), ptr(y), _lib.dtype_code(out_dt), stream_ptr()),
+              "rms_norm")
+    return y
+
+
 class RouteNgramMemoryV2(nn.Module):
     """Inference drop-in for the reference ``RouteNgramMemoryV2`` (sink readout v2)."""
 
@@ -504,6 +524,92 @@ class LngramMemory(nn.Module):
                                           self.routes, self.bits, ptr(codes), _lib.U8, None, stream_ptr()),
                       "route_codes")
         return codes
+
+    def forward_host(self, h: Tensor, h_norm: Tensor | None = None, *, norm_weight: Tensor | None = None,
+                     norm_eps: float = 1e-5, out: Tensor | None = None, groups: int = 4,
+                     synchronize: bool = True) -> Tensor:
+        """``forward`` for a batch held in host memory: h [B, T, d] (pinned CPU for overlap) -> out
+        [B, T, d] on the CPU.  The router input is ``h_norm`` as given (copied in as well) or, with
+        ``norm_weight``, made on the device from h by the block's RMSNorm (``rms_norm``, the
+        reference's ``attn_norm`` at ``ffnmem/model.py:114``), so only h crosses PCIe.
+
+        The batch is split into ``groups`` groups of whole sequences that flow through three CUDA
+        streams -- copy in, forward, copy out -- with two device buffers per stream, so the copy of
+        group g + 1 in, the forward of group g and the copy of group g - 1 out run at the same time
+        (PCIe is full duplex).  The caller's current stream is ordered before the first copy and after
+        the last one.  ``synchronize=False`` returns before the copies out have finished: synchronise
+        the current stream before reading ``out``."""
+        if self.training and torch.is_grad_enabled():
+            raise RuntimeError("lngram_b200 implements the inference forward only")
+        if self.router_input != "hidden":
+            raise ValueError("forward_host supports the hidden-state router (router_input='hidden')")
+        if (h_norm is None) == (norm_weight is None):
+            raise ValueError("give exactly one of h_norm (copied in) or norm_weight (made on the device)")
+        if h.dim() != 3 or h.is_cuda:
+            raise ValueError("h must be a host tensor [B, T, d]")
+        B, T, d = h.shape
+        groups = max(1, min(int(groups), B))
+        while B % groups:
+            groups -= 1
+        Bg = B // groups
+        dev = self.router.weight.device
+        act = self.module._act()
+        if out is None:
+            out = torch.empty(B, T, d, dtype=act, pin_memory=True)
+        w = None if norm_weight is None else norm_weight.detach().to(dev)
+        hn_dtype = (h.dtype if h_norm is None and w is None else
+                    (h_norm.dtype if h_norm is not None else torch.promote_types(act, w.dtype)))
+        key = (Bg, T, d, h.dtype, hn_dtype, str(dev))
+        st = getattr(self, "_host_pipe", None)
+        if st is None or st["key"] != key:
+            mk = lambda dt: [torch.empty(Bg, T, d, device=dev, dtype=dt) for _ in range(2)]  # noqa: E731
+            desc_t, desc_r = self.module.tables_desc(), self.module.readout_desc(self.router.weight)
+            need = _lib.library().lng_memory_workspace_bytes(desc_t, desc_r, Bg * T)
+            st = {"key": key, "h": mk(h.dtype), "hn": mk(hn_dtype), "out": mk(act),
+                  "ws": torch.empty(need, device=dev, dtype=torch.uint8),
+                  "streams": [torch.cuda.Stream(dev) for _ in range(3)]}
+            self._host_pipe = st
+        s_in, s_comp, s_out = st["streams"]
+        cur = torch.cuda.current_stream(dev)
+        start = torch.cuda.Event()
+        start.record(cur)
+        for s in (s_in, s_comp, s_out):
+            s.wait_event(start)
+        ev_in, ev_comp, ev_out = [], [], []
+        for g in range(groups):
+            k = g % 2
+            rows = slice(g * Bg, (g + 1) * Bg)
+            if g >= 2:
+                s_in.wait_event(ev_comp[g - 2])       # slot k's inputs were read by group g - 2
+            with torch.cuda.stream(s_in):
+                st["h"][k].copy_(h[rows], non_blocking=True)
+                if h_norm is not None:
+                    st["hn"][k].copy_(h_norm[rows], non_blocking=True)
+                ev_in.append(torch.cuda.Event())
+                ev_in[-1].record(s_in)
+            s_comp.wait_event(ev_in[g])
+            if g >= 2:
+                s_comp.wait_event(ev_out[g - 2])      # slot k's output was copied out by group g - 2
+            with torch.cuda.stream(s_comp):
+                hd = st["h"][k]
+                if w is not None:
+                    hn = st["hn"][k]
+                    check(_lib.library().lng_rms_norm_model(ptr(hd), _lib.dtype_code(hd.dtype), Bg * T, d, ptr(w),
+                                                            _lib.dtype_code(w.dtype), float(norm_eps), ptr(hn),
+                                                            _lib.dtype_code(hn.dtype), stream_ptr()), "rms_norm")
+                self.forward(hd, st["hn"][k], out=st["out"][k], workspace=st["ws"])
+                ev_comp.append(torch.cuda.Event())
+                ev_comp[-1].record(s_comp)
+            s_out.wait_event(ev_comp[g])
+            with torch.cuda.stream(s_out):
+                out[rows].copy_(st["out"][k], non_blocking=True)
+                ev_out.append(torch.cuda.Event())
+                ev_out[-1].record(s_out)
+        cur.wait_event(ev_out[-1])
+        cur.wait_event(ev_comp[-1])
+        if synchronize:
+            cur.synchronize()
+        return out
 
     def forward(self, h: Tensor, h_norm: Tensor, router_in: Tensor | None = None, *, codes_out: Tensor | None = None,
                 out: Tensor | None = None, workspace: Tensor | None = None) -> Tensor:

@@ -132,7 +132,7 @@ class _DeviceRows:
     """A read-only view of a device table for the oracle: ``rows[idx]`` fetches only those rows."""
 
     def __init__(self, weight: torch.Tensor):
-        self.weight = weight
+        self.weight = weight.detach()
         self.shape = tuple(weight.shape)
 
     def __getitem__(self, idx):
@@ -190,7 +190,7 @@ def test_scaled_table_full_rows_forward_and_addresses(lngram):
     del tok
     # codes from the fp32 router agree with the oracle's away from zero logits
     xs = hn[:, :64].float().cpu().numpy()
-    lg = om.route_logits(xs, mem.router.weight.float().cpu().numpy())
+    lg = om.route_logits(xs, mem.router.weight.detach().float().cpu().numpy())
     want_codes = om.quantize_route_logits(lg, bits)
     flips = (want_codes != cc[:, :64]).mean()
     assert flips < 1e-3, flips

@@ -1,14 +1,16 @@
 // GPU drafter: the state machine and API of the reference C++ drafter
 // (drafting/cpu/drafter.cpp:150-595) with every per-token step on the device.
 //
-// Per token x[t] (the reference's drafting/cpu_drafter.py:1-33 steps 1-6, full vocabulary):
-//   embed2 router features -> fp32 router -> sign codes (lng_embed2_features, lng_route_codes);
-//   rows of the n-grams ending at t (window of the last max(ngrams) codes, zero rows before the
-//   sequence start); the draft readout in folded form (w_qk / w_vo from W_q, the memory's norm +
-//   kv_proj, W_o), RMSNorm(out_norm); logits against the embedding with a fused top-k.
+// Per token x[t] (drafter.cpp:396-545): the SD-C SSM step s = a s + (1 - a) W_in RMSNorm(E[x[t]]) when
+// the bundle has one; embed2 router features [RMSNorm(E[x[t-1]] or start), RMSNorm(E[x[t]])] (+ s for
+// the embed2_ssm router) -> fp32 router -> sign codes; the rows of the n-grams ending at t (window of
+// the last max(ngrams) codes, zero rows before the sequence start); the draft readout in folded form
+// (w_qk / w_vo from W_q, the memory's norm + kv_proj, W_o; + the folded W_sq s for query_ssm),
+// RMSNorm(out_norm); then the logits against the embedding -- over the sketch shortlist when the
+// bundle has sketches (drafter_ext.cuh), else over the whole vocabulary -- with a fused top-k.
 // draft() keeps the drafted tokens on the device: step i+1 reads step i's argmax from device memory,
-// so a gamma-token draft costs one host round trip at the end.  The committed state (tokens, codes)
-// lives on the host, as in the reference, so truncate() is exact rollback.
+// so a gamma-token draft costs one host round trip at the end.  The committed state (tokens, codes,
+// SSM states) lives on the host, as in the reference, so truncate() is exact rollback.
 #pragma once
 
 namespace lng {
@@ -70,10 +72,25 @@ struct lng_drafter {
   __nv_bfloat16* router_w_split = nullptr;  // router weight as bf16 parts W1 | W2 | W3 (made once)
   float *out_norm = nullptr;
   void *w_qk = nullptr, *w_vo = nullptr;
+  int64_t F = 0;              // router feature width: 2d (+ N for the embed2_ssm router)
+  // SD-C SSM (N = 0: none)
+  int64_t N = 0;
+  bool router_ssm = false, query_ssm = false;
+  float ssm_eps = 0;
+  float *ssm_norm = nullptr, *ssm_w_in = nullptr, *ssm_a = nullptr;
+  void* w_sqk = nullptr;      // folded query map of W_sq [qh*Dt, N] (act dtype)
+  // sketch shortlist (K = 0 or cap = 0: full-vocabulary scoring)
+  int64_t K = 0, cap = 0;
+  int ht = 0;                 // hash slots per shortlist item
+  int32_t* sk_ids[LNG_MAX_ORDERS] = {};
+  int32_t* sk_cnt[LNG_MAX_ORDERS] = {};
+  int32_t* fallback = nullptr;
+  int n_fallback = 0;
   std::vector<void*> owned;
   // host state (the reference keeps the same: drafter.cpp:571-574)
   std::vector<int64_t> tokens;
   std::vector<uint8_t> codes;
+  std::vector<float> ssm;     // SSM state after each committed token [length, N]
   std::mutex mu;
   cudaStream_t stream = nullptr;
   // grow-on-demand device workspace
@@ -94,6 +111,7 @@ struct lng_drafter {
     t.memory_dim = md;
     return t;
   }
+  bool has_sketch() const { return K > 0 && cap > 0; }
   ~lng_drafter() {
     for (void* p : owned) cudaFree(p);
     if (ws) cudaFree(ws);
@@ -173,17 +191,33 @@ static int upload_as(lng_drafter* dr, const lng_array* a, int64_t expect, bool w
   return LNG_OK;
 }
 
+// Upload a host int32 array (sketch ids / counts, fallback list).
+static int upload_i32(lng_drafter* dr, const lng_array* a, int64_t expect, int32_t** out) {
+  if (!a) return fail(LNG_ERR_ARGUMENT, "bundle array missing");
+  const int64_t n = array_numel(a);
+  if (expect >= 0 && n != expect)
+    return fail(LNG_ERR_ARGUMENT, std::string("bundle array ") + a->name + " has the wrong size");
+  if (a->dtype != LNG_I32) return fail(LNG_ERR_ARGUMENT, std::string("bundle array ") + a->name + " must be int32");
+  void* p = nullptr;
+  int st = drafter_alloc(dr, size_t(n) * 4, &p);
+  if (st) return st;
+  if (n) LNG_CUDA(cudaMemcpy(p, a->data_host, size_t(n) * 4, cudaMemcpyHostToDevice));
+  *out = static_cast<int32_t*>(p);
+  return LNG_OK;
+}
+
 struct ReadoutBufs {
-  void* x;       // [M, d] embedding rows (E dtype)
-  float* qs;     // [M]
-  void* qa;      // [M, qh*Dt] act
-  void* u;       // [M, qh*Dt] act
-  float* hid;    // [M, d]
-  float* hn;     // [M, d]
-  int64_t* ids;  // [M, k]
-  float* vals;   // [M, k]
+  int64_t rows;  // capacity in items of the per-item buffers below
+  void* x;       // [rows, d] embedding rows (E dtype)
+  float* qs;     // [rows]
+  void* qa;      // [rows, qh*Dt] act
+  void* u;       // [rows, qh*Dt] act
+  float* hid;    // [rows, d]
+  float* hn;     // [rows, d]
+  int64_t* ids;  // [rows, k]
+  float* vals;   // [rows, k]
   void* scratch; size_t scratch_bytes;
-  float* feat;   // [M, 2d]
+  float* feat;   // [rows, F]
 };
 
 static int drafter_ws(lng_drafter* dr, int64_t M, int k, ReadoutBufs* b, size_t extra_bytes, void** extra) {
@@ -192,7 +226,7 @@ static int drafter_ws(lng_drafter* dr, int64_t M, int k, ReadoutBufs* b, size_t 
   const size_t sizes[10] = {al256(size_t(M) * dr->d * es), al256(size_t(M) * 4), al256(size_t(M) * qd * as),
                             al256(size_t(M) * qd * as), al256(size_t(M) * dr->d * 4), al256(size_t(M) * dr->d * 4),
                             al256(size_t(M) * k * 8), al256(size_t(M) * k * 4),
-                            al256(lng_logits_topk_scratch_bytes(M, dr->d, dr->V, k)), al256(size_t(M) * 2 * dr->d * 4)};
+                            al256(lng_logits_topk_scratch_bytes(M, dr->d, dr->V, k)), al256(size_t(M) * dr->F * 4)};
   size_t total = al256(extra_bytes);
   for (size_t s : sizes) total += s;
   if (total > dr->ws_bytes) {
@@ -208,6 +242,7 @@ static int drafter_ws(lng_drafter* dr, int64_t M, int k, ReadoutBufs* b, size_t 
     ptrs[i] = p;
     p += sizes[i];
   }
+  b->rows = M;
   b->x = ptrs[0];
   b->qs = static_cast<float*>(ptrs[1]);
   b->qa = ptrs[2];
@@ -223,40 +258,140 @@ static int drafter_ws(lng_drafter* dr, int64_t M, int k, ReadoutBufs* b, size_t 
   return LNG_OK;
 }
 
-// Codes of M tokens given their previous tokens (device i64 arrays; prev = -1 -> start vector).
-static int drafter_codes(lng_drafter* dr, const int64_t* cur, const int64_t* prev, int64_t M, float* feat,
-                         uint8_t* codes_out, int64_t codes_stride) {
-  lng_stream_t s = reinterpret_cast<lng_stream_t>(dr->stream);
-  int st = lng_embed2_features(cur, prev, M, dr->E, dr->e_dtype, dr->V, dr->d, dr->prev_norm, dr->cur_norm,
-                               dr->start, dr->router_eps, feat, s);
-  if (st) return st;
-  if (codes_stride == dr->R)
-    return route_codes_presplit(feat, M, 2 * dr->d, dr->router_w, dr->router_w_split, dr->R, int32_t(dr->bits),
-                                codes_out, dr->stream);
-  for (int64_t i = 0; i < M; ++i) {  // strided destination (batched drafting): one row at a time
-    st = route_codes_presplit(feat + i * 2 * dr->d, 1, 2 * dr->d, dr->router_w, dr->router_w_split, dr->R,
-                              int32_t(dr->bits), codes_out + i * codes_stride, dr->stream);
-    if (st) return st;
-  }
-  return LNG_OK;
-}
-
-// Readout of M items: embedding rows of `cur`, the item's code window per `src`, top-k (or full logits).
-static int drafter_readout(lng_drafter* dr, const int64_t* cur, int64_t M, const CodeSource& src, int k,
-                           ReadoutBufs& b, float* full_logits) {
+static int gather_embedding(lng_drafter* dr, const int64_t* tok, int64_t n, void* out) {
   cudaStream_t s = dr->stream;
-  lng_stream_t ls = reinterpret_cast<lng_stream_t>(s);
-  const int64_t qd = dr->qh * dr->Dt;
-#define LNG_GR(T) gather_rows_kernel<T><<<grid_for(M * dr->d, 256, 8), 256, 0, s>>>(cur, M, static_cast<const T*>(dr->E), dr->d, dr->V, static_cast<T*>(b.x))
+#define LNG_GR(T) gather_rows_kernel<T><<<grid_for(n * dr->d, 256, 8), 256, 0, s>>>(tok, n, static_cast<const T*>(dr->E), dr->d, dr->V, static_cast<T*>(out))
   if (dr->e_dtype == LNG_F32) LNG_GR(float);
   else if (dr->e_dtype == LNG_BF16) LNG_GR(__nv_bfloat16);
   else LNG_GR(__half);
 #undef LNG_GR
   LNG_LAUNCHED("gather_rows_kernel");
-  int st = lng_rms_rows(b.x, dr->e_dtype, M, dr->d, dr->draft_eps, b.qs, ls);
+  return LNG_OK;
+}
+
+// SSM inputs u[i] = W_in RMSNorm(E[tok[i]]; ssm_norm) (fp32 [n, N]) in chunks of the workspace's rows
+// (ffnmem/memory/ssm.py:40-43; drafter.cpp:399-401).
+static int drafter_ssm_inputs(lng_drafter* dr, const int64_t* tok, int64_t n, ReadoutBufs& b, float* u) {
+  lng_stream_t ls = reinterpret_cast<lng_stream_t>(dr->stream);
+  for (int64_t c0 = 0; c0 < n; c0 += b.rows) {
+    const int64_t m = std::min<int64_t>(b.rows, n - c0);
+    int st = gather_embedding(dr, tok + c0, m, b.x);
+    if (st) return st;
+    st = lng_rms_norm(b.x, dr->e_dtype, m, dr->d, dr->ssm_norm, dr->ssm_eps, b.hid, LNG_F32, ls);
+    if (st) return st;
+    st = lng_gemm(b.hid, LNG_F32, dr->d, dr->ssm_w_in, LNG_F32, dr->d, u + c0 * dr->N, LNG_F32, dr->N, m, dr->N,
+                  dr->d, nullptr, 0, ls);
+    if (st) return st;
+  }
+  return LNG_OK;
+}
+
+// The recurrence over nseq sequences of L inputs each (u [nseq, L, N]) from s0 [nseq, N] (NULL =
+// zeros): the states of positions >= out_from into states [nseq, L - out_from, N].
+static int drafter_ssm_scan(lng_drafter* dr, const float* u, int64_t nseq, int64_t L, const float* s0,
+                            int64_t out_from, float* states) {
+  const int64_t n = nseq * dr->N;
+  ssm_scan_kernel<<<unsigned(ceil_div(n, 128)), 128, 0, dr->stream>>>(u, nseq, L, dr->N, dr->ssm_a, s0, out_from,
+                                                                       states);
+  LNG_LAUNCHED("ssm_scan_kernel");
+  return LNG_OK;
+}
+
+// Codes of M tokens given their previous tokens (device i64 arrays; prev = -1 -> start vector) and,
+// for the embed2_ssm router, their SSM states s_rows [M, N].
+static int drafter_codes(lng_drafter* dr, const int64_t* cur, const int64_t* prev, int64_t M, float* feat,
+                         uint8_t* codes_out, int64_t codes_stride, const float* s_rows) {
+  int st = embed2_features(cur, prev, M, dr->E, dr->e_dtype, dr->V, dr->d, dr->prev_norm, dr->cur_norm, dr->start,
+                           dr->router_eps, feat, dr->F, dr->stream);
   if (st) return st;
-  st = lng_gemm(b.x, dr->e_dtype, dr->d, dr->w_qk, dr->act, dr->d, b.qa, dr->act, qd, M, qd, dr->d, nullptr, 0, ls);
+  if (dr->router_ssm) {
+    LNG_REQUIRE(s_rows, "internal: the SSM router needs the states");
+    copy_cols_kernel<<<grid_for(M * dr->N, 256, 8), 256, 0, dr->stream>>>(s_rows, M, dr->N, feat, dr->F, 2 * dr->d);
+    LNG_LAUNCHED("copy_cols_kernel");
+  }
+  if (codes_stride == dr->R)
+    return route_codes_presplit(feat, M, dr->F, dr->router_w, dr->router_w_split, dr->R, int32_t(dr->bits), codes_out,
+                                dr->stream);
+  for (int64_t i = 0; i < M; ++i) {  // strided destination: one row at a time
+    st = route_codes_presplit(feat + i * dr->F, 1, dr->F, dr->router_w, dr->router_w_split, dr->R, int32_t(dr->bits),
+                              codes_out + i * codes_stride, dr->stream);
+    if (st) return st;
+  }
+  return LNG_OK;
+}
+
+// How a readout scores the vocabulary: the sketch shortlist unless `full` (or no sketch); in trace
+// mode (list_ids != NULL) the shortlist and its logits in list order [M, S].
+struct Scoring {
+  bool full = false;
+  float* full_logits = nullptr;  // [M, V] when full-vocabulary logits are wanted
+  int64_t S = 0;
+  int64_t* list_ids = nullptr;
+  float* list_lg = nullptr;
+};
+
+static int launch_shortlist(lng_drafter* dr, const CodeSource& src, int64_t M, const float* hn, int topk,
+                            int64_t* ids, float* vals, const Scoring& sc) {
+  ShortlistParams p{};
+  p.src = src;
+  for (int o = 0; o < dr->n_orders; ++o) {
+    p.orders[o] = dr->orders[o];
+    p.sk_ids[o] = dr->sk_ids[o];
+    p.sk_cnt[o] = dr->sk_cnt[o];
+  }
+  p.n_orders = dr->n_orders;
+  p.bits = int(dr->bits);
+  p.R = dr->R;
+  p.K = int(dr->K);
+  p.fallback = dr->fallback;
+  p.n_fallback = dr->n_fallback;
+  p.cap = int(dr->cap);
+  p.V = dr->V;
+  p.d = dr->d;
+  p.E = dr->E;
+  p.e_dtype = dr->e_dtype;
+  p.hn = hn;
+  p.M = M;
+  p.ht = dr->ht;
+  p.topk = sc.list_ids ? 0 : topk;
+  p.ids = ids;
+  p.vals = vals;
+  p.S = sc.S;
+  p.list_ids = sc.list_ids;
+  p.list_lg = sc.list_lg;
+  const size_t smem = size_t(dr->ht) * 8 + size_t(dr->d) * 4 + size_t(dr->cap) * 8;
+  auto kern = shortlist_kernel<uint8_t>;
+  LNG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  const int grid = int(std::max<int64_t>(1, std::min<int64_t>(M, int64_t(num_sms()))));
+  kern<<<grid, SL_THREADS, smem, dr->stream>>>(p);
+  LNG_LAUNCHED("shortlist_kernel");
+  return LNG_OK;
+}
+
+// Readout of M items: embedding rows of `cur`, the item's code window per `src`, the SSM states
+// s_rows [M, N] for query_ssm, then top-k (or the trace outputs) per `sc`.
+static int drafter_readout(lng_drafter* dr, const int64_t* cur, int64_t M, const CodeSource& src, int k,
+                           ReadoutBufs& b, const Scoring& sc, const float* s_rows) {
+  cudaStream_t s = dr->stream;
+  lng_stream_t ls = reinterpret_cast<lng_stream_t>(s);
+  const int64_t qd = dr->qh * dr->Dt;
+  int st = gather_embedding(dr, cur, M, b.x);
   if (st) return st;
+  st = lng_rms_rows(b.x, dr->e_dtype, M, dr->d, dr->draft_eps, b.qs, ls);
+  if (st) return st;
+  const float* qscale = b.qs;
+  if (dr->query_ssm) {
+    // qa = rs(x) (x . w_qk^T) + s . w_sqk^T: the SSM term carries no RMS scale (drafter.cpp:505-508)
+    LNG_REQUIRE(s_rows, "internal: the SSM query needs the states");
+    st = lng_gemm(b.x, dr->e_dtype, dr->d, dr->w_qk, dr->act, dr->d, b.qa, dr->act, qd, M, qd, dr->d, b.qs, 0, ls);
+    if (st) return st;
+    st = lng_gemm(s_rows, LNG_F32, dr->N, dr->w_sqk, dr->act, dr->N, b.qa, dr->act, qd, M, qd, dr->N, nullptr, 1, ls);
+    if (st) return st;
+    qscale = nullptr;
+  } else {
+    st = lng_gemm(b.x, dr->e_dtype, dr->d, dr->w_qk, dr->act, dr->d, b.qa, dr->act, qd, M, qd, dr->d, nullptr, 0, ls);
+    if (st) return st;
+  }
   const lng_tables t = dr->tables();
   AttendParams p{};
   p.ts = table_set(&t);
@@ -268,7 +403,7 @@ static int drafter_readout(lng_drafter* dr, const int64_t* cur, int64_t M, const
   p.eps = dr->mem_eps;
   p.sink = dr->sink;
   p.qa = b.qa;
-  p.qscale = b.qs;
+  p.qscale = qscale;
   p.u = b.u;
   st = attend_impl<uint8_t>(&t, p, dr->act, s);
   if (st) return st;
@@ -276,7 +411,8 @@ static int drafter_readout(lng_drafter* dr, const int64_t* cur, int64_t M, const
   if (st) return st;
   st = lng_rms_norm(b.hid, LNG_F32, M, dr->d, dr->out_norm, dr->draft_eps, b.hn, LNG_F32, ls);
   if (st) return st;
-  return lng_logits_topk(b.hn, M, dr->d, dr->E, dr->e_dtype, dr->V, k, b.ids, b.vals, full_logits, b.scratch,
+  if (dr->has_sketch() && !sc.full) return launch_shortlist(dr, src, M, b.hn, k, b.ids, b.vals, sc);
+  return lng_logits_topk(b.hn, M, dr->d, dr->E, dr->e_dtype, dr->V, k, b.ids, b.vals, sc.full_logits, b.scratch,
                          b.scratch_bytes, ls);
 }
 
@@ -287,13 +423,11 @@ extern "C" int lng_drafter_create(const lng_drafter_numbers* num, const lng_arra
   LNG_REQUIRE(num && arrays && out, "NULL pointer");
   *out = nullptr;
   LNG_REQUIRE(act_dtype == LNG_F32 || act_dtype == LNG_BF16, "act dtype must be f32 or bf16");
-  if (num->ssm_dim > 0 || num->router_ssm || num->query_ssm)
-    return fail(LNG_ERR_UNSUPPORTED, "SSM drafters (SD-C) are not implemented by lngram_b200");
-  if (num->sketch_k > 0 && num->shortlist_cap > 0)
-    return fail(LNG_ERR_UNSUPPORTED, "sketch shortlists are not implemented by lngram_b200 (full-vocabulary bundles)");
   LNG_REQUIRE(num->n_orders >= 1 && num->n_orders <= LNG_MAX_ORDERS, "n_orders must be in [1, 4]");
   LNG_REQUIRE(num->q_heads % num->kv_heads == 0 && num->q_heads <= 64, "q_heads must be a multiple of kv_heads");
   LNG_REQUIRE(num->bits >= 1 && num->bits <= 8, "bits must be in [1, 8]");
+  LNG_REQUIRE(num->ssm_dim >= 0 && num->sketch_k >= 0, "bad ssm_dim / sketch_k");
+  LNG_REQUIRE(!(num->router_ssm || num->query_ssm) || num->ssm_dim > 0, "an SSM router / query needs ssm_dim > 0");
   std::unique_ptr<lng_drafter> dr(new lng_drafter());
   dr->d = num->d_model;
   dr->V = num->vocab;
@@ -310,8 +444,15 @@ extern "C" int lng_drafter_create(const lng_drafter_numbers* num, const lng_arra
   dr->router_eps = float(num->router_eps);
   dr->draft_eps = float(num->draft_eps);
   dr->mem_eps = float(num->mem_eps);
+  dr->ssm_eps = float(num->ssm_eps);
   dr->sink = float(num->sink_logit);
   dr->act = act_dtype;
+  dr->N = num->ssm_dim;
+  dr->router_ssm = num->router_ssm != 0;
+  dr->query_ssm = num->query_ssm != 0;
+  dr->F = 2 * dr->d + (dr->router_ssm ? dr->N : 0);
+  dr->K = num->sketch_k;
+  dr->cap = num->shortlist_cap > 0 ? num->shortlist_cap : 0;
   LNG_REQUIRE(std::fabs(num->softmax_scale * std::sqrt(double(num->head_dim)) - 1.0) < 1e-6,
               "softmax_scale must be head_dim^-1/2");
   LNG_CUDA(cudaStreamCreateWithFlags(&dr->stream, cudaStreamNonBlocking));
@@ -342,9 +483,9 @@ extern "C" int lng_drafter_create(const lng_drafter_numbers* num, const lng_arra
   const int64_t KH = D->kv * D->hd, I = D->qh * D->hd;
   if ((st = upload_f32(D, find_array(arrays, n_arrays, "mem_norm"), D->Dt, &mem_norm))) return st;
   if ((st = upload_f32(D, find_array(arrays, n_arrays, "kv_proj"), 2 * KH * D->Dt, &kv_proj))) return st;
-  if ((st = upload_f32(D, find_array(arrays, n_arrays, "router"), D->R * D->bits * 2 * D->d, &D->router_w))) return st;
+  if ((st = upload_f32(D, find_array(arrays, n_arrays, "router"), D->R * D->bits * D->F, &D->router_w))) return st;
   {  // the router weight's bf16x3 split, used by every small-batch code computation of this drafter
-    const int64_t rows = D->R * D->bits, in_dim = 2 * D->d;
+    const int64_t rows = D->R * D->bits, in_dim = D->F;
     void* wsp = nullptr;
     LNG_CUDA(cudaMalloc(&wsp, size_t(rows) * 3 * in_dim * sizeof(__nv_bfloat16)));
     D->owned.push_back(wsp);
@@ -366,6 +507,50 @@ extern "C" int lng_drafter_create(const lng_drafter_numbers* num, const lng_arra
   st = lng_fold_readout(D->d, D->Dt, int32_t(D->qh), int32_t(D->kv), int32_t(D->hd), q_norm, w_q, mem_norm, kv_proj,
                         w_o, D->w_qk, D->w_vo, act_dtype, nullptr);
   if (st) return st;
+  if (D->N > 0) {  // SD-C: the SSM and, for query_ssm, the folded W_sq
+    if ((st = upload_f32(D, find_array(arrays, n_arrays, "ssm_norm"), D->d, &D->ssm_norm))) return st;
+    if ((st = upload_f32(D, find_array(arrays, n_arrays, "ssm_w_in"), D->N * D->d, &D->ssm_w_in))) return st;
+    if ((st = upload_f32(D, find_array(arrays, n_arrays, "ssm_decay"), D->N, &D->ssm_a))) return st;
+    if (D->query_ssm) {
+      float* w_sq = nullptr;
+      if ((st = upload_f32(D, find_array(arrays, n_arrays, "w_sq"), I * D->N, &w_sq))) return st;
+      std::vector<float> ones(size_t(D->N), 1.f);
+      void* onesd = nullptr;
+      if ((st = drafter_alloc(D, size_t(D->N) * 4, &onesd))) return st;
+      LNG_CUDA(cudaMemcpy(onesd, ones.data(), size_t(D->N) * 4, cudaMemcpyHostToDevice));
+      if ((st = drafter_alloc(D, size_t(D->qh * D->Dt * D->N) * as, &D->w_sqk))) return st;
+      st = lng_fold_readout(D->N, D->Dt, int32_t(D->qh), int32_t(D->kv), int32_t(D->hd), static_cast<float*>(onesd),
+                            w_sq, mem_norm, kv_proj, nullptr, D->w_sqk, nullptr, act_dtype, nullptr);
+      if (st) return st;
+    }
+  }
+  if (D->has_sketch()) {  // the sketch shortlist
+    const int64_t cand = int64_t(D->n_orders) * D->R * D->K;
+    int64_t ht = 1;
+    while (ht < 2 * cand) ht <<= 1;
+    if (ht > SL_MAX_SLOTS)
+      return fail(LNG_ERR_UNSUPPORTED, "sketch shortlist: orders x routes x sketch_k = " + std::to_string(cand) +
+                                           " entries per position exceed the " + std::to_string(SL_MAX_SLOTS / 2) +
+                                           " this build sums in shared memory");
+    LNG_REQUIRE(D->V < (int64_t(1) << SL_ID_BITS) - 1, "sketch shortlist: vocabulary too large");
+    LNG_REQUIRE(size_t(ht) * 8 + size_t(D->d) * 4 + size_t(D->cap) * 8 <= 227 * 1024,
+                "sketch shortlist: shortlist_cap too large");
+    D->ht = int(ht);
+    for (int o = 0; o < D->n_orders; ++o) {
+      const int64_t rows = D->R << (D->bits * D->orders[o]);
+      const std::string n = std::to_string(D->orders[o]);
+      if ((st = upload_i32(D, find_array(arrays, n_arrays, ("sketch_ids_" + n).c_str()), rows * D->K, &D->sk_ids[o])))
+        return st;
+      if ((st = upload_i32(D, find_array(arrays, n_arrays, ("sketch_counts_" + n).c_str()), rows * D->K,
+                           &D->sk_cnt[o])))
+        return st;
+    }
+    const lng_array* fb = find_array(arrays, n_arrays, "fallback");
+    if (fb && array_numel(fb) > 0) {
+      if ((st = upload_i32(D, fb, -1, &D->fallback))) return st;
+      D->n_fallback = int(array_numel(fb));
+    }
+  }
   LNG_CUDA(cudaDeviceSynchronize());
   *out = dr.release();
   return LNG_OK;
@@ -378,6 +563,7 @@ extern "C" int lng_drafter_reset(lng_drafter* d) {
   std::lock_guard<std::mutex> lk(d->mu);
   d->tokens.clear();
   d->codes.clear();
+  d->ssm.clear();
   return LNG_OK;
 }
 
@@ -389,6 +575,7 @@ extern "C" int lng_drafter_truncate(lng_drafter* d, int64_t n) {
   if (n < 0 || n > int64_t(d->tokens.size())) return fail(LNG_ERR_STATE, "cannot truncate to " + std::to_string(n));
   d->tokens.resize(size_t(n));
   d->codes.resize(size_t(n * d->R));
+  d->ssm.resize(size_t(n * d->N));
   return LNG_OK;
 }
 
@@ -403,25 +590,49 @@ extern "C" int lng_drafter_committed_codes(const lng_drafter* d, uint8_t* codes_
 
 namespace lng {
 
-// Codes of `n` new tokens after the committed state, on the device; written to codes_host [n, R].
-static int drafter_codes_for(lng_drafter* d, const int64_t* toks_host, int64_t n, uint8_t* codes_host) {
+// Codes (and SSM states) of `n` new tokens after the committed state, on the device; written to
+// codes_host [n, R] (unless the caller's codes replace them) and states_host [n, N].
+static int drafter_codes_for(lng_drafter* d, const int64_t* toks_host, int64_t n, uint8_t* codes_host,
+                             bool own_codes, float* states_host) {
   ReadoutBufs b;
   void* extra = nullptr;
-  const size_t tb = al256(size_t(2 * n) * 8);
-  int st = drafter_ws(d, n, 1, &b, tb + size_t(n * d->R), &extra);
+  const size_t tb = al256(size_t(2 * n) * 8), cb = al256(size_t(n * d->R)), sb = al256(size_t(n * d->N) * 4);
+  const size_t s0b = al256(size_t(d->N) * 4);
+  int st = drafter_ws(d, std::min<int64_t>(n, 4096), 1, &b, tb + cb + 2 * sb + s0b, &extra);
   if (st) return st;
-  int64_t* cur = static_cast<int64_t*>(extra);
+  unsigned char* ex = static_cast<unsigned char*>(extra);
+  int64_t* cur = reinterpret_cast<int64_t*>(ex);
   int64_t* prev = cur + n;
-  uint8_t* cd = static_cast<uint8_t*>(extra) + tb;
+  uint8_t* cd = ex + tb;
+  float* u = reinterpret_cast<float*>(ex + tb + cb);
+  float* states = reinterpret_cast<float*>(ex + tb + cb + sb);
+  float* s0 = reinterpret_cast<float*>(ex + tb + cb + 2 * sb);
   std::vector<int64_t> host(size_t(2 * n));
   for (int64_t i = 0; i < n; ++i) {
     host[size_t(i)] = toks_host[i];
     host[size_t(n + i)] = i > 0 ? toks_host[i - 1] : (d->tokens.empty() ? -1 : d->tokens.back());
   }
   LNG_CUDA(cudaMemcpyAsync(cur, host.data(), size_t(2 * n) * 8, cudaMemcpyHostToDevice, d->stream));
-  st = drafter_codes(d, cur, prev, n, b.feat, cd, d->R);
-  if (st) return st;
-  LNG_CUDA(cudaMemcpyAsync(codes_host, cd, size_t(n * d->R), cudaMemcpyDeviceToHost, d->stream));
+  if (d->N > 0) {
+    const bool have_prev = !d->ssm.empty();
+    if (have_prev)
+      LNG_CUDA(cudaMemcpyAsync(s0, d->ssm.data() + d->ssm.size() - size_t(d->N), size_t(d->N) * 4,
+                               cudaMemcpyHostToDevice, d->stream));
+    st = drafter_ssm_inputs(d, cur, n, b, u);
+    if (st) return st;
+    st = drafter_ssm_scan(d, u, 1, n, have_prev ? s0 : nullptr, 0, states);
+    if (st) return st;
+    LNG_CUDA(cudaMemcpyAsync(states_host, states, size_t(n * d->N) * 4, cudaMemcpyDeviceToHost, d->stream));
+  }
+  if (own_codes) {
+    // the features of more rows than the workspace holds go in workspace-sized pieces
+    for (int64_t c0 = 0; c0 < n; c0 += b.rows) {
+      const int64_t m = std::min<int64_t>(b.rows, n - c0);
+      st = drafter_codes(d, cur + c0, prev + c0, m, b.feat, cd + c0 * d->R, d->R, d->N > 0 ? states + c0 * d->N : nullptr);
+      if (st) return st;
+    }
+    LNG_CUDA(cudaMemcpyAsync(codes_host, cd, size_t(n * d->R), cudaMemcpyDeviceToHost, d->stream));
+  }
   LNG_CUDA(cudaStreamSynchronize(d->stream));
   const int derr = lng_device_error(1);
   if (derr) return fail(LNG_ERR_DEVICE, "device error " + std::to_string(derr) + " (token id out of range?)");
@@ -439,14 +650,16 @@ extern "C" int lng_drafter_commit(lng_drafter* d, const int64_t* tokens_host, in
   for (int64_t i = 0; i < n; ++i)
     if (tokens_host[i] < 0 || tokens_host[i] >= d->V) return fail(LNG_ERR_STATE, "token id out of range");
   std::vector<uint8_t> c(size_t(n * d->R));
-  if (codes_host) {
+  std::vector<float> states(size_t(n * d->N));
+  if (codes_host)
     for (int64_t i = 0; i < n * d->R; ++i) c[size_t(i)] = uint8_t(codes_host[i]);
-  } else {
-    int st = drafter_codes_for(d, tokens_host, n, c.data());
+  if (!codes_host || d->N > 0) {
+    int st = drafter_codes_for(d, tokens_host, n, c.data(), codes_host == nullptr, states.data());
     if (st) return st;
   }
   d->tokens.insert(d->tokens.end(), tokens_host, tokens_host + n);
   d->codes.insert(d->codes.end(), c.begin(), c.end());
+  d->ssm.insert(d->ssm.end(), states.begin(), states.end());
   return LNG_OK;
 }
 
@@ -461,15 +674,20 @@ extern "C" int lng_drafter_draft(lng_drafter* d, int64_t gamma, const int64_t* h
   if (L == 0 && n_hyp == 0) return fail(LNG_ERR_STATE, "draft needs at least one committed or hypothetical token");
   for (int64_t i = 0; i < n_hyp; ++i)
     if (hyp_host[i] < 0 || hyp_host[i] >= d->V) return fail(LNG_ERR_STATE, "token id out of range");
-  const int64_t W = d->maxn, R = d->R;
+  const int64_t W = d->maxn, R = d->R, N = d->N;
   // slots: W-1 history slots, then hyp tokens, then drafted tokens (positions L-W+1 ..)
   const int64_t nslots = (W - 1) + 1 + n_hyp + gamma;  // +1: the last committed token's slot
   const int64_t n_codes = n_hyp + (last_codes ? gamma : std::max<int64_t>(gamma - 1, 0));
   ReadoutBufs b;
   void* extra = nullptr;
+  // SSM states of the slots from W-1 on: row 0 = the last committed token's (zeros if none), then the
+  // hypothesis tokens', then the drafted tokens'
+  const int64_t srows = 1 + n_hyp + gamma;
   const size_t tok_b = al256(size_t(nslots + 1) * 8), seg_b = al256(size_t(gamma * W) * 4), ids_b = al256(size_t(gamma * topk) * 8),
-               val_b = al256(size_t(gamma * topk) * 4), code_b = al256(size_t(nslots * R));
-  int st = drafter_ws(d, std::max<int64_t>(1, n_hyp), topk, &b, tok_b + seg_b + ids_b + val_b + code_b, &extra);
+               val_b = al256(size_t(gamma * topk) * 4), code_b = al256(size_t(nslots * R)),
+               ssm_b = al256(size_t(srows * N) * 4), u_b = al256(size_t(std::max<int64_t>(n_hyp, 1) * N) * 4);
+  int st = drafter_ws(d, std::max<int64_t>(1, n_hyp), topk, &b,
+                      tok_b + seg_b + ids_b + val_b + code_b + ssm_b + u_b, &extra);
   if (st) return st;
   unsigned char* ex = static_cast<unsigned char*>(extra);
   int64_t* dtok = reinterpret_cast<int64_t*>(ex);            // dtok[s + 1] = token of slot s; dtok[0] = -1
@@ -477,6 +695,8 @@ extern "C" int lng_drafter_draft(lng_drafter* d, int64_t gamma, const int64_t* h
   int64_t* dids = reinterpret_cast<int64_t*>(ex + tok_b + seg_b);
   float* dvals = reinterpret_cast<float*>(ex + tok_b + seg_b + ids_b);
   uint8_t* dcodes = ex + tok_b + seg_b + ids_b + val_b;      // [nslots, R]
+  float* dssm = reinterpret_cast<float*>(ex + tok_b + seg_b + ids_b + val_b + code_b);   // [srows, N]
+  float* du = reinterpret_cast<float*>(ex + tok_b + seg_b + ids_b + val_b + code_b + ssm_b);
   // host-side initial slots: the last W committed positions (slot W-1 = position L-1)
   std::vector<int64_t> htok(size_t(nslots + 1), -1);
   std::vector<uint8_t> hcodes(size_t(nslots * R), 0);
@@ -499,22 +719,43 @@ extern "C" int lng_drafter_draft(lng_drafter* d, int64_t gamma, const int64_t* h
   LNG_CUDA(cudaMemcpyAsync(dcodes, hcodes.data(), size_t(nslots * R), cudaMemcpyHostToDevice, d->stream));
   if (gamma > 0)
     LNG_CUDA(cudaMemcpyAsync(dseg, hseg.data(), size_t(gamma * W) * 4, cudaMemcpyHostToDevice, d->stream));
-  // hypothetical tokens: their codes in one batched router pass (prev of slot s is slot s-1)
+  if (N > 0) {
+    if (L > 0)
+      LNG_CUDA(cudaMemcpyAsync(dssm, d->ssm.data() + size_t((L - 1) * N), size_t(N) * 4, cudaMemcpyHostToDevice,
+                               d->stream));
+    else
+      LNG_CUDA(cudaMemsetAsync(dssm, 0, size_t(N) * 4, d->stream));
+  }
+  // hypothetical tokens: their SSM states and codes in one batched pass (prev of slot s is slot s-1)
   if (n_hyp > 0) {
-    st = drafter_codes(d, dtok + W + 1, dtok + W, n_hyp, b.feat, dcodes + W * R, R);
+    if (N > 0) {
+      st = drafter_ssm_inputs(d, dtok + W + 1, n_hyp, b, du);
+      if (st) return st;
+      st = drafter_ssm_scan(d, du, 1, n_hyp, dssm, 0, dssm + N);
+      if (st) return st;
+    }
+    st = drafter_codes(d, dtok + W + 1, dtok + W, n_hyp, b.feat, dcodes + W * R, R, N > 0 ? dssm + N : nullptr);
     if (st) return st;
   }
   for (int64_t g = 0; g < gamma; ++g) {
     const int64_t end = W - 1 + n_hyp + g;  // slot of the current token
+    const float* s_cur = N > 0 ? dssm + (n_hyp + g) * N : nullptr;
     CodeSource src{dcodes + (end - W + 1) * R, 0, 0, W, R, nullptr, nullptr, dseg + g * W, 0, 0};
-    st = drafter_readout(d, dtok + end + 1, 1, src, topk, b, nullptr);
+    st = drafter_readout(d, dtok + end + 1, 1, src, topk, b, Scoring{}, s_cur);
     if (st) return st;
     LNG_CUDA(cudaMemcpyAsync(dids + g * topk, b.ids, size_t(topk) * 8, cudaMemcpyDeviceToDevice, d->stream));
     LNG_CUDA(cudaMemcpyAsync(dvals + g * topk, b.vals, size_t(topk) * 4, cudaMemcpyDeviceToDevice, d->stream));
     if (g + 1 < gamma || last_codes) {
       copy_i64_kernel<<<1, 32, 0, d->stream>>>(b.ids, dtok + end + 2, 1, 1, 1);
       LNG_LAUNCHED("copy_i64_kernel");
-      st = drafter_codes(d, dtok + end + 2, dtok + end + 1, 1, b.feat, dcodes + (end + 1) * R, R);
+      float* s_next = N > 0 ? dssm + (n_hyp + g + 1) * N : nullptr;
+      if (N > 0) {
+        st = drafter_ssm_inputs(d, dtok + end + 2, 1, b, du);
+        if (st) return st;
+        st = drafter_ssm_scan(d, du, 1, 1, s_cur, 0, s_next);
+        if (st) return st;
+      }
+      st = drafter_codes(d, dtok + end + 2, dtok + end + 1, 1, b.feat, dcodes + (end + 1) * R, R, s_next);
       if (st) return st;
     }
   }
@@ -545,49 +786,71 @@ extern "C" int lng_drafter_trace(lng_drafter* d, const int64_t* tokens_host, int
                                  int32_t full, int64_t S, uint8_t* codes_out_host, int64_t* ids_host,
                                  float* logits_host) {
   LNG_REQUIRE(d, "NULL drafter");
-  LNG_REQUIRE(T >= 0 && S == d->V, "full-vocabulary trace: S must equal the vocabulary");
-  (void)full;
+  // the reference's column count: the whole vocabulary unless the shortlist applies (drafter.cpp:333-334)
+  const bool full_vocab = full || !d->has_sketch();
+  const int64_t S_ref = full_vocab ? d->V : d->cap;
+  LNG_REQUIRE(T >= 0 && S == S_ref, "trace: S must be the vocabulary (full or no sketch) or shortlist_cap");
   if (T == 0) return LNG_OK;
   LNG_REQUIRE(tokens_host, "NULL pointer");
   std::lock_guard<std::mutex> lk(d->mu);
   for (int64_t i = 0; i < T; ++i)
     if (tokens_host[i] < 0 || tokens_host[i] >= d->V) return fail(LNG_ERR_STATE, "token id out of range");
-  const int64_t R = d->R;
+  const int64_t R = d->R, N = d->N;
   ReadoutBufs b;
   void* extra = nullptr;
-  const size_t tok_b = al256(size_t(2 * T) * 8), code_b = al256(size_t(T * R)), lg_b = al256(size_t(T * d->V) * 4);
-  int st = drafter_ws(d, T, 1, &b, tok_b + code_b + lg_b, &extra);
+  const size_t tok_b = al256(size_t(2 * T) * 8), code_b = al256(size_t(T * R)), lg_b = al256(size_t(T * S) * 4),
+               li_b = full_vocab ? 0 : al256(size_t(T * S) * 8), ssm_b = al256(size_t(T * N) * 4);
+  int st = drafter_ws(d, T, 1, &b, tok_b + code_b + lg_b + li_b + 2 * ssm_b, &extra);
   if (st) return st;
   unsigned char* ex = static_cast<unsigned char*>(extra);
   int64_t* cur = reinterpret_cast<int64_t*>(ex);
   int64_t* prev = cur + T;
   uint8_t* dcodes = ex + tok_b;
   float* dlog = reinterpret_cast<float*>(ex + tok_b + code_b);
+  int64_t* dlist = full_vocab ? nullptr : reinterpret_cast<int64_t*>(ex + tok_b + code_b + lg_b);
+  float* du = reinterpret_cast<float*>(ex + tok_b + code_b + lg_b + li_b);
+  float* dstates = reinterpret_cast<float*>(ex + tok_b + code_b + lg_b + li_b + ssm_b);
   std::vector<int64_t> host(size_t(2 * T));
   for (int64_t i = 0; i < T; ++i) {
     host[size_t(i)] = tokens_host[i];
     host[size_t(T + i)] = i > 0 ? tokens_host[i - 1] : -1;
   }
   LNG_CUDA(cudaMemcpyAsync(cur, host.data(), size_t(2 * T) * 8, cudaMemcpyHostToDevice, d->stream));
+  if (N > 0) {  // SSM states from the empty state
+    st = drafter_ssm_inputs(d, cur, T, b, du);
+    if (st) return st;
+    st = drafter_ssm_scan(d, du, 1, T, nullptr, 0, dstates);
+    if (st) return st;
+  }
   if (codes_host) {
     std::vector<uint8_t> c(size_t(T * R));
     for (int64_t i = 0; i < T * R; ++i) c[size_t(i)] = uint8_t(codes_host[i]);
     LNG_CUDA(cudaMemcpyAsync(dcodes, c.data(), size_t(T * R), cudaMemcpyHostToDevice, d->stream));
     LNG_CUDA(cudaStreamSynchronize(d->stream));
   } else {
-    st = drafter_codes(d, cur, prev, T, b.feat, dcodes, R);
+    st = drafter_codes(d, cur, prev, T, b.feat, dcodes, R, N > 0 ? dstates : nullptr);
     if (st) return st;
   }
   CodeSource src{dcodes, 1, T, 0, R, nullptr, nullptr, nullptr, 0, T};
-  st = drafter_readout(d, cur, T, src, 1, b, dlog);
+  Scoring sc;
+  sc.full = full_vocab;
+  if (full_vocab) {
+    sc.full_logits = dlog;
+  } else {
+    sc.S = S;
+    sc.list_ids = dlist;
+    sc.list_lg = dlog;
+  }
+  st = drafter_readout(d, cur, T, src, 1, b, sc, N > 0 ? dstates : nullptr);
   if (st) return st;
   if (codes_out_host) LNG_CUDA(cudaMemcpyAsync(codes_out_host, dcodes, size_t(T * R), cudaMemcpyDeviceToHost, d->stream));
-  if (logits_host)
-    LNG_CUDA(cudaMemcpyAsync(logits_host, dlog, size_t(T * d->V) * 4, cudaMemcpyDeviceToHost, d->stream));
+  if (logits_host) LNG_CUDA(cudaMemcpyAsync(logits_host, dlog, size_t(T * S) * 4, cudaMemcpyDeviceToHost, d->stream));
+  if (ids_host && !full_vocab)
+    LNG_CUDA(cudaMemcpyAsync(ids_host, dlist, size_t(T * S) * 8, cudaMemcpyDeviceToHost, d->stream));
   LNG_CUDA(cudaStreamSynchronize(d->stream));
   const int derr = lng_device_error(1);
   if (derr) return fail(LNG_ERR_DEVICE, "device error " + std::to_string(derr) + " during trace");
-  if (ids_host)
+  if (ids_host && full_vocab)
     for (int64_t t = 0; t < T; ++t)
       for (int64_t v = 0; v < d->V; ++v) ids_host[t * d->V + v] = v;
   return LNG_OK;
@@ -600,25 +863,31 @@ extern "C" int lng_drafter_draft_batch(lng_drafter* d, const int64_t* prefix, in
   if (nseq == 0) return LNG_OK;
   LNG_REQUIRE(prefix && tokens_out, "NULL pointer");
   std::lock_guard<std::mutex> lk(d->mu);
-  const int64_t R = d->R, P = plen + gamma;  // positions per sequence in the working buffers
-  // The drafts' code windows reach back n_max - 1 positions from the last prefix token, and the
-  // embed2 router reads only a position's own and previous token (SSM routers are rejected at
-  // create), so only the last `tail` prefix positions need codes; earlier rows of `codes` are never
-  // read.
+  const int64_t R = d->R, N = d->N, P = plen + gamma;  // positions per sequence in the working buffers
+  // The drafts' code windows reach back n_max - 1 positions from the last prefix token and the embed2
+  // router reads a position's own and previous token (and, for SD-C, its SSM state), so only the last
+  // `tail` prefix positions need codes; earlier rows of `codes` are never read.  The SSM state itself
+  // runs over the whole prefix.
   int64_t n_max = 1;
   for (int o = 0; o < d->n_orders; ++o) n_max = std::max<int64_t>(n_max, d->orders[o]);
   const int64_t tail = std::min<int64_t>(plen, n_max);
   ReadoutBufs b;
   void* extra = nullptr;
   const size_t tok_b = al256(size_t(nseq * (P + 1)) * 8), prev_b = al256(size_t(nseq * std::max<int64_t>(2 * tail, 2)) * 8),
-               code_b = al256(size_t(nseq * P * R));
+               code_b = al256(size_t(nseq * P * R)), u_b = al256(size_t(N > 0 ? nseq * plen * N : 0) * 4),
+               st_b = al256(size_t(nseq * tail * N) * 4), cur_b = al256(size_t(2 * nseq * N) * 4);
   const int64_t M = nseq * tail;
-  int st = drafter_ws(d, M, 1, &b, tok_b + prev_b + code_b, &extra);
+  int st = drafter_ws(d, std::max<int64_t>(M, N > 0 ? std::min<int64_t>(nseq * plen, 8192) : M), 1, &b,
+                      tok_b + prev_b + code_b + u_b + st_b + cur_b, &extra);
   if (st) return st;
   unsigned char* ex = static_cast<unsigned char*>(extra);
   int64_t* toks = reinterpret_cast<int64_t*>(ex);  // [nseq, P + 1]: toks[s, 0] = -1, toks[s, 1 + p] = token p
   int64_t* scratch_i = reinterpret_cast<int64_t*>(ex + tok_b);  // [2, nseq * tail]: current, previous tokens
   uint8_t* codes = ex + tok_b + prev_b;             // [nseq, P, R]
+  float* u = reinterpret_cast<float*>(ex + tok_b + prev_b + code_b);                   // [nseq, plen, N]
+  float* tail_states = reinterpret_cast<float*>(ex + tok_b + prev_b + code_b + u_b);   // [nseq, tail, N]
+  float* s_cur = reinterpret_cast<float*>(ex + tok_b + prev_b + code_b + u_b + st_b);  // [nseq, N] x 2
+  float* s_next = s_cur + nseq * N;
   cudaStream_t us = reinterpret_cast<cudaStream_t>(stream);
   cudaEvent_t ev;
   LNG_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
@@ -628,9 +897,17 @@ extern "C" int lng_drafter_draft_batch(lng_drafter* d, const int64_t* prefix, in
   LNG_CUDA(cudaMemsetAsync(toks, 0xff, size_t(nseq * (P + 1)) * 8, d->stream));
   LNG_CUDA(cudaMemcpy2DAsync(toks + 1, size_t(P + 1) * 8, prefix, size_t(plen) * 8, size_t(plen) * 8, size_t(nseq),
                              cudaMemcpyDeviceToDevice, d->stream));
+  const int64_t p0 = plen - tail;
+  if (N > 0) {  // the SSM over every prefix token; the states of the last `tail` positions are kept
+    st = drafter_ssm_inputs(d, prefix, nseq * plen, b, u);
+    if (st) return st;
+    st = drafter_ssm_scan(d, u, nseq, plen, nullptr, p0, tail_states);
+    if (st) return st;
+    LNG_CUDA(cudaMemcpy2DAsync(s_cur, size_t(N) * 4, tail_states + (tail - 1) * N, size_t(tail * N) * 4,
+                               size_t(N) * 4, size_t(nseq), cudaMemcpyDeviceToDevice, d->stream));
+  }
   // tokens of the last `tail` prefix positions (dense [nseq, tail]) and their previous tokens
   // (toks[s, p] is the token before position p, -1 at p = 0)
-  const int64_t p0 = plen - tail;
   LNG_CUDA(cudaMemcpy2DAsync(scratch_i, size_t(tail) * 8, prefix + p0, size_t(plen) * 8, size_t(tail) * 8,
                              size_t(nseq), cudaMemcpyDeviceToDevice, d->stream));
   LNG_CUDA(cudaMemcpy2DAsync(scratch_i + nseq * tail, size_t(tail) * 8, toks + p0, size_t(P + 1) * 8,
@@ -638,9 +915,9 @@ extern "C" int lng_drafter_draft_batch(lng_drafter* d, const int64_t* prefix, in
   // their codes [nseq * tail, R] computed densely, then placed at rows p0 .. plen-1 with stride P * R
   uint8_t* dense = reinterpret_cast<uint8_t*>(b.u);  // reuse: nseq*tail*R bytes <= u's size (M = nseq*tail)
   const size_t dense_need = size_t(nseq * tail * R);
-  const size_t u_bytes = size_t(M) * d->qh * d->Dt * dtype_size(d->act);
+  const size_t u_bytes = size_t(b.rows) * d->qh * d->Dt * dtype_size(d->act);
   LNG_REQUIRE(dense_need <= u_bytes, "internal: code staging buffer too small");
-  st = drafter_codes(d, scratch_i, scratch_i + nseq * tail, nseq * tail, b.feat, dense, R);
+  st = drafter_codes(d, scratch_i, scratch_i + nseq * tail, nseq * tail, b.feat, dense, R, N > 0 ? tail_states : nullptr);
   if (st) return st;
   LNG_CUDA(cudaMemcpy2DAsync(codes + p0 * R, size_t(P * R), dense, size_t(tail * R), size_t(tail * R), size_t(nseq),
                              cudaMemcpyDeviceToDevice, d->stream));
@@ -650,19 +927,30 @@ extern "C" int lng_drafter_draft_batch(lng_drafter* d, const int64_t* prefix, in
     copy_i64_kernel<<<unsigned(ceil_div(nseq, 128)), 128, 0, d->stream>>>(toks + 1 + tpos, scratch_i, nseq, P + 1, 1);
     LNG_LAUNCHED("copy_i64_kernel");
     CodeSource src{codes, nseq, tpos + 1, 0, R, nullptr, nullptr, nullptr, tpos, P};
-    st = drafter_readout(d, scratch_i, nseq, src, 1, b, nullptr);
+    st = drafter_readout(d, scratch_i, nseq, src, 1, b, Scoring{}, N > 0 ? s_cur : nullptr);
     if (st) return st;
     // next tokens -> toks[s, 2 + tpos] and tokens_out[s, g]
     store_draft_kernel<<<unsigned(ceil_div(nseq, 128)), 128, 0, d->stream>>>(b.ids, nseq, toks + 2 + tpos, P + 1,
                                                                              tokens_out + g, gamma);
     LNG_LAUNCHED("store_draft_kernel");
     if (g + 1 < gamma) {
-      // codes of the drafted tokens at position tpos + 1 (strided rows of the code buffer); their
-      // previous tokens are this step's current tokens, still in scratch_i
-      st = lng_embed2_features(b.ids, scratch_i, nseq, d->E, d->e_dtype, d->V, d->d, d->prev_norm,
-                               d->cur_norm, d->start, d->router_eps, b.feat, reinterpret_cast<lng_stream_t>(d->stream));
+      // the drafted tokens' SSM states and their codes at position tpos + 1 (strided rows of the code
+      // buffer); their previous tokens are this step's current tokens, still in scratch_i
+      if (N > 0) {
+        st = drafter_ssm_inputs(d, b.ids, nseq, b, u);
+        if (st) return st;
+        st = drafter_ssm_scan(d, u, nseq, 1, s_cur, 0, s_next);
+        if (st) return st;
+        std::swap(s_cur, s_next);
+      }
+      st = embed2_features(b.ids, scratch_i, nseq, d->E, d->e_dtype, d->V, d->d, d->prev_norm, d->cur_norm, d->start,
+                           d->router_eps, b.feat, d->F, d->stream);
       if (st) return st;
-      st = route_codes_presplit(b.feat, nseq, 2 * d->d, d->router_w, d->router_w_split, R, int32_t(d->bits), dense,
+      if (d->router_ssm) {
+        copy_cols_kernel<<<grid_for(nseq * N, 256, 8), 256, 0, d->stream>>>(s_cur, nseq, N, b.feat, d->F, 2 * d->d);
+        LNG_LAUNCHED("copy_cols_kernel");
+      }
+      st = route_codes_presplit(b.feat, nseq, d->F, d->router_w, d->router_w_split, R, int32_t(d->bits), dense,
                                 d->stream);
       if (st) return st;
       LNG_CUDA(cudaMemcpy2DAsync(codes + (tpos + 1) * R, size_t(P * R), dense, size_t(R), size_t(R), size_t(nseq),

@@ -17,6 +17,7 @@
 #include "router.cuh"
 #include "rowops.cuh"
 #include "topk.cuh"
+#include "drafter_ext.cuh"
 
 static int scratch_alloc(void** p, size_t bytes, cudaStream_t stream);
 
@@ -335,31 +336,40 @@ extern "C" int lng_route_codes_split(const void* x_bf16, int64_t n, int64_t in_d
   return st;
 }
 
-extern "C" int lng_embed2_features(const int64_t* cur, const int64_t* prev, int64_t n, const void* embedding,
-                                   int32_t e_dtype, int64_t vocab, int64_t d, const float* prev_w, const float* cur_w,
-                                   const float* start, float eps, float* out, lng_stream_t stream) {
+namespace lng {
+// embed2 features into rows of stride out_stride (the drafter appends its SSM state after them)
+static int embed2_features(const int64_t* cur, const int64_t* prev, int64_t n, const void* embedding, int32_t e_dtype,
+                           int64_t vocab, int64_t d, const float* prev_w, const float* cur_w, const float* start,
+                           float eps, float* out, int64_t out_stride, cudaStream_t stream) {
   LNG_REQUIRE(n >= 0 && vocab > 0 && d > 0, "bad shape");
   if (n == 0) return LNG_OK;
   LNG_REQUIRE(cur && embedding && prev_w && cur_w && start && out, "NULL pointer");
   const int g = int(n < (int64_t(1) << 20) ? n : (int64_t(1) << 20));
   switch (e_dtype) {
     case LNG_F32:
-      embed2_features_kernel<float><<<g, 128, 0, S(stream)>>>(cur, prev, n, static_cast<const float*>(embedding), vocab,
-                                                               d, prev_w, cur_w, start, eps, out);
+      embed2_features_kernel<float><<<g, 128, 0, stream>>>(cur, prev, n, static_cast<const float*>(embedding), vocab,
+                                                               d, prev_w, cur_w, start, eps, out, out_stride);
       break;
     case LNG_BF16:
-      embed2_features_kernel<__nv_bfloat16><<<g, 128, 0, S(stream)>>>(
-          cur, prev, n, static_cast<const __nv_bfloat16*>(embedding), vocab, d, prev_w, cur_w, start, eps, out);
+      embed2_features_kernel<__nv_bfloat16><<<g, 128, 0, stream>>>(
+          cur, prev, n, static_cast<const __nv_bfloat16*>(embedding), vocab, d, prev_w, cur_w, start, eps, out, out_stride);
       break;
     case LNG_F16:
-      embed2_features_kernel<__half><<<g, 128, 0, S(stream)>>>(cur, prev, n, static_cast<const __half*>(embedding),
-                                                                vocab, d, prev_w, cur_w, start, eps, out);
+      embed2_features_kernel<__half><<<g, 128, 0, stream>>>(cur, prev, n, static_cast<const __half*>(embedding),
+                                                                vocab, d, prev_w, cur_w, start, eps, out, out_stride);
       break;
     default:
       return fail(LNG_ERR_ARGUMENT, "embedding dtype must be f32, bf16 or f16");
   }
   LNG_LAUNCHED("embed2_features_kernel");
   return LNG_OK;
+}
+}  // namespace lng
+
+extern "C" int lng_embed2_features(const int64_t* cur, const int64_t* prev, int64_t n, const void* embedding,
+                                   int32_t e_dtype, int64_t vocab, int64_t d, const float* prev_w, const float* cur_w,
+                                   const float* start, float eps, float* out, lng_stream_t stream) {
+  return embed2_features(cur, prev, n, embedding, e_dtype, vocab, d, prev_w, cur_w, start, eps, out, 2 * d, S(stream));
 }
 
 // ====================================================================== lookup

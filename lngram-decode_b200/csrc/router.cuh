@@ -194,7 +194,8 @@ __global__ void __cluster_dims__(RS_SPLIT, 1, 1) __launch_bounds__(256)
 }
 
 // embed2 router features (ffnmem/memory/router.py:50-69): one 128-thread CTA per item, the
-// previous and current token rows each RMS-normalised with their own weight.
+// previous and current token rows each RMS-normalised with their own weight, written to the first
+// 2d columns of the item's output row (row stride out_stride >= 2d).
 template <typename ET>
 __global__ void __launch_bounds__(128) embed2_features_kernel(const int64_t* __restrict__ cur,
                                                               const int64_t* __restrict__ prev, int64_t n,
@@ -202,7 +203,7 @@ __global__ void __launch_bounds__(128) embed2_features_kernel(const int64_t* __r
                                                               const float* __restrict__ prev_w,
                                                               const float* __restrict__ cur_w,
                                                               const float* __restrict__ start, float eps,
-                                                              float* __restrict__ out) {
+                                                              float* __restrict__ out, int64_t out_stride) {
   __shared__ float red[2][4];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (int64_t item = blockIdx.x; item < n; item += gridDim.x) {
@@ -212,7 +213,7 @@ __global__ void __launch_bounds__(128) embed2_features_kernel(const int64_t* __r
       if (threadIdx.x == 0) atomicCAS(&g_error_word, 0u, (unsigned int)DEV_ERR_TOKEN_RANGE);
       continue;
     }
-    float* o = out + item * 2 * d;
+    float* o = out + item * out_stride;
     float ss[2] = {0.f, 0.f};
 #pragma unroll
     for (int part = 0; part < 2; ++part) {

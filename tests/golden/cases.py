@@ -132,6 +132,12 @@ DRAFT_CASES = {
     # Reference-sized tiny drafter (configs/tiny_cpu_sd.yaml with embed2): orders (2, 3), fp16 tables.
     "tiny": dict(d=64, vocab=256, routes=4, bits=4, ngrams=(2, 3), mem_dim=16, kv_heads=2, head_dim=16,
                  q_heads=2, table_dtype="fp16", bf16=False, w_o_std=0.2),
+    # SD-C: the tiny drafter with a 16-state diagonal SSM read by the router and the query.
+    "tiny_ssm": dict(d=64, vocab=256, routes=4, bits=4, ngrams=(2, 3), mem_dim=16, kv_heads=2, head_dim=16,
+                     q_heads=2, table_dtype="fp16", bf16=False, w_o_std=0.2, ssm=16),
+    # SD-C at the SD-B width (bf16-valued data): 64 states, router and query reading them.
+    "sdb_ssm": dict(d=1024, vocab=32000, routes=182, bits=4, ngrams=(3,), mem_dim=136, kv_heads=4, head_dim=64,
+                    q_heads=4, table_dtype="fp32", bf16=True, w_o_std=0.02, ssm=64),
 }
 
 
@@ -149,7 +155,8 @@ def draft_bundle(case: str) -> tuple[dict, dict]:
         a[f"table_{n}"] = rnd(_normal(2, (r * (1 << bits) ** n, md), 0.02, 10 + i)).astype(tdt)
     a["mem_norm"] = rnd(1.0 + _normal(5, (dt,), 0.1, 10))
     a["kv_proj"] = rnd(_normal(4, (2 * kv * hd, dt), 0.02, 10))
-    a["router"] = _normal(3, (r * bits, 2 * d), 0.02, 10)
+    n_ssm = int(c.get("ssm", 0))
+    a["router"] = _normal(3, (r * bits, 2 * d + n_ssm), 0.02, 10)
     a["router_prev_norm"] = rnd(1.0 + _normal(5, (d,), 0.1, 11))
     a["router_cur_norm"] = rnd(1.0 + _normal(5, (d,), 0.1, 12))
     a["router_start"] = rnd(_normal(5, (d,), 0.02, 13))
@@ -157,10 +164,18 @@ def draft_bundle(case: str) -> tuple[dict, dict]:
     a["w_q"] = rnd(_normal(4, (qh * hd, d), 0.02, 11))
     a["w_o"] = rnd(_normal(4, (d, qh * hd), c["w_o_std"], 12))
     a["out_norm"] = rnd(1.0 + _normal(5, (d,), 0.1, 15))
+    if n_ssm:
+        # ffnmem/memory/ssm.py:23-35: W_in N(0, 0.02), decays geometrically spaced in 1 - a between
+        # 0.5 and 0.001; the bundle stores a = sigmoid(theta) (drafting/export_drafter.py:30)
+        a["ssm_norm"] = rnd(1.0 + _normal(5, (d,), 0.1, 16))
+        a["ssm_w_in"] = rnd(_normal(4, (n_ssm, d), 0.02 if d > 64 else 0.2, 13))
+        one_minus = np.exp(np.linspace(math.log(0.5), math.log(0.001), n_ssm)).astype(F32)
+        a["ssm_decay"] = (F32(1.0) - one_minus).astype(F32)
+        a["w_sq"] = rnd(_normal(4, (qh * hd, n_ssm), 0.02 if d > 64 else 0.2, 14))
     eps = 1e-5
-    config = dict(kind="sd_b", router_kind="embed2", d_model=d, vocab=v, routes=r, bits=bits,
-                  ngrams=list(c["ngrams"]), mem_dim=md, kv_heads=kv, head_dim=hd, q_heads=qh, ssm_dim=0,
-                  query_ssm=False, norm_eps=eps, ssm_eps=eps, router_eps=eps, draft_eps=eps, mem_eps=eps,
+    config = dict(kind="sd_c" if n_ssm else "sd_b", router_kind="embed2_ssm" if n_ssm else "embed2", d_model=d,
+                  vocab=v, routes=r, bits=bits, ngrams=list(c["ngrams"]), mem_dim=md, kv_heads=kv, head_dim=hd,
+                  q_heads=qh, ssm_dim=n_ssm, query_ssm=bool(n_ssm), norm_eps=eps, ssm_eps=eps, router_eps=eps, draft_eps=eps, mem_eps=eps,
                   softmax_scale=hd ** -0.5, sink_logit=math.log(r * 0.5 / 0.5), sketch_k=0, shortlist_cap=0,
                   table_dtype=c["table_dtype"], layer=1, groups=qh // kv, route_token_dim=dt)
     return config, a

@@ -37,10 +37,14 @@ def test_rms_norm_rounds_before_the_weight(lngram, xdt, wdt, d):
     want = _reference_norm(x, w, 1e-5)
     got = lngram.rms_norm(x.to(DEV), w.to(DEV), 1e-5).cpu()
     assert got.dtype == want.dtype == torch.promote_types(xdt, wdt)
-    exact = (got == want).float().mean().item()
-    assert exact >= 0.99, exact
-    # elsewhere off by at most one unit in the last place of the intermediate (x's dtype) rounding
-    ulp = (torch.finfo(xdt).eps + torch.finfo(want.dtype).eps) * want.float().abs()
+    if xdt == torch.bfloat16:
+        # the bf16 rounding of the normalised row absorbs the last-bit differences of 1/rms (the sum
+        # order of the mean differs from torch's), so nearly every element is bit-identical
+        exact = (got == want).float().mean().item()
+        assert exact >= 0.99, exact
+    # elsewhere off by at most one unit in the last place of the intermediate (x's dtype) rounding,
+    # plus a few fp32 units for 1/rms
+    ulp = (torch.finfo(xdt).eps + 4 * torch.finfo(torch.float32).eps) * want.float().abs()
     assert ((got.float() - want.float()).abs() <= 1.01 * ulp).all()
     if xdt == torch.bfloat16 and wdt == torch.float32:
         # the rule matters: without the intermediate rounding most values differ

@@ -105,3 +105,43 @@ def test_reference_cpp_drafter_agrees_with_oracle_shortlist(reference_path):
     assert a.tokens == b.tokens
     np.testing.assert_array_equal(a.topk_ids, b.topk_ids)
     np.testing.assert_array_equal(a.codes, b.codes)
+
+
+@pytest.mark.parametrize("sketch", [False, True])
+def test_reference_drafters_agree_with_oracle_ssm(reference_path, sketch):
+    """SD-C bundles (the SSM read by the router and the query), with and without a sketch shortlist:
+    the reference's RefDrafter and its C++ drafter against the oracle drafter."""
+    from oracle.build import build_reference_drafter, load_reference_drafter
+
+    build_reference_drafter(reference_path)
+    ext = load_reference_drafter()
+    if ext is None:
+        pytest.skip("reference C++ drafter not built")
+    import drafting.cpu_drafter as cd
+    from drafting.export_drafter import Bundle
+
+    cd._EXT = ext
+    config, arrays = cases.draft_bundle("tiny_ssm")
+    if sketch:
+        config = dict(config, sketch_k=4, shortlist_cap=16)
+        arrays = dict(arrays, **cases.random_sketch(config, cap=16))
+    toks = cases.draft_tokens("tiny_ssm", 60, seed=8)
+    ref = cd.RefDrafter(Bundle(config, arrays, {}))
+    cpp = cd.CppDrafter(Bundle(config, arrays, {}), threads=2)
+    ora = OracleDrafter(config, arrays)
+    c_ref, i_ref, l_ref = ref.trace(toks)
+    c_o, i_o, l_o = ora.trace(toks)
+    np.testing.assert_array_equal(c_o, c_ref)
+    np.testing.assert_array_equal(i_o, i_ref)
+    fin = np.isfinite(l_ref)
+    np.testing.assert_array_equal(fin, np.isfinite(l_o))
+    np.testing.assert_allclose(l_o[fin], l_ref[fin], rtol=1e-5, atol=1e-5)
+    _, i_c, l_c = cpp.trace(toks, codes=c_ref)
+    np.testing.assert_array_equal(i_c, i_o)
+    np.testing.assert_allclose(l_c[fin], l_o[fin], atol=1e-4)
+    for d in (cpp, ora):
+        d.commit(toks[:25])
+    a, b = cpp.draft(4, hyp=toks[25:28], last_codes=True), ora.draft(4, hyp=toks[25:28], last_codes=True)
+    assert a.tokens == b.tokens
+    np.testing.assert_array_equal(a.topk_ids, b.topk_ids)
+    np.testing.assert_array_equal(a.codes, b.codes)

@@ -123,12 +123,65 @@ int lng_lookup_route_chunk(const lng_tables* tables, const void* codes, int32_t 
                            const uint8_t* valid_tokens, int64_t target_length, void* out, int32_t out_dtype,
                            lng_stream_t stream);
 
+/* Backward of the training-mode lookup (_lookup_route_chunk with the q surrogate, lngram_v2.py:1047-1113,
+ * :326-447) for codes [B, T, num_routes] and the route chunk [route_start, route_end), given the route
+ * tokens' gradient grad_tokens [B, T, route_end - route_start, Dt] (f32 / bf16 / f16):
+ *   grad_tables[o] (fp32 [rows, memory_dim] per order, accumulated; the array or an entry may be NULL):
+ *     the gathered rows' gradient of every valid window (the nn.Embedding backward);
+ *   grad_q (fp32 [B, T, route_end - route_start, bits], written; NULL = none): the surrogate gradient of
+ *     _LngramSurrogate.backward for q_logits [B, T, q_routes, bits] (fp32) -- exact == 0: one-bit
+ *     counterfactuals (order x bits extra row gathers per window) times scale T p (1 - p), p =
+ *     sigmoid(T q); exact != 0: the expectation over the whole alphabet per digit.  Zero when
+ *     temperature or scale is 0.
+ * The masks of lng_lookup_route_chunk apply (segment_ids, valid_tokens may be NULL).  memory_dim <= 256;
+ * bits <= 8 for the surrogate. */
+int lng_lookup_backward(const lng_tables* tables, const void* codes, int32_t codes_dtype, int64_t B, int64_t T,
+                        int64_t route_start, int64_t route_end, const int64_t* segment_ids, const uint8_t* valid_tokens,
+                        const void* grad_tokens, int32_t grad_dtype, const float* q_logits, int64_t q_routes,
+                        float temperature, float scale, int32_t exact, float* grad_q, float* const* grad_tables,
+                        lng_stream_t stream);
+
 /* Route tokens [M, num_routes, Dt] of the n-grams ending at the LAST slot of explicit code windows
  * codes [M, W, num_routes] (u8 or i32; W >= max order) with per-slot segment ids seg [M, W] (i32,
  * NULL = all one segment): order n is valid iff seg[W-n] == seg[W-1].  This is the windowed lookup
  * of lookup_rows_at (ffnmem/memory/draft.py:26-47) and tree_route_tokens (drafting/tree.py:130-136). */
 int lng_lookup_windows(const lng_tables* tables, const void* codes, int32_t codes_dtype, int64_t M, int64_t W,
                        const int32_t* seg, void* out, int32_t out_dtype, lng_stream_t stream);
+
+/* ------------------------------------------------------------------ host-RAM serving, incremental state */
+
+/* Route tokens [B, n, R, Dt] of the last n positions of codes [B, T, R] (T = h + n: h history codes, then
+ * the n new ones) from tables in the SERVING layout (serving/layout.py:1-18: row r*A^n + sum_k c[t-k] A^k,
+ * the newest code least significant; made by lng_serving_permute).  The tables may live in pinned host
+ * memory mapped for the device (lng_host_map): each row is read across PCIe once with 16-byte loads, no
+ * staging copy -- the zero-copy transfer mode serving/prefetch.py:579-586 leaves unimplemented, a
+ * decode_step row_provider for tables larger than HBM (ffnmem/infer.py:238-240).  Windows that start before
+ * position 0 of the context read zero rows (serving/prefetch.py:186-202).  out: the table dtype;
+ * 16-byte rows. */
+int lng_lookup_serving_rows(const lng_tables* tables, const void* codes, int32_t codes_dtype, int64_t B, int64_t T,
+                            int64_t n, void* out, lng_stream_t stream);
+
+/* The serving-layout copy of one order's v2 table (serving/layout.py:26-43, permute_table): within every
+ * route's block of A^order rows, dst row j = src row reverse_digits(j).  src / dst: any memory the device
+ * can read / write (device, or mapped host); distinct; 16-byte rows. */
+int lng_serving_permute(const void* src, void* dst, int32_t dtype, int64_t routes, int32_t order, int32_t bits,
+                        int64_t mem_dim, lng_stream_t stream);
+
+/* The device address of host memory [host, host + bytes): page-locked memory is used as it is; pageable
+ * memory is pinned and mapped first (cudaHostRegister) and lng_host_unmap releases it.  No reference
+ * counterpart (the reference leaves the zero-copy mode unimplemented, serving/prefetch.py:579-586). */
+int lng_host_map(void* host, size_t bytes, void** device_ptr);
+int lng_host_unmap(void* host);
+
+/* The packed n-gram suffix state of RouteNgramMemoryV2.forward_incremental (lngram_v2.py:1714-1760):
+ * packed [B, R] int32 holds the codes of the last maxn positions, the newest in digit maxn - 1.  With
+ * packed_in == NULL: _pack_suffix of the last min(T, maxn) positions of codes [B, T, R]; otherwise
+ * _advance_packed: packed_in shifted down one digit, codes [B, 1, R] in the top digit.  window_out
+ * (optional, u8 [B, maxn, R]) receives the digits unpacked (slot j = digit j, oldest first), the code
+ * windows of lng_route_attend's window mode.  maxn * bits <= 31. */
+int lng_packed_suffix(const void* codes, int32_t codes_dtype, int64_t B, int64_t T, int64_t R, int32_t bits,
+                      int32_t maxn, const int32_t* packed_in, int32_t* packed_out, uint8_t* window_out,
+                      lng_stream_t stream);
 
 /* ------------------------------------------------------------------ readout (a7 - a11) */
 
@@ -192,6 +245,15 @@ int lng_route_attend(const lng_tables* tables, const void* codes, int32_t codes_
                      float sink_logit,
                      const void* qa, const float* qscale, void* u, int32_t u_dtype, int32_t partial, float* m_out,
                      float* l_out, lng_stream_t stream);
+
+/* lng_route_attend (normalised output) over route tokens the CALLER supplies instead of table rows:
+ * tokens [M, routes, Dt] (f32 / bf16 / f16; zero rows where an n-gram is not valid, as
+ * _lookup_route_chunk gives them).  This is the readout of memory_step(..., route_tokens=)
+ * (ffnmem/infer.py:168-173): the rows a decode_step row_provider returns (infer.py:238-240), e.g. from
+ * host-RAM tables, skip the table lookup.  qa, qscale, u and u_dtype as for lng_route_attend. */
+int lng_route_attend_rows(const void* tokens, int32_t tok_dtype, int64_t M, int64_t routes, int64_t Dt,
+                          int32_t num_heads, float eps, float sink_logit, const void* qa, const float* qscale, void* u,
+                          int32_t u_dtype, lng_stream_t stream);
 
 /* Sink attention with explicit keys and values, the reference's _manual_gqa
  * (lngram_v2.py:1877-1920): q [M, KV*G, HD], k / v [M, KV, R, HD] (dtype f32/bf16/f16), scores

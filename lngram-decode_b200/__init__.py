@@ -9,14 +9,14 @@ behind the C ABI of ``include/lngram_b200.h``.  There is no CPU fallback.
 from . import _lib
 from .bundle import Bundle, load_bundle, read_header, write_bundle
 from .drafter import DraftOut, Drafter, GpuDrafter, make_drafter
-from .memory import LngramMemory, RouteNgramMemoryV2, rms_norm
+from .memory import LngramIncrementalState, LngramMemory, RouteNgramMemoryV2, rms_norm
 
-__all__ = ["Bundle", "DraftOut", "Drafter", "GpuDrafter", "LngramMemory", "RouteNgramMemoryV2", "_lib", "load_bundle",
+__all__ = ["Bundle", "DraftOut", "Drafter", "GpuDrafter", "LngramIncrementalState", "LngramMemory", "RouteNgramMemoryV2", "_lib", "load_bundle",
            "make_drafter", "read_header", "rms_norm", "write_bundle"]
-from .seams import MemoryCache, ancestor_table, memory_step, tree_memory_block, tree_ngram_codes, tree_slots  # noqa: E402
+from .seams import MemoryCache, ancestor_table, decode_memory_step, memory_step, tree_memory_block, tree_ngram_codes, tree_slots  # noqa: E402
 
-__all__ += ["MemoryCache", "ancestor_table", "memory_step", "tree_memory_block", "tree_ngram_codes", "tree_slots"]
-from . import sharded  # noqa: E402
+__all__ += ["MemoryCache", "ancestor_table", "decode_memory_step", "memory_step", "tree_memory_block", "tree_ngram_codes", "tree_slots"]
+from . import serving, sharded  # noqa: E402
 from .sharded import RouteShardedMemory  # noqa: E402
 
-__all__ += ["RouteShardedMemory", "sharded"]
+__all__ += ["RouteShardedMemory", "serving", "sharded"]

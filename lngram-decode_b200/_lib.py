@@ -76,10 +76,18 @@ SIGNATURES = {
     "lng_embed2_features": (C.c_int, [P, P, i64, P, i32, i64, i64, P, P, P, f32, P, P]),
     "lng_table_row_ss": (C.c_int, [PT, C.POINTER(C.c_void_p), P]),
     "lng_lookup_route_chunk": (C.c_int, [PT, P, i32, i64, i64, i64, i64, P, P, i64, P, i32, P]),
+    "lng_lookup_backward": (C.c_int, [PT, P, i32, i64, i64, i64, i64, P, P, P, i32, P, i64, f32, f32, i32, P,
+                                      C.POINTER(C.c_void_p), P]),
     "lng_lookup_windows": (C.c_int, [PT, P, i32, i64, i64, P, P, i32, P]),
+    "lng_lookup_serving_rows": (C.c_int, [PT, P, i32, i64, i64, i64, P, P]),
+    "lng_serving_permute": (C.c_int, [P, P, i32, i64, i32, i32, i64, P]),
+    "lng_host_map": (C.c_int, [P, sz, C.POINTER(P)]),
+    "lng_host_unmap": (C.c_int, [P]),
+    "lng_packed_suffix": (C.c_int, [P, i32, i64, i64, i64, i32, i32, P, P, P, P]),
     "lng_fold_readout": (C.c_int, [i64, i64, i32, i32, i32, P, P, P, P, P, P, P, i32, P]),
     "lng_route_attend": (C.c_int, [PT, P, i32, i64, i64, i64, P, P, P, i64, i64, i64, i32, f32, f32, P, P, P, i32, i32,
                                    P, P, P]),
+    "lng_route_attend_rows": (C.c_int, [P, i32, i64, i64, i64, i32, f32, f32, P, P, P, i32, P]),
     "lng_sink_gqa": (C.c_int, [P, P, P, i32, i64, i32, i32, i64, i32, f32, P, P]),
     "lng_gemm": (C.c_int, [P, i32, i64, P, i32, i64, P, i32, i64, i64, i64, i64, P, i32, P]),
     "lng_rms_rows": (C.c_int, [P, i32, i64, i64, f32, P, P]),

@@ -38,6 +38,10 @@ struct CodeSource {
   const int32_t* seg;          // window mode, [M, W] or null
   int64_t t_offset;      // sequence mode: item t is absolute position t + t_offset (target_length)
   int64_t bstride;       // sequence mode: positions between consecutive batch rows (>= T)
+  int64_t direct;        // > 0: rows mode -- item i, route r reads row i * direct + r of table 0 (the
+                         // caller's route tokens), always valid; codes, windows and masks are unused
+  int serving;           // 1: the serving table layout (the newest code least significant,
+                         // serving/layout.py:1-18) instead of the v2 layout (the oldest least significant)
 };
 
 // ---- pipelined form used by the gather kernels: an item's geometry once, then per-route codes.
@@ -52,6 +56,12 @@ struct ItemGeo {
 __device__ __forceinline__ ItemGeo item_geometry(const CodeSource& s, const int* orders, int n_orders, int64_t item) {
   ItemGeo g;
   g.omask = 0;
+  if (s.direct > 0) {
+    g.cur = item;
+    g.avail = 1;
+    g.omask = 1u;
+    return g;
+  }
   if (s.window > 0) {
     const int64_t W = s.window;
     g.cur = item * W + W - 1;
@@ -86,8 +96,9 @@ template <typename CodeT>
 __device__ __forceinline__ void load_window_codes(const CodeSource& s, const ItemGeo& g, int64_t r, bool route_ok,
                                                   int32_t (&c)[MAXW]) {
   const CodeT* codes = static_cast<const CodeT*>(s.codes);
+  const bool read = route_ok && s.direct == 0;
 #pragma unroll
-  for (int k = 0; k < MAXW; ++k) c[k] = (route_ok && k < g.avail) ? int32_t(codes[(g.cur - k) * s.R + r]) : 0;
+  for (int k = 0; k < MAXW; ++k) c[k] = (read && k < g.avail) ? int32_t(codes[(g.cur - k) * s.R + r]) : 0;
 }
 
 // Table row of order n for window codes c (oldest code least significant), or -1.
@@ -119,6 +130,7 @@ __device__ __forceinline__ int64_t read_code(const CodeSource& s, int64_t pos_ro
 // In sequence mode `item` indexes [B, T_out] with T_out = T - t_offset.
 template <typename CodeT>
 __device__ __forceinline__ int64_t ngram_row(const CodeSource& s, int64_t item, int64_t r, int order, int bits) {
+  if (s.direct > 0) return item * s.direct + r;
   int64_t base;  // codes row of the window's first slot
   if (s.window > 0) {
     const int64_t W = s.window;
@@ -146,7 +158,7 @@ __device__ __forceinline__ int64_t ngram_row(const CodeSource& s, int64_t item, 
       atomicCAS(&g_error_word, 0u, (unsigned int)DEV_ERR_CODE_RANGE);
       return -1;
     }
-    addr |= c << (k * bits);
+    addr |= c << ((s.serving ? order - 1 - k : k) * bits);
   }
   return r * (int64_t(1) << (bits * order)) + addr;
 }

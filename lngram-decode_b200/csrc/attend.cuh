@@ -315,7 +315,9 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
 #pragma unroll
     for (int o = 0; o < LNG_MAX_ORDERS; ++o) {
       if (o >= p.ts.n_orders) break;
-      rows[o] = window_row(pend_c, p.ts.order[o], p.ts.bits, r, r < p.route_end && ((pend_geo.omask >> o) & 1u));
+      rows[o] = p.src.direct > 0 ? (r < p.route_end ? pend_item * p.src.direct + r : -1)
+                                 : window_row(pend_c, p.ts.order[o], p.ts.bits, r,
+                                              r < p.route_end && ((pend_geo.omask >> o) & 1u));
       ss_pend[o] = 0.f;
       if (rows[o] >= 0) {
         if (bulk_lane) bytes += uint32_t(mem_dim * 2);

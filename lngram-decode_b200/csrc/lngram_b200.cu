@@ -18,6 +18,7 @@
 #include "rowops.cuh"
 #include "topk.cuh"
 #include "drafter_ext.cuh"
+#include "surrogate.cuh"
 
 static int scratch_alloc(void** p, size_t bytes, cudaStream_t stream);
 
@@ -463,6 +464,157 @@ extern "C" int lng_lookup_windows(const lng_tables* tables, const void* codes, i
   return launch_lookup<int32_t>(tables, src, M, 0, tables->num_routes, out, out_dtype, S(stream));
 }
 
+// ====================================================================== training-mode lookup backward
+extern "C" int lng_lookup_backward(const lng_tables* tables, const void* codes, int32_t codes_dtype, int64_t B,
+                                   int64_t T, int64_t route_start, int64_t route_end, const int64_t* segment_ids,
+                                   const uint8_t* valid_tokens, const void* grad_tokens, int32_t grad_dtype,
+                                   const float* q_logits, int64_t q_routes, float temperature, float scale,
+                                   int32_t exact, float* grad_q, float* const* grad_tables, lng_stream_t stream) {
+  int st = check_tables(tables);
+  if (st) return st;
+  LNG_REQUIRE(codes_dtype == LNG_U8 || codes_dtype == LNG_I32, "codes dtype must be u8 or i32");
+  LNG_REQUIRE(B >= 0 && T >= 0 && 0 <= route_start && route_start < route_end && route_end <= tables->num_routes,
+              "bad shape or route range");
+  LNG_REQUIRE(grad_dtype == LNG_F32 || grad_dtype == LNG_BF16 || grad_dtype == LNG_F16, "grad dtype must be float");
+  LNG_REQUIRE(tables->memory_dim <= 32 * SG_MAXE, "memory_dim must be <= 256 for the backward");
+  LNG_REQUIRE(!grad_q || (q_logits && q_routes >= route_end && tables->bits <= SG_MAXBITS),
+              "the surrogate needs q_logits over the chunk's routes and bits <= 8");
+  if (B == 0 || T == 0) return LNG_OK;
+  LNG_REQUIRE(codes && grad_tokens, "NULL pointer");
+  LookupGradParams p{};
+  p.ts = table_set(tables);
+  p.table_dtype = tables->table_dtype;
+  p.src = CodeSource{codes, B, T, 0, tables->num_routes, segment_ids, valid_tokens, nullptr, 0, T, 0, 0};
+  p.B = B;
+  p.T = T;
+  p.route_start = route_start;
+  p.Rc = route_end - route_start;
+  p.grad = grad_tokens;
+  p.grad_dtype = grad_dtype;
+  p.q = q_logits;
+  p.Rq = q_routes;
+  p.temperature = temperature;
+  p.scale = scale;
+  p.exact = exact != 0;
+  p.grad_q = grad_q;
+  bool any_tab = false;
+  for (int o = 0; o < tables->n_orders; ++o) {
+    p.gtab[o] = grad_tables ? grad_tables[o] : nullptr;
+    any_tab = any_tab || p.gtab[o];
+  }
+  const int64_t warps = B * T * p.Rc;
+  if (grad_q) {
+    if (temperature == 0.f || scale == 0.f) {
+      LNG_CUDA(cudaMemsetAsync(grad_q, 0, size_t(warps * tables->bits) * 4, S(stream)));
+    } else {
+      const int g = grid_for(warps * 32, 256, 16);
+      if (codes_dtype == LNG_U8) surrogate_grad_kernel<uint8_t><<<g, 256, 0, S(stream)>>>(p);
+      else surrogate_grad_kernel<int32_t><<<g, 256, 0, S(stream)>>>(p);
+      LNG_LAUNCHED("surrogate_grad_kernel");
+    }
+  }
+  if (any_tab) {
+    const int g = grid_for(warps * tables->n_orders * 32, 256, 16);
+    if (codes_dtype == LNG_U8) table_grad_kernel<uint8_t><<<g, 256, 0, S(stream)>>>(p);
+    else table_grad_kernel<int32_t><<<g, 256, 0, S(stream)>>>(p);
+    LNG_LAUNCHED("table_grad_kernel");
+  }
+  return LNG_OK;
+}
+
+// ====================================================================== host-RAM serving and incremental state
+extern "C" int lng_lookup_serving_rows(const lng_tables* tables, const void* codes, int32_t codes_dtype, int64_t B,
+                                       int64_t T, int64_t n, void* out, lng_stream_t stream) {
+  int st = check_tables(tables);
+  if (st) return st;
+  LNG_REQUIRE(codes_dtype == LNG_U8 || codes_dtype == LNG_I32, "codes dtype must be u8 or i32");
+  LNG_REQUIRE(B >= 0 && T >= 1 && n >= 1 && n <= T, "need 1 <= n <= T");
+  if (B == 0) return LNG_OK;
+  LNG_REQUIRE(codes && out, "NULL pointer");
+  const int es = dtype_size(tables->table_dtype);
+  LNG_REQUIRE((tables->memory_dim * es) % 16 == 0, "serving rows must be a whole number of 16-byte vectors");
+  for (int o = 0; o < tables->n_orders; ++o)
+    LNG_REQUIRE((reinterpret_cast<uintptr_t>(tables->tables[o]) & 15) == 0, "table pointers must be 16-byte aligned");
+  LNG_REQUIRE((reinterpret_cast<uintptr_t>(out) & 15) == 0, "output must be 16-byte aligned");
+  TableSet ts = table_set(tables);
+  CodeSource src{codes, B, T, 0, tables->num_routes, nullptr, nullptr, nullptr, T - n, T, 0, 1};
+  const int64_t warps = B * n * tables->num_routes;
+  const int g = grid_for(warps * 32, 256, 16);
+  if (codes_dtype == LNG_U8)
+    lookup_host_kernel<uint8_t><<<g, 256, 0, S(stream)>>>(ts, src, B * n, 0, tables->num_routes, es, static_cast<uint4*>(out));
+  else
+    lookup_host_kernel<int32_t><<<g, 256, 0, S(stream)>>>(ts, src, B * n, 0, tables->num_routes, es, static_cast<uint4*>(out));
+  LNG_LAUNCHED("lookup_host_kernel");
+  return LNG_OK;
+}
+
+extern "C" int lng_serving_permute(const void* src, void* dst, int32_t dtype, int64_t routes, int32_t order,
+                                   int32_t bits, int64_t mem_dim, lng_stream_t stream) {
+  LNG_REQUIRE(routes >= 1 && order >= 1 && bits >= 1 && int64_t(order) * bits <= 40 && mem_dim >= 1, "bad table shape");
+  const int es = dtype_size(dtype);
+  LNG_REQUIRE(es > 0 && (mem_dim * es) % 16 == 0, "rows must be a whole number of 16-byte vectors");
+  LNG_REQUIRE(src && dst && src != dst, "src and dst must be distinct non-NULL buffers");
+  LNG_REQUIRE(((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0,
+              "buffers must be 16-byte aligned");
+  const int64_t rows = routes << (int64_t(bits) * order);
+  serving_permute_kernel<<<grid_for(rows * 32, 256, 16), 256, 0, S(stream)>>>(
+      static_cast<const uint4*>(src), static_cast<uint4*>(dst), rows, order, bits, mem_dim * es / 16);
+  LNG_LAUNCHED("serving_permute_kernel");
+  return LNG_OK;
+}
+
+namespace {
+std::mutex g_host_map_mu;
+std::vector<void*> g_host_registered;  // host ranges this library registered (and so unregisters)
+}  // namespace
+
+extern "C" int lng_host_map(void* host, size_t bytes, void** device_ptr) {
+  LNG_REQUIRE(host && device_ptr && bytes > 0, "NULL pointer or empty range");
+  *device_ptr = nullptr;
+  cudaPointerAttributes attr{};
+  LNG_CUDA(cudaPointerGetAttributes(&attr, host));
+  if (attr.type != cudaMemoryTypeHost) {  // pageable: pin and map it (page-locked memory is already mapped)
+    LNG_CUDA(cudaHostRegister(host, bytes, cudaHostRegisterMapped | cudaHostRegisterPortable));
+    std::lock_guard<std::mutex> lock(g_host_map_mu);
+    g_host_registered.push_back(host);
+  }
+  LNG_CUDA(cudaHostGetDevicePointer(device_ptr, host, 0));
+  return LNG_OK;
+}
+
+extern "C" int lng_host_unmap(void* host) {
+  LNG_REQUIRE(host, "NULL pointer");
+  std::lock_guard<std::mutex> lock(g_host_map_mu);
+  for (size_t i = 0; i < g_host_registered.size(); ++i) {
+    if (g_host_registered[i] == host) {
+      g_host_registered.erase(g_host_registered.begin() + i);
+      LNG_CUDA(cudaHostUnregister(host));
+      return LNG_OK;
+    }
+  }
+  return LNG_OK;  // memory the caller pinned itself stays pinned
+}
+
+extern "C" int lng_packed_suffix(const void* codes, int32_t codes_dtype, int64_t B, int64_t T, int64_t R,
+                                 int32_t bits, int32_t maxn, const int32_t* packed_in, int32_t* packed_out,
+                                 uint8_t* window_out, lng_stream_t stream) {
+  LNG_REQUIRE(codes_dtype == LNG_U8 || codes_dtype == LNG_I32, "codes dtype must be u8 or i32");
+  LNG_REQUIRE(B >= 0 && T >= 1 && R >= 1 && bits >= 1 && maxn >= 1 && int64_t(bits) * maxn <= 31,
+              "bad packed-state shape (maxn * bits must fit 31 bits)");
+  LNG_REQUIRE(!packed_in || T == 1, "advancing the packed state takes one position");
+  if (B == 0) return LNG_OK;
+  LNG_REQUIRE(codes && packed_out, "NULL pointer");
+  const unsigned g = unsigned(ceil_div(B * R, 128));
+  if (codes_dtype == LNG_U8)
+    packed_suffix_kernel<uint8_t><<<g, 128, 0, S(stream)>>>(static_cast<const uint8_t*>(codes), B, T, R, bits, maxn,
+                                                            packed_in, packed_in != nullptr, packed_out, window_out);
+  else
+    packed_suffix_kernel<int32_t><<<g, 128, 0, S(stream)>>>(static_cast<const int32_t*>(codes), B, T, R, bits, maxn,
+                                                            packed_in, packed_in != nullptr, packed_out, window_out);
+  LNG_LAUNCHED("packed_suffix_kernel");
+  return LNG_OK;
+}
+
 // ====================================================================== attention core
 // Warps per CTA and shared-memory stages per warp of the gather kernel come from the token width
 // (AttendMmaCfg): two stages per warp, as many warps (at most 8) as the shared memory holds.
@@ -507,8 +659,11 @@ static int attend_impl(const lng_tables* t, const AttendParams& p, int32_t u_dty
   if (mma_ok) {
     AttendParams q = p;
     q.rows32 = 1;
-    for (int o = 0; o < t->n_orders; ++o)
-      q.rows32 = q.rows32 && (t->num_routes << (int64_t(t->bits) * t->orders[o])) < (int64_t(1) << 31);
+    if (p.src.direct > 0)
+      q.rows32 = p.M * p.src.direct < (int64_t(1) << 31);
+    else
+      for (int o = 0; o < t->n_orders; ++o)
+        q.rows32 = q.rows32 && (t->num_routes << (int64_t(t->bits) * t->orders[o])) < (int64_t(1) << 31);
     bool aligned = (reinterpret_cast<uintptr_t>(p.qa) & 15) == 0 && (reinterpret_cast<uintptr_t>(p.u) & 15) == 0;
     for (int o = 0; o < t->n_orders; ++o) aligned = aligned && (reinterpret_cast<uintptr_t>(t->tables[o]) & 15) == 0;
     if (aligned) {
@@ -590,6 +745,39 @@ extern "C" int lng_route_attend(const lng_tables* tables, const void* codes, int
   p.l_out = l_out;
   if (codes_dtype == LNG_U8) return attend_impl<uint8_t>(tables, p, u_dtype, S(stream));
   return attend_impl<int32_t>(tables, p, u_dtype, S(stream));
+}
+
+extern "C" int lng_route_attend_rows(const void* tokens, int32_t tok_dtype, int64_t M, int64_t routes, int64_t Dt,
+                                     int32_t num_heads, float eps, float sink_logit, const void* qa,
+                                     const float* qscale, void* u, int32_t u_dtype, lng_stream_t stream) {
+  LNG_REQUIRE(M >= 0 && routes >= 1 && Dt >= 1, "bad route-token shape");
+  LNG_REQUIRE(num_heads >= 1 && num_heads <= 64, "num_heads must be in [1, 64]");
+  LNG_REQUIRE(tok_dtype == LNG_F32 || tok_dtype == LNG_BF16 || tok_dtype == LNG_F16, "token dtype must be f32, bf16 or f16");
+  LNG_REQUIRE(u_dtype == LNG_F32 || u_dtype == LNG_BF16 || u_dtype == LNG_F16, "u dtype must be f32, bf16 or f16");
+  if (M == 0) return LNG_OK;
+  LNG_REQUIRE(tokens && qa && u, "NULL pointer");
+  // the tokens as a one-"order" table whose row of (item i, route r) is i * routes + r
+  lng_tables t{};
+  t.n_orders = 1;
+  t.orders[0] = 1;
+  t.tables[0] = tokens;
+  t.table_dtype = tok_dtype;
+  t.bits = 1;
+  t.num_routes = routes;
+  t.memory_dim = Dt;
+  AttendParams p{};
+  p.ts = table_set(&t);
+  p.src = CodeSource{nullptr, 0, 0, 0, routes, nullptr, nullptr, nullptr, 0, 0, routes};
+  p.M = M;
+  p.route_start = 0;
+  p.route_end = routes;
+  p.qh = num_heads;
+  p.eps = eps;
+  p.sink = sink_logit;
+  p.qa = qa;
+  p.qscale = qscale;
+  p.u = u;
+  return attend_impl<uint8_t>(&t, p, u_dtype, S(stream));
 }
 
 // ====================================================================== GEMM

@@ -54,4 +54,76 @@ __global__ void lookup_vec_kernel(TableSet ts, CodeSource src, int64_t M, int64_
   }
 }
 
+// Route tokens from tables the device reaches over PCIe (pinned host memory mapped into the device
+// address space): the same per-(item, route) warp walk with plain 16-byte loads -- no read-only-cache
+// or bulk-copy path -- so each row crosses PCIe once, straight into the output.
+template <typename CodeT>
+__global__ void lookup_host_kernel(TableSet ts, CodeSource src, int64_t M, int64_t route_start, int64_t route_end,
+                                   int elem_bytes, uint4* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nr = route_end - route_start;
+  const int64_t total = M * nr;
+  const int64_t vecs = ts.mem_dim * elem_bytes / 16;
+  for (int64_t w = (blockIdx.x * int64_t(blockDim.x) + threadIdx.x) >> 5; w < total;
+       w += (int64_t(gridDim.x) * blockDim.x) >> 5) {
+    const int64_t item = w / nr;
+    const int64_t r = route_start + w % nr;
+    uint4* dst = out + w * vecs * ts.n_orders;
+    for (int o = 0; o < ts.n_orders; ++o) {
+      const int64_t row = ngram_row<CodeT>(src, item, r, ts.order[o], ts.bits);
+      const uint4* s = reinterpret_cast<const uint4*>(ts.tab[o]) + (row < 0 ? 0 : row) * vecs;
+      for (int64_t j = lane; j < vecs; j += 32) dst[o * vecs + j] = row < 0 ? make_uint4(0, 0, 0, 0) : s[j];
+    }
+  }
+}
+
+// The serving-layout copy of one order's table (serving/layout.py:26-43): within every route's block of
+// A^n rows, row j of dst is row reverse_digits(j) of src (the n base-A digits in reverse order).
+// One warp per destination row, 16-byte vectors.
+__global__ void serving_permute_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, int64_t rows,
+                                       int order, int bits, int64_t vecs) {
+  const int lane = threadIdx.x & 31;
+  const int64_t block = int64_t(1) << (bits * order);
+  const int64_t amask = (int64_t(1) << bits) - 1;
+  for (int64_t row = (blockIdx.x * int64_t(blockDim.x) + threadIdx.x) >> 5; row < rows;
+       row += (int64_t(gridDim.x) * blockDim.x) >> 5) {
+    const int64_t r = row / block, j = row % block;
+    int64_t rev = 0;
+    for (int k = 0; k < order; ++k) rev |= ((j >> (k * bits)) & amask) << ((order - 1 - k) * bits);
+    const uint4* s = src + (r * block + rev) * vecs;
+    uint4* d = dst + row * vecs;
+    for (int64_t v = lane; v < vecs; v += 32) d[v] = s[v];
+  }
+}
+
+// The packed n-gram suffix of the incremental readout (lngram_v2.py:1714-1760): packed[b, r] holds the
+// codes of the last maxn positions, the newest in digit maxn - 1 (digits `bits` wide).  advance == 0
+// packs the last min(T, maxn) positions of codes [B, T, R] (_pack_suffix); advance == 1 shifts
+// packed_in down one digit and puts codes [B, 1, R] in the top digit (_advance_packed).  The digits are
+// also written unpacked as window codes [B, maxn, R] (slot j = digit j) for the window-mode readout.
+template <typename CodeT>
+__global__ void packed_suffix_kernel(const CodeT* __restrict__ codes, int64_t B, int64_t T, int64_t R, int bits,
+                                     int maxn, const int32_t* __restrict__ packed_in, int advance,
+                                     int32_t* __restrict__ packed_out, uint8_t* __restrict__ window) {
+  const int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x;
+  if (i >= B * R) return;
+  const int64_t b = i / R, r = i % R;
+  const uint32_t amask = (1u << bits) - 1;
+  uint32_t v = 0;
+  if (advance) {
+    const uint32_t c = uint32_t(codes[b * R + r]) & amask;
+    v = (uint32_t(packed_in[i]) >> bits) | (c << ((maxn - 1) * bits));
+  } else {
+    const int64_t keep = T < maxn ? T : maxn;
+    const int first = int(maxn - keep);
+    for (int64_t k = 0; k < keep; ++k) {
+      const uint32_t c = uint32_t(codes[(b * T + T - keep + k) * R + r]) & amask;
+      v |= c << ((first + int(k)) * bits);
+    }
+  }
+  packed_out[i] = int32_t(v);
+  if (window)
+    for (int j = 0; j < maxn; ++j) window[(b * maxn + j) * R + r] = uint8_t((v >> (j * bits)) & amask);
+}
+
 }  // namespace lng

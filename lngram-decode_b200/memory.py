@@ -6,13 +6,15 @@
 ``ffnmem/memory/wrapper.py:50-125`` (router in fp32, sign codes, module forward).
 
 Every method dispatches to the C ABI (``include/lngram_b200.h``) on the tensors' CUDA device and
-current stream.  There is no CPU path: CPU tensors raise.  Training (gradients through the
-surrogate of ``lngram_v2.py:328-465``) is outside this build's scope and raises as well.
+current stream.  There is no CPU path: CPU tensors raise.  Training: ``_lookup_route_chunk`` carries
+the reference's backward (the tables' row gradient and the q surrogate of ``lngram_v2.py:326-447``);
+the readout (``forward``, ``_project_*``, ``_manual_gqa``) is inference-only and raises in training mode.
 """
 
 from __future__ import annotations
 
 import math
+from dataclasses import dataclass
 from typing import Optional, Sequence
 
 import torch
@@ -89,6 +91,75 @@ def rms_norm(x: Tensor, weight: Tensor | None, eps: float) -> Tensor:
     return y
 
 
+@dataclass
+class LngramIncrementalState:
+    """The side state of ``forward_incremental`` that travels with an attention KV cache
+    (``lngram_v2.py:187-204``): the last max_order - 1 route codes [B, H, R], the packed n-gram suffix
+    [B, R] int32 (newest code in the top digit), how many positions it holds, and the conv history
+    [B, d, left_padding] of normalised outputs."""
+
+    route_history: Optional[Tensor] = None
+    packed_route_state: Optional[Tensor] = None
+    route_state_length: int = 0
+    conv_history: Optional[Tensor] = None
+
+    def index_select(self, indices: Tensor) -> "LngramIncrementalState":
+        """The rows ``indices`` of every tensor (beam reordering), as the reference's ``index_select``."""
+        def select(value: Optional[Tensor]) -> Optional[Tensor]:
+            return None if value is None else value.index_select(0, indices.to(value.device))
+
+        return LngramIncrementalState(select(self.route_history), select(self.packed_route_state),
+                                      int(self.route_state_length), select(self.conv_history))
+
+
+class _TrainLookup(torch.autograd.Function):
+    """Route tokens of the lookup kernel with the reference's backward (``lng_lookup_backward``): the
+    gathered rows' gradient into each order table and, when ``q_logits`` is given, the surrogate's
+    route-logit gradient (``lngram_v2.py:326-447``)."""
+
+    @staticmethod
+    def forward(ctx, module, codes, q_logits, route_start, route_end, seg, val, *tables):
+        with torch.no_grad():
+            tokens = module._lookup_tokens(codes, route_start, route_end, seg, val, None)
+        ctx.module, ctx.rs, ctx.re = module, route_start, route_end
+        ctx.has = (q_logits is not None, seg is not None, val is not None)
+        empty = codes.new_empty(0)
+        ctx.save_for_backward(codes, q_logits if q_logits is not None else empty, seg if seg is not None else empty,
+                              val if val is not None else empty)
+        return tokens
+
+    @staticmethod
+    def backward(ctx, grad):
+        codes, q, seg, val = ctx.saved_tensors
+        has_q, has_seg, has_val = ctx.has
+        m = ctx.module
+        b, t, _ = codes.shape
+        rs, re = ctx.rs, ctx.re
+        grad = grad.contiguous()
+        tables = [m.tables[f"ngram_{n}"].weight for n in m.ngrams]
+        need = ctx.needs_input_grad[7:]
+        gtabs = [torch.zeros(w.shape, device=w.device, dtype=torch.float32) if nd else None
+                 for w, nd in zip(tables, need)]
+        arr = (_lib.C.c_void_p * _lib.MAX_ORDERS)(*([ptr(g) for g in gtabs] + [None] * (_lib.MAX_ORDERS - len(gtabs))))
+        grad_q = q32 = gq = None
+        if has_q and ctx.needs_input_grad[2]:
+            q32 = q.float().contiguous()
+            gq = torch.empty(b, t, re - rs, m.bits_per_route, device=q.device, dtype=torch.float32)
+        with torch.cuda.device(grad.device):
+            check(_lib.library().lng_lookup_backward(
+                m.tables_desc(with_ss=False), ptr(codes), _lib.U8 if codes.dtype == torch.uint8 else _lib.I32, b, t,
+                rs, re, ptr(seg) if has_seg else None, ptr(val) if has_val else None, ptr(grad),
+                _lib.dtype_code(grad.dtype), ptr(q32), q.shape[2] if q32 is not None else 0,
+                m.q_surrogate_temperature, m.q_surrogate_scale, int(m.q_surrogate_mode == "exact"), ptr(gq), arr,
+                stream_ptr()), "lookup backward")
+        if gq is not None:
+            grad_q = torch.zeros(q.shape, device=q.device, dtype=torch.float32)
+            grad_q[:, :, rs:re] = gq
+            grad_q = grad_q.to(q.dtype)
+        tgrads = [None if g is None else g.to(w.dtype) for g, w in zip(gtabs, tables)]
+        return (None, None, grad_q, None, None, None, None, *tgrads)
+
+
 class RouteNgramMemoryV2(nn.Module):
     """Inference drop-in for the reference ``RouteNgramMemoryV2`` (sink readout v2)."""
 
@@ -142,6 +213,14 @@ class RouteNgramMemoryV2(nn.Module):
         if self.execution_mode not in {"full", "streaming", "auto"}:
             raise ValueError("execution_mode must be full, streaming, or auto")
         self.stream_route_chunk_size = int(stream_route_chunk_size)
+        if float(q_surrogate_temperature) < 0.0:
+            raise ValueError("q_surrogate_temperature must be non-negative")
+        self.q_surrogate_enable = bool(q_surrogate_enable)
+        self.q_surrogate_mode = str(q_surrogate_mode).lower()
+        if self.q_surrogate_mode not in {"exact", "approximate"}:
+            raise ValueError("q_surrogate_mode must be exact or approximate")
+        self.q_surrogate_temperature = float(q_surrogate_temperature)
+        self.q_surrogate_scale = float(q_surrogate_scale)
         mass = float(sink_initial_active_mass)
         if not math.isfinite(mass) or not 0.0 < mass < 1.0:
             raise ValueError("sink_initial_active_mass must be finite and in (0, 1)")
@@ -288,11 +367,32 @@ class RouteNgramMemoryV2(nn.Module):
             return codes.contiguous(), _lib.U8
         return codes.to(torch.int32).contiguous(), _lib.I32
 
+    def _use_surrogate(self, q_logits: Optional[Tensor]) -> bool:
+        """``lngram_v2.py:1019-1025``."""
+        return bool(self.q_surrogate_enable and self.training and torch.is_grad_enabled() and q_logits is not None)
+
     def _lookup_route_chunk(self, route_codes: Tensor, q_logits_btrm: Optional[Tensor], route_start: int,
                             route_end: int, segment_ids: Optional[Tensor], valid_tokens: Optional[Tensor],
                             target_length: Optional[int] = None) -> Tensor:
-        """``lngram_v2.py:1047-1113``: route tokens [B, T', R', Dt] in the table dtype (exact copies)."""
-        self._guard()
+        """``lngram_v2.py:1047-1113``: route tokens [B, T', R', Dt] in the table dtype (exact copies).  In
+        training mode with gradients enabled the tokens carry the backward of the reference: the rows'
+        gradient into the order tables and, with ``q_logits_btrm`` [B, T, R, bits] and the surrogate
+        enabled, its route-logit gradient (``_LngramSurrogate``, ``:326-447``)."""
+        if self.training and torch.is_grad_enabled():
+            use_sur = self._use_surrogate(q_logits_btrm)
+            if use_sur and target_length is not None:
+                raise RuntimeError("cached inference cannot use surrogate gradients")
+            codes, _ = self._codes(route_codes)
+            seg = None if segment_ids is None else segment_ids.to(device=codes.device, dtype=torch.int64).contiguous()
+            val = None if valid_tokens is None else valid_tokens.to(device=codes.device, dtype=torch.bool).contiguous()
+            tables = [self.tables[f"ngram_{n}"].weight for n in self.ngrams]
+            tokens = _TrainLookup.apply(self, codes, q_logits_btrm if use_sur else None, int(route_start),
+                                        int(route_end), seg, val, *tables)
+            return tokens if target_length is None else tokens[:, -int(target_length):]
+        return self._lookup_tokens(route_codes, route_start, route_end, segment_ids, valid_tokens, target_length)
+
+    def _lookup_tokens(self, route_codes: Tensor, route_start: int, route_end: int, segment_ids: Optional[Tensor],
+                       valid_tokens: Optional[Tensor], target_length: Optional[int] = None) -> Tensor:
         b, t, _ = route_codes.shape
         codes, cdt = self._codes(route_codes)
         tout = t if target_length is None else min(int(target_length), t)
@@ -404,6 +504,73 @@ class RouteNgramMemoryV2(nn.Module):
             raise ValueError(f"q_logits shape={tuple(q_logits.shape)}, expected {(b, t, self.route_logits_dim)}")
         self._guard()
         return self.forward_codes(hidden_states, route_codes_btr, segment_ids, valid_tokens)
+
+    @torch.no_grad()
+    def forward_incremental(self, hidden_states: Tensor, route_codes_btr: Tensor,
+                            state: Optional[LngramIncrementalState] = None) -> tuple[Tensor, LngramIncrementalState]:
+        """``lngram_v2.py:1763-1829``: the exact prompt / decode forward of T new positions after ``state``.
+        T = 1 reads the rows through the packed suffix (``_advance_packed`` / ``_lookup_packed``: a code
+        window whose valid slots are the state's length); T > 1 looks up the context [history, codes]
+        and packs its suffix (``_pack_suffix``).  The conv runs over [conv history, new normalised
+        outputs].  Returns (output [B, T, d], the new state)."""
+        if self.training:
+            raise RuntimeError("forward_incremental is inference-only; call eval() first")
+        from .seams import _readout
+
+        if state is None:
+            state = LngramIncrementalState()
+        b, t, _ = hidden_states.shape
+        if tuple(route_codes_btr.shape) != (b, t, self.num_routes):
+            raise ValueError("incremental route code shape mismatch")
+        h = _cuda(hidden_states, "hidden_states")
+        dev = h.device
+        act = self._act()
+        h = h.to(act).contiguous()
+        R, bits, maxn = self.num_routes, self.bits_per_route, self.max_ngram_order
+        cdt = torch.uint8 if bits <= 8 else torch.int32
+        cc = _lib.U8 if bits <= 8 else _lib.I32
+        codes = route_codes_btr.to(device=dev, dtype=cdt).contiguous()
+        ctx = codes if state.route_history is None else torch.cat(
+            (state.route_history.to(device=dev, dtype=cdt), codes), 1).contiguous()
+        lib = _lib.library()
+        s = stream_ptr()
+        packed = torch.empty(b, R, dtype=torch.int32, device=dev)
+        with torch.cuda.device(dev):
+            if t == 1:
+                pin = (torch.zeros(b, R, dtype=torch.int32, device=dev) if state.packed_route_state is None
+                       else state.packed_route_state.to(device=dev, dtype=torch.int32).contiguous())
+                window = torch.empty(b, maxn, R, dtype=torch.uint8, device=dev)
+                check(lib.lng_packed_suffix(ptr(codes), cc, b, 1, R, bits, maxn, ptr(pin), ptr(packed), ptr(window), s),
+                      "advance packed state")
+                length = min(int(state.route_state_length) + 1, maxn)
+                seg = (torch.arange(maxn, device=dev) >= maxn - length).to(torch.int32).expand(b, maxn).contiguous()
+                mixed = _readout(self, h, self.tables_desc(), window, _lib.U8, b, 0, maxn, seg, 0)
+            else:
+                mixed = _readout(self, h, self.tables_desc(), ctx, cc, b, ctx.shape[1], 0, None, t)
+                check(lib.lng_packed_suffix(ptr(ctx), cc, b, ctx.shape[1], R, bits, maxn, None, ptr(packed), None, s),
+                      "pack suffix")
+                length = min(int(state.route_state_length) + t, maxn)
+                if state.route_state_length == 0 and state.route_history is None:
+                    length = min(ctx.shape[1], maxn)
+            conv = self.short_conv
+            lp, k, dil, d = conv.left_padding, conv.kernel_size, conv.dilation, self.hidden_size
+            cache = torch.zeros(b, lp + t, d, dtype=act, device=dev)
+            if state.conv_history is not None and lp:
+                cache[:, :lp] = state.conv_history.to(device=dev, dtype=act).transpose(1, 2)
+            base = torch.arange(b, device=dev) * (lp + t)
+            pos = lp + torch.arange(t, device=dev)
+            new_slot = (base[:, None] + pos[None]).reshape(-1).contiguous()
+            lags = torch.tensor([(k - 1 - tap) * dil for tap in range(k)], device=dev)
+            slot = (base[:, None, None] + pos[None, :, None] - lags[None, None, :]).reshape(b * t, k).contiguous()
+            out = torch.empty(b * t, d, dtype=act, device=dev)
+            check(lib.lng_conv_window(self.readout_desc(), ptr(mixed), b * t, ptr(cache), ptr(new_slot), ptr(slot),
+                                      ptr(out), s), "conv window")
+        hist = self.route_history_length
+        new_state = LngramIncrementalState(
+            route_history=ctx[:, ctx.shape[1] - hist:].contiguous() if hist else ctx[:, :0],
+            packed_route_state=packed, route_state_length=int(length),
+            conv_history=cache[:, cache.shape[1] - lp:].transpose(1, 2).contiguous() if lp else cache[:, :0].transpose(1, 2))
+        return out.view(b, t, d), new_state
 
     def forward_codes(self, h: Tensor, codes: Optional[Tensor], segment_ids=None, valid_tokens=None, router_x=None,
                       router_w=None, codes_out: Optional[Tensor] = None, out: Optional[Tensor] = None,

@@ -3,6 +3,9 @@
 * ``memory_step`` -- ``ffnmem/infer.py:152-182``: the memory output of n new positions after L
   cached ones: codes over the context [history + new], the fused gather + sink attention on the
   last n positions, the folded output map, and the short conv over the cached normalised outputs.
+* ``decode_memory_step`` -- the memory block of ``decode_step(..., row_provider=)``
+  (``ffnmem/infer.py:207-251``): rows from a row provider (e.g. ``serving.ZeroCopyGather``) replace the
+  table lookup.
 * ``tree_memory_block`` -- the memory part of ``tree_verify_step`` (``drafting/tree.py:165-195``):
   every node's n-gram window and conv window follow its ancestors, then the cached positions.
 * ``tree_slots`` / ``tree_ngram_codes`` -- the node windows of ``drafting/tree.py:96-127``, built from a
@@ -74,6 +77,28 @@ def tree_ngram_codes(parent, codes: Tensor, history: Tensor | None = None, hist:
     return seq[:, idx] * ok[None, :, :, None].to(codes.dtype), ok
 
 
+def _readout_rows(m, h: Tensor, tokens: Tensor) -> Tensor:
+    """The readout over caller-supplied route tokens [B, n, R, Dt] (no table lookup)."""
+    lib = _lib.library()
+    f = m.folded()
+    act = m._act()
+    h = h.to(act).contiguous()
+    M = h.numel() // m.hidden_size
+    qd = m.readout_num_heads * m.route_token_dim
+    rs = torch.empty(M, device=h.device, dtype=torch.float32)
+    check(lib.lng_rms_rows(ptr(h), _lib.dtype_code(act), M, m.hidden_size, m.eps, ptr(rs), stream_ptr()), "rms")
+    tdt = m.tables[f"ngram_{m.ngrams[0]}"].weight.dtype
+    tokens = tokens.to(device=h.device, dtype=tdt).contiguous()
+    if tuple(tokens.shape[-2:]) != (m.num_routes, m.route_token_dim) or tokens.numel() != M * m.num_routes * m.route_token_dim:
+        raise ValueError(f"route_tokens must be [B, n, {m.num_routes}, {m.route_token_dim}]")
+    qa = m._linear(h.view(M, -1), f["w_qk"])
+    u = torch.empty(M, qd, device=h.device, dtype=act)
+    check(lib.lng_route_attend_rows(ptr(tokens), _lib.dtype_code(tdt), M, m.num_routes, m.route_token_dim,
+                                    m.readout_num_heads, m.eps, m.readout_sink_logit, ptr(qa), ptr(rs), ptr(u),
+                                    _lib.dtype_code(act), stream_ptr()), "route_attend_rows")
+    return m._linear(u, f["w_vo"])
+
+
 def _readout(m, h: Tensor, tables, codes, cdt, B, T, window, seg, target_length):
     """qa = h . w_qk^T, qscale = 1/rms(h), fused attention, mixed = u . w_vo^T."""
     lib = _lib.library()
@@ -100,19 +125,24 @@ def _conv(m, mixed: Tensor, cache: MemoryCache, new_slot: Tensor, slot: Tensor) 
 
 
 @torch.no_grad()
-def memory_step(m, cache: MemoryCache, h: Tensor, codes_new: Tensor, route_codes_ctx: Tensor | None = None) -> Tensor:
+def memory_step(m, cache: MemoryCache, h: Tensor, codes_new: Tensor, route_codes_ctx: Tensor | None = None,
+                route_tokens: Tensor | None = None) -> Tensor:
     """``ffnmem/infer.py:152-182``: output [B, n, d] for n new positions after ``cache.length``.  The new
     codes and conv inputs are written into the cache; ``cache.length`` is left to the caller (the
-    reference's ``decode_step`` advances it after all layers)."""
+    reference's ``decode_step`` advances it after all layers).  ``route_tokens`` [B, n, R, Dt] (optional):
+    rows supplied by the caller (host-RAM serving, a row provider); the table lookup is skipped."""
     B, n, d = h.shape
     L = cache.length
     if L + n > cache.max_len:
         raise ValueError(f"cache full: {L} + {n} > {cache.max_len}")
     cache.codes[:, L:L + n] = codes_new.to(torch.uint8)
-    hist = m.route_history_length
-    ctx = cache.codes[:, max(0, L - hist):L + n] if route_codes_ctx is None else route_codes_ctx.to(torch.uint8)
-    ctx = ctx.contiguous()
-    mixed = _readout(m, h, m.tables_desc(), ctx, _lib.U8, B, ctx.shape[1], 0, None, n)
+    if route_tokens is not None:
+        mixed = _readout_rows(m, h, route_tokens)
+    else:
+        hist = m.route_history_length
+        ctx = cache.codes[:, max(0, L - hist):L + n] if route_codes_ctx is None else route_codes_ctx.to(torch.uint8)
+        ctx = ctx.contiguous()
+        mixed = _readout(m, h, m.tables_desc(), ctx, _lib.U8, B, ctx.shape[1], 0, None, n)
     k, dil = m.short_conv.kernel_size, m.short_conv.dilation
     dev = h.device
     pos = L + torch.arange(n, device=dev)
@@ -176,3 +206,20 @@ def tree_memory_block(m, cache: MemoryCache, h: Tensor, codes: Tensor, parent) -
     cache.codes[:, L:L + n] = codes
     out = _conv(m, mixed, cache, plan["new_slot"], plan["slot"])
     return out.view(B, n, d)
+
+
+@torch.no_grad()
+def decode_memory_step(mem, cache: MemoryCache, h: Tensor, h_norm: Tensor, row_provider=None, pos: int = 0,
+                       router_in: Tensor | None = None) -> Tensor:
+    """The memory block of ``decode_step`` (``ffnmem/infer.py:207-251``, lines 230-240): the router's codes
+    of the n new positions, then ``row_provider(pos, cache, codes_new) -> route tokens [B, n, R, Dt] | None``
+    -- called after the codes are known and before they are written to the cache (``cache.length`` is
+    still L), as the reference calls it -- and ``memory_step`` on those rows (or on the tables when it
+    returns None or there is no provider).  ``mem`` is an ``LngramMemory``; the caller advances
+    ``cache.length`` after the step, as ``decode_step`` does after all layers."""
+    x = h_norm if mem.router_input == "hidden" else router_in
+    if x is None:
+        raise ValueError(f"router_input={mem.router_input} needs router_in")
+    codes = mem.route_codes(x)
+    rows = None if row_provider is None else row_provider(pos, cache, codes)
+    return memory_step(mem.module, cache, h, codes, route_tokens=rows)

@@ -459,3 +459,88 @@ def tree_memory_block(h: np.ndarray, codes: np.ndarray, parent, code_history: np
     window = ci[:, idx] * ok[None, :, :, None].astype(F32)          # [B, n, lp+1, d]
     conv_out = conv_window(window.reshape(b * n, lp + 1, -1), p).reshape(b, n, -1)
     return (mixed + conv_out).astype(F32)
+
+
+# --------------------------------------------------------------------------- incremental state / serving layout
+def pack_suffix(codes: np.ndarray, maxn: int, bits: int) -> np.ndarray:
+    """``lngram_v2.py:1714-1726`` (_pack_suffix): the last min(T, maxn) codes of [B, T, R] packed into
+    int32 [B, R], the newest in digit maxn - 1."""
+    t = codes.shape[1]
+    keep = min(t, maxn)
+    out = np.zeros((codes.shape[0], codes.shape[2]), np.int64)
+    for off in range(keep):
+        out |= codes[:, t - keep + off].astype(np.int64) << ((maxn - keep + off) * bits)
+    return out.astype(np.int32)
+
+
+def advance_packed(packed: np.ndarray | None, current: np.ndarray, maxn: int, bits: int) -> np.ndarray:
+    """``lngram_v2.py:1728-1740`` (_advance_packed): shift down one digit, the new codes in the top digit."""
+    p = np.zeros(current.shape, np.int64) if packed is None else packed.astype(np.int64)
+    return ((p >> bits) | (current.astype(np.int64) << ((maxn - 1) * bits))).astype(np.int32)
+
+
+def reverse_digits(n_digits: int, bits: int) -> np.ndarray:
+    """``serving/layout.py:26-34``: j -> j with its n base-2^bits digits reversed."""
+    j = np.arange((1 << bits) ** n_digits, dtype=np.int64)
+    out = np.zeros_like(j)
+    for k in range(n_digits):
+        out |= ((j >> (k * bits)) & ((1 << bits) - 1)) << ((n_digits - 1 - k) * bits)
+    return out
+
+
+def serving_table(table: np.ndarray, routes: int, order: int, bits: int) -> np.ndarray:
+    """``serving/layout.py:37-42`` (permute_table): row j of each route block = v2 row reverse_digits(j)."""
+    block = (1 << bits) ** order
+    return table.reshape(routes, block, -1)[:, reverse_digits(order, bits)].reshape(table.shape)
+
+
+def surrogate_backward(grad_tokens: np.ndarray, codes: np.ndarray, q: np.ndarray, tables: dict, ngrams, bits: int,
+                       route_start: int, route_end: int, temperature: float, scale: float, exact: bool,
+                       segment_ids: np.ndarray | None = None, valid_tokens: np.ndarray | None = None):
+    """Backward of the training lookup (``lngram_v2.py:1047-1113``) through ``_LngramSurrogate``
+    (``:359-447``), per order: the rows' gradient into the table (dict order -> {row: grad}) and the
+    route-logit gradient [B, T, R', bits] (approximate: one-bit counterfactuals; exact: the alphabet)."""
+    b, t, _ = codes.shape
+    rp = route_end - route_start
+    A = 1 << bits
+    md = next(iter(tables.values())).shape[1]
+    p = (1.0 / (1.0 + np.exp(-temperature * q[:, :, route_start:route_end].astype(F32)))).astype(F32)
+    grad_q = np.zeros((b, t, rp, bits), F32)
+    tgrad = {}
+    for oi, order in enumerate(ngrams):
+        vl = t - order + 1
+        tgrad[order] = {}
+        if vl <= 0:
+            continue
+        g = grad_tokens[..., oi * md:(oi + 1) * md].astype(F32)
+        mask = valid_mask(order, b, t, segment_ids, valid_tokens)
+        gv = g[:, order - 1:] * mask[:, order - 1:, None, None]
+        idx = row_indices(codes, order, bits, route_start, route_end)        # [B, VL, R']
+        table = tables[order].astype(F32)
+        for bb, ii, rr in zip(*np.nonzero(mask[:, order - 1:, None].repeat(rp, 2))):
+            row = int(idx[bb, ii, rr])
+            tgrad[order][row] = tgrad[order].get(row, 0) + gv[bb, ii, rr]
+        if temperature == 0.0 or scale == 0.0:
+            continue
+        gq = np.zeros_like(grad_q)
+        cur = (table[idx] * gv).sum(-1)
+        for e in range(order):
+            if exact:
+                src = codes[:, e:e + vl, route_start:route_end].astype(np.int64)
+                sp = p[:, e:e + vl]
+                base = idx - src * (A ** e)
+                for c in range(A):
+                    d = (table[base + c * (A ** e)] * gv).sum(-1)
+                    cb = np.array([(c >> j) & 1 for j in range(bits)], F32)
+                    cp = np.where(cb.astype(bool), sp, 1.0 - sp).prod(-1)
+                    gq[:, e:e + vl] += (cp[..., None] * (cb - sp) * d[..., None]) * F32(scale * temperature)
+            else:
+                for j in range(bits):
+                    m = 1 << (e * bits + j)
+                    fd = (table[idx ^ m] * gv).sum(-1)
+                    sign = np.where((idx & m) != 0, -1.0, 1.0).astype(F32)
+                    gq[:, e:e + vl, :, j] += (fd - cur) * sign
+        if not exact:
+            gq = gq * (F32(scale * temperature) * p * (1.0 - p))
+        grad_q += gq
+    return grad_q, tgrad

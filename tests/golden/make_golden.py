@@ -218,6 +218,103 @@ def write_draft_case(case: str, n_trace: int, with_cpp: bool) -> None:
     print(f"draft_{case}.npz", {k: np.shape(v) for k, v in out.items()})
 
 
+INCREMENTAL_CALLS = (10, 1, 1, 1, 1, 1, 3, 1, 1)   # positions per forward_incremental call (a prefill, steps, a chunk)
+
+
+def write_incremental(case: str) -> None:
+    """``RouteNgramMemoryV2.forward_incremental`` (``lngram_v2.py:1763-1829``): a prefill, single steps and a
+    multi-position chunk, with the state after every call, and the full forward of the same positions."""
+    import torch
+
+    mem = reference_memory(case)
+    m = mem.module
+    inp = cases.memory_inputs(case)
+    T = sum(INCREMENTAL_CALLS)
+    h = _t(inp["h"][:, :T])
+    with torch.no_grad():
+        codes = m.quantize_route_logits(mem.route_logits(_t(inp["x"][:, :T])))
+        outs, state, t0 = [], None, 0
+        out = {"codes": codes.numpy().astype(np.uint8), "in_h": inp["h"][:, :T]}
+        for i, n in enumerate(INCREMENTAL_CALLS):
+            y, state = m.forward_incremental(h[:, t0:t0 + n], codes[:, t0:t0 + n], state)
+            outs.append(y.numpy())
+            out[f"packed_{i}"] = state.packed_route_state.numpy()
+            out[f"length_{i}"] = np.asarray(state.route_state_length)
+            t0 += n
+        out["outputs"] = np.concatenate(outs, 1)
+        out["route_history"] = state.route_history.numpy()
+        out["conv_history"] = state.conv_history.numpy()
+        out["full"] = m(h, codes).numpy()
+    np.savez_compressed(HERE / f"incremental_{case}.npz", **out)
+    print(f"incremental_{case}.npz", {k: np.shape(v) for k, v in out.items()})
+
+
+def write_serving(case: str) -> None:
+    """The serving row layout (``serving/layout.py``): sampled rows of ``permute_tables`` and the route
+    tokens ``serving_route_tokens`` reads from it, next to the v2 lookup's."""
+    import torch
+    from serving.layout import permute_tables, serving_route_tokens
+
+    mem = reference_memory(case)
+    m = mem.module
+    inp = cases.memory_inputs(case)
+    with torch.no_grad():
+        codes = m.quantize_route_logits(mem.route_logits(_t(inp["x"])))
+        tabs = permute_tables(m)
+        out = {"codes": codes.numpy().astype(np.uint8)}
+        rng = np.random.default_rng(17)
+        for n, t in tabs.items():
+            idx = np.sort(rng.choice(t.shape[0], size=min(512, t.shape[0]), replace=False))
+            out[f"rows_idx_{n}"] = idx
+            out[f"rows_{n}"] = t[torch.from_numpy(idx)].numpy()
+        out["tokens"] = serving_route_tokens(tabs, codes, m.ngrams, m.bits_per_route).numpy()
+        out["tokens_v2"] = m._lookup_route_chunk(codes, None, 0, m.num_routes, None, None).numpy()
+    np.savez_compressed(HERE / f"serving_{case}.npz", **out)
+    print(f"serving_{case}.npz", {k: np.shape(v) for k, v in out.items()})
+
+
+SURROGATE_CASES = (("tiny_multi", "approximate", 1, 3), ("tiny_multi", "exact", 0, 4), ("scaled_slice", "approximate", 0, 3),
+                   ("scaled_slice", "exact", 1, 2))
+
+
+def write_surrogate() -> None:
+    """The training-mode lookup's backward (``lngram_v2.py:1047-1113`` with ``_LngramSurrogate``,
+    ``:326-447``): q_logits.grad and the tables' row gradients for a seeded token gradient."""
+    import torch
+
+    out = {}
+    for i, (case, mode, rs, re) in enumerate(SURROGATE_CASES):
+        mem = reference_memory(case)
+        m = mem.module
+        m.q_surrogate_mode = mode
+        m.q_surrogate_temperature = 0.7
+        m.q_surrogate_scale = 1.3
+        m.train()
+        inp = cases.memory_inputs(case)
+        seg = _t(inp["segment_ids"]) if "segment_ids" in inp else None
+        valid = _t(inp["valid_tokens"]) if "valid_tokens" in inp else None
+        with torch.no_grad():
+            logits = mem.route_logits(_t(inp["x"]))
+            codes = m.quantize_route_logits(logits)
+        b, t = codes.shape[:2]
+        q = logits.view(b, t, m.num_routes, m.bits_per_route).clone().requires_grad_(True)
+        tok = m._lookup_route_chunk(codes, q, rs, re, seg, valid)
+        gen = torch.Generator().manual_seed(50 + i)
+        g = torch.randn(tok.shape, generator=gen)
+        (tok * g).sum().backward()
+        out[f"c{i}_grad_tokens"] = g.numpy()
+        out[f"c{i}_codes"] = codes.numpy().astype(np.uint8)
+        out[f"c{i}_q"] = q.detach().numpy()
+        out[f"c{i}_grad_q"] = q.grad.numpy()
+        for n in m.ngrams:
+            gw = m.tables[f"ngram_{n}"].weight.grad
+            rows = torch.nonzero(gw.abs().sum(-1) > 0).view(-1)
+            out[f"c{i}_rows_{n}"] = rows.numpy()
+            out[f"c{i}_grad_table_{n}"] = gw[rows].numpy()
+    np.savez_compressed(HERE / "surrogate_backward.npz", **out)
+    print("surrogate_backward.npz", {k: np.shape(v) for k, v in out.items()})
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--reference", default=os.environ.get("LNGRAM_REFERENCE") or str(HERE.parents[2] / "reference"))
@@ -227,7 +324,7 @@ def main(argv=None) -> None:
     import torch
 
     torch.set_num_threads(max(1, os.cpu_count() or 1))
-    todo = args.only or ["memory", "seams", "draft"]
+    todo = args.only or ["memory", "seams", "draft", "incremental", "serving", "surrogate"]
     if "memory" in todo:
         for case in cases.MEMORY_CASES:
             write_memory_case(case)
@@ -236,6 +333,13 @@ def main(argv=None) -> None:
     if "draft" in todo:
         write_draft_case("tiny", 60, with_cpp=True)
         write_draft_case("sdb", 24, with_cpp=True)
+    if "incremental" in todo:
+        write_incremental("tiny_multi")
+        write_incremental("scaled_slice")
+    if "serving" in todo:
+        write_serving("tiny_multi")
+    if "surrogate" in todo:
+        write_surrogate()
 
 
 if __name__ == "__main__":

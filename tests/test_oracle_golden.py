@@ -175,3 +175,60 @@ def test_c_oracle_matches_numpy_oracle():
     packed = np.empty((50, 184), np.uint8)
     lib.oracle_pack_codes(logits.ctypes.data, 50, 184, 4, packed.ctypes.data)
     np.testing.assert_array_equal(packed, om.quantize_route_logits(logits, 4))
+
+
+def test_packed_incremental_state_matches_reference_fixture(golden):
+    """The packed n-gram suffix after every forward_incremental call (lngram_v2.py:1714-1760)."""
+    from tests.golden.make_golden import INCREMENTAL_CALLS
+
+    for case in ("tiny_multi", "scaled_slice"):
+        g = golden(f"incremental_{case}")
+        c = cases.MEMORY_CASES[case]
+        maxn, bits = max(c["ngrams"]), c["bits"]
+        codes = g["codes"].astype(np.int64)
+        packed, t0, length = None, 0, 0
+        for i, n in enumerate(INCREMENTAL_CALLS):
+            if n == 1:
+                packed = om.advance_packed(packed, codes[:, t0], maxn, bits)
+                length = min(length + 1, maxn)
+            else:
+                ctx = codes[:, max(0, t0 - (maxn - 1)):t0 + n]
+                packed = om.pack_suffix(ctx, maxn, bits)
+                length = min(ctx.shape[1], maxn) if t0 == 0 else min(length + n, maxn)
+            np.testing.assert_array_equal(packed, g[f"packed_{i}"])
+            assert length == int(g[f"length_{i}"])
+            t0 += n
+
+
+def test_serving_layout_matches_reference_fixture(golden):
+    g = golden("serving_tiny_multi")
+    c = cases.MEMORY_CASES["tiny_multi"]
+    p = cases.memory_params("tiny_multi")
+    for n in c["ngrams"]:
+        st = om.serving_table(p[f"tables.ngram_{n}.weight"], c["routes"], n, c["bits"])
+        np.testing.assert_array_equal(st[g[f"rows_idx_{n}"]], g[f"rows_{n}"])
+    # the serving tokens are the v2 tokens (serving/layout.py:15-17)
+    np.testing.assert_array_equal(g["tokens"], g["tokens_v2"])
+
+
+def test_surrogate_backward_matches_reference_fixture(golden):
+    """The training lookup's backward restated (lngram_v2.py:326-447) against the reference's autograd."""
+    from tests.golden.make_golden import SURROGATE_CASES
+
+    g = golden("surrogate_backward")
+    for i, (case, mode, rs, re) in enumerate(SURROGATE_CASES):
+        c = cases.MEMORY_CASES[case]
+        p = cases.memory_params(case)
+        inp = cases.memory_inputs(case)
+        tables = {n: p[f"tables.ngram_{n}.weight"] for n in c["ngrams"]}
+        gq, tg = om.surrogate_backward(g[f"c{i}_grad_tokens"], g[f"c{i}_codes"].astype(np.int64), g[f"c{i}_q"],
+                                       tables, c["ngrams"], c["bits"], rs, re, 0.7, 1.3, mode == "exact",
+                                       inp.get("segment_ids"), inp.get("valid_tokens"))
+        want = g[f"c{i}_grad_q"][:, :, rs:re]
+        assert_fp32_close(gq, want, rtol=1e-4, what=f"case {i} grad_q")
+        assert not g[f"c{i}_grad_q"][:, :, :rs].any() and not g[f"c{i}_grad_q"][:, :, re:].any()
+        for n in c["ngrams"]:
+            rows = g[f"c{i}_rows_{n}"]
+            got = np.stack([tg[n].get(int(r), np.zeros(c["mem_dim"], np.float32)) for r in rows])
+            assert_fp32_close(got, g[f"c{i}_grad_table_{n}"], what=f"case {i} table {n} grad")
+            assert set(int(r) for r, v in tg[n].items() if np.any(v != 0)) <= set(rows.tolist())

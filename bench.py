@@ -408,9 +408,11 @@ def time_e2e(mem, inputs, args, world) -> dict:
     hosts = [h.cpu().pin_memory() for h, _ in inputs]
     out_host = torch.empty(SB["B"], SB["T"], SB["d"], dtype=torch.bfloat16).pin_memory()
 
+    groups = int(getattr(args, "e2e_groups", E2E_GROUPS))
+
     def step(i):
         mem.forward_host(hosts[i % 2], norm_weight=mem.attn_norm_weight, norm_eps=1e-5, out=out_host,
-                         groups=E2E_GROUPS, synchronize=False)
+                         groups=groups, synchronize=False)
 
     for i in range(args.warmup):
         step(i)
@@ -427,7 +429,7 @@ def time_e2e(mem, inputs, args, world) -> dict:
     return {"value": M * world * args.steps / (ms / 1e3), "unit": "positions/s",
             "h2d_bytes_per_step": hosts[0].numel() * 2, "d2h_bytes_per_step": out_host.numel() * 2,
             "ms_per_step": ms / args.steps,
-            "call": f"LngramMemory.forward_host(h, norm_weight=attn_norm.weight, groups={E2E_GROUPS}): h in, "
+            "call": f"LngramMemory.forward_host(h, norm_weight=attn_norm.weight, groups={groups}): h in, "
                     "h_norm on the device, output out; copies overlapped with the forward"}
 
 
@@ -758,9 +760,11 @@ def time_tree_attend(pkg, mem, cache, node_inputs, parent, steps, flush):
 SCALED = dict(B=64, T=4096, d=1024, routes=184, bits=5, ngrams=(4,), mem_dim=136, q_heads=16, kv_heads=4, head_dim=64)
 # sequence groups of the route-sharded forward: each group's reduce-scatter overlaps the next group's gather
 SCALED_CHUNKS = 4
+# route shards of the scaled table at N > 1 (the rest of the GPUs split the sequences)
+SCALED_ROUTE_SHARDS = 2
 
 
-def build_scaled_shard(pkg, dev, rank: int, world: int, seed: int = 0):
+def build_scaled_shard(pkg, dev, rank: int, world: int, seed: int = 0, group=None, group_m=None):
     """This rank's block of routes of the scaled layer (tables N(0, 0.02) bf16, filled route chunk by
     route chunk from a seed per global route, so every world size holds the same table), with the
     readout weights and router rows seeded identically on every rank."""
@@ -787,7 +791,7 @@ def build_scaled_shard(pkg, dev, rank: int, world: int, seed: int = 0):
                                        .to(torch.bfloat16))
         router = torch.randn(c["routes"] * c["bits"], c["d"], device=dev, generator=g) * 0.02
         mem.router.weight.copy_(router[r0 * c["bits"]:r1 * c["bits"]])
-    return mem, pkg.RouteShardedMemory(mem, rank, world, routes_total=c["routes"])
+    return mem, pkg.RouteShardedMemory(mem, rank, world, group=group, routes_total=c["routes"], group_m=group_m)
 
 
 def run_scaled(args, rank, world, local) -> dict:
@@ -798,17 +802,24 @@ def run_scaled(args, rank, world, local) -> dict:
     dev = torch.device("cuda", local)
     c = SCALED
     B, T, d = c["B"], c["T"], c["d"]
-    mem, shard = build_scaled_shard(pkg, dev, rank, world)
+    # route x data grid: route_shards ranks split the routes of one layer copy and share a block of
+    # sequences; the world / route_shards such groups split the batch (no exchange between groups)
+    rs = min(int(getattr(args, "route_shards", SCALED_ROUTE_SHARDS)), world)
+    place = pkg.sharded.route_data_grid(world, rs, rank) if world > 1 else pkg.sharded.GridPlace(0, 1, 1)
+    mem, shard = build_scaled_shard(pkg, dev, place.route_index, rs, group=place.group, group_m=place.group_m)
     g = torch.Generator(device=dev).manual_seed(500)        # the same hidden states on every rank
     h = torch.randn(B, T, d, device=dev, generator=g).to(torch.bfloat16)
     hf = h.float()
     hn = (hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + 1e-5)).to(torch.bfloat16)
     del hf
     M = B * T
-    if world == 1:   # the whole table on one GPU: the fused single-GPU forward
-        out = torch.empty(B, T, d, device=dev, dtype=torch.bfloat16)
+    Bl = B // place.data_shards                             # this rank's route group's sequences
+    h, hn = h[place.data_index * Bl:(place.data_index + 1) * Bl], hn[place.data_index * Bl:(place.data_index + 1) * Bl]
+    Ml = Bl * T
+    if rs == 1:   # the whole table on every GPU of the group: the fused single-GPU forward
+        out = torch.empty(Bl, T, d, device=dev, dtype=torch.bfloat16)
         ws = torch.empty(lib.library().lng_memory_workspace_bytes(mem.module.tables_desc(),
-                                                                  mem.module.readout_desc(mem.router.weight), M),
+                                                                  mem.module.readout_desc(mem.router.weight), Ml),
                          device=dev, dtype=torch.uint8)
 
         def step(i):
@@ -840,29 +851,29 @@ def run_scaled(args, rank, world, local) -> dict:
         codes = mem.route_codes(hn)
         f = m.folded()
         qd = m.readout_num_heads * m.route_token_dim
-        rs = torch.empty(M, device=dev, dtype=torch.float32)
+        rsq = torch.empty(Ml, device=dev, dtype=torch.float32)
         L = lib.library()
         s = lib.stream_ptr()
-        lib.check(L.lng_rms_rows(h.data_ptr(), lib.BF16, M, d, m.eps, rs.data_ptr(), s))
-        qa = m._linear(h.view(M, d), f["w_qk"])
-        u = torch.empty(M, m.readout_num_heads, m.route_token_dim, device=dev, dtype=torch.float32)
-        ml = torch.empty(M, m.readout_num_heads, device=dev, dtype=torch.float32)
+        lib.check(L.lng_rms_rows(h.data_ptr(), lib.BF16, Ml, d, m.eps, rsq.data_ptr(), s))
+        qa = m._linear(h.reshape(Ml, d), f["w_qk"])
+        u = torch.empty(Ml, m.readout_num_heads, m.route_token_dim, device=dev, dtype=torch.float32)
+        ml = torch.empty(Ml, m.readout_num_heads, device=dev, dtype=torch.float32)
         ll = torch.empty_like(ml)
         desc = shard._tables_desc()
-        att_ms = kernel_ms(lambda: lib.check(L.lng_route_attend(desc, codes.data_ptr(), lib.U8, B, T, 0, None, None,
+        att_ms = kernel_ms(lambda: lib.check(L.lng_route_attend(desc, codes.data_ptr(), lib.U8, Bl, T, 0, None, None,
                                                                 None, 0, 0, Rl, m.readout_num_heads, m.eps,
-                                                                shard.sink_logit, qa.data_ptr(), rs.data_ptr(),
+                                                                shard.sink_logit, qa.data_ptr(), rsq.data_ptr(),
                                                                 u.data_ptr(), lib.F32, 1, ml.data_ptr(),
                                                                 ll.data_ptr(), s)), 3)
         del u, qa
-        phases = time_scaled_phases(pkg, shard, h, hn, world) if world > 1 else None
+        phases = time_scaled_phases(pkg, shard, h, hn, world) if rs > 1 else None
         launches = count_launches(lambda: step(0), fallback=0)
         dev_err = lib.device_error(clear=True)
     if dev_err:
         raise RuntimeError(f"device error word {dev_err} after the timed region")
     pk = peaks()
     Dt = m.route_token_dim
-    att_bytes = M * (Rl * Dt * 2 + qd * 2 + m.readout_num_heads * (Dt + 2) * 4 + Rl)
+    att_bytes = Ml * (Rl * Dt * 2 + qd * 2 + m.readout_num_heads * (Dt + 2) * 4 + Rl)
     achieved = att_bytes / (att_ms / 1e3) / 1e9
     table_gb = c["routes"] * (1 << c["bits"]) ** c["ngrams"][0] * c["mem_dim"] * 2 / 1e9
     return {
@@ -873,8 +884,10 @@ def run_scaled(args, rank, world, local) -> dict:
         "config": {"workload": "scaled", "batch": B, "seq_len": T, "d_model": d, "routes": c["routes"],
                    "routes_per_gpu": Rl, "bits": c["bits"], "ngrams": list(c["ngrams"]), "mem_dim": c["mem_dim"],
                    "table_gb": round(table_gb, 1),
-                   "parallelism": f"route-sharded (NCCL max all-reduce + bf16 reduce-scatter by sequence blocks, "
-                                  f"{SCALED_CHUNKS} overlapped groups)" if world > 1 else "single GPU (whole table)",
+                   "parallelism": (f"route {rs} x data {place.data_shards}: route-sharded groups of {rs} GPUs (NCCL "
+                                   f"max all-reduce + bf16 reduce-scatter by sequence blocks, {SCALED_CHUNKS} "
+                                   f"overlapped groups), sequences split across the groups")
+                                  if world > 1 else "single GPU (whole table)",
                    "l2": f"inputs larger than L2 ({table_gb:.0f} GB table, 1.07 GB h + h_norm)"},
         "roofline": {"bound": "hbm", "kernel": "attend_mma_kernel (partial mode, this rank's routes)",
                      "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
@@ -882,9 +895,9 @@ def run_scaled(args, rank, world, local) -> dict:
                      "ms_per_launch": att_ms},
         "gpu_launches": launches["per_step"] * args.steps, "launch_count": launches,
         "phases_ms": phases,
-        "nccl_bytes_per_rank": None if world == 1 else {
-            "all_reduce_max_fp32": M * m.readout_num_heads * 4,
-            "reduce_scatter_sent_bf16": int(M * m.readout_num_heads * (Dt + 1) * 2 * (world - 1) / world),
+        "nccl_bytes_per_rank": None if rs == 1 else {
+            "all_reduce_max_fp32": Ml * m.readout_num_heads * 4,
+            "reduce_scatter_sent_bf16": int(Ml * m.readout_num_heads * (Dt + 1) * 2 * (rs - 1) / rs),
             "note": "per forward; each of the SCALED_CHUNKS groups moves its share"},
         "clocks": clk.summary(),
     }
@@ -919,10 +932,10 @@ def time_scaled_phases(pkg, shard, h, hn, world) -> dict:
         tm("rescale", lambda: shard.rescale(mloc, mg, pack))
     else:
         mloc, lloc, u = tm("partial (codes + rms + query gemm + gather)", lambda: shard.partial(hc, xc))
-        mg = tm("all_reduce_max", lambda: pkg.sharded.all_reduce_max(mloc.clone()))
+        mg = tm("all_reduce_max", lambda: pkg.sharded.all_reduce_max(mloc.clone(), shard.group_m or shard.group))
         pack = tm("pack", lambda: shard.pack(mloc, mg, lloc, u))
-    mine = tm("reduce_scatter", lambda: pkg.sharded.reduce_scatter_rows(pack.view(Bc * T, -1)))
-    tm("finish (unpack + output gemm + conv)", lambda: shard.finish(mine, Bc // world, T))
+    mine = tm("reduce_scatter", lambda: pkg.sharded.reduce_scatter_rows(pack.view(Bc * T, -1), shard.group))
+    tm("finish (unpack + output gemm + conv)", lambda: shard.finish(mine, Bc // shard.world, T))
     return res
 
 
@@ -1070,6 +1083,9 @@ def main(argv=None) -> int:
     ap.add_argument("--batch", type=int, default=SB["B"], help="sb_prefill sequences per GPU (32 = the SB configuration; "
                     "smaller for ncu)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-groups", type=int, default=E2E_GROUPS, help="sequence groups of the pipelined e2e call")
+    ap.add_argument("--route-shards", type=int, default=SCALED_ROUTE_SHARDS,
+                    help="scaled table at N > 1: GPUs per route-sharded group (the groups split the sequences)")
     ap.add_argument("--no-extras", action="store_true", help="sb_prefill only: skip the SD-B / tree / scaled "
                     "sub-objects of the default line")
     args = ap.parse_args(argv)

@@ -703,9 +703,11 @@ class LngramMemory(nn.Module):
         The batch is split into ``groups`` groups of whole sequences that flow through three CUDA
         streams -- copy in, forward, copy out -- with two device buffers per stream, so the copy of
         group g + 1 in, the forward of group g and the copy of group g - 1 out run at the same time
-        (PCIe is full duplex).  The caller's current stream is ordered before the first copy and after
-        the last one.  ``synchronize=False`` returns before the copies out have finished: synchronise
-        the current stream before reading ``out``."""
+        (PCIe is full duplex).  The forward follows the caller's pending work on the current stream, and
+        the current stream is ordered after the last copy out; the copies in of ``h`` wait only for their
+        device buffers, so back-to-back calls overlap.  ``synchronize=False`` returns before the copies
+        out have finished: synchronise the current stream before reading ``out``, and do not rewrite
+        ``h`` before then."""
         if self.training and torch.is_grad_enabled():
             raise RuntimeError("lngram_b200 implements the inference forward only")
         if self.router_input != "hidden":
@@ -738,25 +740,28 @@ class LngramMemory(nn.Module):
             self._host_pipe = st
         s_in, s_comp, s_out = st["streams"]
         cur = torch.cuda.current_stream(dev)
+        # the forward reads the module's parameters: it follows the caller's pending work; the copies in
+        # only wait for the buffer slot they overwrite to be free (events kept across calls, so one
+        # call's copies in overlap the previous call's last forward and copies out)
         start = torch.cuda.Event()
         start.record(cur)
-        for s in (s_in, s_comp, s_out):
-            s.wait_event(start)
-        ev_in, ev_comp, ev_out = [], [], []
+        s_comp.wait_event(start)
+        last_comp, last_out = st.setdefault("last_comp", [None, None]), st.setdefault("last_out", [None, None])
+        ev_out = None
         for g in range(groups):
             k = g % 2
             rows = slice(g * Bg, (g + 1) * Bg)
-            if g >= 2:
-                s_in.wait_event(ev_comp[g - 2])       # slot k's inputs were read by group g - 2
+            if last_comp[k] is not None:
+                s_in.wait_event(last_comp[k])        # slot k's inputs were read by an earlier group
             with torch.cuda.stream(s_in):
                 st["h"][k].copy_(h[rows], non_blocking=True)
                 if h_norm is not None:
                     st["hn"][k].copy_(h_norm[rows], non_blocking=True)
-                ev_in.append(torch.cuda.Event())
-                ev_in[-1].record(s_in)
-            s_comp.wait_event(ev_in[g])
-            if g >= 2:
-                s_comp.wait_event(ev_out[g - 2])      # slot k's output was copied out by group g - 2
+                ev_in = torch.cuda.Event()
+                ev_in.record(s_in)
+            s_comp.wait_event(ev_in)
+            if last_out[k] is not None:
+                s_comp.wait_event(last_out[k])       # slot k's output was copied out by an earlier group
             with torch.cuda.stream(s_comp):
                 hd = st["h"][k]
                 if w is not None:
@@ -765,15 +770,16 @@ class LngramMemory(nn.Module):
                                                             _lib.dtype_code(w.dtype), float(norm_eps), ptr(hn),
                                                             _lib.dtype_code(hn.dtype), stream_ptr()), "rms_norm")
                 self.forward(hd, st["hn"][k], out=st["out"][k], workspace=st["ws"])
-                ev_comp.append(torch.cuda.Event())
-                ev_comp[-1].record(s_comp)
-            s_out.wait_event(ev_comp[g])
+                ev_comp = torch.cuda.Event()
+                ev_comp.record(s_comp)
+            last_comp[k] = ev_comp
+            s_out.wait_event(ev_comp)
             with torch.cuda.stream(s_out):
                 out[rows].copy_(st["out"][k], non_blocking=True)
-                ev_out.append(torch.cuda.Event())
-                ev_out[-1].record(s_out)
-        cur.wait_event(ev_out[-1])
-        cur.wait_event(ev_comp[-1])
+                ev_out = torch.cuda.Event()
+                ev_out.record(s_out)
+            last_out[k] = ev_out
+        cur.wait_event(ev_out)                       # copies out run in order on s_out: the last covers all
         if synchronize:
             cur.synchronize()
         return out

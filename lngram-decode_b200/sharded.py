@@ -43,6 +43,31 @@ def route_bounds(routes: int, world: int) -> list[tuple[int, int]]:
     return out
 
 
+class GridPlace:
+    """A rank's place in a route x data grid of ``world`` ranks: ``route_shards`` consecutive ranks hold the
+    route blocks of one layer copy and process the same block of sequences; the ``data_shards`` such groups
+    split the batch by whole sequences (data parallel, no exchange between groups)."""
+
+    def __init__(self, rank: int, world: int, route_shards: int, group=None, group_m=None):
+        self.route_index, self.route_shards = rank % route_shards, route_shards
+        self.data_index, self.data_shards = rank // route_shards, world // route_shards
+        self.group, self.group_m = group, group_m
+
+
+def route_data_grid(world: int, route_shards: int, rank: int) -> GridPlace:
+    """This rank's ``GridPlace`` and the communicators of its route group (one for the state exchange,
+    one for the max all-reduce, so the two do not queue behind each other).  Collective: every rank
+    creates every group, in the same order, as torch.distributed requires."""
+    if route_shards < 1 or world % route_shards:
+        raise ValueError(f"route_shards={route_shards} must divide the world size {world}")
+    groups = []
+    for d in range(world // route_shards):
+        ranks = list(range(d * route_shards, (d + 1) * route_shards))
+        groups.append((dist.new_group(ranks), dist.new_group(ranks)) if route_shards > 1 else (None, None))
+    g, gm = groups[rank // route_shards]
+    return GridPlace(rank, world, route_shards, g, gm)
+
+
 def all_reduce_max(t: Tensor, group=None) -> Tensor:
     if dist.is_initialized() and dist.get_world_size(group) > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
@@ -64,10 +89,14 @@ def reduce_scatter_rows(t: Tensor, group=None) -> Tensor:
 class RouteShardedMemory:
     """One rank's share of a route-sharded ``LngramMemory``."""
 
-    def __init__(self, full: LngramMemory, rank: int, world: int, group=None, routes_total: int | None = None):
+    def __init__(self, full: LngramMemory, rank: int, world: int, group=None, routes_total: int | None = None,
+                 group_m=None):
         """``full`` holds every route (its rows of this rank are sliced out), or -- with
         ``routes_total`` -- only this rank's block of routes already (its sink logit must then be the
-        whole layer's, log(routes_total (1 - mass) / mass))."""
+        whole layer's, log(routes_total (1 - mass) / mass)).  ``rank`` / ``world`` are the position and
+        size of the route group ``group`` (the default group when None); ``group_m`` is a second
+        communicator over the same ranks for the max all-reduce (``route_data_grid`` makes both; without
+        it one is created here, collectively over ``group``'s ranks)."""
         m = full.module
         self.rank, self.world, self.group = int(rank), int(world), group
         self.R_total = int(routes_total) if routes_total is not None else m.num_routes
@@ -102,8 +131,8 @@ class RouteShardedMemory:
         # the max all-reduce runs on its own communicator, so it does not queue behind the previous
         # group's reduce-scatter (collectives of one communicator run in order on one stream);
         # created collectively, so every rank constructs its shard at the same point
-        self.group_m = None
-        if dist.is_initialized() and dist.get_world_size(group) > 1:
+        self.group_m = group_m
+        if group_m is None and world > 1 and dist.is_initialized() and dist.get_world_size(group) > 1:
             ranks = dist.get_process_group_ranks(group) if group is not None else list(range(dist.get_world_size()))
             self.group_m = dist.new_group(ranks)
         self.ss = {}

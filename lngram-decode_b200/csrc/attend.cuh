@@ -649,4 +649,5 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
   }
 }
 
+
 }  // namespace lng

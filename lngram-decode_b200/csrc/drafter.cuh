@@ -96,6 +96,9 @@ struct lng_drafter {
   // grow-on-demand device workspace
   void* ws = nullptr;
   size_t ws_bytes = 0;
+  // draft_batch replays: one CUDA graph per (prefix, output, shape, workspace) seen before (null:
+  // that launch sequence could not be captured, run it directly)
+  std::map<std::tuple<const void*, const void*, int64_t, int64_t, int64_t, const void*>, cudaGraphExec_t> graphs;
 
   lng_tables tables() const {
     lng_tables t{};
@@ -113,6 +116,8 @@ struct lng_drafter {
   }
   bool has_sketch() const { return K > 0 && cap > 0; }
   ~lng_drafter() {
+    for (auto& kv : graphs)
+      if (kv.second) cudaGraphExecDestroy(kv.second);
     for (void* p : owned) cudaFree(p);
     if (ws) cudaFree(ws);
     if (stream) cudaStreamDestroy(stream);
@@ -856,43 +861,26 @@ extern "C" int lng_drafter_trace(lng_drafter* d, const int64_t* tokens_host, int
   return LNG_OK;
 }
 
-extern "C" int lng_drafter_draft_batch(lng_drafter* d, const int64_t* prefix, int64_t nseq, int64_t plen, int64_t gamma,
-                                       int64_t* tokens_out, lng_stream_t stream) {
-  LNG_REQUIRE(d, "NULL drafter");
-  LNG_REQUIRE(nseq >= 0 && plen >= 1 && gamma >= 1, "need nseq >= 0, plen >= 1, gamma >= 1");
-  if (nseq == 0) return LNG_OK;
-  LNG_REQUIRE(prefix && tokens_out, "NULL pointer");
-  std::lock_guard<std::mutex> lk(d->mu);
-  const int64_t R = d->R, N = d->N, P = plen + gamma;  // positions per sequence in the working buffers
-  // The drafts' code windows reach back n_max - 1 positions from the last prefix token and the embed2
-  // router reads a position's own and previous token (and, for SD-C, its SSM state), so only the last
-  // `tail` prefix positions need codes; earlier rows of `codes` are never read.  The SSM state itself
-  // runs over the whole prefix.
-  int64_t n_max = 1;
-  for (int o = 0; o < d->n_orders; ++o) n_max = std::max<int64_t>(n_max, d->orders[o]);
-  const int64_t tail = std::min<int64_t>(plen, n_max);
-  ReadoutBufs b;
-  void* extra = nullptr;
-  const size_t tok_b = al256(size_t(nseq * (P + 1)) * 8), prev_b = al256(size_t(nseq * std::max<int64_t>(2 * tail, 2)) * 8),
-               code_b = al256(size_t(nseq * P * R)), u_b = al256(size_t(N > 0 ? nseq * plen * N : 0) * 4),
-               st_b = al256(size_t(nseq * tail * N) * 4), cur_b = al256(size_t(2 * nseq * N) * 4);
-  const int64_t M = nseq * tail;
-  int st = drafter_ws(d, std::max<int64_t>(M, N > 0 ? std::min<int64_t>(nseq * plen, 8192) : M), 1, &b,
-                      tok_b + prev_b + code_b + u_b + st_b + cur_b, &extra);
-  if (st) return st;
+namespace lng {
+
+struct DraftBatchPlan {
+  int64_t nseq, plen, gamma, tail, P;
+  size_t tok_b, prev_b, code_b, u_b, st_b, cur_b;
+};
+
+// Every device operation of one draft_batch call on d->stream (the workspace already sized).
+static int enqueue_draft_batch(lng_drafter* d, const DraftBatchPlan& pl, const int64_t* prefix, int64_t* tokens_out,
+                               ReadoutBufs& b, void* extra) {
+  const int64_t R = d->R, N = d->N, nseq = pl.nseq, plen = pl.plen, gamma = pl.gamma, tail = pl.tail, P = pl.P;
+  int st = LNG_OK;
   unsigned char* ex = static_cast<unsigned char*>(extra);
   int64_t* toks = reinterpret_cast<int64_t*>(ex);  // [nseq, P + 1]: toks[s, 0] = -1, toks[s, 1 + p] = token p
-  int64_t* scratch_i = reinterpret_cast<int64_t*>(ex + tok_b);  // [2, nseq * tail]: current, previous tokens
-  uint8_t* codes = ex + tok_b + prev_b;             // [nseq, P, R]
-  float* u = reinterpret_cast<float*>(ex + tok_b + prev_b + code_b);                   // [nseq, plen, N]
-  float* tail_states = reinterpret_cast<float*>(ex + tok_b + prev_b + code_b + u_b);   // [nseq, tail, N]
-  float* s_cur = reinterpret_cast<float*>(ex + tok_b + prev_b + code_b + u_b + st_b);  // [nseq, N] x 2
+  int64_t* scratch_i = reinterpret_cast<int64_t*>(ex + pl.tok_b);  // [2, nseq * tail]: current, previous tokens
+  uint8_t* codes = ex + pl.tok_b + pl.prev_b;             // [nseq, P, R]
+  float* u = reinterpret_cast<float*>(ex + pl.tok_b + pl.prev_b + pl.code_b);                       // [nseq, plen, N]
+  float* tail_states = reinterpret_cast<float*>(ex + pl.tok_b + pl.prev_b + pl.code_b + pl.u_b);    // [nseq, tail, N]
+  float* s_cur = reinterpret_cast<float*>(ex + pl.tok_b + pl.prev_b + pl.code_b + pl.u_b + pl.st_b);  // [nseq, N] x 2
   float* s_next = s_cur + nseq * N;
-  cudaStream_t us = reinterpret_cast<cudaStream_t>(stream);
-  cudaEvent_t ev;
-  LNG_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
-  LNG_CUDA(cudaEventRecord(ev, us));
-  LNG_CUDA(cudaStreamWaitEvent(d->stream, ev, 0));
   // token matrix with a -1 column for the start vector, then prefix codes in one batched pass
   LNG_CUDA(cudaMemsetAsync(toks, 0xff, size_t(nseq * (P + 1)) * 8, d->stream));
   LNG_CUDA(cudaMemcpy2DAsync(toks + 1, size_t(P + 1) * 8, prefix, size_t(plen) * 8, size_t(plen) * 8, size_t(nseq),
@@ -955,6 +943,82 @@ extern "C" int lng_drafter_draft_batch(lng_drafter* d, const int64_t* prefix, in
       if (st) return st;
       LNG_CUDA(cudaMemcpy2DAsync(codes + (tpos + 1) * R, size_t(P * R), dense, size_t(R), size_t(R), size_t(nseq),
                                  cudaMemcpyDeviceToDevice, d->stream));
+    }
+  }
+  return LNG_OK;
+}
+
+}  // namespace lng
+
+extern "C" int lng_drafter_draft_batch(lng_drafter* d, const int64_t* prefix, int64_t nseq, int64_t plen, int64_t gamma,
+                                       int64_t* tokens_out, lng_stream_t stream) {
+  LNG_REQUIRE(d, "NULL drafter");
+  LNG_REQUIRE(nseq >= 0 && plen >= 1 && gamma >= 1, "need nseq >= 0, plen >= 1, gamma >= 1");
+  if (nseq == 0) return LNG_OK;
+  LNG_REQUIRE(prefix && tokens_out, "NULL pointer");
+  std::lock_guard<std::mutex> lk(d->mu);
+  const int64_t R = d->R, N = d->N;
+  // The drafts' code windows reach back n_max - 1 positions from the last prefix token and the embed2
+  // router reads a position's own and previous token (and, for SD-C, its SSM state), so only the last
+  // `tail` prefix positions need codes; earlier rows of `codes` are never read.  The SSM state itself
+  // runs over the whole prefix.
+  int64_t n_max = 1;
+  for (int o = 0; o < d->n_orders; ++o) n_max = std::max<int64_t>(n_max, d->orders[o]);
+  DraftBatchPlan pl;
+  pl.nseq = nseq;
+  pl.plen = plen;
+  pl.gamma = gamma;
+  pl.tail = std::min<int64_t>(plen, n_max);
+  pl.P = plen + gamma;  // positions per sequence in the working buffers
+  pl.tok_b = al256(size_t(nseq * (pl.P + 1)) * 8);
+  pl.prev_b = al256(size_t(nseq * std::max<int64_t>(2 * pl.tail, 2)) * 8);
+  pl.code_b = al256(size_t(nseq * pl.P * R));
+  pl.u_b = al256(size_t(N > 0 ? nseq * plen * N : 0) * 4);
+  pl.st_b = al256(size_t(nseq * pl.tail * N) * 4);
+  pl.cur_b = al256(size_t(2 * nseq * N) * 4);
+  const int64_t M = nseq * pl.tail;
+  ReadoutBufs b;
+  void* extra = nullptr;
+  int st = drafter_ws(d, std::max<int64_t>(M, N > 0 ? std::min<int64_t>(nseq * plen, 8192) : M), 1, &b,
+                      pl.tok_b + pl.prev_b + pl.code_b + pl.u_b + pl.st_b + pl.cur_b, &extra);
+  if (st) return st;
+  cudaStream_t us = reinterpret_cast<cudaStream_t>(stream);
+  cudaEvent_t ev;
+  LNG_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+  LNG_CUDA(cudaEventRecord(ev, us));
+  LNG_CUDA(cudaStreamWaitEvent(d->stream, ev, 0));
+  // The same call again (same buffers, shape and workspace) replays the graph of its launches (about
+  // sixty small kernels and copies per gamma = 4 draft): launch overhead instead of launch latency.
+  const auto key = std::make_tuple(static_cast<const void*>(prefix), static_cast<const void*>(tokens_out), nseq, plen,
+                                   gamma, static_cast<const void*>(d->ws));
+  auto it = d->graphs.find(key);
+  if (it != d->graphs.end() && it->second) {
+    LNG_CUDA(cudaGraphLaunch(it->second, d->stream));
+  } else {
+    st = enqueue_draft_batch(d, pl, prefix, tokens_out, b, extra);
+    if (st) {
+      cudaEventDestroy(ev);
+      return st;
+    }
+    if (it == d->graphs.end()) {
+      // capture the same launches for the next call; a sequence that cannot be captured runs directly
+      if (d->graphs.size() >= 16) {
+        for (auto& kv : d->graphs)
+          if (kv.second) cudaGraphExecDestroy(kv.second);
+        d->graphs.clear();
+      }
+      cudaGraphExec_t exec = nullptr;
+      cudaGraph_t graph = nullptr;
+      if (cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+        const int cst = enqueue_draft_batch(d, pl, prefix, tokens_out, b, extra);
+        const cudaError_t ce = cudaStreamEndCapture(d->stream, &graph);
+        if (cst == LNG_OK && ce == cudaSuccess && graph &&
+            cudaGraphInstantiate(&exec, graph, 0) != cudaSuccess)
+          exec = nullptr;
+        if (graph) cudaGraphDestroy(graph);
+      }
+      (void)cudaGetLastError();  // a failed capture leaves no error behind for the next call
+      d->graphs[key] = exec;
     }
   }
   LNG_CUDA(cudaEventRecord(ev, d->stream));

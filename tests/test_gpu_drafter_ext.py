@@ -185,3 +185,29 @@ def test_extension_class_api(lngram):
     assert torch.equal(roi, oi)
     fin = torch.isfinite(rol)
     assert_fp32_close(ol[fin].numpy(), rol[fin].numpy(), rtol=1e-4, what="C++ class trace logits")
+
+
+@pytest.mark.parametrize("case,sketch", [("tiny_ssm", True), ("tiny", False)])
+def test_draft_batch_replays_read_new_prefixes(lngram, case, sketch):
+    """Repeated draft_batch calls on the same buffers (the library replays a captured graph of the first
+    call's launches) draft from the prefix contents of each call, as fresh per-sequence drafts do."""
+    d, _, _ = pair(lngram, case, sketch)
+    nseq, plen, gamma = 5, 11, 4
+    prefix = torch.empty(nseq, plen, dtype=torch.int64, device=DEV)
+    out = torch.empty(nseq, gamma, dtype=torch.int64, device=DEV)
+    for it in range(4):
+        p = np.stack([cases.draft_tokens(case, plen, seed=100 * it + s) for s in range(nseq)])
+        prefix.copy_(torch.from_numpy(p))
+        got = d.draft_batch(prefix, gamma, out=out).cpu().numpy()
+        for s in range(nseq):
+            d.reset()
+            d.commit(p[s].tolist())
+            assert got[s].tolist() == d.draft(gamma).tokens, (it, s)
+    # another shape on the same drafter, then the first again
+    short = d.draft_batch(prefix[:3, 4:], 2).cpu().numpy()
+    for s in range(3):
+        d.reset()
+        d.commit(p[s, 4:].tolist())
+        assert short[s].tolist() == d.draft(2).tokens, s
+    again = d.draft_batch(prefix, gamma, out=out).cpu().numpy()
+    assert np.array_equal(again, got)

@@ -3,7 +3,7 @@
 // drafting/cpu/drafter.cpp:537-556 ((logit desc, id asc)).
 //
 // One CTA owns 256 vocabulary rows (two 128-lane TMEM accumulators, M side) and BN draft rows
-// (N side).  The fp32 draft rows are split once (split_rows_bf16x3_kernel) into three bf16 parts
+// (N side; for BN <= 64 the three parts of the draft rows form one N = 3 BN operand).  The fp32 draft rows are split once (split_rows_bf16x3_kernel) into three bf16 parts
 // h = h1 + h2 + h3 (exact to ~2^-24 relative); the vocabulary tile and the three parts of each
 // 64-element k block arrive by TMA (128-byte swizzle, K-major),
 // so logits = E . h1 + E . h2 + E . h3 accumulate in fp32 with every bf16 x bf16 product exact:
@@ -29,7 +29,13 @@ struct LtCfg {
   static constexpr uint32_t B_PART = BN * TC_BK * 2;       // one bf16 part of the draft rows
   static constexpr uint32_t STAGE_BYTES = A_BYTES + 3 * B_PART;
   static constexpr int STAGES = (224 * 1024) / STAGE_BYTES > 6 ? 6 : (224 * 1024) / STAGE_BYTES;
-  static constexpr uint32_t TMEM_COLS = 2 * BN;
+  // The three parts sit back to back in a stage (3 BN rows of 128 bytes), so while 3 BN <= 256 one
+  // MMA of N = 3 BN multiplies the vocabulary tile by all of them, each part into its own column
+  // block, summed in the epilogue: a third of the MMA instructions, each three times as wide.
+  static constexpr bool STACKED = 3 * BN <= 256;
+  static constexpr uint32_t ACC_COLS = STACKED ? 3 * BN : BN;  // accumulator columns per vocabulary half
+  static constexpr uint32_t TMEM_COLS = 2 * ACC_COLS <= 32 ? 32 : 2 * ACC_COLS <= 64 ? 64 : 2 * ACC_COLS <= 128 ? 128
+                                        : 2 * ACC_COLS <= 256 ? 256 : 512;
   static constexpr size_t SMEM = size_t(STAGES) * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
   static_assert(STAGES >= 2, "pipeline needs two stages");
   static_assert(B_PART % 1024 == 0 && A_BYTES % 1024 == 0, "swizzle atoms must stay 1024-byte aligned");
@@ -118,8 +124,8 @@ __global__ void __launch_bounds__(128, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {  // MMA issuer: 4 k steps x 3 parts x 2 vocabulary halves per stage
-      constexpr uint32_t idesc = umma_idesc_bf16(128, BN);
+    if (lane == 0) {  // MMA issuer: 4 k steps x (1 stacked or 3) parts x 2 vocabulary halves per stage
+      constexpr uint32_t idesc = umma_idesc_bf16(128, int(Cfg::STACKED ? 3 * BN : BN));
       for (int kb = 0; kb < KB; ++kb) {
         const int s = kb % STAGES;
         if (!mbar_wait_bounded(&full[s], uint32_t((kb / STAGES) & 1), &g_error_word, DEV_ERR_WAIT_TIMEOUT)) break;
@@ -129,11 +135,11 @@ __global__ void __launch_bounds__(128, 1)
 #pragma unroll
         for (int kk = 0; kk < TC_BK / 16; ++kk) {
 #pragma unroll
-          for (int part = 0; part < 3; ++part) {
+          for (int part = 0; part < (Cfg::STACKED ? 1 : 3); ++part) {
             const uint64_t db = umma_desc_sw128(st + Cfg::A_BYTES + part * Cfg::B_PART);
             const uint32_t acc = (kb | kk | part) != 0 ? 1u : 0u;
             umma_bf16(tmem, da0 + uint64_t(2 * kk), db + uint64_t(2 * kk), idesc, acc);
-            umma_bf16(tmem + uint32_t(BN), da1 + uint64_t(2 * kk), db + uint64_t(2 * kk), idesc, acc);
+            umma_bf16(tmem + Cfg::ACC_COLS, da1 + uint64_t(2 * kk), db + uint64_t(2 * kk), idesc, acc);
           }
         }
         umma_commit(&empty[s]);
@@ -157,7 +163,19 @@ __global__ void __launch_bounds__(128, 1)
     float xa[16] = {}, xb[16] = {};
     if (acc_ok) {
       tmem_ld16(tl + uint32_t(c), xa);
-      tmem_ld16(tl + uint32_t(BN + c), xb);
+      tmem_ld16(tl + Cfg::ACC_COLS + uint32_t(c), xb);
+      if (Cfg::STACKED) {  // logits = part 1 + (part 2 + part 3): the small corrections first
+        float ya[16], yb[16], za[16], zb[16];
+        tmem_ld16(tl + uint32_t(BN + c), ya);
+        tmem_ld16(tl + Cfg::ACC_COLS + uint32_t(BN + c), yb);
+        tmem_ld16(tl + uint32_t(2 * BN + c), za);
+        tmem_ld16(tl + Cfg::ACC_COLS + uint32_t(2 * BN + c), zb);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          xa[i] += ya[i] + za[i];
+          xb[i] += yb[i] + zb[i];
+        }
+      }
     }
 #pragma unroll
     for (int i = 0; i < 16; ++i) {

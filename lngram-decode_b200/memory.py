@@ -703,11 +703,12 @@ class LngramMemory(nn.Module):
         The batch is split into ``groups`` groups of whole sequences that flow through three CUDA
         streams -- copy in, forward, copy out -- with two device buffers per stream, so the copy of
         group g + 1 in, the forward of group g and the copy of group g - 1 out run at the same time
-        (PCIe is full duplex).  The forward follows the caller's pending work on the current stream, and
-        the current stream is ordered after the last copy out; the copies in of ``h`` wait only for their
-        device buffers, so back-to-back calls overlap.  ``synchronize=False`` returns before the copies
-        out have finished: synchronise the current stream before reading ``out``, and do not rewrite
-        ``h`` before then."""
+        (PCIe is full duplex).  The forward follows the caller's pending work on the current stream; the
+        copies in of ``h`` wait only for their device buffers.  ``synchronize=True`` returns once ``out``
+        is written.  ``synchronize=False`` returns with the copies out in flight and leaves the current
+        stream unordered after them, so a next call's copies in and forwards overlap this call's last
+        forward and copies out; call ``wait_host()`` (orders the current stream after the last copy out)
+        or ``torch.cuda.synchronize()`` before reading ``out``, and do not rewrite ``h`` before then."""
         if self.training and torch.is_grad_enabled():
             raise RuntimeError("lngram_b200 implements the inference forward only")
         if self.router_input != "hidden":
@@ -779,10 +780,17 @@ class LngramMemory(nn.Module):
                 ev_out = torch.cuda.Event()
                 ev_out.record(s_out)
             last_out[k] = ev_out
-        cur.wait_event(ev_out)                       # copies out run in order on s_out: the last covers all
+        st["tail"] = ev_out                          # copies out run in order on s_out: the last covers all
         if synchronize:
-            cur.synchronize()
+            cur.wait_event(ev_out)
+            ev_out.synchronize()
         return out
+
+    def wait_host(self) -> None:
+        """Order the current stream after the last copy out of ``forward_host`` (no-op before the first)."""
+        st = getattr(self, "_host_pipe", None)
+        if st is not None and st.get("tail") is not None:
+            torch.cuda.current_stream(st["h"][0].device).wait_event(st["tail"])
 
     def forward(self, h: Tensor, h_norm: Tensor, router_in: Tensor | None = None, *, codes_out: Tensor | None = None,
                 out: Tensor | None = None, workspace: Tensor | None = None) -> Tensor:

@@ -80,7 +80,14 @@ def test_forward_host_equals_device_forward(lngram, groups):
         got_made = mem.forward_host(h_host, norm_weight=w, norm_eps=1e-5, groups=groups)
         out = torch.empty(B, T, d, dtype=torch.bfloat16).pin_memory()
         mem.forward_host(h_host, norm_weight=w, out=out, groups=groups, synchronize=False)
+        h2 = torch.randn(B, T, d, generator=torch.Generator().manual_seed(5)).to(torch.bfloat16).pin_memory()
+        out2 = torch.empty(B, T, d, dtype=torch.bfloat16).pin_memory()
+        mem.forward_host(h2, norm_weight=w, out=out2, groups=groups, synchronize=False)   # overlaps the first
+        mem.wait_host()
         torch.cuda.current_stream().synchronize()
+        h2d = h2.to(DEV)
+        want2 = torch.cat([mem(h2d[i:i + Bg], lngram.rms_norm(h2d[i:i + Bg], w, 1e-5)) for i in range(0, B, Bg)]).cpu()
+    assert torch.equal(out2, want2)
     assert not got_copied.is_cuda
     assert torch.equal(got_copied, want)
     assert torch.equal(got_made, want)

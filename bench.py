@@ -776,8 +776,10 @@ def time_tree_attend(pkg, mem, cache, node_inputs, parent, steps, flush):
 SCALED = dict(B=64, T=4096, d=1024, routes=184, bits=5, ngrams=(4,), mem_dim=136, q_heads=16, kv_heads=4, head_dim=64)
 # sequence groups of the route-sharded forward: each group's reduce-scatter overlaps the next group's gather
 SCALED_CHUNKS = 4
-# route shards of the scaled table at N > 1 (the rest of the GPUs split the sequences)
-SCALED_ROUTE_SHARDS = 2
+# route shards of the scaled table at N > 1: every GPU (0, the configuration: 23 routes per GPU at 8);
+# the ``route_data_grid`` sub-object uses GRID_ROUTE_SHARDS (the other GPUs split the sequences)
+SCALED_ROUTE_SHARDS = 0
+GRID_ROUTE_SHARDS = 2
 
 
 def build_scaled_shard(pkg, dev, rank: int, world: int, seed: int = 0, group=None, group_m=None):
@@ -820,7 +822,10 @@ def run_scaled(args, rank, world, local) -> dict:
     B, T, d = c["B"], c["T"], c["d"]
     # route x data grid: route_shards ranks split the routes of one layer copy and share a block of
     # sequences; the world / route_shards such groups split the batch (no exchange between groups)
-    rs = min(int(getattr(args, "route_shards", SCALED_ROUTE_SHARDS)), world)
+    rs = int(getattr(args, "route_shards", SCALED_ROUTE_SHARDS)) or world
+    rs = min(rs, world)
+    if world % rs:
+        raise ValueError(f"--route-shards {rs} must divide the {world} GPUs")
     place = pkg.sharded.route_data_grid(world, rs, rank) if world > 1 else pkg.sharded.GridPlace(0, 1, 1)
     mem, shard = build_scaled_shard(pkg, dev, place.route_index, rs, group=place.group, group_m=place.group_m)
     g = torch.Generator(device=dev).manual_seed(500)        # the same hidden states on every rank
@@ -1101,7 +1106,8 @@ def main(argv=None) -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-groups", type=int, default=E2E_GROUPS, help="sequence groups of the pipelined e2e call")
     ap.add_argument("--route-shards", type=int, default=SCALED_ROUTE_SHARDS,
-                    help="scaled table at N > 1: GPUs per route-sharded group (the groups split the sequences)")
+                    help="scaled table at N > 1: GPUs per route-sharded group (the groups split the sequences; "
+                    "0 = all N GPUs, the configuration's layout)")
     ap.add_argument("--no-extras", action="store_true", help="sb_prefill only: skip the SD-B / tree / scaled "
                     "sub-objects of the default line")
     args = ap.parse_args(argv)
@@ -1124,12 +1130,18 @@ def main(argv=None) -> int:
         sub = argparse.Namespace(**vars(args))
         sub.steps, sub.warmup = min(args.steps, 10), max(3, min(args.warmup, 3))
         line["workloads"] = {}
-        for wl in ("sdb_draft", "tree_verify", "scaled"):
+        runs = [("sdb_draft", "sdb_draft", None), ("tree_verify", "tree_verify", None),
+                ("route_sharded", "scaled", 0)]
+        if world > GRID_ROUTE_SHARDS and world % GRID_ROUTE_SHARDS == 0:
+            runs.append(("route_data_grid", "scaled", GRID_ROUTE_SHARDS))
+        for key, wl, shards in runs:
             torch.cuda.empty_cache()
+            if shards is not None:
+                sub.route_shards = shards
             res = globals()[RUNNERS[wl]](sub, rank, world, local)
             if rank == 0 and world == 1 and not args.no_cpu_baseline and wl in cpu_arms:
                 res["cpu_baseline"] = cpu_arms[wl](budget_s=6.0)
-            line["workloads"]["route_sharded" if wl == "scaled" else wl] = summarize(res)
+            line["workloads"][key] = summarize(res)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

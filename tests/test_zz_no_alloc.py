@@ -5,7 +5,7 @@ replayed inside a CUDA graph, or a serving process whose allocator only hands ou
 so the library offers a variant whose scratch lives in a fixed 4 MiB array inside the library.  This
 file checks, through the C ABI, that two calls in a row give exactly what the buffer-taking entry
 point gives, and that sizes beyond the array are refused with a clear error.  It is collected last
-(file name) and also runs alone in a fresh process.
+(file name).
 """
 
 from __future__ import annotations

@@ -34,6 +34,9 @@ struct AttendParams {
   float* m_out;
   float* l_out;
   int rows32;      // every table row index fits int32 (the tensor-core gather's cooperative copies)
+  int64_t route_split;  // the tensor-core kernel's SPLIT form (partial mode 1): block row y takes routes
+                        // [route_start + y split, + split) and writes state y of [gridDim.y, M, ...];
+                        // only y = 0 seeds the sink
 };
 
 // ------------------------------------------------------------------ generic CUDA-core version
@@ -230,7 +233,7 @@ struct AttendMmaCfg {
   static_assert(FIT >= 1, "route token too wide for the tensor-core gather");
 };
 
-template <typename CodeT, typename T, int DT, int WARPS, int STAGES>
+template <typename CodeT, typename T, int DT, int WARPS, int STAGES, bool SPLIT = false>
 __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) {
   using Cfg = AttendMmaCfg<DT>;
   constexpr int C = Cfg::C, KT = Cfg::KT, NTU = Cfg::NTU, ROWB = Cfg::ROWB, SB = Cfg::STAGE_BYTES;
@@ -240,13 +243,19 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
   unsigned char* stage_base = smem_raw + size_t(warp) * STAGES * SB;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw + size_t(WARPS) * STAGES * SB) + warp * STAGES;
 
-  const int nch = int((p.route_end - p.route_start + C - 1) / C);
+  // this block's routes (a route split gives every block row y its own slice and state)
+  // (the unsplit form reads the bounds straight from the parameters, as before the split existed)
+  const int64_t split_lo = SPLIT ? p.route_start + int64_t(blockIdx.y) * p.route_split : 0;
+  const int64_t split_hi = SPLIT ? min(split_lo + p.route_split, p.route_end) : 0;
+#define LNG_RLO (SPLIT ? split_lo : p.route_start)
+#define LNG_RHI (SPLIT ? split_hi : p.route_end)
+  const int nch = int((LNG_RHI - LNG_RLO + C - 1) / C);
   const int64_t gwarp = int64_t(blockIdx.x) * WARPS + warp;
   const int64_t nwarps = int64_t(gridDim.x) * WARPS;
   const int64_t my_items = gwarp < p.M ? (p.M - 1 - gwarp) / nwarps + 1 : 0;
   const int jobs = int(my_items * nch);
   // partial 2 / 4: a route shard whose state leaves the sink to another shard
-  const bool sink_in = p.partial != 2 && p.partial != 4;
+  const bool sink_in = p.partial != 2 && p.partial != 4 && (!SPLIT || blockIdx.y == 0);
   const int mem_dim = int(p.ts.mem_dim);
 
   if (lane == 0) {
@@ -276,8 +285,8 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
     pend_chunk = pf_chunk;
     pend_item = pf_item;
     if (pf_chunk == 0) pend_qs = p.qscale ? __ldg(p.qscale + pf_item) : 1.f;
-    const int64_t r = p.route_start + int64_t(pf_chunk) * C + lane;
-    load_window_codes<CodeT>(p.src, pf_geo, r, r < p.route_end, pend_c);
+    const int64_t r = LNG_RLO + int64_t(pf_chunk) * C + lane;
+    load_window_codes<CodeT>(p.src, pf_geo, r, r < LNG_RHI, pend_c);
     if (++pf_chunk == nch) {
       pf_chunk = 0;
       pf_item += nwarps;
@@ -308,16 +317,16 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
   const bool bulk_lane = !coop;
   auto issue = [&](int s) {
     flush_ss();
-    const int64_t r = p.route_start + int64_t(pend_chunk) * C + lane;
+    const int64_t r = LNG_RLO + int64_t(pend_chunk) * C + lane;
     unsigned char* row_smem = stage_base + s * SB + lane * ROWB;
     int64_t rows[LNG_MAX_ORDERS];
     uint32_t bytes = 0;
 #pragma unroll
     for (int o = 0; o < LNG_MAX_ORDERS; ++o) {
       if (o >= p.ts.n_orders) break;
-      rows[o] = p.src.direct > 0 ? (r < p.route_end ? pend_item * p.src.direct + r : -1)
+      rows[o] = p.src.direct > 0 ? (r < LNG_RHI ? pend_item * p.src.direct + r : -1)
                                  : window_row(pend_c, p.ts.order[o], p.ts.bits, r,
-                                              r < p.route_end && ((pend_geo.omask >> o) & 1u));
+                                              r < LNG_RHI && ((pend_geo.omask >> o) & 1u));
       ss_pend[o] = 0.f;
       if (rows[o] >= 0) {
         if (bulk_lane) bytes += uint32_t(mem_dim * 2);
@@ -508,7 +517,7 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
     // rescaling.
     constexpr float BIG = std::is_same<T, __nv_bfloat16>::value ? 64.f : 4.f;  // f16 P: exp(BIG) * rx < 65504
     const float big2 = sink2 + BIG * LOG2E;
-    const int64_t rbase = p.route_start + int64_t(chunk) * C;
+    const int64_t rbase = LNG_RLO + int64_t(chunk) * C;
     float rxv[4][2];
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt)
@@ -525,12 +534,12 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
         sv[nt][b + 2] = sacc[nt][b + 2] * c;
       }
     }
-    if (rbase + C > p.route_end) {  // the item's last chunk is ragged: routes past the end take no part
+    if (rbase + C > LNG_RHI) {  // the item's last chunk is ragged: routes past the end take no part
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
         for (int h = 0; h < 4; ++h)
-          if (rbase + nt * 8 + t4 * 2 + (h & 1) >= p.route_end) sv[nt][h] = -INFINITY;
+          if (rbase + nt * 8 + t4 * 2 + (h & 1) >= LNG_RHI) sv[nt][h] = -INFINITY;
     }
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt)
@@ -626,14 +635,15 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
             p.m_out[item * p.qh + row] = m_r[i] * LN2;
           }
         } else if (p.partial) {
-          float* uo = static_cast<float*>(p.u) + obase + row * DT;
+          const int64_t ys = SPLIT ? int64_t(blockIdx.y) * p.M * p.qh : 0;  // state y of a route split
+          float* uo = static_cast<float*>(p.u) + ys * DT + obase + row * DT;
 #pragma unroll
           for (int nt = 0; nt < NTU; ++nt) {
             *reinterpret_cast<float2*>(uo + nt * 8 + t4 * 2) = make_float2(uacc[nt][i * 2], uacc[nt][i * 2 + 1]);
           }
           if (t4 == 0) {
-            p.m_out[item * p.qh + row] = m_r[i] * LN2;
-            p.l_out[item * p.qh + row] = l[i];
+            p.m_out[ys + item * p.qh + row] = m_r[i] * LN2;
+            p.l_out[ys + item * p.qh + row] = l[i];
           }
         } else {
           const float inv = 1.f / fmaxf(l[i], 1.17549435e-38f);
@@ -648,6 +658,43 @@ __global__ void __launch_bounds__(WARPS * 32) attend_mma_kernel(AttendParams p) 
     }
   }
 }
+#undef LNG_RLO
+#undef LNG_RHI
 
+// The states of a route split (attend_mma_kernel with route_split, partial mode 1: u unnormalised,
+// m the offset, l the weight sum with the sink in state 0) -> the normalised readout, as the unsplit
+// kernel's mode 0 writes it: u = sum_y e^(m_y - m) u_y / sum_y e^(m_y - m) l_y, m = max_y m_y.
+// One thread per (item, head, 4 dims); y in order, so the result does not depend on the schedule.
+template <typename T>
+__global__ void attend_split_combine_kernel(const float* __restrict__ u, const float* __restrict__ m,
+                                            const float* __restrict__ l, int splits, int64_t M, int qh, int Dt,
+                                            T* __restrict__ out) {
+  const int64_t rows = M * qh;
+  const int q4 = Dt / 4;
+  for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < rows * q4; e += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = e / q4;
+    const int j = int(e - r * q4) * 4;
+    float mx = -INFINITY;
+    for (int y = 0; y < splits; ++y) mx = fmaxf(mx, m[y * rows + r]);
+    float lsum = 0.f, a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    for (int y = 0; y < splits; ++y) {
+      const float ly = l[y * rows + r];
+      if (ly == 0.f) continue;  // no valid route and no sink in this slice
+      const float w = __expf(m[y * rows + r] - mx);
+      const float4 v = *reinterpret_cast<const float4*>(u + (y * rows + r) * Dt + j);
+      lsum = fmaf(w, ly, lsum);
+      a0 = fmaf(w, v.x, a0);
+      a1 = fmaf(w, v.y, a1);
+      a2 = fmaf(w, v.z, a2);
+      a3 = fmaf(w, v.w, a3);
+    }
+    const float inv = 1.f / fmaxf(lsum, 1.17549435e-38f);
+    T* o = out + r * Dt + j;
+    o[0] = from_f32<T>(a0 * inv);
+    o[1] = from_f32<T>(a1 * inv);
+    o[2] = from_f32<T>(a2 * inv);
+    o[3] = from_f32<T>(a3 * inv);
+  }
+}
 
 }  // namespace lng

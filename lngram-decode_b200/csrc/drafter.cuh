@@ -96,9 +96,13 @@ struct lng_drafter {
   // grow-on-demand device workspace
   void* ws = nullptr;
   size_t ws_bytes = 0;
-  // draft_batch replays: one CUDA graph per (prefix, output, shape, workspace) seen before (null:
-  // that launch sequence could not be captured, run it directly)
-  std::map<std::tuple<const void*, const void*, int64_t, int64_t, int64_t, const void*>, cudaGraphExec_t> graphs;
+  // draft_batch replays: per (shape, workspace), the calls seen and the CUDA graph of the launches
+  // (captured at the second call; null: not yet, or the sequence could not be captured)
+  struct BatchGraph {
+    int calls = 0;
+    cudaGraphExec_t exec = nullptr;
+  };
+  std::map<std::tuple<int64_t, int64_t, int64_t, const void*>, BatchGraph> graphs;
 
   lng_tables tables() const {
     lng_tables t{};
@@ -117,7 +121,7 @@ struct lng_drafter {
   bool has_sketch() const { return K > 0 && cap > 0; }
   ~lng_drafter() {
     for (auto& kv : graphs)
-      if (kv.second) cudaGraphExecDestroy(kv.second);
+      if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
     for (void* p : owned) cudaFree(p);
     if (ws) cudaFree(ws);
     if (stream) cudaStreamDestroy(stream);
@@ -865,15 +869,19 @@ namespace lng {
 
 struct DraftBatchPlan {
   int64_t nseq, plen, gamma, tail, P;
-  size_t tok_b, prev_b, code_b, u_b, st_b, cur_b;
+  size_t pre_b, out_b, tok_b, prev_b, code_b, u_b, st_b, cur_b;
+  size_t total() const { return pre_b + out_b + tok_b + prev_b + code_b + u_b + st_b + cur_b; }
 };
 
-// Every device operation of one draft_batch call on d->stream (the workspace already sized).
-static int enqueue_draft_batch(lng_drafter* d, const DraftBatchPlan& pl, const int64_t* prefix, int64_t* tokens_out,
-                               ReadoutBufs& b, void* extra) {
+// Every device operation of one draft_batch call on d->stream (the workspace already sized): from the
+// prefix copy in the workspace to the drafted tokens in the workspace, so a captured graph of it
+// depends on the shape and the workspace only.
+static int enqueue_draft_batch(lng_drafter* d, const DraftBatchPlan& pl, ReadoutBufs& b, void* extra) {
   const int64_t R = d->R, N = d->N, nseq = pl.nseq, plen = pl.plen, gamma = pl.gamma, tail = pl.tail, P = pl.P;
   int st = LNG_OK;
-  unsigned char* ex = static_cast<unsigned char*>(extra);
+  const int64_t* prefix = static_cast<const int64_t*>(extra);                                      // [nseq, plen]
+  int64_t* tokens_out = reinterpret_cast<int64_t*>(static_cast<unsigned char*>(extra) + pl.pre_b);  // [nseq, gamma]
+  unsigned char* ex = static_cast<unsigned char*>(extra) + pl.pre_b + pl.out_b;
   int64_t* toks = reinterpret_cast<int64_t*>(ex);  // [nseq, P + 1]: toks[s, 0] = -1, toks[s, 1 + p] = token p
   int64_t* scratch_i = reinterpret_cast<int64_t*>(ex + pl.tok_b);  // [2, nseq * tail]: current, previous tokens
   uint8_t* codes = ex + pl.tok_b + pl.prev_b;             // [nseq, P, R]
@@ -970,6 +978,8 @@ extern "C" int lng_drafter_draft_batch(lng_drafter* d, const int64_t* prefix, in
   pl.gamma = gamma;
   pl.tail = std::min<int64_t>(plen, n_max);
   pl.P = plen + gamma;  // positions per sequence in the working buffers
+  pl.pre_b = al256(size_t(nseq * plen) * 8);
+  pl.out_b = al256(size_t(nseq * gamma) * 8);
   pl.tok_b = al256(size_t(nseq * (pl.P + 1)) * 8);
   pl.prev_b = al256(size_t(nseq * std::max<int64_t>(2 * pl.tail, 2)) * 8);
   pl.code_b = al256(size_t(nseq * pl.P * R));
@@ -979,48 +989,48 @@ extern "C" int lng_drafter_draft_batch(lng_drafter* d, const int64_t* prefix, in
   const int64_t M = nseq * pl.tail;
   ReadoutBufs b;
   void* extra = nullptr;
-  int st = drafter_ws(d, std::max<int64_t>(M, N > 0 ? std::min<int64_t>(nseq * plen, 8192) : M), 1, &b,
-                      pl.tok_b + pl.prev_b + pl.code_b + pl.u_b + pl.st_b + pl.cur_b, &extra);
+  int st = drafter_ws(d, std::max<int64_t>(M, N > 0 ? std::min<int64_t>(nseq * plen, 8192) : M), 1, &b, pl.total(),
+                      &extra);
   if (st) return st;
   cudaStream_t us = reinterpret_cast<cudaStream_t>(stream);
   cudaEvent_t ev;
   LNG_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
   LNG_CUDA(cudaEventRecord(ev, us));
   LNG_CUDA(cudaStreamWaitEvent(d->stream, ev, 0));
-  // The same call again (same buffers, shape and workspace) replays the graph of its launches (about
-  // sixty small kernels and copies per gamma = 4 draft): launch overhead instead of launch latency.
-  const auto key = std::make_tuple(static_cast<const void*>(prefix), static_cast<const void*>(tokens_out), nseq, plen,
-                                   gamma, static_cast<const void*>(d->ws));
-  auto it = d->graphs.find(key);
-  if (it != d->graphs.end() && it->second) {
-    LNG_CUDA(cudaGraphLaunch(it->second, d->stream));
+  LNG_CUDA(cudaMemcpyAsync(extra, prefix, size_t(nseq * plen) * 8, cudaMemcpyDeviceToDevice, d->stream));
+  // The second call of a shape (same workspace) captures the launches as a CUDA graph and later calls
+  // replay it (about sixty small kernels and copies per gamma = 4 draft): launch overhead instead of
+  // launch latency.  One-off shapes run directly.
+  const auto key = std::make_tuple(nseq, plen, gamma, static_cast<const void*>(d->ws));
+  if (d->graphs.size() >= 16 && !d->graphs.count(key)) {
+    for (auto& kv : d->graphs)
+      if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+    d->graphs.clear();
+  }
+  lng_drafter::BatchGraph& g = d->graphs[key];
+  if (g.exec) {
+    LNG_CUDA(cudaGraphLaunch(g.exec, d->stream));
   } else {
-    st = enqueue_draft_batch(d, pl, prefix, tokens_out, b, extra);
+    st = enqueue_draft_batch(d, pl, b, extra);
     if (st) {
       cudaEventDestroy(ev);
       return st;
     }
-    if (it == d->graphs.end()) {
-      // capture the same launches for the next call; a sequence that cannot be captured runs directly
-      if (d->graphs.size() >= 16) {
-        for (auto& kv : d->graphs)
-          if (kv.second) cudaGraphExecDestroy(kv.second);
-        d->graphs.clear();
-      }
-      cudaGraphExec_t exec = nullptr;
+    if (++g.calls == 2) {
+      // capture the same launches for the next calls; a sequence that cannot be captured runs directly
       cudaGraph_t graph = nullptr;
       if (cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
-        const int cst = enqueue_draft_batch(d, pl, prefix, tokens_out, b, extra);
+        const int cst = enqueue_draft_batch(d, pl, b, extra);
         const cudaError_t ce = cudaStreamEndCapture(d->stream, &graph);
-        if (cst == LNG_OK && ce == cudaSuccess && graph &&
-            cudaGraphInstantiate(&exec, graph, 0) != cudaSuccess)
-          exec = nullptr;
+        if (cst == LNG_OK && ce == cudaSuccess && graph && cudaGraphInstantiate(&g.exec, graph, 0) != cudaSuccess)
+          g.exec = nullptr;
         if (graph) cudaGraphDestroy(graph);
       }
       (void)cudaGetLastError();  // a failed capture leaves no error behind for the next call
-      d->graphs[key] = exec;
     }
   }
+  LNG_CUDA(cudaMemcpyAsync(tokens_out, static_cast<unsigned char*>(extra) + pl.pre_b, size_t(nseq * gamma) * 8,
+                           cudaMemcpyDeviceToDevice, d->stream));
   LNG_CUDA(cudaEventRecord(ev, d->stream));
   LNG_CUDA(cudaStreamWaitEvent(us, ev, 0));
   LNG_CUDA(cudaEventDestroy(ev));

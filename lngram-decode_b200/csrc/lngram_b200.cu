@@ -634,15 +634,75 @@ static int launch_attend_mma(const AttendParams& p, cudaStream_t stream) {
   return LNG_OK;
 }
 
+// Few items leave most SMs idle with one warp per item walking every route chunk in turn (a 64-sequence
+// draft step: 8 blocks of 8 warps, 6 chunks each), so the routes are split over block rows instead:
+// row y takes a slice of whole 32-route chunks and writes its own (m, l, u) state, and
+// attend_split_combine_kernel merges the slices.  Only as many slices as keep every block in one
+// wave (one block per SM); none once the items alone fill half the SMs.
+template <int DT, typename CodeT, typename T>
+static int launch_attend_mma_split(const AttendParams& p, cudaStream_t stream, bool* used) {
+  using Cfg = AttendMmaCfg<DT>;
+  *used = false;
+  const int64_t R = p.route_end - p.route_start;
+  const int64_t chunks = ceil_div(R, int64_t(Cfg::C));
+  const int64_t blocks = ceil_div(std::max<int64_t>(p.M, 1), int64_t(Cfg::WARPS));
+  if (p.partial != 0 || 2 * blocks > num_sms()) return LNG_OK;
+  int64_t splits = std::min<int64_t>(chunks, num_sms() / blocks);
+  if (splits < 2) return LNG_OK;
+  const int64_t per = ceil_div(chunks, splits) * Cfg::C;  // routes per slice, whole chunks
+  splits = ceil_div(R, per);
+  if (splits < 2) return LNG_OK;
+  const size_t rows = size_t(p.M) * p.qh;
+  const size_t bytes = al256(rows * splits * DT * 4) + 2 * al256(rows * splits * 4);
+  void* buf = nullptr;
+  int st = scratch_alloc(&buf, bytes, stream);
+  if (st) return st;
+  float* su = static_cast<float*>(buf);
+  float* sm = reinterpret_cast<float*>(static_cast<unsigned char*>(buf) + al256(rows * splits * DT * 4));
+  float* sl = sm + al256(rows * splits * 4) / 4;
+  AttendParams q = p;
+  q.partial = 1;
+  q.route_split = per;
+  q.u = su;
+  q.m_out = sm;
+  q.l_out = sl;
+  constexpr int WARPS = Cfg::WARPS, STAGES = Cfg::STAGES;
+  const size_t smem = size_t(WARPS) * STAGES * Cfg::STAGE_BYTES + size_t(WARPS) * STAGES * sizeof(uint64_t);
+  auto kern = attend_mma_kernel<CodeT, T, DT, WARPS, STAGES, true>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e == cudaSuccess) {
+    const dim3 grid{unsigned(blocks), unsigned(splits), 1u};
+    kern<<<grid, WARPS * 32, smem, stream>>>(q);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) {
+    attend_split_combine_kernel<T><<<grid_for(int64_t(rows) * (DT / 4), 256, 8), 256, 0, stream>>>(
+        su, sm, sl, int(splits), p.M, p.qh, DT, static_cast<T*>(p.u));
+    e = cudaGetLastError();
+  }
+  cudaFreeAsync(buf, stream);
+  if (e != cudaSuccess) return cuda_status(e, "attend_mma_kernel (route split)");
+  *used = true;
+  return LNG_OK;
+}
+
+template <int DT, typename CodeT, typename T>
+static int launch_attend_mma_any(const AttendParams& p, cudaStream_t stream) {
+  bool used = false;
+  const int st = launch_attend_mma_split<DT, CodeT, T>(p, stream, &used);
+  if (st || used) return st;
+  return launch_attend_mma<DT, CodeT, T>(p, stream);
+}
+
 template <typename CodeT, typename T>
 static int dispatch_attend_mma(int64_t Dt, const AttendParams& p, cudaStream_t stream) {
   switch (Dt) {
-    case 32: return launch_attend_mma<32, CodeT, T>(p, stream);
-    case 64: return launch_attend_mma<64, CodeT, T>(p, stream);
-    case 128: return launch_attend_mma<128, CodeT, T>(p, stream);
-    case 136: return launch_attend_mma<136, CodeT, T>(p, stream);
-    case 256: return launch_attend_mma<256, CodeT, T>(p, stream);
-    case 272: return launch_attend_mma<272, CodeT, T>(p, stream);
+    case 32: return launch_attend_mma_any<32, CodeT, T>(p, stream);
+    case 64: return launch_attend_mma_any<64, CodeT, T>(p, stream);
+    case 128: return launch_attend_mma_any<128, CodeT, T>(p, stream);
+    case 136: return launch_attend_mma_any<136, CodeT, T>(p, stream);
+    case 256: return launch_attend_mma_any<256, CodeT, T>(p, stream);
+    case 272: return launch_attend_mma_any<272, CodeT, T>(p, stream);
     default: return LNG_ERR_UNSUPPORTED;
   }
 }

@@ -233,6 +233,22 @@ def test_sb_full_size_forward_matches_oracle_on_slices(lngram):
         assert_bf16_close(oc[b, t], want, what=f"position ({b}, {t})")
 
 
+def test_few_positions_match_the_full_batch(lngram):
+    """A forward over few positions (the gather splits the routes over block rows and merges the slices;
+    the GEMMs split K) gives the rows of the same sequences in a large batch (no splits) within bf16."""
+    mem = gpu_memory(lngram, "sb_slice", torch.bfloat16)
+    g = torch.Generator(device=DEV).manual_seed(21)
+    B, T, d = 96, 16, 1024
+    h = torch.randn(B, T, d, device=DEV, generator=g).to(torch.bfloat16)
+    hn = lngram.rms_norm(h, torch.ones(d, device=DEV, dtype=torch.bfloat16), 1e-5)
+    with torch.no_grad():
+        codes = mem.route_codes(hn)                           # the same codes for both (rows identical)
+        full = mem.module.forward_codes(h, codes).float()
+        for b0, nb in ((0, 1), (5, 2), (40, 4)):               # 16, 32 and 64 positions
+            few = mem.module.forward_codes(h[b0:b0 + nb].contiguous(), codes[b0:b0 + nb].contiguous()).float()
+            assert_bf16_close(few.cpu().numpy(), full[b0:b0 + nb].cpu().numpy(), what=f"sequences {b0}..{b0 + nb}")
+
+
 def test_out_of_range_codes_are_flagged_not_read(lngram):
     """A code >= 2^bits is caught by the kernel's own check: the window reads zeros and the
     device error word says so (no out-of-bounds access)."""

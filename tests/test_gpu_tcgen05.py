@@ -32,6 +32,8 @@ def gemm(lngram, a, b, out_dtype, rowscale=None):
 
 @pytest.mark.parametrize("m,n,k", [(128, 256, 64), (256, 128, 1024), (65536 // 16, 2176, 1024), (300, 1024, 2176),
                                    (129, 136, 72), (1, 16, 16), (777, 520, 200),
+                                   # few rows: K split over CTAs, fp32 partials summed by a second kernel
+                                   (64, 2176, 1024), (64, 1024, 2176), (1, 2176, 1024), (100, 1000, 512),
                                    # two-SM (cta_group::2) form: 256-row pair tiles, ragged rows / columns
                                    (8192 + 77, 2176, 1024), (8704, 1024, 2176), (9000, 100, 64)])
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
@@ -44,6 +46,25 @@ def test_tc_gemm_matches_fp32_reference(lngram, m, n, k, out_dtype):
     tol = 1e-5 if out_dtype == torch.float32 else 1e-2
     err = (got - want).abs().max().item()
     assert err <= tol * want.abs().max().item() + 1e-6, (m, n, k, err)
+
+
+def test_tc_gemm_split_k_rowscale_and_output_stride(lngram):
+    """The few-rows form (K split over CTAs) with a row scale and an output row stride above N."""
+    lib = lngram._lib
+    g = torch.Generator(device=DEV).manual_seed(4)
+    m, n, k = 64, 2176, 1024
+    a = torch.randn(m, k, device=DEV, generator=g).to(torch.bfloat16)
+    b = torch.randn(n, k, device=DEV, generator=g).to(torch.bfloat16)
+    rs = torch.rand(m, device=DEV, generator=g) + 0.5
+    for out_dtype in (torch.float32, torch.bfloat16):
+        c = torch.full((m, n + 64), 7.0, device=DEV, dtype=out_dtype)
+        lib.check(lib.library().lng_gemm(a.data_ptr(), lib.BF16, k, b.data_ptr(), lib.BF16, k, c.data_ptr(),
+                                         lib.dtype_code(out_dtype), n + 64, m, n, k, rs.data_ptr(), 0,
+                                         lib.stream_ptr()))
+        want = (a.float() @ b.float().T) * rs[:, None]
+        tol = 1e-5 if out_dtype == torch.float32 else 1e-2
+        assert (c[:, :n].float() - want).abs().max().item() <= tol * want.abs().max().item()
+        assert torch.all(c[:, n:] == 7.0)                    # the row padding is not written
 
 
 def test_tc_gemm_rowscale_and_strided_operands(lngram):

@@ -48,6 +48,113 @@ __global__ void store_draft_kernel(const int64_t* __restrict__ ids, int64_t n, i
   }
 }
 
+// The draft step's first two launches in one: item i's token ids[i * id_stride] (also copied to
+// ids_dense[i] when given), its embedding row to out[i] and 1/rms of that row to rs[i] -- the row's
+// sum of squares read back from `out` exactly as rms_rows_kernel reads it, so rs is bit-identical.
+template <typename T>
+__global__ void gather_rms_kernel(const int64_t* __restrict__ ids, int64_t id_stride, int64_t n,
+                                  const T* __restrict__ E, int64_t d, int64_t vocab, float eps, T* __restrict__ out,
+                                  float* __restrict__ rs, int64_t* __restrict__ ids_dense) {
+  const int lane = threadIdx.x & 31;
+  const bool vec = d % Vec16<T>::N == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+  for (int64_t row = (blockIdx.x * int64_t(blockDim.x) + threadIdx.x) >> 5; row < n;
+       row += (int64_t(gridDim.x) * blockDim.x) >> 5) {
+    const int64_t id = ids[row * id_stride];
+    const bool ok = id >= 0 && id < vocab;
+    if (lane == 0) {
+      if (ids_dense) ids_dense[row] = id;
+      if (!ok) atomicCAS(&g_error_word, 0u, (unsigned int)DEV_ERR_TOKEN_RANGE);
+    }
+    T* o = out + row * d;
+    for (int64_t j = lane; j < d; j += 32) o[j] = ok ? E[id * d + j] : from_f32<T>(0.f);
+    __syncwarp();
+    const float ss = row_sumsq(o, d, vec, lane);
+    if (lane == 0) rs[row] = rsqrtf(ss / float(d) + eps);
+  }
+}
+
+// The draft head's output RMSNorm (rms_norm_reg_kernel's arithmetic, fp32 rows in registers) that
+// also writes the normalised row's three bf16 parts (split_rows_bf16x3_kernel's arithmetic) for the
+// tensor-core logits: parts [n, 3d] = (y1 | y2 | y3).
+__global__ void __launch_bounds__(256) norm_split_kernel(const float* __restrict__ x, int64_t n, int64_t d, int nv,
+                                                         const float* __restrict__ w, float eps, float* __restrict__ y,
+                                                         __nv_bfloat16* __restrict__ parts) {
+  constexpr int N = Vec16<float>::N;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (row >= n) return;
+  const float* xr = x + row * d;
+  float v[RN_NV][N];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < RN_NV; ++i) {
+    if (i < nv) {
+      Vec16<float>::load(xr + (int64_t(i) * 32 + lane) * N, v[i]);
+#pragma unroll
+      for (int k = 0; k < N; ++k) ss = fmaf(v[i][k], v[i][k], ss);
+    }
+  }
+  const float r = rsqrtf(warp_sum(ss) / float(d) + eps);
+  float* yr = y + row * d;
+  __nv_bfloat16* pr = parts + row * 3 * d;
+#pragma unroll
+  for (int i = 0; i < RN_NV; ++i) {
+    if (i < nv) {
+      const int64_t j0 = (int64_t(i) * 32 + lane) * N;
+#pragma unroll
+      for (int k = 0; k < N; ++k) {
+        const float yv = w ? v[i][k] * r * w[j0 + k] : v[i][k] * r;
+        yr[j0 + k] = yv;
+        const __nv_bfloat16 a = __float2bfloat16_rn(yv);
+        const float r1 = yv - __bfloat162float(a);
+        const __nv_bfloat16 b = __float2bfloat16_rn(r1);
+        pr[j0 + k] = a;
+        pr[d + j0 + k] = b;
+        pr[2 * d + j0 + k] = __float2bfloat16_rn(r1 - __bfloat162float(b));
+      }
+    }
+  }
+}
+
+// Top-1 of each draft row from the per-tile candidates (topk_merge_kernel at k = 1: the best in
+// (value desc, id asc) order), written to ids / vals and, for the batched draft, straight into the
+// token matrix and the caller's output (store_draft_kernel's two stores).
+__global__ void top1_merge_store_kernel(const float* __restrict__ cand_v, const int64_t* __restrict__ cand_i, int64_t n,
+                                        int64_t nchunks, int64_t* __restrict__ ids, float* __restrict__ vals,
+                                        int64_t* __restrict__ toks, int64_t ts, int64_t* __restrict__ out, int64_t os) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (blockIdx.x * int64_t(blockDim.x) + threadIdx.x) >> 5;
+  if (row >= n) return;
+  const float* cv = cand_v + row * nchunks;
+  const int64_t* ci = cand_i + row * nchunks;
+  float bv = -INFINITY;
+  int64_t bi = INT64_MAX;
+  for (int64_t c = lane; c < nchunks; c += 32) {
+    const float v = cv[c];
+    const int64_t id = ci[c];
+    if (id >= 0 && tk_better(v, id, bv, bi)) {
+      bv = v;
+      bi = id;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (tk_better(ov, oi, bv, bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  if (lane == 0) {
+    const int64_t id = bi == INT64_MAX ? -1 : bi;
+    ids[row] = id;
+    vals[row] = bi == INT64_MAX ? -INFINITY : bv;
+    if (toks) toks[row * ts] = id;
+    if (out) out[row * os] = id;
+  }
+}
+
 __global__ void f32_to_bf16_kernel(const float* __restrict__ in, int64_t n, __nv_bfloat16* __restrict__ out) {
   for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < n; e += int64_t(gridDim.x) * blockDim.x)
     out[e] = __float2bfloat16_rn(in[e]);
@@ -227,15 +334,17 @@ struct ReadoutBufs {
   float* vals;   // [rows, k]
   void* scratch; size_t scratch_bytes;
   float* feat;   // [rows, F]
+  __nv_bfloat16* feat_parts;  // [rows, 3F] the router features' bf16x3 parts
 };
 
 static int drafter_ws(lng_drafter* dr, int64_t M, int k, ReadoutBufs* b, size_t extra_bytes, void** extra) {
   const size_t es = size_t(dtype_size(dr->e_dtype)), as = size_t(dtype_size(dr->act));
   const size_t qd = size_t(dr->qh * dr->Dt);
-  const size_t sizes[10] = {al256(size_t(M) * dr->d * es), al256(size_t(M) * 4), al256(size_t(M) * qd * as),
+  const size_t sizes[11] = {al256(size_t(M) * dr->d * es), al256(size_t(M) * 4), al256(size_t(M) * qd * as),
                             al256(size_t(M) * qd * as), al256(size_t(M) * dr->d * 4), al256(size_t(M) * dr->d * 4),
                             al256(size_t(M) * k * 8), al256(size_t(M) * k * 4),
-                            al256(lng_logits_topk_scratch_bytes(M, dr->d, dr->V, k)), al256(size_t(M) * dr->F * 4)};
+                            al256(lng_logits_topk_scratch_bytes(M, dr->d, dr->V, k)), al256(size_t(M) * dr->F * 4),
+                            al256(size_t(M) * 3 * dr->F * 2)};
   size_t total = al256(extra_bytes);
   for (size_t s : sizes) total += s;
   if (total > dr->ws_bytes) {
@@ -246,8 +355,8 @@ static int drafter_ws(lng_drafter* dr, int64_t M, int k, ReadoutBufs* b, size_t 
     dr->ws_bytes = total;
   }
   unsigned char* p = static_cast<unsigned char*>(dr->ws);
-  void* ptrs[10];
-  for (int i = 0; i < 10; ++i) {
+  void* ptrs[11];
+  for (int i = 0; i < 11; ++i) {
     ptrs[i] = p;
     p += sizes[i];
   }
@@ -263,6 +372,7 @@ static int drafter_ws(lng_drafter* dr, int64_t M, int k, ReadoutBufs* b, size_t 
   b->scratch = ptrs[8];
   b->scratch_bytes = sizes[8];
   b->feat = static_cast<float*>(ptrs[9]);
+  b->feat_parts = static_cast<__nv_bfloat16*>(ptrs[10]);
   if (extra) *extra = extra_bytes ? p : nullptr;
   return LNG_OK;
 }
@@ -309,9 +419,12 @@ static int drafter_ssm_scan(lng_drafter* dr, const float* u, int64_t nseq, int64
 // Codes of M tokens given their previous tokens (device i64 arrays; prev = -1 -> start vector) and,
 // for the embed2_ssm router, their SSM states s_rows [M, N].
 static int drafter_codes(lng_drafter* dr, const int64_t* cur, const int64_t* prev, int64_t M, float* feat,
-                         uint8_t* codes_out, int64_t codes_stride, const float* s_rows) {
+                         uint8_t* codes_out, int64_t codes_stride, const float* s_rows,
+                         __nv_bfloat16* feat_parts = nullptr) {
+  // the token-only router's features go to the tensor cores already split into bf16 parts
+  __nv_bfloat16* parts = (!dr->router_ssm && codes_stride == dr->R && M <= 256) ? feat_parts : nullptr;
   int st = embed2_features(cur, prev, M, dr->E, dr->e_dtype, dr->V, dr->d, dr->prev_norm, dr->cur_norm, dr->start,
-                           dr->router_eps, feat, dr->F, dr->stream);
+                           dr->router_eps, feat, dr->F, dr->stream, parts, dr->F);
   if (st) return st;
   if (dr->router_ssm) {
     LNG_REQUIRE(s_rows, "internal: the SSM router needs the states");
@@ -320,7 +433,7 @@ static int drafter_codes(lng_drafter* dr, const int64_t* cur, const int64_t* pre
   }
   if (codes_stride == dr->R)
     return route_codes_presplit(feat, M, dr->F, dr->router_w, dr->router_w_split, dr->R, int32_t(dr->bits), codes_out,
-                                dr->stream);
+                                dr->stream, parts);
   for (int64_t i = 0; i < M; ++i) {  // strided destination: one row at a time
     st = route_codes_presplit(feat + i * dr->F, 1, dr->F, dr->router_w, dr->router_w_split, dr->R, int32_t(dr->bits),
                               codes_out + i * codes_stride, dr->stream);
@@ -377,17 +490,67 @@ static int launch_shortlist(lng_drafter* dr, const CodeSource& src, int64_t M, c
   return LNG_OK;
 }
 
-// Readout of M items: embedding rows of `cur`, the item's code window per `src`, the SSM states
-// s_rows [M, N] for query_ssm, then top-k (or the trace outputs) per `sc`.
+// Where a batched draft stores each step's top-1 besides ids: the token matrix and the caller's output
+// (strided), written by the merge kernel itself.
+struct DraftStore {
+  int64_t* toks = nullptr;
+  int64_t ts = 0;
+  int64_t* out = nullptr;
+  int64_t os = 0;
+};
+
+// Draft-head logits + top-k over the whole vocabulary on lng_logits_topk's scratch layout; `presplit`:
+// the three bf16 parts of hn are in place already (norm_split_kernel); with `store` and k = 1 the merge
+// also writes the drafted tokens.
+static int drafter_logits(lng_drafter* dr, ReadoutBufs& b, int64_t M, int k, float* full_logits, bool presplit,
+                          const DraftStore* store) {
+  const int64_t nch = ceil_div(dr->V, TK_VC);
+  LNG_REQUIRE(b.scratch_bytes >= lng_logits_topk_scratch_bytes(M, dr->d, dr->V, k), "internal: logits scratch");
+  const uintptr_t base = (reinterpret_cast<uintptr_t>(b.scratch) + 255) & ~uintptr_t(255);
+  int64_t* cand_i = reinterpret_cast<int64_t*>(base);
+  float* cand_v = reinterpret_cast<float*>(cand_i + M * nch * k);
+  auto* split = reinterpret_cast<__nv_bfloat16*>(base + al256(topk_cand_bytes(M, dr->V, k)));
+  int st = logits_chunks(b.hn, M, dr->d, dr->E, dr->e_dtype, dr->V, k, cand_v, cand_i, full_logits, split, dr->stream,
+                         presplit);
+  if (st) return st;
+  if (store && k == 1) {
+    top1_merge_store_kernel<<<unsigned(ceil_div(M * 32, 256)), 256, 0, dr->stream>>>(
+        cand_v, cand_i, M, nch, b.ids, b.vals, store->toks, store->ts, store->out, store->os);
+    LNG_LAUNCHED("top1_merge_store_kernel");
+  } else {
+    topk_merge_kernel<<<unsigned(ceil_div(M * 32, 256)), 256, 0, dr->stream>>>(cand_v, cand_i, M, nch, k, b.ids,
+                                                                              b.vals);
+    LNG_LAUNCHED("topk_merge_kernel");
+    if (store) {
+      store_draft_kernel<<<unsigned(ceil_div(M, 128)), 128, 0, dr->stream>>>(b.ids, M, store->toks, store->ts,
+                                                                             store->out, store->os);
+      LNG_LAUNCHED("store_draft_kernel");
+    }
+  }
+  return LNG_OK;
+}
+
+// Readout of M items: embedding rows of the tokens cur[i * cur_stride] (copied densely to cur_dense
+// when given), the item's code window per `src`, the SSM states s_rows [M, N] for query_ssm, then
+// top-k (or the trace outputs) per `sc`; `store`: where the batched draft's top-1 goes as well.
 static int drafter_readout(lng_drafter* dr, const int64_t* cur, int64_t M, const CodeSource& src, int k,
-                           ReadoutBufs& b, const Scoring& sc, const float* s_rows) {
+                           ReadoutBufs& b, const Scoring& sc, const float* s_rows, int64_t cur_stride = 1,
+                           int64_t* cur_dense = nullptr, const DraftStore* store = nullptr) {
   cudaStream_t s = dr->stream;
   lng_stream_t ls = reinterpret_cast<lng_stream_t>(s);
   const int64_t qd = dr->qh * dr->Dt;
-  int st = gather_embedding(dr, cur, M, b.x);
-  if (st) return st;
-  st = lng_rms_rows(b.x, dr->e_dtype, M, dr->d, dr->draft_eps, b.qs, ls);
-  if (st) return st;
+  int st = LNG_OK;
+  {  // embedding rows and their 1/rms in one launch
+    const int g = grid_for(M * 32, 256, 16);
+#define LNG_GRMS(T)                                                                                            \
+  gather_rms_kernel<T><<<g, 256, 0, s>>>(cur, cur_stride, M, static_cast<const T*>(dr->E), dr->d, dr->V,     \
+                                         dr->draft_eps, static_cast<T*>(b.x), b.qs, cur_dense)
+    if (dr->e_dtype == LNG_F32) LNG_GRMS(float);
+    else if (dr->e_dtype == LNG_BF16) LNG_GRMS(__nv_bfloat16);
+    else LNG_GRMS(__half);
+#undef LNG_GRMS
+    LNG_LAUNCHED("gather_rms_kernel");
+  }
   const float* qscale = b.qs;
   if (dr->query_ssm) {
     // qa = rs(x) (x . w_qk^T) + s . w_sqk^T: the SSM term carries no RMS scale (drafter.cpp:505-508)
@@ -418,11 +581,30 @@ static int drafter_readout(lng_drafter* dr, const int64_t* cur, int64_t M, const
   if (st) return st;
   st = lng_gemm(b.u, dr->act, qd, dr->w_vo, dr->act, qd, b.hid, LNG_F32, dr->d, M, dr->d, qd, nullptr, 0, ls);
   if (st) return st;
-  st = lng_rms_norm(b.hid, LNG_F32, M, dr->d, dr->out_norm, dr->draft_eps, b.hn, LNG_F32, ls);
-  if (st) return st;
-  if (dr->has_sketch() && !sc.full) return launch_shortlist(dr, src, M, b.hn, k, b.ids, b.vals, sc);
-  return lng_logits_topk(b.hn, M, dr->d, dr->E, dr->e_dtype, dr->V, k, b.ids, b.vals, sc.full_logits, b.scratch,
-                         b.scratch_bytes, ls);
+  const bool shortlist = dr->has_sketch() && !sc.full;
+  // full-vocabulary logits on the tensor cores: the output norm also writes the rows' bf16 parts
+  const int64_t vec_elems = 32 * Vec16<float>::N;
+  const bool fuse = !shortlist && logits_tc_ok(dr->d, dr->E, dr->e_dtype, dr->V) && dr->d % vec_elems == 0 &&
+                    dr->d / vec_elems <= RN_NV;
+  if (fuse) {
+    const uintptr_t base = (reinterpret_cast<uintptr_t>(b.scratch) + 255) & ~uintptr_t(255);
+    auto* parts = reinterpret_cast<__nv_bfloat16*>(base + al256(topk_cand_bytes(M, dr->V, k)));
+    norm_split_kernel<<<unsigned(ceil_div(M, 8)), 256, 0, s>>>(b.hid, M, dr->d, int(dr->d / vec_elems), dr->out_norm,
+                                                               dr->draft_eps, b.hn, parts);
+    LNG_LAUNCHED("norm_split_kernel");
+  } else {
+    st = lng_rms_norm(b.hid, LNG_F32, M, dr->d, dr->out_norm, dr->draft_eps, b.hn, LNG_F32, ls);
+    if (st) return st;
+  }
+  if (shortlist) {
+    st = launch_shortlist(dr, src, M, b.hn, k, b.ids, b.vals, sc);
+    if (st || !store) return st;
+    store_draft_kernel<<<unsigned(ceil_div(M, 128)), 128, 0, s>>>(b.ids, M, store->toks, store->ts, store->out,
+                                                                  store->os);
+    LNG_LAUNCHED("store_draft_kernel");
+    return LNG_OK;
+  }
+  return drafter_logits(dr, b, M, k, sc.full_logits, fuse, store);
 }
 
 }  // namespace lng
@@ -913,22 +1095,24 @@ static int enqueue_draft_batch(lng_drafter* d, const DraftBatchPlan& pl, Readout
   const size_t dense_need = size_t(nseq * tail * R);
   const size_t u_bytes = size_t(b.rows) * d->qh * d->Dt * dtype_size(d->act);
   LNG_REQUIRE(dense_need <= u_bytes, "internal: code staging buffer too small");
-  st = drafter_codes(d, scratch_i, scratch_i + nseq * tail, nseq * tail, b.feat, dense, R, N > 0 ? tail_states : nullptr);
+  st = drafter_codes(d, scratch_i, scratch_i + nseq * tail, nseq * tail, b.feat, dense, R, N > 0 ? tail_states : nullptr,
+                     b.feat_parts);
   if (st) return st;
   LNG_CUDA(cudaMemcpy2DAsync(codes + p0 * R, size_t(P * R), dense, size_t(tail * R), size_t(tail * R), size_t(nseq),
                              cudaMemcpyDeviceToDevice, d->stream));
   for (int64_t g = 0; g < gamma; ++g) {
     const int64_t tpos = plen - 1 + g;  // position of the current token in every sequence
-    // current tokens toks[s, 1 + tpos] -> gather into a dense [nseq] vector
-    copy_i64_kernel<<<unsigned(ceil_div(nseq, 128)), 128, 0, d->stream>>>(toks + 1 + tpos, scratch_i, nseq, P + 1, 1);
-    LNG_LAUNCHED("copy_i64_kernel");
+    // the readout reads the current tokens toks[s, 1 + tpos] in place (copied densely to scratch_i)
+    // and its merge stores the next tokens at toks[s, 2 + tpos] and tokens_out[s, g]
     CodeSource src{codes, nseq, tpos + 1, 0, R, nullptr, nullptr, nullptr, tpos, P};
-    st = drafter_readout(d, scratch_i, nseq, src, 1, b, Scoring{}, N > 0 ? s_cur : nullptr);
+    DraftStore store;
+    store.toks = toks + 2 + tpos;
+    store.ts = P + 1;
+    store.out = tokens_out + g;
+    store.os = gamma;
+    st = drafter_readout(d, toks + 1 + tpos, nseq, src, 1, b, Scoring{}, N > 0 ? s_cur : nullptr, P + 1, scratch_i,
+                         &store);
     if (st) return st;
-    // next tokens -> toks[s, 2 + tpos] and tokens_out[s, g]
-    store_draft_kernel<<<unsigned(ceil_div(nseq, 128)), 128, 0, d->stream>>>(b.ids, nseq, toks + 2 + tpos, P + 1,
-                                                                             tokens_out + g, gamma);
-    LNG_LAUNCHED("store_draft_kernel");
     if (g + 1 < gamma) {
       // the drafted tokens' SSM states and their codes at position tpos + 1 (strided rows of the code
       // buffer); their previous tokens are this step's current tokens, still in scratch_i
@@ -939,15 +1123,7 @@ static int enqueue_draft_batch(lng_drafter* d, const DraftBatchPlan& pl, Readout
         if (st) return st;
         std::swap(s_cur, s_next);
       }
-      st = embed2_features(b.ids, scratch_i, nseq, d->E, d->e_dtype, d->V, d->d, d->prev_norm, d->cur_norm, d->start,
-                           d->router_eps, b.feat, d->F, d->stream);
-      if (st) return st;
-      if (d->router_ssm) {
-        copy_cols_kernel<<<grid_for(nseq * N, 256, 8), 256, 0, d->stream>>>(s_cur, nseq, N, b.feat, d->F, 2 * d->d);
-        LNG_LAUNCHED("copy_cols_kernel");
-      }
-      st = route_codes_presplit(b.feat, nseq, d->F, d->router_w, d->router_w_split, R, int32_t(d->bits), dense,
-                                d->stream);
+      st = drafter_codes(d, b.ids, scratch_i, nseq, b.feat, dense, R, N > 0 ? s_cur : nullptr, b.feat_parts);
       if (st) return st;
       LNG_CUDA(cudaMemcpy2DAsync(codes + (tpos + 1) * R, size_t(P * R), dense, size_t(R), size_t(R), size_t(nseq),
                                  cudaMemcpyDeviceToDevice, d->stream));

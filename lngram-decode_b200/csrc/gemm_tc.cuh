@@ -736,6 +736,65 @@ inline bool tc_aligned(const void* p, int64_t ld) {
   return (reinterpret_cast<uintptr_t>(p) & 15) == 0 && (ld % 8) == 0;
 }
 
+// Few rows (a draft step's 64): the (row tile, column tile) grid alone would leave most SMs idle with
+// each CTA streaming all of K, so K is split over `splits` CTAs per tile as well, each writing an fp32
+// partial product [M, N] (rowscale applied) at partials + s * M * N; splitk_reduce_kernel sums them.
+// Returns the split count to use (1: the plain GEMM is better).
+inline int tc_gemm_small_m_splits(int64_t M, int64_t N, int64_t K) {
+  constexpr int BN = 128;
+  const int64_t tiles = ((M + TC_BM - 1) / TC_BM) * ((N + BN - 1) / BN);
+  const int64_t kb = (K + TC_BK - 1) / TC_BK;
+  if (M > TC_BM || 2 * tiles > num_sms() || kb < 4) return 1;
+  return int(std::min<int64_t>(kb / 2, num_sms() / tiles));
+}
+
+inline int tc_gemm_bf16_splitk(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int64_t ldb,
+                               float* partials, int splits, int64_t M, int64_t N, int64_t K, const float* rowscale,
+                               cudaStream_t stream) {
+  if (!tc_aligned(A, lda) || !tc_aligned(B, ldb) || K < 16 || N < 16 || M < 1 || (N % 4))
+    return LNG_ERR_UNSUPPORTED;
+  CUtensorMap ta, tb;
+  int st = make_tmap_bf16(&ta, A, M, K, lda, TC_BM);
+  if (st) return st;
+  st = make_tmap_bf16(&tb, B, N, K, ldb, 128);
+  if (st) return st;
+  TcGemmParams p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.a_kperiod = (K + TC_BK - 1) / TC_BK * TC_BK;  // no wrap
+  p.C = partials;
+  p.ldc = N;
+  p.c_dtype = LNG_F32;
+  p.rowscale = rowscale;
+  p.splits = splits;
+  p.split_stride = M * N;
+  return launch_tc_gemm<128, 0>(ta, tb, p, stream);
+}
+
+// C[M, N] (+ ldc) = sum over s of partials[s] (fp32, [M, N] each), in split order.
+template <typename CT>
+__global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int64_t M, int64_t N,
+                                     CT* __restrict__ C, int64_t ldc) {
+  const int64_t n4 = N / 4, total = M * n4, stride = M * N;
+  for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < total; e += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = e / n4, c = (e - r * n4) * 4;
+    float4 a = *reinterpret_cast<const float4*>(part + r * N + c);
+    for (int s = 1; s < splits; ++s) {
+      const float4 b = *reinterpret_cast<const float4*>(part + s * stride + r * N + c);
+      a.x += b.x;
+      a.y += b.y;
+      a.z += b.z;
+      a.w += b.w;
+    }
+    CT* o = C + r * ldc + c;
+    o[0] = from_f32<CT>(a.x);
+    o[1] = from_f32<CT>(a.y);
+    o[2] = from_f32<CT>(a.z);
+    o[3] = from_f32<CT>(a.w);
+  }
+}
+
 // Plain bf16 GEMM on the tensor cores; LNG_ERR_UNSUPPORTED when the operands do not meet TMA rules.
 inline int tc_gemm_bf16(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int64_t ldb, void* C,
                         int32_t c_dtype, int64_t ldc, int64_t M, int64_t N, int64_t K, const float* rowscale,

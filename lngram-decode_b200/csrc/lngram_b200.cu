@@ -187,27 +187,31 @@ __global__ void __launch_bounds__(256) router_reduce_pack_kernel(const float* __
 // Scratch (x parts, W parts, partials) comes from the library pool and is released on `stream`.
 static int tc_router_small_f32(const float* x, int64_t n, int64_t in_dim, int64_t x_stride, const float* w,
                                int64_t routes, int32_t bits, void* codes, int codes_i32, float* logits,
-                               cudaStream_t stream, const __nv_bfloat16* w_split = nullptr) {
-  if (in_dim % TC_BK != 0 || x_stride != in_dim || n < 1 || n > 256 || (reinterpret_cast<uintptr_t>(x) & 15))
+                               cudaStream_t stream, const __nv_bfloat16* w_split = nullptr,
+                               const __nv_bfloat16* x_split = nullptr) {
+  if (in_dim % TC_BK != 0 || x_stride != in_dim || n < 1 || n > 256 || (reinterpret_cast<uintptr_t>(x) & 15) ||
+      (reinterpret_cast<uintptr_t>(x_split) & 15))
     return LNG_ERR_UNSUPPORTED;
   const int64_t cols = routes * bits;
   const int64_t m_tiles = (cols + TC_BM - 1) / TC_BM;
   const int npairs = 6;
   const int64_t KB = npairs * (in_dim / TC_BK);
-  int splits = int((num_sms() + m_tiles - 1) / m_tiles);
+  // whole waves only: m_tiles x splits CTAs on at most the SM count
+  int splits = int(std::max<int64_t>(1, num_sms() / m_tiles));
   if (splits > KB) splits = int(KB);
   const int BN = n <= 64 ? 64 : n <= 128 ? 128 : 256;
   const int64_t ldp = (n + 3) & ~int64_t(3);  // partial rows padded so the epilogue's 16-byte stores stay aligned
-  const size_t xs_b = al256(size_t(n) * 3 * in_dim * 2), ws_b = w_split ? 0 : al256(size_t(cols) * 3 * in_dim * 2),
-               ps_b = al256(size_t(splits) * cols * ldp * 4);
+  // x_split: the rows' bf16x3 parts [n, 3 in_dim] made by the caller (embed2 features write them)
+  const size_t xs_b = x_split ? 0 : al256(size_t(n) * 3 * in_dim * 2),
+               ws_b = w_split ? 0 : al256(size_t(cols) * 3 * in_dim * 2), ps_b = al256(size_t(splits) * cols * ldp * 4);
   void* scratch = nullptr;
   int st = scratch_alloc(&scratch, xs_b + ws_b + ps_b, stream);
   if (st) return st;
-  auto* xs = static_cast<__nv_bfloat16*>(scratch);
+  auto* xs = x_split ? const_cast<__nv_bfloat16*>(x_split) : static_cast<__nv_bfloat16*>(scratch);
   auto* ws = w_split ? const_cast<__nv_bfloat16*>(w_split)
                      : reinterpret_cast<__nv_bfloat16*>(static_cast<unsigned char*>(scratch) + xs_b);
   auto* ps = reinterpret_cast<float*>(static_cast<unsigned char*>(scratch) + xs_b + ws_b);
-  split_rows_bf16x3_kernel<<<grid_for(n * in_dim, 256, 16), 256, 0, stream>>>(x, n, in_dim, xs);
+  if (!x_split) split_rows_bf16x3_kernel<<<grid_for(n * in_dim, 256, 16), 256, 0, stream>>>(x, n, in_dim, xs);
   if (!w_split) split_bf16x3_kernel<<<grid_for(cols * in_dim, 256, 16), 256, 0, stream>>>(w, cols, in_dim, ws);
   CUtensorMap ta, tb;
   st = make_tmap_bf16(&ta, ws, cols, 3 * in_dim, 3 * in_dim, TC_BM);
@@ -256,9 +260,10 @@ namespace lng {
 // fixed weight, e.g. the drafter): the small-batch tensor-core path skips the per-call split.
 static int route_codes_presplit(const float* x, int64_t n, int64_t in_dim, const float* w,
                                 const __nv_bfloat16* w_split, int64_t routes, int32_t bits, uint8_t* codes,
-                                cudaStream_t stream) {
+                                cudaStream_t stream, const __nv_bfloat16* x_split = nullptr) {
   if (n >= 1 && n <= 256 && w_split) {
-    const int st = tc_router_small_f32(x, n, in_dim, in_dim, w, routes, bits, codes, 0, nullptr, stream, w_split);
+    const int st = tc_router_small_f32(x, n, in_dim, in_dim, w, routes, bits, codes, 0, nullptr, stream, w_split,
+                                       x_split);
     if (st != LNG_ERR_UNSUPPORTED) return st;
   }
   return lng_route_codes(x, LNG_F32, n, in_dim, in_dim, w, routes, bits, codes, LNG_U8, nullptr,
@@ -343,7 +348,8 @@ namespace lng {
 // embed2 features into rows of stride out_stride (the drafter appends its SSM state after them)
 static int embed2_features(const int64_t* cur, const int64_t* prev, int64_t n, const void* embedding, int32_t e_dtype,
                            int64_t vocab, int64_t d, const float* prev_w, const float* cur_w, const float* start,
-                           float eps, float* out, int64_t out_stride, cudaStream_t stream) {
+                           float eps, float* out, int64_t out_stride, cudaStream_t stream,
+                           __nv_bfloat16* split = nullptr, int64_t split_width = 0) {
   LNG_REQUIRE(n >= 0 && vocab > 0 && d > 0, "bad shape");
   if (n == 0) return LNG_OK;
   LNG_REQUIRE(cur && embedding && prev_w && cur_w && start && out, "NULL pointer");
@@ -351,15 +357,18 @@ static int embed2_features(const int64_t* cur, const int64_t* prev, int64_t n, c
   switch (e_dtype) {
     case LNG_F32:
       embed2_features_kernel<float><<<g, 128, 0, stream>>>(cur, prev, n, static_cast<const float*>(embedding), vocab,
-                                                               d, prev_w, cur_w, start, eps, out, out_stride);
+                                                               d, prev_w, cur_w, start, eps, out, out_stride, split,
+                                                               split_width);
       break;
     case LNG_BF16:
       embed2_features_kernel<__nv_bfloat16><<<g, 128, 0, stream>>>(
-          cur, prev, n, static_cast<const __nv_bfloat16*>(embedding), vocab, d, prev_w, cur_w, start, eps, out, out_stride);
+          cur, prev, n, static_cast<const __nv_bfloat16*>(embedding), vocab, d, prev_w, cur_w, start, eps, out, out_stride,
+          split, split_width);
       break;
     case LNG_F16:
       embed2_features_kernel<__half><<<g, 128, 0, stream>>>(cur, prev, n, static_cast<const __half*>(embedding),
-                                                                vocab, d, prev_w, cur_w, start, eps, out, out_stride);
+                                                                vocab, d, prev_w, cur_w, start, eps, out, out_stride,
+                                                                split, split_width);
       break;
     default:
       return fail(LNG_ERR_ARGUMENT, "embedding dtype must be f32, bf16 or f16");
@@ -851,6 +860,27 @@ extern "C" int lng_gemm(const void* A, int32_t a_dtype, int64_t lda, const void*
   if (M == 0 || N == 0) return LNG_OK;
   LNG_REQUIRE(A && Bm && C, "NULL pointer");
   if (a_dtype == LNG_BF16 && b_dtype == LNG_BF16 && !accumulate) {
+    const int splits = tc_gemm_small_m_splits(M, N, K);
+    if (splits > 1 && (c_dtype == LNG_F32 || c_dtype == LNG_BF16) && N % 4 == 0) {
+      void* part = nullptr;
+      int st = scratch_alloc(&part, size_t(splits) * M * N * sizeof(float), S(stream));
+      if (st) return st;
+      st = tc_gemm_bf16_splitk(static_cast<const __nv_bfloat16*>(A), lda, static_cast<const __nv_bfloat16*>(Bm), ldb,
+                               static_cast<float*>(part), splits, M, N, K, rowscale, S(stream));
+      if (st == LNG_OK) {
+        const int g = grid_for(M * (N / 4), 256, 8);
+        if (c_dtype == LNG_F32)
+          splitk_reduce_kernel<float><<<g, 256, 0, S(stream)>>>(static_cast<float*>(part), splits, M, N,
+                                                                static_cast<float*>(C), ldc);
+        else
+          splitk_reduce_kernel<__nv_bfloat16><<<g, 256, 0, S(stream)>>>(static_cast<float*>(part), splits, M, N,
+                                                                        static_cast<__nv_bfloat16*>(C), ldc);
+        const cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) st = cuda_status(e, "splitk_reduce_kernel");
+      }
+      cudaFreeAsync(part, S(stream));
+      if (st != LNG_ERR_UNSUPPORTED) return st;
+    }
     const int st = tc_gemm_bf16(static_cast<const __nv_bfloat16*>(A), lda, static_cast<const __nv_bfloat16*>(Bm), ldb,
                                 C, c_dtype, ldc, M, N, K, rowscale, S(stream));
     if (st != LNG_ERR_UNSUPPORTED) return st;
@@ -1350,11 +1380,13 @@ namespace {
 // bf16 with TMA-compatible shapes, the CUDA-core kernel otherwise.
 int logits_chunks(const float* h, int64_t n, int64_t d, const void* embedding, int32_t e_dtype, int64_t vocab,
                   int32_t k, float* cand_v, int64_t* cand_i, float* logits, __nv_bfloat16* split,
-                  cudaStream_t stream) {
+                  cudaStream_t stream, bool presplit = false) {
   const int64_t nch = ceil_div(vocab, TK_VC);
   if (split && logits_tc_ok(d, embedding, e_dtype, vocab)) {
-    split_rows_bf16x3_kernel<<<grid_for(n * d, 256, 16), 256, 0, stream>>>(h, n, d, split);
-    LNG_LAUNCHED("split_rows_bf16x3_kernel");
+    if (!presplit) {  // presplit: the caller wrote the three parts of h to `split` already
+      split_rows_bf16x3_kernel<<<grid_for(n * d, 256, 16), 256, 0, stream>>>(h, n, d, split);
+      LNG_LAUNCHED("split_rows_bf16x3_kernel");
+    }
     const int bn = n <= 32 ? 32 : n <= 64 ? 64 : 128;
     CUtensorMap te, th;
     int st = make_tmap_bf16(&te, embedding, vocab, d, d, LT_BM);

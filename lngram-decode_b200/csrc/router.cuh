@@ -195,7 +195,8 @@ __global__ void __cluster_dims__(RS_SPLIT, 1, 1) __launch_bounds__(256)
 
 // embed2 router features (ffnmem/memory/router.py:50-69): one 128-thread CTA per item, the
 // previous and current token rows each RMS-normalised with their own weight, written to the first
-// 2d columns of the item's output row (row stride out_stride >= 2d).
+// 2d columns of the item's output row (row stride out_stride >= 2d); with `split`, also the row's three
+// bf16 parts [3 x split_width] (split_width = the router's input width) for the tensor-core router.
 template <typename ET>
 __global__ void __launch_bounds__(128) embed2_features_kernel(const int64_t* __restrict__ cur,
                                                               const int64_t* __restrict__ prev, int64_t n,
@@ -203,7 +204,9 @@ __global__ void __launch_bounds__(128) embed2_features_kernel(const int64_t* __r
                                                               const float* __restrict__ prev_w,
                                                               const float* __restrict__ cur_w,
                                                               const float* __restrict__ start, float eps,
-                                                              float* __restrict__ out, int64_t out_stride) {
+                                                              float* __restrict__ out, int64_t out_stride,
+                                                              __nv_bfloat16* __restrict__ split = nullptr,
+                                                              int64_t split_width = 0) {
   __shared__ float red[2][4];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (int64_t item = blockIdx.x; item < n; item += gridDim.x) {
@@ -236,7 +239,17 @@ __global__ void __launch_bounds__(128) embed2_features_kernel(const int64_t* __r
 #pragma unroll 8
       for (int64_t j = threadIdx.x; j < d; j += blockDim.x) {
         const float v = tok >= 0 ? to_f32(E[tok * d + j]) : start[j];
-        o[part * d + j] = v * rs * wv[j];
+        const float y = v * rs * wv[j];
+        o[part * d + j] = y;
+        if (split) {  // the row's three bf16 parts (split_rows_bf16x3_kernel's arithmetic), for the router
+          const __nv_bfloat16 a = __float2bfloat16_rn(y);
+          const float r1 = y - __bfloat162float(a);
+          const __nv_bfloat16 b = __float2bfloat16_rn(r1);
+          __nv_bfloat16* xs = split + item * 3 * split_width + part * d + j;
+          xs[0] = a;
+          xs[split_width] = b;
+          xs[2 * split_width] = __float2bfloat16_rn(r1 - __bfloat162float(b));
+        }
       }
     }
     __syncthreads();

@@ -80,6 +80,7 @@ __global__ void __launch_bounds__(256) norm_split_kernel(const float* __restrict
                                                          const float* __restrict__ w, float eps, float* __restrict__ y,
                                                          __nv_bfloat16* __restrict__ parts) {
   constexpr int N = Vec16<float>::N;
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the logits kernel may start its set-up
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   if (row >= n) return;
@@ -511,7 +512,7 @@ static int drafter_logits(lng_drafter* dr, ReadoutBufs& b, int64_t M, int k, flo
   float* cand_v = reinterpret_cast<float*>(cand_i + M * nch * k);
   auto* split = reinterpret_cast<__nv_bfloat16*>(base + al256(topk_cand_bytes(M, dr->V, k)));
   int st = logits_chunks(b.hn, M, dr->d, dr->E, dr->e_dtype, dr->V, k, cand_v, cand_i, full_logits, split, dr->stream,
-                         presplit);
+                         presplit, presplit);
   if (st) return st;
   if (store && k == 1) {
     top1_merge_store_kernel<<<unsigned(ceil_div(M * 32, 256)), 256, 0, dr->stream>>>(

@@ -1380,7 +1380,7 @@ namespace {
 // bf16 with TMA-compatible shapes, the CUDA-core kernel otherwise.
 int logits_chunks(const float* h, int64_t n, int64_t d, const void* embedding, int32_t e_dtype, int64_t vocab,
                   int32_t k, float* cand_v, int64_t* cand_i, float* logits, __nv_bfloat16* split,
-                  cudaStream_t stream, bool presplit = false) {
+                  cudaStream_t stream, bool presplit = false, bool dependent = false) {
   const int64_t nch = ceil_div(vocab, TK_VC);
   if (split && logits_tc_ok(d, embedding, e_dtype, vocab)) {
     if (!presplit) {  // presplit: the caller wrote the three parts of h to `split` already
@@ -1394,11 +1394,27 @@ int logits_chunks(const float* h, int64_t n, int64_t d, const void* embedding, i
     st = make_tmap_bf16(&th, split, n, 3 * d, 3 * d, bn);
     if (st) return st;
     dim3 grid(unsigned(ceil_div(n, bn)), unsigned(nch));
+    // dependent: a programmatic dependent launch -- the kernel's start (set-up, first vocabulary tiles)
+    // overlaps the kernel before it, which writes the split rows (griddepcontrol in both)
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
 #define LNG_LT(BN)                                                                                          \
   do {                                                                                                      \
     auto kern = logits_tc_topk_kernel<BN>;                                                                  \
     LNG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(LtCfg<BN>::SMEM))); \
-    kern<<<grid, 128, LtCfg<BN>::SMEM, stream>>>(te, th, n, d, vocab, k, cand_v, cand_i, logits);             \
+    if (dependent) {                                                                                        \
+      cudaLaunchConfig_t cfg{};                                                                             \
+      cfg.gridDim = grid;                                                                                   \
+      cfg.blockDim = dim3(128);                                                                             \
+      cfg.dynamicSmemBytes = LtCfg<BN>::SMEM;                                                               \
+      cfg.stream = stream;                                                                                  \
+      cfg.attrs = pdl;                                                                                      \
+      cfg.numAttrs = 1;                                                                                     \
+      LNG_CUDA(cudaLaunchKernelEx(&cfg, kern, te, th, n, d, vocab, k, cand_v, cand_i, logits));              \
+    } else {                                                                                                \
+      kern<<<grid, 128, LtCfg<BN>::SMEM, stream>>>(te, th, n, d, vocab, k, cand_v, cand_i, logits);           \
+    }                                                                                                       \
   } while (0)
     if (bn == 32) LNG_LT(32);
     else if (bn == 64) LNG_LT(64);

@@ -109,14 +109,24 @@ __global__ void __launch_bounds__(128, 1)
 
   if (warp == 0) {
     if (lane == 0) {  // TMA producer
+      // The vocabulary tiles do not depend on the kernel before this one (launched as a programmatic
+      // dependent, this kernel may start while that one still writes the draft rows' parts): the
+      // first stages' tiles are requested before waiting for it, the parts after.
+      const int pre = KB < STAGES ? KB : STAGES;
+      for (int kb = 0; kb < pre; ++kb) {
+        mbar_arrive_expect_tx(&full[kb], Cfg::STAGE_BYTES);
+        tma_load_2d(base + size_t(kb) * Cfg::STAGE_BYTES, &tma_e, int32_t(kb * TC_BK), int32_t(v0), &full[kb]);
+      }
+      asm volatile("griddepcontrol.wait;" ::: "memory");  // no-op unless launched as a dependent
       for (int kb = 0; kb < KB; ++kb) {
         const int s = kb % STAGES;
-        if (kb >= STAGES &&
-            !mbar_wait_bounded(&empty[s], uint32_t(((kb / STAGES) - 1) & 1), &g_error_word, DEV_ERR_WAIT_TIMEOUT))
-          break;
         uint8_t* st = base + size_t(s) * Cfg::STAGE_BYTES;
-        mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
-        tma_load_2d(st, &tma_e, int32_t(kb * TC_BK), int32_t(v0), &full[s]);
+        if (kb >= pre) {
+          if (!mbar_wait_bounded(&empty[s], uint32_t(((kb / STAGES) - 1) & 1), &g_error_word, DEV_ERR_WAIT_TIMEOUT))
+            break;
+          mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+          tma_load_2d(st, &tma_e, int32_t(kb * TC_BK), int32_t(v0), &full[s]);
+        }
 #pragma unroll
         for (int part = 0; part < 3; ++part)
           tma_load_2d(st + Cfg::A_BYTES + part * Cfg::B_PART, &tma_h, int32_t(part * d + kb * TC_BK), int32_t(r0),

@@ -161,9 +161,19 @@ def ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+_cur_device = getattr(torch._C, "_cuda_getDevice", None)
+
+
 def stream_ptr(stream: torch.cuda.Stream | None = None) -> int:
-    s = stream if stream is not None else torch.cuda.current_stream()
-    return s.cuda_stream
+    """The cudaStream_t (as an int) of ``stream``, or of the current device's current stream: read
+    straight from torch's C layer when it offers the call (a Stream object per call costs ~10 us of
+    host time, which the short decode / tree steps would otherwise spend once per launch)."""
+    if stream is not None:
+        return stream.cuda_stream
+    if _raw_stream is not None and _cur_device is not None and torch.cuda.is_initialized():
+        return int(_raw_stream(_cur_device()))
+    return torch.cuda.current_stream().cuda_stream
 
 
 def device_error(clear: bool = True) -> int:

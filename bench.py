@@ -199,9 +199,8 @@ def sb_inputs(pkg, mem, dev, seed: int):
 
 
 def layer_bytes_per_position() -> int:
-    """Algorithmic bytes of the memory lookup per position (the rows a position must read, plus its hidden
-    state in and output out): the R rows
-    of every order (bf16) + the hidden state in + the output out (d bf16 each) = 54,144 B at SB."""
+    """Algorithmic bytes of the memory lookup per position: the R rows of every order (bf16) a position
+    must read + its hidden state in + its output out (d bf16 each) = 54,144 B at SB."""
     c = SB
     dt = len(c["ngrams"]) * c["mem_dim"]
     return c["routes"] * dt * 2 + 2 * c["d"] * 2

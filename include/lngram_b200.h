@@ -414,6 +414,21 @@ int lng_drafter_trace(lng_drafter* d, const int64_t* tokens_host, int64_t T, con
 int lng_drafter_draft_batch(lng_drafter* d, const int64_t* prefix, int64_t nseq, int64_t plen, int64_t gamma,
                             int64_t* tokens_out, lng_stream_t stream);
 
+/* The in-context online-count mixer of the acceptance harness (drafting/drafters.py:117-143,
+ * OnlineCounts(codes, x, orders, bits, vocab, kappa).mix(p, win, real, deadline)).  One record: codes
+ * [T, R] (i64) and tokens x [T] (i64) give the verified pairs (t, x[t+1]), t < T-1, each keyed per order n
+ * and route r by the row of the n-gram ending at t (drafting/build_sketches.py:186-197; -1 for t < n-1).
+ * Query j's window win [N, W, R] (i64) with real [N, W] (u8) gives its rows (drafters.py:99-107; -1 unless
+ * the last n slots are real).  w[j, t] = the (n, r) rows pair t shares with query j, for t <= deadline[j]
+ * (i64 [N]); out [N, V] = (1 - lam) p + lam sc / max(tot, 1e-9) with sc[j, v] = sum of w[j, t] over pairs
+ * whose next token is v, tot = sum_t w, lam = n_eff / (n_eff + kappa), n_eff = tot / (R n_orders), in
+ * the reference's fp32 operation order (bit-identical results).  p, out: f32 [N, V], may alias.  All
+ * device pointers; n_orders <= 8, orders in [1, 8], bits * order <= 40. */
+int lng_online_counts_mix(const int64_t* codes, int64_t T, int64_t R, const int32_t* orders_host, int32_t n_orders,
+                          int32_t bits, const int64_t* x, const int64_t* win, const uint8_t* real, int64_t N, int64_t W,
+                          const int64_t* deadline, const float* p, int64_t V, float kappa, float* out,
+                          lng_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -8,10 +8,10 @@ behind the C ABI of ``include/lngram_b200.h``.  There is no CPU fallback.
 
 from . import _lib
 from .bundle import Bundle, load_bundle, read_header, write_bundle
-from .drafter import DraftOut, Drafter, GpuDrafter, make_drafter
+from .drafter import DraftOut, Drafter, GpuDrafter, OnlineCounts, make_drafter
 from .memory import LngramIncrementalState, LngramMemory, RouteNgramMemoryV2, rms_norm
 
-__all__ = ["Bundle", "DraftOut", "Drafter", "GpuDrafter", "LngramIncrementalState", "LngramMemory", "RouteNgramMemoryV2", "_lib", "load_bundle",
+__all__ = ["Bundle", "DraftOut", "Drafter", "GpuDrafter", "LngramIncrementalState", "OnlineCounts", "LngramMemory", "RouteNgramMemoryV2", "_lib", "load_bundle",
            "make_drafter", "read_header", "rms_norm", "write_bundle"]
 from .seams import MemoryCache, ancestor_table, decode_memory_step, memory_step, tree_memory_block, tree_ngram_codes, tree_slots  # noqa: E402
 

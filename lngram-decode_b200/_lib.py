@@ -115,6 +115,7 @@ SIGNATURES = {
     "lng_drafter_draft": (C.c_int, [P, i64, P, i64, i32, i32, P, P, P, P]),
     "lng_drafter_trace": (C.c_int, [P, P, i64, P, i32, i64, P, P, P]),
     "lng_drafter_draft_batch": (C.c_int, [P, P, i64, i64, i64, P, P]),
+    "lng_online_counts_mix": (C.c_int, [P, i64, i64, P, i32, i32, P, P, P, i64, i64, P, P, i64, f32, P, P]),
 }
 
 _LIB = None

@@ -104,7 +104,10 @@ template <int BN>
 struct TcCfg {
   static constexpr uint32_t A_BYTES = TC_BM * TC_BK * 2;
   static constexpr uint32_t B_BYTES = BN * TC_BK * 2;
-  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  // two k blocks per stage ([A0 | A1 | B0 | B1], half the stage handshakes) whenever three such stages
+  // fit; one otherwise (BN = 256)
+  static constexpr int KPS = (200 * 1024) / (2 * (A_BYTES + B_BYTES)) >= 3 ? 2 : 1;
+  static constexpr uint32_t STAGE_BYTES = KPS * (A_BYTES + B_BYTES);
   static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
   // two accumulators (tile i and tile i + 1) of BN columns each, allocated as a power of two
   static constexpr uint32_t TMEM_COLS = 2 * BN <= 32 ? 32 : 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
@@ -184,25 +187,28 @@ __global__ void __launch_bounds__(192, 1)
         int kb0, kb1, sp;
         tile_of(t, m0, n0, kb0, kb1, sp);
         bool ok = true;
-        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; kb += Cfg::KPS, ++it) {
           const int s = int(it % STAGES);
           if (it >= uint32_t(STAGES) && !wait(&empty[s], ((it / STAGES) - 1) & 1)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+          const int nk = kb1 - kb < Cfg::KPS ? kb1 - kb : Cfg::KPS;  // k blocks in this stage
+          mbar_arrive_expect_tx(&full[s], uint32_t(nk) * (Cfg::A_BYTES + Cfg::B_BYTES));
           uint8_t* st = base + size_t(s) * Cfg::STAGE_BYTES;
-          int32_t ka, kbx;
-          if (p.npairs > 0) {
-            const int pr = kb / pkb, kk = (kb - pr * pkb) * TC_BK;
-            ka = int32_t(p.a_part[pr] * p.part_k + kk);
-            kbx = int32_t(p.b_part[pr] * p.part_k + kk);
-          } else {
-            ka = int32_t((int64_t(kb) * TC_BK) % p.a_kperiod);
-            kbx = int32_t(kb * TC_BK);
+          for (int j = 0; j < nk; ++j) {
+            int32_t ka, kbx;
+            if (p.npairs > 0) {
+              const int pr = (kb + j) / pkb, kk = (kb + j - pr * pkb) * TC_BK;
+              ka = int32_t(p.a_part[pr] * p.part_k + kk);
+              kbx = int32_t(p.b_part[pr] * p.part_k + kk);
+            } else {
+              ka = int32_t((int64_t(kb + j) * TC_BK) % p.a_kperiod);
+              kbx = int32_t((kb + j) * TC_BK);
+            }
+            tma_load_2d(st + j * Cfg::A_BYTES, &tma_a, ka, int32_t(m0), &full[s]);
+            tma_load_2d(st + Cfg::KPS * Cfg::A_BYTES + j * Cfg::B_BYTES, &tma_b, kbx, int32_t(n0), &full[s]);
           }
-          tma_load_2d(st, &tma_a, ka, int32_t(m0), &full[s]);
-          tma_load_2d(st + Cfg::A_BYTES, &tma_b, kbx, int32_t(n0), &full[s]);
         }
         if (!ok) break;
       }
@@ -220,7 +226,7 @@ __global__ void __launch_bounds__(192, 1)
         tc_fence_after();
         const uint32_t d = tmem + ab * uint32_t(BN);
         bool ok = true;
-        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; kb += Cfg::KPS, ++it) {
           const int s = int(it % STAGES);
           if (!wait(&full[s], (it / STAGES) & 1)) {
             ok = false;
@@ -228,11 +234,15 @@ __global__ void __launch_bounds__(192, 1)
           }
           tc_fence_after();
           const uint8_t* st = base + size_t(s) * Cfg::STAGE_BYTES;
-          const uint64_t da = umma_desc_sw128(st), db = umma_desc_sw128(st + Cfg::A_BYTES);
+          const int nk = kb1 - kb < Cfg::KPS ? kb1 - kb : Cfg::KPS;
+          for (int j = 0; j < nk; ++j) {
+            const uint64_t da = umma_desc_sw128(st + j * Cfg::A_BYTES),
+                           db = umma_desc_sw128(st + Cfg::KPS * Cfg::A_BYTES + j * Cfg::B_BYTES);
 #pragma unroll
-          for (int k = 0; k < TC_BK / 16; ++k)
-            // advance 16 bf16 = 32 bytes along K inside the swizzle atom (+2 in 16-byte units)
-            umma_bf16(d, da + uint64_t(2 * k), db + uint64_t(2 * k), idesc, (kb != kb0 || k != 0) ? 1u : 0u);
+            for (int k = 0; k < TC_BK / 16; ++k)
+              // advance 16 bf16 = 32 bytes along K inside the swizzle atom (+2 in 16-byte units)
+              umma_bf16(d, da + uint64_t(2 * k), db + uint64_t(2 * k), idesc, (kb + j != kb0 || k != 0) ? 1u : 0u);
+          }
           umma_commit(&empty[s]);
         }
         if (!ok) break;

@@ -21,6 +21,7 @@
 #include "topk.cuh"
 #include "drafter_ext.cuh"
 #include "surrogate.cuh"
+#include "online.cuh"
 
 static int scratch_alloc(void** p, size_t bytes, cudaStream_t stream);
 
@@ -1518,6 +1519,75 @@ extern "C" int lng_logits_topk_static(const float* h, int64_t n, int64_t d, cons
   if (st) return st;
   topk_merge_kernel<<<unsigned(ceil_div(n * 32, 256)), 256, 0, S(stream)>>>(cand_v, cand_i, n, nch, k, ids, vals);
   LNG_LAUNCHED("topk_merge_kernel (static scratch)");
+  return LNG_OK;
+}
+
+// ====================================================================== online counts (acceptance harness)
+extern "C" int lng_online_counts_mix(const int64_t* codes, int64_t T, int64_t R, const int32_t* orders_host,
+                                     int32_t n_orders, int32_t bits, const int64_t* x, const int64_t* win,
+                                     const uint8_t* real, int64_t N, int64_t W, const int64_t* deadline, const float* p,
+                                     int64_t V, float kappa, float* out, lng_stream_t stream) {
+  LNG_REQUIRE(T >= 0 && R > 0 && N >= 0 && V > 0 && W >= 1, "bad online-counts shape");
+  LNG_REQUIRE(n_orders >= 1 && n_orders <= OC_MAX_ORDERS && orders_host, "n_orders must be in [1, 8]");
+  LNG_REQUIRE(bits >= 1 && bits <= 16, "bits must be in [1, 16]");
+  OnlineParams op{};
+  for (int o = 0; o < n_orders; ++o) {
+    LNG_REQUIRE(orders_host[o] >= 1 && orders_host[o] <= 8 && orders_host[o] <= W && int64_t(bits) * orders_host[o] <= 40,
+                "orders must be in [1, min(8, W)] with bits x order <= 40");
+    op.orders[o] = orders_host[o];
+  }
+  if (N == 0) return LNG_OK;
+  LNG_REQUIRE(p && out && win && real && deadline, "NULL pointer");
+  cudaStream_t s = S(stream);
+  if (T < 2) {  // no verified pair: out = p
+    if (out != p) LNG_CUDA(cudaMemcpyAsync(out, p, size_t(N * V) * 4, cudaMemcpyDeviceToDevice, s));
+    return LNG_OK;
+  }
+  LNG_REQUIRE(codes && x, "NULL pointer");
+  op.codes = codes;
+  op.T = T;
+  op.R = R;
+  op.n_orders = n_orders;
+  op.bits = bits;
+  op.x = x;
+  op.win = win;
+  op.real = real;
+  op.N = N;
+  op.W = W;
+  op.deadline = deadline;
+  op.V = V;
+  const int64_t T1 = T - 1;
+  const size_t keys_b = al256(size_t(n_orders) * T1 * R * 8), q_b = al256(size_t(n_orders) * N * R * 8),
+               tot_b = al256(size_t(N) * 4), sc_b = size_t(N) * V * 4;
+  // p and out may alias: the votes go to a scratch of their own then
+  const bool alias = p == out;
+  void* buf = nullptr;
+  int st = scratch_alloc(&buf, keys_b + q_b + tot_b + (alias ? sc_b : 0), s);
+  if (st) return st;
+  auto* keys = static_cast<int64_t*>(buf);
+  auto* q = reinterpret_cast<int64_t*>(static_cast<unsigned char*>(buf) + keys_b);
+  auto* tot = reinterpret_cast<float*>(static_cast<unsigned char*>(buf) + keys_b + q_b);
+  float* sc = alias ? reinterpret_cast<float*>(static_cast<unsigned char*>(buf) + keys_b + q_b + tot_b) : out;
+  cudaError_t e = cudaMemsetAsync(tot, 0, size_t(N) * 4, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(sc, 0, sc_b, s);
+  if (e == cudaSuccess) {
+    online_keys_kernel<<<grid_for(int64_t(n_orders) * T1 * R, 256, 8), 256, 0, s>>>(op, keys);
+    online_queries_kernel<<<grid_for(int64_t(n_orders) * N * R, 256, 8), 256, 0, s>>>(op, q);
+    const dim3 g(unsigned(std::min<int64_t>(ceil_div(T1, 128), 1024)), unsigned(N));
+    online_votes_kernel<<<g, 128, 0, s>>>(op, keys, q, tot, sc);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess && alias) {
+    // the mix reads p and the votes element by element: move the votes into out after p is read
+    online_mix_kernel<<<grid_for(N * V, 256, 8), 256, 0, s>>>(p, tot, N, V, float(R * n_orders), kappa, sc);
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaMemcpyAsync(out, sc, sc_b, cudaMemcpyDeviceToDevice, s);
+  } else if (e == cudaSuccess) {
+    online_mix_kernel<<<grid_for(N * V, 256, 8), 256, 0, s>>>(p, tot, N, V, float(R * n_orders), kappa, out);
+    e = cudaGetLastError();
+  }
+  cudaFreeAsync(buf, s);
+  if (e != cudaSuccess) return cuda_status(e, "online counts");
   return LNG_OK;
 }
 

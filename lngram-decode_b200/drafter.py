@@ -300,3 +300,42 @@ def make_drafter(bundle, impl: str = "b200", **kw):
     if impl != "b200":
         raise ValueError(f"unknown drafter impl {impl!r}")
     return GpuDrafter(bundle, **kw)
+
+
+class OnlineCounts:
+    """``drafting/drafters.py:117-143``: in-context (order, route, row) -> next-token counts from one
+    record's verified pairs, mixed into a drafter's distribution on the GPU (``lng_online_counts_mix``:
+    the same fp32 results as the reference).  ``codes`` [T, R] and ``x`` [T] are the record's codes and
+    tokens; ``route_chunk`` is accepted for the reference's signature (the kernel compares every route
+    at once)."""
+
+    def __init__(self, codes: torch.Tensor, x: torch.Tensor, orders, bits: int, vocab: int, kappa: float = 1.0,
+                 route_chunk: int = 32):
+        if codes.dim() != 2 or x.dim() != 1 or codes.shape[0] != x.shape[0]:
+            raise ValueError("codes must be [T, R] and x [T]")
+        self.codes = codes.to(torch.int64).contiguous()
+        self.x = x.to(device=self.codes.device, dtype=torch.int64).contiguous()
+        self.nxt = self.x[1:]
+        self.orders, self.bits, self.vocab, self.kappa, self.rc = tuple(int(n) for n in orders), int(bits), \
+            int(vocab), float(kappa), int(route_chunk)
+        self.routes = self.codes.shape[1]
+        self._orders = (C.c_int32 * len(self.orders))(*self.orders)
+
+    def mix(self, p: torch.Tensor, win: torch.Tensor, real: torch.Tensor, deadline: torch.Tensor) -> torch.Tensor:
+        """p [N, V]; only pairs t <= deadline[j] (token t+1 verified for row j) count."""
+        dev = self.codes.device
+        if not dev.type == "cuda":
+            raise RuntimeError("OnlineCounts runs on the GPU: give it device tensors")
+        n_rows, W = win.shape[0], win.shape[1]
+        p = p.to(device=dev, dtype=torch.float32).contiguous()
+        win = win.to(device=dev, dtype=torch.int64).contiguous()
+        real = real.to(device=dev, dtype=torch.uint8).contiguous()
+        deadline = deadline.to(device=dev, dtype=torch.int64).reshape(n_rows).contiguous()
+        out = torch.empty_like(p)
+        with torch.cuda.device(dev):
+            _lib.check(_lib.library().lng_online_counts_mix(
+                self.codes.data_ptr(), self.codes.shape[0], self.routes, self._orders, len(self.orders), self.bits,
+                self.x.data_ptr(), win.data_ptr(), real.data_ptr(), n_rows, W, deadline.data_ptr(), p.data_ptr(),
+                p.shape[1], self.kappa, out.data_ptr(), _lib.stream_ptr()), "online counts")
+        return out
+

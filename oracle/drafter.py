@@ -258,3 +258,57 @@ class OracleDrafter:
             m = min(len(sl), s_dim)
             out_i[t, :m], out_l[t, :m] = sl[:m], lg[:m]
         return out_c, out_i, out_l
+
+
+# ------------------------------------------------------------------ online counts (acceptance harness)
+def ngram_rows_seq(codes: np.ndarray, order: int, bits: int) -> np.ndarray:
+    """``drafting/build_sketches.py:186-197`` (``seq_rows``) for one record: rows [T, R] of the n-grams
+    ending at each t (oldest code least significant, route offset r * 2^(bits order)); -1 for t < order-1."""
+    T, R = codes.shape
+    c = codes.astype(np.int64)
+    out = np.full((T, R), -1, np.int64)
+    if T >= order:
+        addr = c[: T - order + 1].copy()
+        for e in range(1, order):
+            addr |= c[e: e + T - order + 1] << (e * bits)
+        out[order - 1:] = np.arange(R, dtype=np.int64) * (1 << (bits * order)) + addr
+    return out
+
+
+def ngram_rows_window(win: np.ndarray, real: np.ndarray, order: int, bits: int) -> np.ndarray:
+    """``drafting/drafters.py:99-107`` (``window_rows``): rows [N, R] of the n-gram ending at each window's
+    last slot, -1 unless its last ``order`` slots are all real."""
+    N, W, R = win.shape
+    c = win[:, W - order:].astype(np.int64)
+    addr = c[:, 0].copy()
+    for e in range(1, order):
+        addr |= c[:, e] << (e * bits)
+    rows = np.arange(R, dtype=np.int64) * (1 << (bits * order)) + addr
+    ok = real[:, W - order:].all(1)
+    return np.where(ok[:, None], rows, -1)
+
+
+def online_counts_mix(codes, x, orders, bits: int, vocab: int, kappa: float, p, win, real, deadline) -> np.ndarray:
+    """``drafting/drafters.py:117-143`` (``OnlineCounts(codes, x, ...).mix(p, win, real, deadline)``): the
+    record's verified pairs (t, x[t+1]) vote for x[t+1] with weight w[j, t] = the (order, route) rows that
+    pair t shares with query window j (pairs t <= deadline[j] only); the votes' distribution is mixed
+    into p with lambda = n_eff / (n_eff + kappa), n_eff = sum_t w / (R x orders), in the reference's
+    fp32 operation order."""
+    codes = np.asarray(codes)
+    T, R = codes.shape
+    nxt = np.asarray(x, np.int64)[1:]
+    p = np.asarray(p, F32)
+    N = p.shape[0]
+    w = np.zeros((N, T - 1), F32)
+    for n in orders:
+        keys = ngram_rows_seq(codes, n, bits)[:-1]                       # pairs t = 0 .. T-2
+        q = ngram_rows_window(np.asarray(win), np.asarray(real, bool), n, bits)
+        w += ((keys[None] == q[:, None]) & (q[:, None] >= 0)).sum(-1).astype(F32)
+    w = w * (np.arange(T - 1)[None] <= np.asarray(deadline)[:, None]).astype(F32)
+    tot = w.sum(1, keepdims=True, dtype=F32)
+    sc = np.zeros((N, vocab), F32)
+    for j in range(N):
+        np.add.at(sc[j], nxt, w[j])
+    n_eff = (tot / F32(R * len(orders))).astype(F32)
+    lam = (n_eff / (n_eff + F32(kappa))).astype(F32)
+    return ((F32(1) - lam) * p + (lam * sc) / np.maximum(tot, F32(1e-9))).astype(F32)

@@ -315,6 +315,49 @@ def write_surrogate() -> None:
     print("surrogate_backward.npz", {k: np.shape(v) for k, v in out.items()})
 
 
+ONLINE_CASES = (((3,), 4, 1.0), ((1, 2), 2, 0.5))   # (orders, bits, kappa)
+
+
+def online_inputs(i: int, orders, bits: int) -> dict:
+    """Seeded inputs of an online-counts case: a record's codes [T, R] and tokens [T] with repeated
+    stretches (so in-context n-grams recur), windows [N, W, R] of it with leading non-real slots, the
+    verified-pair deadlines and a distribution p [N, V]."""
+    rng = np.random.default_rng(70 + i)
+    T, R, V, N = 48, 6, 50, 9
+    W = max(orders)
+    codes = rng.integers(0, 1 << bits, (T, R))
+    x = rng.integers(0, V, T)
+    codes[20:30] = codes[5:15]                      # a repeated stretch of codes and tokens
+    x[20:30] = x[5:15]
+    last = rng.integers(0, T - 1, N)
+    last[0] = 0
+    pos = last[:, None] - (W - 1) + np.arange(W)[None]
+    real = pos >= 0
+    win = codes[np.clip(pos, 0, None)] * real[..., None]
+    p = rng.random((N, V)).astype(np.float32)
+    p /= p.sum(-1, keepdims=True)
+    return {"codes": codes.astype(np.int64), "x": x.astype(np.int64), "win": win.astype(np.int64), "real": real,
+            "deadline": (last - 1).astype(np.int64), "p": p, "vocab": V}
+
+
+def write_online() -> None:
+    """The online-count mixer of the acceptance harness (``drafting/drafters.py:117-143``) on seeded
+    records: the mixed distribution for each case."""
+    import torch
+    from drafting.drafters import OnlineCounts
+
+    out = {}
+    for i, (orders, bits, kappa) in enumerate(ONLINE_CASES):
+        inp = online_inputs(i, orders, bits)
+        oc = OnlineCounts(_t(inp["codes"]), _t(inp["x"]), orders, bits, inp["vocab"], kappa)
+        mixed = oc.mix(_t(inp["p"]), _t(inp["win"]), _t(inp["real"]), _t(inp["deadline"]))
+        for k, v in inp.items():
+            out[f"c{i}_{k}"] = np.asarray(v)
+        out[f"c{i}_mixed"] = mixed.numpy()
+    np.savez_compressed(HERE / "online_counts.npz", **out)
+    print("online_counts.npz", {k: np.shape(v) for k, v in out.items()})
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--reference", default=os.environ.get("LNGRAM_REFERENCE") or str(HERE.parents[2] / "reference"))
@@ -324,7 +367,7 @@ def main(argv=None) -> None:
     import torch
 
     torch.set_num_threads(max(1, os.cpu_count() or 1))
-    todo = args.only or ["memory", "seams", "draft", "incremental", "serving", "surrogate"]
+    todo = args.only or ["memory", "seams", "draft", "incremental", "serving", "surrogate", "online"]
     if "memory" in todo:
         for case in cases.MEMORY_CASES:
             write_memory_case(case)
@@ -340,6 +383,8 @@ def main(argv=None) -> None:
         write_serving("tiny_multi")
     if "surrogate" in todo:
         write_surrogate()
+    if "online" in todo:
+        write_online()
 
 
 if __name__ == "__main__":

@@ -232,3 +232,16 @@ def test_surrogate_backward_matches_reference_fixture(golden):
             got = np.stack([tg[n].get(int(r), np.zeros(c["mem_dim"], np.float32)) for r in rows])
             assert_fp32_close(got, g[f"c{i}_grad_table_{n}"], what=f"case {i} table {n} grad")
             assert set(int(r) for r, v in tg[n].items() if np.any(v != 0)) <= set(rows.tolist())
+
+
+def test_online_counts_oracle_matches_reference(golden):
+    """The online-count mixer restated (``oracle.drafter.online_counts_mix``) equals the reference's
+    ``OnlineCounts.mix`` bit for bit on the fixture's records (mixed and unmixed rows, deadlines of -1)."""
+    from oracle.drafter import online_counts_mix
+    from tests.golden.make_golden import ONLINE_CASES
+
+    g = golden("online_counts")
+    for i, (orders, bits, kappa) in enumerate(ONLINE_CASES):
+        got = online_counts_mix(g[f"c{i}_codes"], g[f"c{i}_x"], orders, bits, int(g[f"c{i}_vocab"]), kappa,
+                                g[f"c{i}_p"], g[f"c{i}_win"], g[f"c{i}_real"], g[f"c{i}_deadline"])
+        np.testing.assert_array_equal(got, g[f"c{i}_mixed"])

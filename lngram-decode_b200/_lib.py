@@ -7,6 +7,7 @@ built and a CUDA device of compute capability 10.x is present.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes as C
 from pathlib import Path
 
@@ -164,6 +165,15 @@ def ptr(t: torch.Tensor | None) -> int | None:
 
 _raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
 _cur_device = getattr(torch._C, "_cuda_getDevice", None)
+
+
+def on_device(device):
+    """``torch.cuda.device(device)`` unless ``device`` is current already (then a no-op context): the
+    guard's own device lookups cost microseconds of host time on every library call."""
+    idx = device.index if isinstance(device, torch.device) else device
+    if idx is None or (_cur_device is not None and torch.cuda.is_initialized() and _cur_device() == idx):
+        return contextlib.nullcontext()
+    return torch.cuda.device(device)
 
 
 def stream_ptr(stream: torch.cuda.Stream | None = None) -> int:

@@ -104,7 +104,7 @@ class Drafter:
                 arr[i].shape[j] = s
         handle = C.c_void_p()
         lib = _lib.library()
-        with torch.cuda.device(self.device):
+        with _lib.on_device(self.device):
             _raise(lib.lng_drafter_create(C.byref(nums), arr, len(tensors), _lib.dtype_code(act_dtype),
                                           C.byref(handle)), "Drafter")
         self._keep = None  # the library holds device copies
@@ -142,7 +142,7 @@ class Drafter:
             if cc.ndim != 2 or cc.shape != (len(toks), self.R):
                 raise RuntimeError("codes must be [n, R]")
             cp = cc.ctypes.data
-        with torch.cuda.device(self.device):
+        with _lib.on_device(self.device):
             _raise(_lib.library().lng_drafter_commit(self._h, toks.ctypes.data, len(toks), cp), "commit")
 
     def draft(self, gamma: int, hyp, topk: int = 3, last_codes: bool = False):
@@ -157,7 +157,7 @@ class Drafter:
         lg = np.full((max(gamma, 1), k), -np.inf, np.float32)
         n_codes = len(hypa) + (gamma if last_codes else max(gamma - 1, 0))
         codes = np.zeros((max(n_codes, 1), self.R), np.uint8)
-        with torch.cuda.device(self.device):
+        with _lib.on_device(self.device):
             _raise(_lib.library().lng_drafter_draft(self._h, gamma, hypa.ctypes.data if len(hypa) else None, len(hypa),
                                                     k, int(bool(last_codes)), toks.ctypes.data, ids.ctypes.data,
                                                     lg.ctypes.data, codes.ctypes.data), "draft")
@@ -184,7 +184,7 @@ class Drafter:
         oi = np.full((T, S), -1, np.int64)
         ol = np.full((T, S), -np.inf, np.float32)
         if T:
-            with torch.cuda.device(self.device):
+            with _lib.on_device(self.device):
                 _raise(_lib.library().lng_drafter_trace(self._h, toks.ctypes.data, T, cp, int(bool(full)), S,
                                                         oc.ctypes.data, oi.ctypes.data, ol.ctypes.data), "trace")
         return torch.from_numpy(oc), torch.from_numpy(oi), torch.from_numpy(ol)
@@ -199,7 +199,7 @@ class Drafter:
         nseq, plen = prefix.shape
         if out is None:
             out = torch.empty(nseq, gamma, device=self.device, dtype=torch.int64)
-        with torch.cuda.device(self.device):
+        with _lib.on_device(self.device):
             _lib.check(_lib.library().lng_drafter_draft_batch(self._h, prefix.data_ptr(), nseq, plen, int(gamma),
                                                               out.data_ptr(), _lib.stream_ptr()), "draft_batch")
         return out
@@ -332,7 +332,7 @@ class OnlineCounts:
         real = real.to(device=dev, dtype=torch.uint8).contiguous()
         deadline = deadline.to(device=dev, dtype=torch.int64).reshape(n_rows).contiguous()
         out = torch.empty_like(p)
-        with torch.cuda.device(dev):
+        with _lib.on_device(dev):
             _lib.check(_lib.library().lng_online_counts_mix(
                 self.codes.data_ptr(), self.codes.shape[0], self.routes, self._orders, len(self.orders), self.bits,
                 self.x.data_ptr(), win.data_ptr(), real.data_ptr(), n_rows, W, deadline.data_ptr(), p.data_ptr(),

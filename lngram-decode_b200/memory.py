@@ -83,7 +83,7 @@ def rms_norm(x: Tensor, weight: Tensor | None, eps: float) -> Tensor:
     out_dt = x.dtype if weight is None else torch.promote_types(x.dtype, weight.dtype)
     d = x.shape[-1]
     y = torch.empty(x.shape, device=x.device, dtype=out_dt)
-    with torch.cuda.device(x.device):
+    with _lib.on_device(x.device):
         check(_lib.library().lng_rms_norm_model(ptr(x), _lib.dtype_code(x.dtype), x.numel() // d, d, ptr(weight),
                                                 _lib.dtype_code(weight.dtype) if weight is not None else 0,
                                                 float(eps), ptr(y), _lib.dtype_code(out_dt), stream_ptr()),
@@ -145,7 +145,7 @@ class _TrainLookup(torch.autograd.Function):
         if has_q and ctx.needs_input_grad[2]:
             q32 = q.float().contiguous()
             gq = torch.empty(b, t, re - rs, m.bits_per_route, device=q.device, dtype=torch.float32)
-        with torch.cuda.device(grad.device):
+        with _lib.on_device(grad.device):
             check(_lib.library().lng_lookup_backward(
                 m.tables_desc(with_ss=False), ptr(codes), _lib.U8 if codes.dtype == torch.uint8 else _lib.I32, b, t,
                 rs, re, ptr(seg) if has_seg else None, ptr(val) if has_val else None, ptr(grad),
@@ -271,7 +271,7 @@ class RouteNgramMemoryV2(nn.Module):
         desc = self.tables_desc(with_ss=False)
         arr = (_lib.C.c_void_p * _lib.MAX_ORDERS)(*([ss[n].data_ptr() for n in self.ngrams] +
                                                     [None] * (_lib.MAX_ORDERS - len(self.ngrams))))
-        with torch.cuda.device(ws[0].device):
+        with _lib.on_device(ws[0].device):
             check(_lib.library().lng_table_row_ss(desc, arr, stream_ptr()), "table row sums of squares")
         self._ss, self._ss_key = ss, key
         return ss
@@ -319,7 +319,7 @@ class RouteNgramMemoryV2(nn.Module):
         qh, dt, d = self.readout_num_heads, self.route_token_dim, self.hidden_size
         w_qk = torch.empty(qh * dt, d, device=dev, dtype=act)
         w_vo = torch.empty(d, qh * dt, device=dev, dtype=act)
-        with torch.cuda.device(dev):
+        with _lib.on_device(dev):
             check(lib.lng_fold_readout(d, dt, qh, self.readout_num_kv_heads, self.readout_head_dim, ptr(f32[0]),
                                        ptr(f32[1]), ptr(f32[2]), ptr(f32[3]), ptr(f32[4]), ptr(w_qk), ptr(w_vo),
                                        _lib.dtype_code(act), stream_ptr()), "fold readout")
@@ -356,7 +356,7 @@ class RouteNgramMemoryV2(nn.Module):
         x = _cuda(q_logits, "q_logits").float().contiguous()
         out = torch.empty(*x.shape[:-1], self.num_routes, device=x.device, dtype=torch.int32)
         n = x.numel() // self.route_logits_dim
-        with torch.cuda.device(x.device):
+        with _lib.on_device(x.device):
             check(_lib.library().lng_quantize_route_logits(ptr(x), n, self.num_routes, self.bits_per_route, ptr(out),
                                                            _lib.I32, stream_ptr()), "quantize_route_logits")
         return out
@@ -401,7 +401,7 @@ class RouteNgramMemoryV2(nn.Module):
         seg = None if segment_ids is None else segment_ids.to(device=codes.device, dtype=torch.int64).contiguous()
         val = None if valid_tokens is None else valid_tokens.to(device=codes.device, dtype=torch.bool).contiguous()
         desc = self.tables_desc()
-        with torch.cuda.device(codes.device):
+        with _lib.on_device(codes.device):
             check(_lib.library().lng_lookup_route_chunk(desc, ptr(codes), cdt, b, t, int(route_start), int(route_end),
                                                         ptr(seg), ptr(val), int(tout) if target_length is not None else 0,
                                                         ptr(out), _lib.dtype_code(out.dtype), stream_ptr()),
@@ -416,7 +416,7 @@ class RouteNgramMemoryV2(nn.Module):
         m = x.numel() // k
         n = w.shape[0]
         out = torch.empty(*x.shape[:-1], n, device=x.device, dtype=out_dtype or x.dtype)
-        with torch.cuda.device(x.device):
+        with _lib.on_device(x.device):
             check(_lib.library().lng_gemm(ptr(x), _lib.dtype_code(x.dtype), k, ptr(w), _lib.dtype_code(w.dtype), k,
                                           ptr(out), _lib.dtype_code(out.dtype), n, m, n, k, None, 0, stream_ptr()),
                   "gemm")
@@ -427,7 +427,7 @@ class RouteNgramMemoryV2(nn.Module):
         d = x.shape[-1]
         wf = w.detach().float().contiguous()
         out = torch.empty_like(x)
-        with torch.cuda.device(x.device):
+        with _lib.on_device(x.device):
             check(_lib.library().lng_rms_norm(ptr(x), _lib.dtype_code(x.dtype), x.numel() // d, d, ptr(wf), self.eps,
                                               ptr(out), _lib.dtype_code(out.dtype), stream_ptr()), "rms_norm")
         return out
@@ -466,7 +466,7 @@ class RouteNgramMemoryV2(nn.Module):
         k, v = key.contiguous(), value.contiguous()
         r = k.shape[-2]
         out = torch.empty(b, t, self.readout_num_heads, self.readout_head_dim, device=q.device, dtype=q.dtype)
-        with torch.cuda.device(q.device):
+        with _lib.on_device(q.device):
             check(_lib.library().lng_sink_gqa(ptr(q), ptr(k), ptr(v), _lib.dtype_code(q.dtype), b * t,
                                               self.readout_num_kv_heads, self.readout_groups, r, self.readout_head_dim,
                                               self.readout_sink_logit, ptr(out), stream_ptr()), "_manual_gqa")
@@ -485,7 +485,7 @@ class RouteNgramMemoryV2(nn.Module):
         seg = None if segment_ids is None else segment_ids.to(device=mixed.device, dtype=torch.int64).contiguous()
         val = None if valid_tokens is None else valid_tokens.to(device=mixed.device, dtype=torch.bool).contiguous()
         desc = self.readout_desc()
-        with torch.cuda.device(mixed.device):
+        with _lib.on_device(mixed.device):
             check(_lib.library().lng_conv_finish(desc, ptr(mixed.contiguous()), b, t, ptr(seg), ptr(val), ptr(out),
                                                  None, stream_ptr()), "conv finish")
         return out
@@ -535,7 +535,7 @@ class RouteNgramMemoryV2(nn.Module):
         lib = _lib.library()
         s = stream_ptr()
         packed = torch.empty(b, R, dtype=torch.int32, device=dev)
-        with torch.cuda.device(dev):
+        with _lib.on_device(dev):
             if t == 1:
                 pin = (torch.zeros(b, R, dtype=torch.int32, device=dev) if state.packed_route_state is None
                        else state.packed_route_state.to(device=dev, dtype=torch.int32).contiguous())
@@ -604,7 +604,7 @@ class RouteNgramMemoryV2(nn.Module):
         need = lib.lng_memory_workspace_bytes(desc_t, desc_r, b * t)
         if workspace is None or workspace.numel() < need:
             workspace = torch.empty(need, device=h.device, dtype=torch.uint8)
-        with torch.cuda.device(h.device):
+        with _lib.on_device(h.device):
             check(lib.lng_memory_forward(desc_t, desc_r, b, t, ptr(h), xptr, xdt, cptr, cdt, ptr(seg), ptr(val),
                                          ptr(out), ptr(codes_out), ptr(workspace), workspace.numel(), stream_ptr()),
                   "memory forward")
@@ -649,7 +649,7 @@ class LngramMemory(nn.Module):
         n = x.numel() // x.shape[-1]
         logits = torch.empty(*x.shape[:-1], w.shape[0], device=x.device, dtype=torch.float32)
         codes = torch.empty(*x.shape[:-1], self.routes, device=x.device, dtype=torch.uint8)
-        with torch.cuda.device(x.device):
+        with _lib.on_device(x.device):
             check(_lib.library().lng_route_codes(ptr(x), _lib.dtype_code(x.dtype), n, x.shape[-1], x.shape[-1], ptr(w),
                                                  self.routes, self.bits, ptr(codes), _lib.U8, ptr(logits), stream_ptr()),
                   "route_logits")
@@ -666,7 +666,7 @@ class LngramMemory(nn.Module):
             return self._split
         wf = w.detach().float().contiguous()
         split = torch.empty(wf.shape[0], 3 * wf.shape[1], device=wf.device, dtype=torch.bfloat16)
-        with torch.cuda.device(wf.device):
+        with _lib.on_device(wf.device):
             check(_lib.library().lng_router_prepare(ptr(wf), wf.shape[0], wf.shape[1], ptr(split), stream_ptr()),
                   "router_prepare")
         self._split, self._split_key = split, key
@@ -681,7 +681,7 @@ class LngramMemory(nn.Module):
         codes = torch.empty(*x.shape[:-1], self.routes, device=x.device, dtype=torch.uint8)
         split = self.router_split() if x.dtype == torch.bfloat16 else None
         lib = _lib.library()
-        with torch.cuda.device(x.device):
+        with _lib.on_device(x.device):
             if split is not None:
                 check(lib.lng_route_codes_split(ptr(x), n, x.shape[-1], x.shape[-1], ptr(split), self.routes,
                                                 self.bits, ptr(codes), stream_ptr()), "route_codes")

@@ -48,7 +48,7 @@ def permute_table(weight: Tensor, routes: int, order: int, bits: int) -> Tensor:
     if not w.is_cuda and not w.is_pinned():
         w = w.pin_memory()
     dev = w.device if w.is_cuda else torch.device("cuda", torch.cuda.current_device())
-    with torch.cuda.device(dev):
+    with _lib.on_device(dev):
         check(_lib.library().lng_serving_permute(_device_address(w), _device_address(out), _lib.dtype_code(w.dtype),
                                                  routes, order, bits, w.shape[1], stream_ptr()), "serving permute")
         if not w.is_cuda:
@@ -129,7 +129,7 @@ class ZeroCopyGather:
         ctx = torch.cat((codes_all[:, L - h0:L].to(self.device, torch.uint8),
                          codes_new.to(self.device, torch.uint8)), 1).contiguous()
         out = torch.empty(b, n, r, len(ht.ngrams) * ht.dim, device=self.device, dtype=ht.dtype)
-        with torch.cuda.device(self.device):
+        with _lib.on_device(self.device):
             check(_lib.library().lng_lookup_serving_rows(ht.descriptor(), ptr(ctx), _lib.U8, b, h0 + n, n, ptr(out),
                                                          stream_ptr()), "zero-copy gather")
         self.rows_read += b * n * r * len(ht.ngrams)

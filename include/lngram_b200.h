@@ -300,6 +300,21 @@ int lng_conv_finish(const lng_readout* ro, const void* mixed, int64_t B, int64_t
 int lng_conv_window(const lng_readout* ro, const void* mixed, int64_t n, void* cache, const int64_t* new_slot,
                     const int64_t* slot, void* out, lng_stream_t stream);
 
+/* A draft tree's memory block in one call (drafting/tree.py:178-195; the steps of tree_memory_block): the
+ * n nodes of each of B sequences after L cached positions.  Node i's code window (W = history + 1 slots,
+ * oldest first) reads slot gidx[i, w] of [the last h0 cached codes | the nodes' new codes], zero where
+ * gok[i, w] == 0; seg [B*n, W] (i32) marks the window's valid slots for the row rule.  The nodes' codes
+ * codes_new [B, n, R] (u8) are written to cache_codes [B, max_len, R] at L .. L+n-1; the readout (1/rms(h),
+ * folded query, gather + sink attention over the windows, output map) gives mixed; lng_conv_window's
+ * step then writes the nodes' conv inputs to cache_conv [B*max_len, d] at new_slot and gives out
+ * [B, n, d] from the taps at slot [B*n, k].  h, out: act dtype; gidx: i64 [n, W]; gok: u8 [n, W]. */
+size_t lng_tree_workspace_bytes(const lng_tables* tables, const lng_readout* ro, int64_t B, int64_t n, int64_t W);
+int lng_tree_memory_block(const lng_tables* tables, const lng_readout* ro, int64_t B, int64_t n, int64_t W,
+                          int64_t L, int64_t h0, int64_t max_len, const void* h, const uint8_t* codes_new,
+                          uint8_t* cache_codes, void* cache_conv, const int64_t* gidx, const uint8_t* gok,
+                          const int32_t* seg, const int64_t* slot, const int64_t* new_slot, void* out, void* workspace,
+                          size_t workspace_bytes, lng_stream_t stream);
+
 /* Workspace bytes needed by lng_memory_forward for M = B*T positions and Dt / R of `tables`. */
 size_t lng_memory_workspace_bytes(const lng_tables* tables, const lng_readout* ro, int64_t M);
 

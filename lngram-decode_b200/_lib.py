@@ -116,6 +116,9 @@ SIGNATURES = {
     "lng_drafter_draft": (C.c_int, [P, i64, P, i64, i32, i32, P, P, P, P]),
     "lng_drafter_trace": (C.c_int, [P, P, i64, P, i32, i64, P, P, P]),
     "lng_drafter_draft_batch": (C.c_int, [P, P, i64, i64, i64, P, P]),
+    "lng_tree_workspace_bytes": (C.c_size_t, [PT, PR, i64, i64, i64]),
+    "lng_tree_memory_block": (C.c_int, [PT, PR, i64, i64, i64, i64, i64, i64, P, P, P, P, P, P, P, P, P, P, P,
+                                        C.c_size_t, P]),
     "lng_online_counts_mix": (C.c_int, [P, i64, i64, P, i32, i32, P, P, P, i64, i64, P, P, i64, f32, P, P]),
 }
 

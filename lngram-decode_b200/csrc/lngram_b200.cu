@@ -1273,6 +1273,72 @@ extern "C" int lng_memory_forward(const lng_tables* tables, const lng_readout* r
                         S(stream));
 }
 
+namespace {
+struct TreeLayout {
+  size_t ctx, rs, qa, u, mixed, total;
+};
+TreeLayout tree_layout(const lng_tables* t, const lng_readout* ro, int64_t B, int64_t n, int64_t W) {
+  const int64_t M = B * n, Dt = int64_t(t->n_orders) * t->memory_dim;
+  const size_t es = size_t(dtype_size(ro->act_dtype));
+  TreeLayout L{};
+  size_t off = 0;
+  L.ctx = off;   off += al256(size_t(M) * W * t->num_routes);
+  L.rs = off;    off += al256(size_t(M) * 4);
+  L.qa = off;    off += al256(size_t(M) * ro->num_heads * Dt * es);
+  L.u = off;     off += al256(size_t(M) * ro->num_heads * Dt * es);
+  L.mixed = off; off += al256(size_t(M) * ro->hidden * es);
+  L.total = off;
+  return L;
+}
+}  // namespace
+
+extern "C" size_t lng_tree_workspace_bytes(const lng_tables* tables, const lng_readout* ro, int64_t B, int64_t n,
+                                           int64_t W) {
+  if (!tables || !ro || B < 0 || n < 0 || W < 1) return 0;
+  return tree_layout(tables, ro, B, n, W).total;
+}
+
+extern "C" int lng_tree_memory_block(const lng_tables* tables, const lng_readout* ro, int64_t B, int64_t n, int64_t W,
+                                     int64_t L, int64_t h0, int64_t max_len, const void* h, const uint8_t* codes_new,
+                                     uint8_t* cache_codes, void* cache_conv, const int64_t* gidx, const uint8_t* gok,
+                                     const int32_t* seg, const int64_t* slot, const int64_t* new_slot, void* out,
+                                     void* workspace, size_t workspace_bytes, lng_stream_t stream) {
+  int st = check_tables(tables);
+  if (st) return st;
+  st = check_readout(ro);
+  if (st) return st;
+  LNG_REQUIRE(B >= 0 && n >= 0 && W >= 1 && L >= 0 && h0 >= 0 && h0 <= L && L + n <= max_len, "bad tree shape");
+  const int64_t M = B * n;
+  if (M == 0) return LNG_OK;
+  LNG_REQUIRE(h && codes_new && cache_codes && cache_conv && gidx && gok && seg && slot && new_slot && out && ro->w_qk &&
+                  ro->w_vo, "NULL pointer");
+  const TreeLayout Ly = tree_layout(tables, ro, B, n, W);
+  LNG_REQUIRE(workspace && workspace_bytes >= Ly.total, "workspace too small (see lng_tree_workspace_bytes)");
+  unsigned char* ws = static_cast<unsigned char*>(workspace);
+  const int64_t R = tables->num_routes, Dt = int64_t(tables->n_orders) * tables->memory_dim;
+  const int64_t QD = int64_t(ro->num_heads) * Dt;
+  const int act = ro->act_dtype;
+  cudaStream_t s = S(stream);
+  uint8_t* ctx = ws + Ly.ctx;
+  tree_windows_kernel<<<grid_for(M * (W + 1) * R, 256, 8), 256, 0, s>>>(codes_new, cache_codes, B, n, W, R, L, h0,
+                                                                        max_len, gidx, gok, ctx);
+  LNG_LAUNCHED("tree_windows_kernel");
+  float* rs = reinterpret_cast<float*>(ws + Ly.rs);
+  st = lng_rms_rows(h, act, M, ro->hidden, ro->eps, rs, stream);
+  if (st) return st;
+  void* qa = ws + Ly.qa;
+  st = lng_gemm(h, act, ro->hidden, ro->w_qk, act, ro->hidden, qa, act, QD, M, QD, ro->hidden, nullptr, 0, stream);
+  if (st) return st;
+  void* u = ws + Ly.u;
+  st = lng_route_attend(tables, ctx, LNG_U8, M, 0, W, nullptr, nullptr, seg, 0, 0, R, ro->num_heads, ro->eps,
+                        ro->sink_logit, qa, rs, u, act, 0, nullptr, nullptr, stream);
+  if (st) return st;
+  void* mixed = ws + Ly.mixed;
+  st = lng_gemm(u, act, QD, ro->w_vo, act, QD, mixed, act, ro->hidden, M, ro->hidden, QD, nullptr, 0, stream);
+  if (st) return st;
+  return lng_conv_window(ro, mixed, M, cache_conv, new_slot, slot, out, stream);
+}
+
 extern "C" int lng_attend_rescale(const float* m_local, const float* m_glob, float* l, float* u, int64_t M,
                                   int32_t num_heads, int64_t Dt, lng_stream_t stream) {
   LNG_REQUIRE(M >= 0 && num_heads > 0 && Dt > 0, "bad shape");

@@ -126,4 +126,30 @@ __global__ void packed_suffix_kernel(const CodeT* __restrict__ codes, int64_t B,
     for (int j = 0; j < maxn; ++j) window[(b * maxn + j) * R + r] = uint8_t((v >> (j * bits)) & amask);
 }
 
+// A tree's node windows: ctx[b, i, w, r] = gok[i, w] ? (gidx[i, w] < h0 ? the cached code at L - h0 + gidx
+// : the new code of node gidx - h0) : 0; and the nodes' new codes stored in the cache at L .. L+n-1 (slots
+// disjoint from the history read here, so one launch does both).
+__global__ void tree_windows_kernel(const uint8_t* __restrict__ codes_new, uint8_t* cache_codes, int64_t B, int64_t n,
+                                    int64_t W, int64_t R, int64_t L, int64_t h0, int64_t max_len,
+                                    const int64_t* __restrict__ gidx, const uint8_t* __restrict__ gok,
+                                    uint8_t* __restrict__ ctx) {
+  const int64_t nctx = B * n * W * R, nnew = B * n * R;
+  for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < nctx + nnew;
+       e += int64_t(gridDim.x) * blockDim.x) {
+    if (e < nctx) {
+      const int64_t r = e % R, w = (e / R) % W, i = (e / (R * W)) % n, b = e / (R * W * n);
+      uint8_t v = 0;
+      if (gok[i * W + w]) {
+        const int64_t g = gidx[i * W + w];
+        v = g < h0 ? cache_codes[(b * max_len + L - h0 + g) * R + r] : codes_new[(b * n + g - h0) * R + r];
+      }
+      ctx[e] = v;
+    } else {
+      const int64_t f = e - nctx, r = f % R, i = (f / R) % n, b = f / (R * n);
+      cache_codes[(b * max_len + L + i) * R + r] = codes_new[f];
+    }
+  }
+}
+
 }  // namespace lng
+

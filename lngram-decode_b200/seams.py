@@ -176,6 +176,7 @@ def _tree_plan(parent, L: int, B: int, max_len: int, hist: int, k: int, dil: int
     slot = torch.where(tslot[None] >= 0, base + tslot[None], torch.full_like(tslot[None], -1))
     new_slot = (torch.arange(B, device=device) * max_len)[:, None] + L + torch.arange(n, device=device)[None]
     plan = {"h0": h0, "gidx": gidx, "gok": gok[None, :, :, None].to(torch.uint8),
+            "gok_nw": gok.to(torch.uint8).contiguous(),
             "seg": gok.to(torch.int32)[None].expand(B, n, hist + 1).reshape(B * n, hist + 1).contiguous(),
             "slot": slot.reshape(B * n, k).contiguous(), "new_slot": new_slot.reshape(-1).contiguous()}
     if len(_TREE_PLANS) > 64:
@@ -197,15 +198,19 @@ def tree_memory_block(m, cache: MemoryCache, h: Tensor, codes: Tensor, parent) -
     hist = m.route_history_length
     k, dil = m.short_conv.kernel_size, m.short_conv.dilation
     plan = _tree_plan(parent, L, B, cache.max_len, hist, k, dil, h.device)
-    codes = codes.to(torch.uint8)
-    allc = torch.cat((cache.codes[:, L - plan["h0"]:L], codes), 1)
-    ctx = allc[:, plan["gidx"]] * plan["gok"]                            # [B, n, hist + 1, R]
+    codes = codes.to(device=h.device, dtype=torch.uint8).contiguous()
+    h = h.to(m._act()).contiguous()
     W = hist + 1
-    mixed = _readout(m, h, m.tables_desc(), ctx.reshape(B * n, W, -1).contiguous(), _lib.U8, B * n, 0, W,
-                     plan["seg"], 0)
-    cache.codes[:, L:L + n] = codes
-    out = _conv(m, mixed, cache, plan["new_slot"], plan["slot"])
-    return out.view(B, n, d)
+    # one library call: node windows (+ the nodes' codes into the cache), readout, conv window
+    tables, ro = m.tables_desc(), m.readout_desc()
+    lib = _lib.library()
+    ws = torch.empty(lib.lng_tree_workspace_bytes(tables, ro, B, n, W), device=h.device, dtype=torch.uint8)
+    out = torch.empty(B, n, d, device=h.device, dtype=h.dtype)
+    check(lib.lng_tree_memory_block(tables, ro, B, n, W, L, plan["h0"], cache.max_len, ptr(h), ptr(codes),
+                                    ptr(cache.codes), ptr(cache.conv_in), ptr(plan["gidx"]), ptr(plan["gok_nw"]),
+                                    ptr(plan["seg"]), ptr(plan["slot"]), ptr(plan["new_slot"]), ptr(out), ptr(ws),
+                                    ws.numel(), stream_ptr()), "tree memory block")
+    return out
 
 
 @torch.no_grad()

@@ -560,7 +560,7 @@ class RouteNgramMemoryV2(nn.Module):
             base = torch.arange(b, device=dev) * (lp + t)
             pos = lp + torch.arange(t, device=dev)
             new_slot = (base[:, None] + pos[None]).reshape(-1).contiguous()
-            lags = torch.tensor([(k - 1 - tap) * dil for tap in range(k)], device=dev)
+            lags = (k - 1 - torch.arange(k, device=dev)) * dil     # made on the device: no host copy
             slot = (base[:, None, None] + pos[None, :, None] - lags[None, None, :]).reshape(b * t, k).contiguous()
             out = torch.empty(b * t, d, dtype=act, device=dev)
             check(lib.lng_conv_window(self.readout_desc(), ptr(mixed), b * t, ptr(cache), ptr(new_slot), ptr(slot),

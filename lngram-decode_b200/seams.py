@@ -124,6 +124,12 @@ def _conv(m, mixed: Tensor, cache: MemoryCache, new_slot: Tensor, slot: Tensor) 
     return out
 
 
+def _conv_lags(k: int, dil: int, device) -> Tensor:
+    """Tap lags (k - 1 - tap) * dil, made on the device (a tensor built from a Python list would be a
+    host-to-device copy on every decode step)."""
+    return (k - 1 - torch.arange(k, device=device)) * dil
+
+
 @torch.no_grad()
 def memory_step(m, cache: MemoryCache, h: Tensor, codes_new: Tensor, route_codes_ctx: Tensor | None = None,
                 route_tokens: Tensor | None = None) -> Tensor:
@@ -148,7 +154,7 @@ def memory_step(m, cache: MemoryCache, h: Tensor, codes_new: Tensor, route_codes
     pos = L + torch.arange(n, device=dev)
     base = (torch.arange(B, device=dev) * cache.max_len)[:, None]
     new_slot = (base + pos[None, :]).reshape(-1).contiguous()
-    lags = torch.tensor([(k - 1 - tap) * dil for tap in range(k)], device=dev)
+    lags = _conv_lags(k, dil, dev)
     src = pos[:, None] - lags[None, :]                                    # [n, k]
     slot = torch.where(src[None] >= 0, base[:, :, None] + src[None], torch.full_like(src[None], -1))
     out = _conv(m, mixed, cache, new_slot, slot.reshape(B * n, k).contiguous())

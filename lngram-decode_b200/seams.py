@@ -38,11 +38,27 @@ class MemoryCache:
         self.length = length
 
 
+_ANCESTORS: dict = {}
+
+
 def ancestor_table(parent, depth: int, device=None) -> tuple[Tensor, Tensor]:
     """(anc, level) of a draft tree: anc[j, i] = the j-th ancestor of node i (anc[0] = i, -1 above
     the root) for j <= depth, and level[i] = the node's distance from the root.  Built on the device
-    by repeated gathers through the parent array (one gather per level), not per node."""
-    par = torch.as_tensor([int(x) for x in parent], dtype=torch.long, device=device)
+    by repeated gathers through the parent array (one gather per level), not per node, and kept per
+    (parent array, depth, device): a decode loop verifies the same tree shape step after step."""
+    key = (tuple(int(x) for x in parent), int(depth), str(device))
+    hit = _ANCESTORS.get(key)
+    if hit is not None:
+        return hit
+    res = _ancestor_table(key[0], depth, device)
+    if len(_ANCESTORS) > 64:
+        _ANCESTORS.clear()
+    _ANCESTORS[key] = res
+    return res
+
+
+def _ancestor_table(parent, depth: int, device) -> tuple[Tensor, Tensor]:
+    par = torch.as_tensor(parent, dtype=torch.long, device=device)
     n = par.numel()
     cur = torch.arange(n, dtype=torch.long, device=device)
     rows = [cur]

@@ -163,35 +163,46 @@ class RouteShardedMemory:
     def forward(self, h: Tensor, router_x: Tensor, chunks: int = 1) -> Tensor:
         """h, router_x [B, T, *] (the same on every rank) -> this rank's B / world sequences.
 
-        With ``chunks`` > 1 the batch is processed in that many groups of whole sequences, and each
-        group's reduce-scatter runs on NCCL's stream while the next group is gathered; the rank then
-        returns the r-th block of every group, in group order (chunks = 1: the r-th block of B)."""
+        With ``chunks`` > 1 the batch is processed in that many groups of whole sequences, pipelined:
+        a group's max all-reduce (on its own communicator) runs while the next group is gathered, its
+        reduce-scatter while the group after that is gathered; the rank then returns the r-th block of
+        every group, in group order (chunks = 1: the r-th block of B)."""
         B, T, d = h.shape
         if B % (self.world * chunks):
             raise ValueError("the batch must split into whole sequences per rank and chunk")
         Bc = B // chunks
-        outs, pending = [], None
-        for c in range(chunks):
-            hc, xc = h[c * Bc:(c + 1) * Bc], router_x[c * Bc:(c + 1) * Bc]
-            if self.packed:
-                mloc, pack = self.partial_packed(hc, xc)
-                mglob = all_reduce_max(mloc.clone(), self.group_m if self.group_m is not None else self.group)
-                self.rescale(mloc, mglob, pack)
+        multi = self.world > 1 and dist.is_initialized()
+        gm = self.group_m if self.group_m is not None else self.group
+        outs, staged, pending = [], None, None
+        for c in range(chunks + 1):
+            cur = None
+            if c < chunks:  # gather group c; start its max all-reduce
+                hc, xc = h[c * Bc:(c + 1) * Bc], router_x[c * Bc:(c + 1) * Bc]
+                state = self.partial_packed(hc, xc) if self.packed else self.partial(hc, xc)
+                mglob = state[0].clone()
+                work_m = dist.all_reduce(mglob, op=dist.ReduceOp.MAX, group=gm, async_op=True) if multi else None
+                cur = (state, mglob, work_m)
+            if staged is not None:  # group c - 1: rescale to the global offsets, start its reduce-scatter
+                state, mglob, work_m = staged
+                if work_m is not None:
+                    work_m.wait()  # the current stream waits for the maximum
+                if self.packed:
+                    mloc, pack = state
+                    self.rescale(mloc, mglob, pack)
+                else:
+                    mloc, lloc, u = state
+                    pack = self.pack(mloc, mglob, lloc, u)
                 pack = pack.view(Bc * T, -1)
-                del mloc, mglob
-            else:
-                mloc, lloc, u = self.partial(hc, xc)
-                mglob = all_reduce_max(mloc.clone(), self.group)
-                pack = self.pack(mloc, mglob, lloc, u).view(Bc * T, -1)
-                del mloc, lloc, u
-            if self.world > 1 and dist.is_initialized():
-                mine = torch.empty((Bc * T // self.world, pack.shape[1]), device=pack.device, dtype=pack.dtype)
-                work = dist.reduce_scatter_tensor(mine, pack, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
-            else:
-                mine, work = pack, None
-            if pending is not None:
-                outs.append(self._finish_pending(pending, T))
-            pending = (work, mine, pack)  # the pack stays referenced until its reduction is done
+                if multi:
+                    mine = torch.empty((Bc * T // self.world, pack.shape[1]), device=pack.device, dtype=pack.dtype)
+                    work = dist.reduce_scatter_tensor(mine, pack, op=dist.ReduceOp.SUM, group=self.group,
+                                                      async_op=True)
+                else:
+                    mine, work = pack, None
+                if pending is not None:
+                    outs.append(self._finish_pending(pending, T))
+                pending = (work, mine, pack)  # the pack stays referenced until its reduction is done
+            staged = cur
         outs.append(self._finish_pending(pending, T))
         return outs[0] if len(outs) == 1 else torch.cat(outs, 0)
 

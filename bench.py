@@ -856,6 +856,7 @@ def run_scaled(args, rank, world, local) -> dict:
     B, T, d = c["B"], c["T"], c["d"]
     # route x data grid: route_shards ranks split the routes of one layer copy and share a block of
     # sequences; the world / route_shards such groups split the batch (no exchange between groups)
+    chunks = int(getattr(args, "scaled_chunks", SCALED_CHUNKS))
     rs = int(getattr(args, "route_shards", SCALED_ROUTE_SHARDS)) or world
     rs = min(rs, world)
     if world % rs:
@@ -881,7 +882,7 @@ def run_scaled(args, rank, world, local) -> dict:
             mem(h, hn, out=out, workspace=ws)
     else:
         def step(i):
-            shard.forward(h, hn, chunks=SCALED_CHUNKS)
+            shard.forward(h, hn, chunks=chunks)
 
     with torch.no_grad(), ClockSampler(local) as clk:
         time.sleep(0.5)
@@ -940,7 +941,7 @@ def run_scaled(args, rank, world, local) -> dict:
                    "routes_per_gpu": Rl, "bits": c["bits"], "ngrams": list(c["ngrams"]), "mem_dim": c["mem_dim"],
                    "table_gb": round(table_gb, 1),
                    "parallelism": (f"route {rs} x data {place.data_shards}: route-sharded groups of {rs} GPUs (NCCL "
-                                   f"max all-reduce + bf16 reduce-scatter by sequence blocks, {SCALED_CHUNKS} "
+                                   f"max all-reduce + bf16 reduce-scatter by sequence blocks, {chunks} "
                                    f"overlapped groups), sequences split across the groups")
                                   if world > 1 else "single GPU (whole table)",
                    "l2": f"inputs larger than L2 ({table_gb:.0f} GB table, 1.07 GB h + h_norm)"},
@@ -1142,6 +1143,8 @@ def main(argv=None) -> int:
     ap.add_argument("--route-shards", type=int, default=SCALED_ROUTE_SHARDS,
                     help="scaled table at N > 1: GPUs per route-sharded group (the groups split the sequences; "
                     "0 = all N GPUs, the configuration's layout)")
+    ap.add_argument("--scaled-chunks", type=int, default=SCALED_CHUNKS,
+                    help="scaled table at N > 1: sequence groups pipelined through the route exchange")
     ap.add_argument("--no-extras", action="store_true", help="sb_prefill only: skip the SD-B / tree / scaled "
                     "sub-objects of the default line")
     args = ap.parse_args(argv)
